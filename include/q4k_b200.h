@@ -1,0 +1,229 @@
+/*
+ * q4k_b200 — C ABI of the B200 (sm_100a) Qwen3-4B Q4_K_M decode hot path.
+ *
+ * Plain pointers and sizes only. Device pointers are CUDA device addresses
+ * on the current device; `stream` is a cudaStream_t (NULL = legacy default
+ * stream, as the reference's kernels use). Every function returns a status:
+ *
+ *   Q4K_OK (0)        success
+ *   Q4K_EINVAL (1)    invalid argument   (the reference throws std::invalid_argument)
+ *   Q4K_ERANGE (2)    size/capacity out of range (std::out_of_range / std::length_error)
+ *   Q4K_ECUDA (3)     CUDA launch/runtime failure (std::runtime_error from check_launch)
+ *
+ * and q4k_last_error() returns the calling thread's last message. Kernels
+ * are asynchronous on `stream` unless stated otherwise; zero-size work
+ * returns Q4K_OK without launching (the reference's behaviour).
+ *
+ * Reference paths below are relative to the poytaytoy/Qwen3-4B-Q4_K_M-
+ * Inference-Engine source tree.
+ */
+#ifndef Q4K_B200_H
+#define Q4K_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define Q4K_OK 0
+#define Q4K_EINVAL 1
+#define Q4K_ERANGE 2
+#define Q4K_ECUDA 3
+
+/* GGML tensor type ids (the GGUF file's values). */
+#define Q4K_TYPE_F32 0
+#define Q4K_TYPE_F16 1
+#define Q4K_TYPE_Q4_K 12
+#define Q4K_TYPE_Q6_K 14
+
+/* Epilogues of q4k_matmul_ex. */
+#define Q4K_EPI_STORE 0  /* y = W x                                   */
+#define Q4K_EPI_ADD 1    /* y += W x (residual update)                */
+#define Q4K_EPI_SWIGLU 2 /* y = silu(W0 x) * (W1 x), two weights      */
+#define Q4K_EPI_ARGMAX 3 /* *token = argmax_n (W x)[n]; y optional    */
+
+const char* q4k_last_error(void);
+int q4k_abi_version(void);
+
+/* ---------------------------------------------------------------- weights */
+
+/* Device bytes of a tensor with ne0 inputs per row and ne1 rows in this
+ * library's device layout (Q4_K: GGUF rows verbatim; Q6_K: per-row planar
+ * re-layout of the same bytes; F32: as is). Replaces the size the
+ * reference's Weight computes from the GGUF tensor (src/Weight.cpp:53-61). */
+size_t q4k_weight_device_bytes(int type, int64_t ne0, int64_t ne1);
+
+/* Copies a tensor given in GGUF file layout (host memory) into `device`
+ * (q4k_weight_device_bytes(type, ne0, ne1) bytes, 16-byte aligned) in the
+ * device layout. Replaces Weight::Weight(const GGUF&, name) +
+ * DeviceBuffer(src, bytes) (src/Weight.cpp:6-23, :53-61); synchronises
+ * `stream` before returning, as DeviceBuffer does. */
+int q4k_weight_upload(int type, int64_t ne0, int64_t ne1, const void* host_gguf, void* device, void* stream);
+
+/* Deterministic synthetic tensor `name` (seed, GGUF layout) into host memory
+ * (ne1 * GGUF row bytes). Replaces GGUF::read_tensor_data for the model file
+ * the tests use (src/GGUF.cpp:131-145); no counterpart in the reference's
+ * arithmetic. */
+int q4k_synth_tensor_host(uint64_t seed, const char* name, int type, int64_t ne0, int64_t ne1, void* host_gguf);
+
+/* The same tensor generated on the device directly in the device layout. */
+int q4k_synth_tensor_device(uint64_t seed, const char* name, int type, int64_t ne0, int64_t ne1, void* device,
+                            void* stream);
+
+/* Elements [index_base, index_base + n) of the fp16 N(0,1) stream `name`
+ * (the KV-cache fill), and elements [0, n) of the fp32 N(0,1) stream
+ * `name` (synthetic activations), on the host or the device. */
+int q4k_synth_f16_host(uint64_t seed, const char* name, uint64_t index_base, size_t n, uint16_t* out);
+int q4k_synth_f32_host(uint64_t seed, const char* name, size_t n, float* out);
+int q4k_synth_f32_device(uint64_t seed, const char* name, size_t n, float* out, void* stream);
+
+/* ------------------------------------------------ kernels (Kernels.hpp) */
+
+/* kernels::rms_norm (include/Kernels.hpp:54-55, src/cuda/rms_norm.cu:30-39).
+ * `scale` is the F32 gamma of `width` floats. */
+int q4k_rms_norm(const float* input, const float* scale, float* output, size_t rows, size_t width, float epsilon,
+                 void* stream);
+
+/* kernels::matmul (include/Kernels.hpp:57-61, src/cuda/matmul.cu:130-166).
+ * weight: device layout of a Q4_K/Q6_K tensor, ne0 = K inputs (multiple of
+ * 256), ne1 = N output rows (only rows [0, ne1) are read). input [rows][K],
+ * output [rows][N]. The activation is quantised to Q8 in the kernel (no
+ * workspace), so concurrent calls on different streams are independent. */
+int q4k_matmul(const float* input, const void* weight, int type, int64_t ne0, int64_t ne1, float* output,
+               size_t rows, void* stream);
+
+/* kernels::rope (include/Kernels.hpp:63-64, src/cuda/rope.cu:32-39). */
+int q4k_rope(float* input, size_t tokens, size_t heads, size_t head_dim, size_t position_offset, float frequency_base,
+             void* stream);
+
+/* kernels::attention (include/Kernels.hpp:66-68, src/cuda/attention.cu:94-110):
+ * fp32 causal GQA, q/output [tokens][query_heads][head_dim], k/v
+ * [query_offset + tokens][kv_heads * head_dim], head_dim in [1, 256]. */
+int q4k_attention(const float* q, const float* k, const float* v, float* output, size_t tokens, size_t query_heads,
+                  size_t kv_heads, size_t head_dim, size_t query_offset, void* stream);
+
+/* kernels::residual_add (include/Kernels.hpp:70, src/cuda/residual_add.cu:15-20). */
+int q4k_residual_add(float* state, const float* branch, size_t count, void* stream);
+
+/* kernels::silu_multiply (include/Kernels.hpp:72, src/cuda/silu_multiply.cu:15-23). */
+int q4k_silu_multiply(const float* gate, const float* up, float* output, size_t count, void* stream);
+
+/* kernels::dequantize_embeddings (include/Kernels.hpp:74-75,
+ * src/cuda/embedding.cu:65-84): rows of GGUF-layout packed data (row_bytes
+ * apart) to fp32, bit-identical to the reference. */
+int q4k_dequantize_embeddings(const void* packed, float* output, size_t rows, size_t width, size_t row_bytes,
+                              int type, void* stream);
+
+/* kernels::argmax (include/Kernels.hpp:77, src/cuda/argmax.cu:72-98):
+ * largest logit, lowest index on ties; synchronises and writes *result on
+ * the host, as the reference does. */
+int q4k_argmax(const float* logits, size_t vocabulary_size, uint32_t* result, void* stream);
+
+/* ------------------------------------------ fused entry points (new) */
+
+/* Fused product over 1..4 weights sharing one activation (the reference
+ * issues one kernels::matmul per weight, src/Engine.cpp:83-85, :98-101).
+ * norm_gamma (optional, K floats): RMSNorm the input rows first
+ * (rms_norm.cu fused in). epilogue: Q4K_EPI_*. For SWIGLU pass two weights
+ * (gate, up) and one output; for ARGMAX one weight, rows == 1, outputs[0]
+ * optional logits, *token_device receives the index, and `scratch` must be
+ * q4k_matmul_argmax_scratch_bytes() bytes zeroed once before first use. */
+int q4k_matmul_ex(const float* input, const float* norm_gamma, float epsilon, int count, const void* const* weights,
+                  const int* types, const int64_t* out_rows, float* const* outputs, int64_t ne0, size_t rows,
+                  int epilogue, uint32_t* token_device, void* scratch, void* stream);
+size_t q4k_matmul_argmax_scratch_bytes(void);
+
+/* Decode attention for one token over an fp16 KV cache (new): fuses the
+ * per-head q/k RMSNorm (src/Engine.cpp:87-88), RoPE (:89-90), the K/V cache
+ * write and split-K attention (:92). qkv = [q | k | v] raw projections of
+ * the token; caches are [kv_heads][capacity][128] fp16 for one layer;
+ * *position_device is the token's position. head_dim must be 128 and
+ * query_heads == 4 * kv_heads. scratch: q4k_attention_decode_scratch_bytes
+ * bytes, zeroed once before first use. */
+int q4k_attention_decode_f16(const float* qkv, const float* q_gamma, const float* k_gamma, uint16_t* k_cache,
+                             uint16_t* v_cache, int capacity, const int* position_device, int query_heads,
+                             int kv_heads, int head_dim, float epsilon, float rope_base, float* output,
+                             void* scratch, void* stream);
+size_t q4k_attention_decode_scratch_bytes(int query_heads, int kv_heads);
+
+/* ------------------------------------------------------- decode engine */
+
+/* Replaces Engine / ChatSession (src/Engine.cpp:14-114,
+ * include/ChatSession.hpp:10-52) for the decode hot path: all weights and an
+ * fp16 KV cache resident on one GPU (or sharded over tp_world GPUs, one
+ * process each), the layer loop captured as one CUDA graph per step. */
+typedef struct q4k_engine q4k_engine;
+
+typedef struct {
+    int layers, hidden, heads, kv_heads, head_dim, ffn, vocab;
+    float eps, rope_base;
+    int capacity; /* KV-cache positions */
+    int tp_rank, tp_world;
+    int device;
+} q4k_engine_config;
+
+/* Qwen3-4B: 36 layers, 2560 hidden, 32/8 heads of 128, ffn 9728, vocab
+ * 151936, eps 1e-6, rope base 1e6. */
+void q4k_engine_config_qwen3_4b(q4k_engine_config* cfg, int capacity);
+
+/* Tensor i (0 <= i < 11*layers + 2) of the model: GGUF name, type and
+ * shape (ne0 inputs, ne1 rows) of the Q4_K_M synthetic model (Q6_K for
+ * attn_v, the ffn_down of even layers and token_embd). Returns Q4K_ERANGE
+ * past the end. */
+int q4k_model_tensor(const q4k_engine_config* cfg, int i, char* name, size_t name_len, int* type, int64_t* ne0,
+                     int64_t* ne1);
+
+/* Rows [n0, n1) and super-blocks [b0, b1) of tensor i that rank `rank` of
+ * `world` holds (Megatron-style: q/k/v/gate/up split by rows, attn_output
+ * and ffn_down by whole super-blocks of their inputs, norms and token_embd
+ * replicated). No reference counterpart: the reference runs on one GPU. */
+int q4k_tp_shard(const q4k_engine_config* cfg, int i, int rank, int world, int64_t* n0, int64_t* n1, int64_t* b0,
+                 int64_t* b1);
+
+/* nccl_id: 128 bytes from q4k_nccl_unique_id on rank 0, shared by the
+ * caller (NULL when tp_world == 1). */
+int q4k_nccl_unique_id(void* id128);
+int q4k_engine_create(const q4k_engine_config* cfg, const void* nccl_id, q4k_engine** out);
+int q4k_engine_destroy(q4k_engine* engine);
+
+/* Weights: all synthetic (device-generated, identical bytes to
+ * q4k_synth_tensor_host), or one tensor at a time from GGUF-layout host
+ * memory (this rank's shard is cut out here). */
+int q4k_engine_load_synthetic(q4k_engine* engine, uint64_t seed);
+int q4k_engine_set_tensor(q4k_engine* engine, const char* name, int type, int64_t ne0, int64_t ne1,
+                          const void* host_gguf);
+
+/* KV cache: positions [0, n) of every layer filled with fp16 N(0,1):
+ * element (head, pos, d) of layer L is element
+ * (head * 2^20 + pos) * 128 + d of stream "kv.{L}.k" / "kv.{L}.v"
+ * (q4k_synth_f16_host), heads counted over all kv_heads. read_kv copies one
+ * layer's [kv_heads/tp_world][capacity][128] K and V back to the host. */
+int q4k_engine_fill_kv_synthetic(q4k_engine* engine, uint64_t seed, int n);
+int q4k_engine_read_kv(q4k_engine* engine, int layer, uint16_t* k_host, uint16_t* v_host);
+
+/* One decode step (Engine::inference for one new token, src/Engine.cpp:37-114):
+ * embeds `token` at `position`, runs every layer and the output head, and
+ * returns the greedy next token. logits_host (vocab floats, this rank's
+ * shard when tp_world > 1; may be NULL) and hidden_host ((layers+1) * hidden
+ * floats: the residual stream after the embedding and after each layer; may
+ * be NULL, only with tp_world == 1) are optional. Synchronous. */
+int q4k_engine_decode(q4k_engine* engine, uint32_t token, int position, uint32_t* next_token, float* logits_host,
+                      float* hidden_host);
+
+/* `steps` greedy decode steps with the token fed back on the device; one
+ * graph launch per step and no host synchronisation between steps.
+ * advance != 0: position increases by one per step; advance == 0: every
+ * step decodes at `position` again (fixed context). tokens_host receives
+ * the `steps` generated tokens (may be NULL). Synchronous at the end. */
+int q4k_engine_generate(q4k_engine* engine, uint32_t token, int position, int steps, int advance,
+                        uint32_t* tokens_host);
+
+/* Stream the engine launches on (cudaStream_t), e.g. to time with events. */
+void* q4k_engine_stream(q4k_engine* engine);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,486 @@
+// The C ABI (include/q4k_b200.h): argument checks that mirror the
+// reference's (each cited), launches, and error-code translation.
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <cmath>
+#include <cstring>
+#include <limits>
+#include <string>
+#include <vector>
+
+#include "engine.h"
+#include "ops.h"
+#include "q4k_format.h"
+#include "q4k_internal.h"
+
+#define Q4K_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+thread_local std::string g_last_error;
+
+template <class F>
+int guarded(F&& f) {
+    try {
+        f();
+        return Q4K_OK;
+    } catch (const q4k::Error& e) {
+        g_last_error = e.what();
+        return e.status;
+    } catch (const std::bad_alloc&) {
+        g_last_error = "out of host memory";
+        return Q4K_ECUDA;
+    } catch (const std::exception& e) {
+        g_last_error = e.what();
+        return Q4K_ECUDA;
+    }
+}
+
+[[noreturn]] void invalid(const char* msg) { throw q4k::Error(Q4K_EINVAL, msg); }
+
+void launched(cudaError_t e) { q4k::cuda_check(e, "CUDA kernel launch failed"); }
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+bool quantised(int type) { return type == Q4K_TYPE_Q4_K || type == Q4K_TYPE_Q6_K; }
+
+void check_matrix(int type, int64_t ne0, int64_t ne1) {
+    // matmul.cu:132-136
+    if (!quantised(type)) invalid("matmul supports Q4_K and Q6_K weights only");
+    if (ne0 <= 0 || ne0 % 256 != 0 || ne1 <= 0 || ne0 > (1 << 24) || ne1 > (1 << 30))
+        invalid("Invalid matmul weight dimensions");
+}
+
+}  // namespace
+
+Q4K_API const char* q4k_last_error(void) { return g_last_error.c_str(); }
+
+Q4K_API int q4k_abi_version(void) { return 1; }
+
+Q4K_API size_t q4k_weight_device_bytes(int type, int64_t ne0, int64_t ne1) {
+    if (ne0 <= 0 || ne1 <= 0) return 0;
+    if (quantised(type) && ne0 % 256) return 0;
+    return (size_t)ne1 * q4k_device_row_bytes(type, (size_t)ne0);
+}
+
+Q4K_API int q4k_weight_upload(int type, int64_t ne0, int64_t ne1, const void* host_gguf, void* device, void* stream) {
+    return guarded([&] {
+        if (type == Q4K_TYPE_F32) {
+            if (ne0 <= 0 || ne1 <= 0 || !host_gguf || !device) invalid("invalid F32 tensor");
+            q4k::cuda_check(cudaMemcpyAsync(device, host_gguf, sizeof(float) * ne0 * ne1, cudaMemcpyHostToDevice,
+                                            as_stream(stream)),
+                            "upload");
+            q4k::cuda_check(cudaStreamSynchronize(as_stream(stream)), "upload");
+            return;
+        }
+        check_matrix(type, ne0, ne1);
+        if (!host_gguf || !device || reinterpret_cast<uintptr_t>(device) % 16)
+            invalid("upload needs host data and a 16-byte aligned device buffer");
+        const size_t raw = (size_t)ne1 * q4k_gguf_row_bytes(type, (size_t)ne0);
+        void* tmp = nullptr;
+        q4k::cuda_check(cudaMallocAsync(&tmp, raw, as_stream(stream)), "cudaMallocAsync");
+        cudaError_t e = cudaMemcpyAsync(tmp, host_gguf, raw, cudaMemcpyHostToDevice, as_stream(stream));
+        if (e == cudaSuccess)
+            e = q4k::relayout(tmp, type, (size_t)ne0, 0, (size_t)ne1, 0, (size_t)ne0 / 256, device, as_stream(stream));
+        cudaFreeAsync(tmp, as_stream(stream));
+        if (e == cudaSuccess) e = cudaStreamSynchronize(as_stream(stream));
+        q4k::cuda_check(e, "Host-to-device copy failed");
+    });
+}
+
+Q4K_API int q4k_synth_tensor_host(uint64_t seed, const char* name, int type, int64_t ne0, int64_t ne1,
+                                  void* host_gguf) {
+    return guarded([&] {
+        if (!name || !host_gguf || ne0 <= 0 || ne1 <= 0) invalid("invalid synthetic tensor request");
+        const uint64_t key = q4k_tensor_key(seed, name);
+        uint8_t* out = static_cast<uint8_t*>(host_gguf);
+        if (type == Q4K_TYPE_F32) {
+            float* f = static_cast<float*>(host_gguf);
+            for (int64_t i = 0; i < ne0 * ne1; ++i) f[i] = q4k_synth_gamma(key, (uint64_t)i);
+        } else if (type == Q4K_TYPE_Q4_K || type == Q4K_TYPE_Q6_K) {
+            if (ne0 % 256) invalid("quantised rows must hold whole super-blocks");
+            const int64_t blocks = ne1 * (ne0 / 256);
+            for (int64_t b = 0; b < blocks; ++b) {
+                if (type == Q4K_TYPE_Q4_K)
+                    q4k_synth_q4k_block(key, (uint64_t)b, out + b * Q4K_Q4_BLOCK);
+                else
+                    q4k_synth_q6k_block(key, (uint64_t)b, out + b * Q4K_Q6_BLOCK);
+            }
+        } else {
+            invalid("unsupported synthetic tensor type");
+        }
+    });
+}
+
+Q4K_API int q4k_synth_tensor_device(uint64_t seed, const char* name, int type, int64_t ne0, int64_t ne1, void* device,
+                                    void* stream) {
+    return guarded([&] {
+        if (!name || !device || ne0 <= 0 || ne1 <= 0) invalid("invalid synthetic tensor request");
+        const uint64_t key = q4k_tensor_key(seed, name);
+        cudaStream_t s = as_stream(stream);
+        if (type == Q4K_TYPE_F32) {
+            launched(q4k::synth_gamma(key, static_cast<float*>(device), (size_t)(ne0 * ne1), s));
+            return;
+        }
+        check_matrix(type, ne0, ne1);
+        const size_t raw = (size_t)ne1 * q4k_gguf_row_bytes(type, (size_t)ne0);
+        void* tmp = nullptr;
+        q4k::cuda_check(cudaMallocAsync(&tmp, raw, s), "cudaMallocAsync");
+        cudaError_t e = q4k::synth_raw(key, type, (size_t)ne0, (size_t)ne1, tmp, s);
+        if (e == cudaSuccess) e = q4k::relayout(tmp, type, (size_t)ne0, 0, (size_t)ne1, 0, (size_t)ne0 / 256, device, s);
+        cudaFreeAsync(tmp, s);
+        launched(e);
+    });
+}
+
+// Elements [index_base, index_base + n) of the fp16 N(0,1) stream `name`.
+Q4K_API int q4k_synth_f16_host(uint64_t seed, const char* name, uint64_t index_base, size_t n, uint16_t* out) {
+    return guarded([&] {
+        if (!name || (!out && n)) invalid("invalid synthetic request");
+        const uint64_t key = q4k_tensor_key(seed, name);
+        for (size_t i = 0; i < n; ++i) out[i] = q4k_synth_f16(key, index_base + i);
+    });
+}
+
+// Elements [0, n) of the fp32 N(0,1) stream `name` (synthetic activations).
+Q4K_API int q4k_synth_f32_host(uint64_t seed, const char* name, size_t n, float* out) {
+    return guarded([&] {
+        if (!name || (!out && n)) invalid("invalid synthetic request");
+        const uint64_t key = q4k_tensor_key(seed, name);
+        for (size_t i = 0; i < n; ++i) out[i] = q4k_synth_f32(key, i);
+    });
+}
+
+Q4K_API int q4k_synth_f32_device(uint64_t seed, const char* name, size_t n, float* out, void* stream) {
+    return guarded([&] {
+        if (!name || (!out && n)) invalid("invalid synthetic request");
+        if (n) launched(q4k::synth_f32(q4k_tensor_key(seed, name), out, n, as_stream(stream)));
+    });
+}
+
+Q4K_API int q4k_rms_norm(const float* input, const float* scale, float* output, size_t rows, size_t width,
+                         float epsilon, void* stream) {
+    return guarded([&] {
+        if (rows == 0) return;
+        // rms_norm.cu:34-36
+        if (width == 0 || !(epsilon > 0.0f) || !scale || !input || !output)
+            invalid("RMSNorm requires an F32 scale matching the row width and positive epsilon");
+        launched(q4k::rms_norm(input, scale, output, rows, width, epsilon, as_stream(stream)));
+    });
+}
+
+Q4K_API int q4k_matmul(const float* input, const void* weight, int type, int64_t ne0, int64_t ne1, float* output,
+                       size_t rows, void* stream) {
+    return guarded([&] {
+        check_matrix(type, ne0, ne1);
+        if (rows == 0) return;
+        if (!input || !weight || !output) invalid("matmul requires device buffers");
+        if (reinterpret_cast<uintptr_t>(input) % 16 || reinterpret_cast<uintptr_t>(weight) % 16)
+            invalid("matmul input and weight must be 16-byte aligned");
+        if (rows > (size_t)std::numeric_limits<int>::max() / 8) invalid("too many rows");
+        q4k::GemvRequest r;
+        r.nseg = 1;
+        r.seg[0] = {static_cast<const uint8_t*>(weight), output, type, (int)ne1};
+        r.K = (int)ne0;
+        r.M = (int)rows;
+        r.x = input;
+        r.ldy = (int)ne1;
+        r.epilogue = q4k::EPI_STORE;
+        launched(q4k::launch_gemv(r, as_stream(stream)));
+    });
+}
+
+Q4K_API int q4k_rope(float* input, size_t tokens, size_t heads, size_t head_dim, size_t position_offset,
+                     float frequency_base, void* stream) {
+    return guarded([&] {
+        if (tokens == 0) return;
+        // rope.cu:34-35
+        if (heads == 0 || head_dim == 0 || head_dim % 2 != 0 || !(frequency_base > 0.0f))
+            invalid("RoPE requires heads, an even head dimension and a positive frequency base");
+        if (!input) invalid("RoPE requires a buffer");
+        launched(q4k::rope(input, tokens, heads, head_dim, position_offset, frequency_base, as_stream(stream)));
+    });
+}
+
+Q4K_API int q4k_attention(const float* q, const float* k, const float* v, float* output, size_t tokens,
+                          size_t query_heads, size_t kv_heads, size_t head_dim, size_t query_offset, void* stream) {
+    return guarded([&] {
+        if (tokens == 0) return;
+        // attention.cu:98-105
+        if (!q || !k || !v || !output || kv_heads == 0 || query_heads == 0 || query_heads % kv_heads != 0 ||
+            head_dim == 0 || head_dim > 256 ||
+            tokens > static_cast<size_t>(std::numeric_limits<int>::max()) / query_heads ||
+            tokens > std::numeric_limits<size_t>::max() / query_heads / head_dim / sizeof(float))
+            invalid("Attention requires valid buffers, divisible Q/KV heads and head_dim in [1, 256]");
+        const size_t max_cached = std::numeric_limits<size_t>::max() / kv_heads / head_dim / sizeof(float);
+        if (tokens > max_cached || query_offset > max_cached - tokens) invalid("Attention cache dimensions overflow");
+        launched(q4k::attention_f32(q, k, v, output, tokens, query_heads, kv_heads, head_dim, query_offset,
+                                    as_stream(stream)));
+    });
+}
+
+Q4K_API int q4k_residual_add(float* state, const float* branch, size_t count, void* stream) {
+    return guarded([&] {
+        if (count == 0) return;
+        if (!state || !branch) invalid("residual_add requires buffers");
+        launched(q4k::residual_add(state, branch, count, as_stream(stream)));
+    });
+}
+
+Q4K_API int q4k_silu_multiply(const float* gate, const float* up, float* output, size_t count, void* stream) {
+    return guarded([&] {
+        if (count == 0) return;
+        if (!gate || !up || !output) invalid("silu_multiply requires buffers");
+        launched(q4k::silu_multiply(gate, up, output, count, as_stream(stream)));
+    });
+}
+
+Q4K_API int q4k_dequantize_embeddings(const void* packed, float* output, size_t rows, size_t width, size_t row_bytes,
+                                      int type, void* stream) {
+    return guarded([&] {
+        if (rows == 0) return;
+        // embedding.cu:69-70
+        if (!quantised(type)) invalid("Unsupported embedding storage type");
+        if (!packed || !output || width == 0 || width % 256 ||
+            row_bytes < q4k_gguf_row_bytes(type, width))
+            invalid("dequantize_embeddings requires whole super-blocks per row");
+        launched(q4k::dequantize_raw(packed, output, rows, width, row_bytes, type, as_stream(stream)));
+    });
+}
+
+Q4K_API int q4k_argmax(const float* logits, size_t vocabulary_size, uint32_t* result, void* stream) {
+    return guarded([&] {
+        // argmax.cu:73-74
+        if (!logits || vocabulary_size == 0 || vocabulary_size > UINT32_MAX || !result)
+            invalid("Invalid argmax input");
+        cudaStream_t s = as_stream(stream);
+        const size_t scratch_bytes = q4k::argmax_scratch_bytes() + 64;
+        void* scratch = nullptr;
+        q4k::cuda_check(cudaMallocAsync(&scratch, scratch_bytes, s), "cudaMallocAsync");
+        uint32_t* dev_result = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(scratch) + q4k::argmax_scratch_bytes());
+        cudaError_t e = cudaMemsetAsync(scratch, 0, 256, s);
+        if (e == cudaSuccess) e = q4k::argmax(logits, vocabulary_size, dev_result, scratch, s);
+        uint32_t host = 0;
+        if (e == cudaSuccess) e = cudaMemcpyAsync(&host, dev_result, sizeof host, cudaMemcpyDeviceToHost, s);
+        cudaFreeAsync(scratch, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        q4k::cuda_check(e, "CUDA argmax failed");
+        *result = host;
+    });
+}
+
+Q4K_API size_t q4k_matmul_argmax_scratch_bytes(void) { return 256 + 1024 * 8; }
+
+Q4K_API int q4k_matmul_ex(const float* input, const float* norm_gamma, float epsilon, int count,
+                          const void* const* weights, const int* types, const int64_t* out_rows, float* const* outputs,
+                          int64_t ne0, size_t rows, int epilogue, uint32_t* token_device, void* scratch,
+                          void* stream) {
+    return guarded([&] {
+        if (count < 1 || count > q4k::kMaxSegments || !weights || !types || !out_rows || !outputs)
+            invalid("matmul_ex needs 1..4 weights");
+        if (epilogue < Q4K_EPI_STORE || epilogue > Q4K_EPI_ARGMAX) invalid("unknown epilogue");
+        if (rows == 0) return;
+        if (!input || reinterpret_cast<uintptr_t>(input) % 16) invalid("input must be a 16-byte aligned buffer");
+        if (norm_gamma && !(epsilon > 0.0f)) invalid("RMSNorm requires a positive epsilon");
+        q4k::GemvRequest r;
+        r.nseg = count;
+        for (int i = 0; i < count; ++i) {
+            check_matrix(types[i], ne0, out_rows[i]);
+            if (!weights[i] || reinterpret_cast<uintptr_t>(weights[i]) % 16) invalid("weights must be 16-byte aligned");
+            float* y = epilogue == Q4K_EPI_SWIGLU ? outputs[0] : outputs[i];
+            if (!y && epilogue != Q4K_EPI_ARGMAX) invalid("missing output buffer");
+            r.seg[i] = {static_cast<const uint8_t*>(weights[i]), y, types[i], (int)out_rows[i]};
+        }
+        if (epilogue == Q4K_EPI_SWIGLU && (count != 2 || out_rows[0] != out_rows[1] || types[0] != types[1]))
+            invalid("SWIGLU needs two weights of the same type and shape");
+        if (epilogue == Q4K_EPI_ARGMAX) {
+            if (count != 1 || rows != 1 || !token_device || !scratch) invalid("ARGMAX needs one weight, one row");
+            uint8_t* sb = static_cast<uint8_t*>(scratch);
+            r.argmax.counter = reinterpret_cast<unsigned*>(sb);
+            r.argmax.cand_score = reinterpret_cast<float*>(sb + 256);
+            r.argmax.cand_index = reinterpret_cast<uint32_t*>(sb + 256 + 1024 * 4);
+            r.argmax.token = token_device;
+        }
+        if (epilogue != Q4K_EPI_ARGMAX && count > 1 && epilogue != Q4K_EPI_SWIGLU) {
+            // independent outputs per weight: each [rows][out_rows[i]] when rows == 1
+            if (rows != 1) invalid("several weights with separate outputs need rows == 1");
+        }
+        r.K = (int)ne0;
+        r.M = (int)rows;
+        r.x = input;
+        r.gamma = norm_gamma;
+        r.eps = epsilon;
+        r.ldy = (int)out_rows[0];
+        r.epilogue = epilogue;
+        launched(q4k::launch_gemv(r, as_stream(stream)));
+    });
+}
+
+Q4K_API size_t q4k_attention_decode_scratch_bytes(int query_heads, int kv_heads) {
+    if (kv_heads <= 0 || query_heads <= 0) return 0;
+    const int splits = q4k::decode_attention_splits(kv_heads);
+    return 256 + sizeof(float) * (size_t)query_heads * splits * (q4k::kDecodeHeadDim + 2);
+}
+
+Q4K_API int q4k_attention_decode_f16(const float* qkv, const float* q_gamma, const float* k_gamma, uint16_t* k_cache,
+                                     uint16_t* v_cache, int capacity, const int* position_device, int query_heads,
+                                     int kv_heads, int head_dim, float epsilon, float rope_base, float* output,
+                                     void* scratch, void* stream) {
+    return guarded([&] {
+        if (!qkv || !q_gamma || !k_gamma || !k_cache || !v_cache || !position_device || !output || !scratch)
+            invalid("decode attention requires device buffers");
+        if (head_dim != q4k::kDecodeHeadDim || kv_heads <= 0 || query_heads != 4 * kv_heads || capacity <= 0)
+            invalid("decode attention supports head_dim 128 with 4 query heads per KV head");
+        if (!(epsilon > 0.0f) || !(rope_base > 0.0f)) invalid("epsilon and rope base must be positive");
+        if (reinterpret_cast<uintptr_t>(k_cache) % 16 || reinterpret_cast<uintptr_t>(v_cache) % 16)
+            invalid("KV caches must be 16-byte aligned");
+        const int splits = q4k::decode_attention_splits(kv_heads);
+        uint8_t* sb = static_cast<uint8_t*>(scratch);
+        q4k::DecodeAttnArgs a;
+        a.qkv = qkv;
+        a.q_gamma = q_gamma;
+        a.k_gamma = k_gamma;
+        a.k_cache = k_cache;
+        a.v_cache = v_cache;
+        a.capacity = capacity;
+        a.position = position_device;
+        a.heads = query_heads;
+        a.kv_heads = kv_heads;
+        a.eps = epsilon;
+        a.rope_base = rope_base;
+        a.counters = reinterpret_cast<unsigned*>(sb);
+        a.partial_ml = reinterpret_cast<float*>(sb + 256);
+        a.partial_o = a.partial_ml + (size_t)query_heads * splits * 2;
+        a.out = output;
+        a.err = nullptr;
+        a.splits = splits;
+        launched(q4k::decode_attention(a, as_stream(stream), false));
+    });
+}
+
+// ---------------------------------------------------------------- engine
+
+struct q4k_engine {
+    q4k::Engine impl;
+    q4k_engine(const q4k_engine_config& c, const void* id) : impl(c, id) {}
+};
+
+Q4K_API void q4k_engine_config_qwen3_4b(q4k_engine_config* c, int capacity) {
+    if (!c) return;
+    std::memset(c, 0, sizeof *c);
+    c->layers = 36;
+    c->hidden = 2560;
+    c->heads = 32;
+    c->kv_heads = 8;
+    c->head_dim = 128;
+    c->ffn = 9728;
+    c->vocab = 151936;
+    c->eps = 1e-6f;
+    c->rope_base = 1000000.0f;
+    c->capacity = capacity;
+    c->tp_rank = 0;
+    c->tp_world = 1;
+    c->device = 0;
+}
+
+Q4K_API int q4k_model_tensor(const q4k_engine_config* cfg, int i, char* name, size_t name_len, int* type,
+                             int64_t* ne0, int64_t* ne1) {
+    return guarded([&] {
+        if (!cfg) invalid("config required");
+        const auto specs = q4k::model_tensors(*cfg);
+        if (i < 0 || (size_t)i >= specs.size()) throw q4k::Error(Q4K_ERANGE, "tensor index out of range");
+        const auto& t = specs[i];
+        if (name && name_len) {
+            std::strncpy(name, t.name.c_str(), name_len - 1);
+            name[name_len - 1] = 0;
+        }
+        if (type) *type = t.type;
+        if (ne0) *ne0 = t.ne0;
+        if (ne1) *ne1 = t.ne1;
+    });
+}
+
+Q4K_API int q4k_tp_shard(const q4k_engine_config* cfg, int i, int rank, int world, int64_t* n0, int64_t* n1,
+                         int64_t* b0, int64_t* b1) {
+    return guarded([&] {
+        if (!cfg || world < 1 || rank < 0 || rank >= world || !n0 || !n1 || !b0 || !b1) invalid("bad shard request");
+        const auto specs = q4k::model_tensors(*cfg);
+        if (i < 0 || (size_t)i >= specs.size()) throw q4k::Error(Q4K_ERANGE, "tensor index out of range");
+        const auto s = q4k::tp_slice(*cfg, specs[i], rank, world);
+        *n0 = s.n0;
+        *n1 = s.n1;
+        *b0 = s.b0;
+        *b1 = s.b1;
+    });
+}
+
+Q4K_API int q4k_nccl_unique_id(void* id128) {
+    return guarded([&] {
+        if (!id128) invalid("buffer required");
+        ncclUniqueId id;
+        const ncclResult_t r = ncclGetUniqueId(&id);
+        if (r != ncclSuccess) throw q4k::Error(Q4K_ECUDA, std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+        static_assert(sizeof id == 128, "NCCL unique id is 128 bytes");
+        std::memcpy(id128, &id, sizeof id);
+    });
+}
+
+Q4K_API int q4k_engine_create(const q4k_engine_config* cfg, const void* nccl_id, q4k_engine** out) {
+    return guarded([&] {
+        if (!cfg || !out) invalid("config and output required");
+        *out = nullptr;
+        *out = new q4k_engine(*cfg, nccl_id);
+    });
+}
+
+Q4K_API int q4k_engine_destroy(q4k_engine* e) {
+    return guarded([&] { delete e; });
+}
+
+Q4K_API int q4k_engine_load_synthetic(q4k_engine* e, uint64_t seed) {
+    return guarded([&] {
+        if (!e) invalid("engine required");
+        e->impl.load_synthetic(seed);
+    });
+}
+
+Q4K_API int q4k_engine_set_tensor(q4k_engine* e, const char* name, int type, int64_t ne0, int64_t ne1,
+                                  const void* host_gguf) {
+    return guarded([&] {
+        if (!e || !name || !host_gguf) invalid("engine, name and data required");
+        e->impl.set_tensor(name, type, ne0, ne1, host_gguf);
+    });
+}
+
+Q4K_API int q4k_engine_fill_kv_synthetic(q4k_engine* e, uint64_t seed, int n) {
+    return guarded([&] {
+        if (!e) invalid("engine required");
+        e->impl.fill_kv_synthetic(seed, n);
+    });
+}
+
+Q4K_API int q4k_engine_read_kv(q4k_engine* e, int layer, uint16_t* k_host, uint16_t* v_host) {
+    return guarded([&] {
+        if (!e) invalid("engine required");
+        e->impl.read_kv(layer, k_host, v_host);
+    });
+}
+
+Q4K_API int q4k_engine_decode(q4k_engine* e, uint32_t token, int position, uint32_t* next_token, float* logits_host,
+                              float* hidden_host) {
+    return guarded([&] {
+        if (!e || !next_token) invalid("engine and output required");
+        *next_token = e->impl.decode(token, position, logits_host, hidden_host);
+    });
+}
+
+Q4K_API int q4k_engine_generate(q4k_engine* e, uint32_t token, int position, int steps, int advance,
+                                uint32_t* tokens_host) {
+    return guarded([&] {
+        if (!e) invalid("engine required");
+        e->impl.generate(token, position, steps, advance, tokens_host);
+    });
+}
+
+Q4K_API void* q4k_engine_stream(q4k_engine* e) { return e ? static_cast<void*>(e->impl.stream()) : nullptr; }

@@ -1,0 +1,576 @@
+// Qwen3 decode engine (replaces Engine::inference / ChatSession of the
+// reference for one new token per step: src/Engine.cpp:37-114,
+// include/ChatSession.hpp:10-52).
+//
+// Per step, on one stream, captured once as a CUDA graph:
+//   embed            token row of token_embd -> x            (EmbedLookup.cpp:49-78)
+//   per layer:
+//     gemv  QKV      rmsnorm(x, attn_norm) -> q|k|v          (Engine.cpp:82-85)
+//     attention      q/k norm + RoPE + KV write + split-K     (Engine.cpp:87-92)
+//     gemv  O        x += W_o att                            (Engine.cpp:94-95)
+//     gemv  gate/up  act = silu(W_g n) * (W_u n), n = rmsnorm(x, ffn_norm)  (:97-100)
+//     gemv  down     x += W_d act                            (Engine.cpp:101-102)
+//   gemv  head       rmsnorm(x, output_norm), W_embd, argmax (Engine.cpp:105-111)
+//   finish           record the token, advance the position
+// Every kernel after the first is launched with programmatic stream
+// serialisation, so each product's weight stream starts while its
+// predecessor drains. With tp_world > 1 the projections are sharded
+// Megatron-style and the row-parallel outputs are summed with NCCL.
+#include "engine.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+
+#include "ops.h"
+#include "q4k_device.cuh"
+#include "q4k_internal.h"
+
+namespace q4k {
+
+void cuda_check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw Error(Q4K_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+static void nccl_check(ncclResult_t r, const char* what) {
+    if (r != ncclSuccess) throw Error(Q4K_ECUDA, std::string(what) + ": " + ncclGetErrorString(r));
+}
+
+namespace {
+
+constexpr uint64_t kKvIndexStride = 1ull << 20;  // positions per head in the KV generator's index space
+
+const char* const kSlotNames[11] = {"attn_norm", "attn_q",     "attn_k",   "attn_v",   "attn_q_norm", "attn_k_norm",
+                                    "attn_output", "ffn_norm", "ffn_gate", "ffn_up",   "ffn_down"};
+
+__global__ void finish_step_kernel(uint32_t* token, int* pos, const int* advance, uint32_t* history,
+                                   unsigned* history_n, unsigned history_cap, const uint32_t* tp_cand, int world) {
+    pdl_wait();
+    if (threadIdx.x != 0) return;
+    if (tp_cand) {
+        // Greedy choice over the shards (argmax.cu ordering): larger logit,
+        // then lower index.
+        float bs = __uint_as_float(tp_cand[0]);
+        uint32_t bi = tp_cand[1];
+        for (int r = 1; r < world; ++r) {
+            const float s = __uint_as_float(tp_cand[2 * r]);
+            const uint32_t i = tp_cand[2 * r + 1];
+            if (candidate_better(s, i, bs, bi)) {
+                bs = s;
+                bi = i;
+            }
+        }
+        *token = bi;
+    }
+    const unsigned n = *history_n;
+    if (n < history_cap) history[n] = *token;
+    *history_n = n + 1;
+    *pos += *advance;
+}
+
+}  // namespace
+
+std::vector<TensorSpec> model_tensors(const q4k_engine_config& c) {
+    std::vector<TensorSpec> out;
+    char buf[96];
+    for (int i = 0; i < c.layers; ++i) {
+        for (int s = 0; s < 11; ++s) {
+            std::snprintf(buf, sizeof buf, "blk.%d.%s.weight", i, kSlotNames[s]);
+            TensorSpec t;
+            t.name = buf;
+            t.layer = i;
+            t.slot = s;
+            const int64_t qd = (int64_t)c.heads * c.head_dim, kvd = (int64_t)c.kv_heads * c.head_dim;
+            switch (s) {
+                case 0: case 7: t.type = Q4K_TYPE_F32; t.ne0 = c.hidden; t.ne1 = 1; break;
+                case 4: case 5: t.type = Q4K_TYPE_F32; t.ne0 = c.head_dim; t.ne1 = 1; break;
+                case 1: t.type = Q4K_TYPE_Q4_K; t.ne0 = c.hidden; t.ne1 = qd; break;
+                case 2: t.type = Q4K_TYPE_Q4_K; t.ne0 = c.hidden; t.ne1 = kvd; break;
+                case 3: t.type = Q4K_TYPE_Q6_K; t.ne0 = c.hidden; t.ne1 = kvd; break;
+                case 6: t.type = Q4K_TYPE_Q4_K; t.ne0 = qd; t.ne1 = c.hidden; break;
+                case 8: case 9: t.type = Q4K_TYPE_Q4_K; t.ne0 = c.hidden; t.ne1 = c.ffn; break;
+                case 10: t.type = (i % 2 == 0) ? Q4K_TYPE_Q6_K : Q4K_TYPE_Q4_K; t.ne0 = c.ffn; t.ne1 = c.hidden; break;
+            }
+            out.push_back(t);
+        }
+    }
+    TensorSpec on;
+    on.name = "output_norm.weight";
+    on.type = Q4K_TYPE_F32;
+    on.ne0 = c.hidden;
+    on.ne1 = 1;
+    on.slot = 0;
+    out.push_back(on);
+    TensorSpec te;
+    te.name = "token_embd.weight";
+    te.type = Q4K_TYPE_Q6_K;
+    te.ne0 = c.hidden;
+    te.ne1 = c.vocab;
+    te.slot = 1;
+    out.push_back(te);
+    return out;
+}
+
+// Megatron-style sharding (column-parallel q/k/v/gate/up, row-parallel
+// attn_output/ffn_down on whole super-blocks, replicated norms and
+// token_embd; the output head's vocab rows are split in enqueue_step).
+TensorSlice tp_slice(const q4k_engine_config& c, const TensorSpec& t, int rank, int world) {
+    const int64_t nb = t.ne0 / 256;
+    TensorSlice s{0, t.ne1, 0, nb};
+    if (t.layer < 0 || world <= 1) return s;
+    const int64_t qd = (int64_t)c.heads / world * c.head_dim, kvd = (int64_t)c.kv_heads / world * c.head_dim;
+    const int64_t fb = c.ffn / 256, f0 = fb * rank / world, f1 = fb * (rank + 1) / world;
+    switch (t.slot) {
+        case 1: s.n0 = rank * qd; s.n1 = s.n0 + qd; break;
+        case 2: case 3: s.n0 = rank * kvd; s.n1 = s.n0 + kvd; break;
+        case 6: s.b0 = rank * qd / 256; s.b1 = s.b0 + qd / 256; break;
+        case 8: case 9: s.n0 = f0 * 256; s.n1 = f1 * 256; break;
+        case 10: s.b0 = f0; s.b1 = f1; break;
+        default: break;
+    }
+    return s;
+}
+
+Engine::Engine(const q4k_engine_config& cfg, const void* nccl_id) : c_(cfg) {
+    const auto& c = c_;
+    if (c.layers <= 0 || c.hidden <= 0 || c.hidden % 256 || c.heads <= 0 || c.kv_heads <= 0 ||
+        c.head_dim != kDecodeHeadDim || c.heads != 4 * c.kv_heads || c.ffn <= 0 || c.ffn % 256 || c.vocab <= 0 ||
+        c.capacity <= 0 || !(c.eps > 0.0f) || !(c.rope_base > 0.0f))
+        throw Error(Q4K_EINVAL, "unsupported engine configuration (head_dim must be 128 and heads = 4 * kv_heads)");
+    world_ = c.tp_world > 0 ? c.tp_world : 1;
+    rank_ = c.tp_rank;
+    if (rank_ < 0 || rank_ >= world_ || c.kv_heads % world_)
+        throw Error(Q4K_EINVAL, "tp_world must divide kv_heads and 0 <= tp_rank < tp_world");
+    Hl_ = c.heads / world_;
+    KVHl_ = c.kv_heads / world_;
+    qd_ = Hl_ * c.head_dim;
+    kvd_ = KVHl_ * c.head_dim;
+    const int64_t fb = c.ffn / 256;
+    ffn_b0_ = fb * rank_ / world_;
+    ffn_b1_ = fb * (rank_ + 1) / world_;
+    ffn_l_ = (int)((ffn_b1_ - ffn_b0_) * 256);
+    vocab0_ = (int64_t)c.vocab * rank_ / world_;
+    vocab1_ = (int64_t)c.vocab * (rank_ + 1) / world_;
+    if (ffn_l_ <= 0 || qd_ % 256) throw Error(Q4K_EINVAL, "tensor-parallel shards must hold whole super-blocks");
+
+    cuda_check(cudaSetDevice(c.device), "cudaSetDevice");
+    cuda_check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+    if (world_ > 1) {
+        if (!nccl_id) throw Error(Q4K_EINVAL, "tp_world > 1 needs an NCCL unique id");
+        ncclUniqueId id;
+        std::memcpy(&id, nccl_id, sizeof id);
+        nccl_check(ncclCommInitRank(&comm_, world_, id, rank_), "ncclCommInitRank");
+    }
+
+    layers_.resize(c.layers);
+    have_.assign(11 * (size_t)c.layers + 2, false);
+    splits_ = decode_attention_splits(KVHl_);
+    const int H = c.hidden;
+    x_ = static_cast<float*>(alloc(sizeof(float) * H));
+    qkv_ = static_cast<float*>(alloc(sizeof(float) * (qd_ + 2 * kvd_)));
+    att_ = static_cast<float*>(alloc(sizeof(float) * qd_));
+    act_ = static_cast<float*>(alloc(sizeof(float) * ffn_l_));
+    partial_ = static_cast<float*>(alloc(sizeof(float) * H));
+    logits_ = static_cast<float*>(alloc(sizeof(float) * (vocab1_ - vocab0_)));
+    hidden_ = static_cast<float*>(alloc(sizeof(float) * H * (c.layers + 1)));
+    token_ = static_cast<uint32_t*>(alloc(64));
+    pos_ = static_cast<int*>(alloc(64));
+    advance_ = static_cast<int*>(alloc(64));
+    err_ = static_cast<int*>(alloc(64));
+    history_ = static_cast<uint32_t*>(alloc(sizeof(uint32_t) * (size_t)c.capacity));
+    history_n_ = static_cast<unsigned*>(alloc(64));
+    const size_t kv_elems = (size_t)c.layers * KVHl_ * c.capacity * c.head_dim;
+    kcache_ = static_cast<uint16_t*>(alloc(kv_elems * 2));
+    vcache_ = static_cast<uint16_t*>(alloc(kv_elems * 2));
+    attn_part_o_ = static_cast<float*>(alloc(sizeof(float) * (size_t)Hl_ * splits_ * c.head_dim));
+    attn_part_ml_ = static_cast<float*>(alloc(sizeof(float) * (size_t)Hl_ * splits_ * 2));
+    attn_counters_ = static_cast<unsigned*>(alloc(sizeof(unsigned) * KVHl_));
+    am_score_ = static_cast<float*>(alloc(sizeof(float) * 1024));
+    am_index_ = static_cast<uint32_t*>(alloc(sizeof(uint32_t) * 1024));
+    am_counter_ = static_cast<unsigned*>(alloc(64));
+    tp_cand_local_ = static_cast<float*>(alloc(64));
+    tp_cand_all_ = static_cast<float*>(alloc(sizeof(float) * 2 * world_ + 64));
+    cuda_check(cudaMallocHost(&host_io_, 64), "cudaMallocHost");
+    cuda_check(cudaStreamSynchronize(stream_), "init");
+}
+
+Engine::~Engine() {
+    if (exec_) cudaGraphExecDestroy(exec_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    if (comm_) ncclCommDestroy(comm_);
+    for (void* p : allocations_) cudaFree(p);
+    if (host_io_) cudaFreeHost(host_io_);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+void* Engine::alloc(size_t bytes) {
+    void* p = nullptr;
+    cuda_check(cudaMalloc(&p, std::max<size_t>(bytes, 256)), "cudaMalloc");
+    allocations_.push_back(p);
+    cuda_check(cudaMemsetAsync(p, 0, std::max<size_t>(bytes, 256), stream_), "cudaMemset");
+    return p;
+}
+
+Engine::Slice Engine::shard_of(const TensorSpec& t) const { return tp_slice(c_, t, rank_, world_); }
+
+void** Engine::tensor_slot(const TensorSpec& t, int** type_slot) {
+    *type_slot = nullptr;
+    if (t.layer < 0) {
+        if (t.slot == 0) return reinterpret_cast<void**>(&output_norm_);
+        *type_slot = &t_embd_;
+        return reinterpret_cast<void**>(&token_embd_);
+    }
+    Layer& L = layers_[t.layer];
+    switch (t.slot) {
+        case 0: return reinterpret_cast<void**>(&L.attn_norm);
+        case 1: *type_slot = &L.tq; return reinterpret_cast<void**>(&L.q);
+        case 2: *type_slot = &L.tk; return reinterpret_cast<void**>(&L.k);
+        case 3: *type_slot = &L.tv; return reinterpret_cast<void**>(&L.v);
+        case 4: return reinterpret_cast<void**>(&L.q_norm);
+        case 5: return reinterpret_cast<void**>(&L.k_norm);
+        case 6: *type_slot = &L.to; return reinterpret_cast<void**>(&L.o);
+        case 7: return reinterpret_cast<void**>(&L.ffn_norm);
+        case 8: *type_slot = &L.tgate; return reinterpret_cast<void**>(&L.gate);
+        case 9: *type_slot = &L.tup; return reinterpret_cast<void**>(&L.up);
+        default: *type_slot = &L.tdown; return reinterpret_cast<void**>(&L.down);
+    }
+}
+
+// raw_device: the full tensor in GGUF layout on the device (F32: the values).
+void Engine::place(const TensorSpec& t, const void* raw_device) {
+    int* type_slot = nullptr;
+    void** slot = tensor_slot(t, &type_slot);
+    if (t.type == Q4K_TYPE_F32) {
+        if (!*slot) *slot = alloc(sizeof(float) * t.ne0 * t.ne1);
+        cuda_check(cudaMemcpyAsync(*slot, raw_device, sizeof(float) * t.ne0 * t.ne1, cudaMemcpyDeviceToDevice,
+                                   stream_),
+                   "copy tensor");
+    } else {
+        const Slice s = shard_of(t);
+        const size_t bytes = (size_t)(s.n1 - s.n0) * q4k_device_row_bytes(t.type, (size_t)(s.b1 - s.b0) * 256);
+        *slot = alloc(bytes);
+        *type_slot = t.type;
+        cuda_check(relayout(raw_device, t.type, (size_t)t.ne0, (size_t)s.n0, (size_t)s.n1, (size_t)s.b0,
+                            (size_t)s.b1, *slot, stream_),
+                   "relayout");
+    }
+}
+
+void Engine::load_synthetic(uint64_t seed) {
+    const auto specs = model_tensors(c_);
+    size_t max_raw = 0;
+    for (const auto& t : specs) max_raw = std::max(max_raw, (size_t)t.ne1 * q4k_gguf_row_bytes(t.type, t.ne0));
+    void* tmp = nullptr;
+    cuda_check(cudaMalloc(&tmp, max_raw), "cudaMalloc");
+    try {
+        for (size_t i = 0; i < specs.size(); ++i) {
+            const auto& t = specs[i];
+            const uint64_t key = q4k_tensor_key(seed, t.name.c_str());
+            if (t.type == Q4K_TYPE_F32)
+                cuda_check(synth_gamma(key, static_cast<float*>(tmp), (size_t)t.ne0 * t.ne1, stream_), "synth");
+            else
+                cuda_check(synth_raw(key, t.type, (size_t)t.ne0, (size_t)t.ne1, tmp, stream_), "synth");
+            place(t, tmp);
+            have_[i] = true;
+        }
+        cuda_check(cudaStreamSynchronize(stream_), "load_synthetic");
+    } catch (...) {
+        cudaStreamSynchronize(stream_);
+        cudaFree(tmp);
+        throw;
+    }
+    cudaFree(tmp);
+    loaded_ = true;
+}
+
+void Engine::set_tensor(const std::string& name, int type, int64_t ne0, int64_t ne1, const void* host_gguf) {
+    const auto specs = model_tensors(c_);
+    size_t idx = specs.size();
+    for (size_t i = 0; i < specs.size(); ++i)
+        if (specs[i].name == name) idx = i;
+    if (idx == specs.size()) throw Error(Q4K_EINVAL, "unknown tensor " + name);
+    const auto& t = specs[idx];
+    if (t.ne0 != ne0 || t.ne1 != ne1) throw Error(Q4K_EINVAL, "tensor " + name + " has the wrong shape");
+    if (type != t.type && !(t.slot == 10 && t.layer >= 0 && (type == Q4K_TYPE_Q4_K || type == Q4K_TYPE_Q6_K)))
+        throw Error(Q4K_EINVAL, "tensor " + name + " has an unsupported type");
+    TensorSpec ts = t;
+    ts.type = type;
+    const size_t bytes = (size_t)ne1 * q4k_gguf_row_bytes(type, ne0);
+    void* tmp = nullptr;
+    cuda_check(cudaMalloc(&tmp, bytes), "cudaMalloc");
+    cudaError_t e = cudaMemcpyAsync(tmp, host_gguf, bytes, cudaMemcpyHostToDevice, stream_);
+    if (e == cudaSuccess) {
+        try {
+            place(ts, tmp);
+        } catch (...) {
+            cudaStreamSynchronize(stream_);
+            cudaFree(tmp);
+            throw;
+        }
+        e = cudaStreamSynchronize(stream_);
+    }
+    cudaFree(tmp);
+    cuda_check(e, "set_tensor");
+    have_[idx] = true;
+    loaded_ = std::all_of(have_.begin(), have_.end(), [](bool b) { return b; });
+    if (exec_) {
+        cudaGraphExecDestroy(exec_);
+        exec_ = nullptr;
+    }
+}
+
+void Engine::fill_kv_synthetic(uint64_t seed, int n) {
+    if (n < 0 || n > c_.capacity) throw Error(Q4K_ERANGE, "KV fill beyond capacity");
+    char name[64];
+    for (int L = 0; L < c_.layers; ++L) {
+        for (int kv = 0; kv < 2; ++kv) {
+            std::snprintf(name, sizeof name, "kv.%d.%c", L, kv ? 'v' : 'k');
+            const uint64_t key = q4k_tensor_key(seed, name);
+            uint16_t* base = (kv ? vcache_ : kcache_) + (size_t)L * KVHl_ * c_.capacity * c_.head_dim;
+            for (int h = 0; h < KVHl_; ++h) {
+                const uint64_t hg = (uint64_t)rank_ * KVHl_ + h;
+                cuda_check(synth_f16(key, base + (size_t)h * c_.capacity * c_.head_dim, (size_t)n * c_.head_dim,
+                                     hg * kKvIndexStride * c_.head_dim, stream_),
+                           "synth kv");
+            }
+        }
+    }
+    cuda_check(cudaStreamSynchronize(stream_), "fill_kv");
+}
+
+void Engine::read_kv(int layer, uint16_t* k_host, uint16_t* v_host) {
+    if (layer < 0 || layer >= c_.layers) throw Error(Q4K_ERANGE, "layer out of range");
+    const size_t n = (size_t)KVHl_ * c_.capacity * c_.head_dim;
+    if (k_host)
+        cuda_check(cudaMemcpyAsync(k_host, kcache_ + (size_t)layer * n, n * 2, cudaMemcpyDeviceToHost, stream_), "read");
+    if (v_host)
+        cuda_check(cudaMemcpyAsync(v_host, vcache_ + (size_t)layer * n, n * 2, cudaMemcpyDeviceToHost, stream_), "read");
+    cuda_check(cudaStreamSynchronize(stream_), "read_kv");
+}
+
+void Engine::enqueue_step(bool record_hidden) {
+    const auto& c = c_;
+    const int H = c.hidden;
+    auto gemv = [&](GemvRequest& r) { cuda_check(launch_gemv(r, stream_), "gemv launch"); };
+    auto snapshot = [&](int i) {
+        if (record_hidden)
+            cuda_check(cudaMemcpyAsync(hidden_ + (size_t)i * H, x_, sizeof(float) * H, cudaMemcpyDeviceToDevice,
+                                       stream_),
+                       "snapshot");
+    };
+    auto all_reduce_into_x = [&]() {
+        nccl_check(ncclAllReduce(partial_, partial_, H, ncclFloat, ncclSum, comm_, stream_), "ncclAllReduce");
+        cuda_check(residual_add(x_, partial_, H, stream_), "residual_add");
+    };
+
+    cuda_check(embed_rows(token_embd_, t_embd_, H, c.vocab, token_, 1, x_, err_, stream_, false), "embed");
+    snapshot(0);
+    for (int i = 0; i < c.layers; ++i) {
+        const Layer& L = layers_[i];
+        const size_t kv_layer = (size_t)i * KVHl_ * c.capacity * c.head_dim;
+        {
+            GemvRequest r;
+            r.nseg = 3;
+            r.seg[0] = {L.q, qkv_, L.tq, qd_};
+            r.seg[1] = {L.k, qkv_ + qd_, L.tk, kvd_};
+            r.seg[2] = {L.v, qkv_ + qd_ + kvd_, L.tv, kvd_};
+            r.K = H;
+            r.x = x_;
+            r.gamma = L.attn_norm;
+            r.eps = c.eps;
+            r.epilogue = EPI_STORE;
+            r.err = err_;
+            r.pdl = true;
+            gemv(r);
+        }
+        {
+            DecodeAttnArgs a;
+            a.qkv = qkv_;
+            a.q_gamma = L.q_norm;
+            a.k_gamma = L.k_norm;
+            a.k_cache = kcache_ + kv_layer;
+            a.v_cache = vcache_ + kv_layer;
+            a.capacity = c.capacity;
+            a.position = pos_;
+            a.heads = Hl_;
+            a.kv_heads = KVHl_;
+            a.eps = c.eps;
+            a.rope_base = c.rope_base;
+            a.partial_o = attn_part_o_;
+            a.partial_ml = attn_part_ml_;
+            a.counters = attn_counters_;
+            a.out = att_;
+            a.err = err_;
+            a.splits = splits_;
+            cuda_check(decode_attention(a, stream_, true), "attention launch");
+        }
+        {
+            GemvRequest r;
+            r.nseg = 1;
+            r.seg[0] = {L.o, world_ > 1 ? partial_ : x_, L.to, H};
+            r.K = qd_;
+            r.x = att_;
+            r.epilogue = world_ > 1 ? EPI_STORE : EPI_ADD;
+            r.err = err_;
+            r.pdl = true;
+            gemv(r);
+            if (world_ > 1) all_reduce_into_x();
+        }
+        {
+            GemvRequest r;
+            r.nseg = 2;
+            r.seg[0] = {L.gate, act_, L.tgate, ffn_l_};
+            r.seg[1] = {L.up, act_, L.tup, ffn_l_};
+            r.K = H;
+            r.x = x_;
+            r.gamma = L.ffn_norm;
+            r.eps = c.eps;
+            r.epilogue = EPI_SWIGLU;
+            r.err = err_;
+            r.pdl = true;
+            gemv(r);
+        }
+        {
+            GemvRequest r;
+            r.nseg = 1;
+            r.seg[0] = {L.down, world_ > 1 ? partial_ : x_, L.tdown, H};
+            r.K = ffn_l_;
+            r.x = act_;
+            r.epilogue = world_ > 1 ? EPI_STORE : EPI_ADD;
+            r.err = err_;
+            r.pdl = true;
+            gemv(r);
+            if (world_ > 1) all_reduce_into_x();
+        }
+        snapshot(i + 1);
+    }
+    {
+        GemvRequest r;
+        r.nseg = 1;
+        const size_t row_bytes = q4k_device_row_bytes(t_embd_, H);
+        r.seg[0] = {token_embd_ + (size_t)vocab0_ * row_bytes, logits_, t_embd_, (int)(vocab1_ - vocab0_)};
+        r.K = H;
+        r.x = x_;
+        r.gamma = output_norm_;
+        r.eps = c.eps;
+        r.epilogue = EPI_ARGMAX;
+        r.argmax.cand_score = am_score_;
+        r.argmax.cand_index = am_index_;
+        r.argmax.counter = am_counter_;
+        r.argmax.index_base = (uint32_t)vocab0_;
+        if (world_ > 1) {
+            r.argmax.token = reinterpret_cast<uint32_t*>(tp_cand_local_) + 1;
+            r.argmax.score = tp_cand_local_;
+        } else {
+            r.argmax.token = token_;
+        }
+        r.err = err_;
+        r.pdl = true;
+        gemv(r);
+    }
+    if (world_ > 1)
+        nccl_check(ncclAllGather(tp_cand_local_, tp_cand_all_, 2, ncclUint32, comm_, stream_), "ncclAllGather");
+    {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(1);
+        cfg.blockDim = dim3(32);
+        cfg.stream = stream_;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cuda_check(cudaLaunchKernelEx(&cfg, finish_step_kernel, token_, pos_, (const int*)advance_, history_,
+                                      history_n_, (unsigned)c.capacity,
+                                      world_ > 1 ? reinterpret_cast<const uint32_t*>(tp_cand_all_) : nullptr, world_),
+                   "finish launch");
+    }
+}
+
+void Engine::ensure_graph() {
+    if (exec_) return;
+    cudaGraph_t graph = nullptr;
+    cuda_check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "begin capture");
+    try {
+        enqueue_step(false);
+    } catch (...) {
+        cudaStreamEndCapture(stream_, &graph);
+        if (graph) cudaGraphDestroy(graph);
+        throw;
+    }
+    cuda_check(cudaStreamEndCapture(stream_, &graph), "end capture");
+    const cudaError_t e = cudaGraphInstantiate(&exec_, graph, 0);
+    cudaGraphDestroy(graph);
+    cuda_check(e, "graph instantiate");
+}
+
+void Engine::check_device_error() {
+    int err = 0;
+    cuda_check(cudaMemcpyAsync(&host_io_[3], err_, sizeof(int), cudaMemcpyDeviceToHost, stream_), "read err");
+    cuda_check(cudaStreamSynchronize(stream_), "step");
+    err = (int)host_io_[3];
+    if (err) {
+        cudaMemsetAsync(err_, 0, sizeof(int), stream_);
+        cudaStreamSynchronize(stream_);
+        char msg[96];
+        std::snprintf(msg, sizeof msg, "device reported error bits 0x%x", err);
+        throw Error((err & (ERR_BAD_POSITION | ERR_BAD_TOKEN)) ? Q4K_ERANGE : Q4K_ECUDA, msg);
+    }
+}
+
+uint32_t Engine::decode(uint32_t token, int position, float* logits_host, float* hidden_host) {
+    if (!loaded_) throw Error(Q4K_EINVAL, "weights are not loaded");
+    if (token >= (uint32_t)c_.vocab) throw Error(Q4K_ERANGE, "Token ID out of range");
+    if (position < 0 || position >= c_.capacity) throw Error(Q4K_ERANGE, "KV cache capacity exceeded");
+    if (hidden_host && world_ > 1) throw Error(Q4K_EINVAL, "hidden snapshots need tp_world == 1");
+    host_io_[0] = token;
+    host_io_[1] = (uint32_t)position;
+    host_io_[2] = 0;
+    cuda_check(cudaMemcpyAsync(token_, &host_io_[0], 4, cudaMemcpyHostToDevice, stream_), "h2d");
+    cuda_check(cudaMemcpyAsync(pos_, &host_io_[1], 4, cudaMemcpyHostToDevice, stream_), "h2d");
+    cuda_check(cudaMemcpyAsync(advance_, &host_io_[2], 4, cudaMemcpyHostToDevice, stream_), "h2d");
+    cuda_check(cudaMemsetAsync(history_n_, 0, 4, stream_), "memset");
+    if (hidden_host) {
+        enqueue_step(true);
+    } else {
+        ensure_graph();
+        cuda_check(cudaGraphLaunch(exec_, stream_), "graph launch");
+    }
+    cuda_check(cudaMemcpyAsync(&host_io_[4], token_, 4, cudaMemcpyDeviceToHost, stream_), "d2h");
+    if (logits_host)
+        cuda_check(cudaMemcpyAsync(logits_host, logits_, sizeof(float) * (vocab1_ - vocab0_), cudaMemcpyDeviceToHost,
+                                   stream_),
+                   "d2h logits");
+    if (hidden_host)
+        cuda_check(cudaMemcpyAsync(hidden_host, hidden_, sizeof(float) * c_.hidden * (c_.layers + 1),
+                                   cudaMemcpyDeviceToHost, stream_),
+                   "d2h hidden");
+    check_device_error();
+    return host_io_[4];
+}
+
+void Engine::generate(uint32_t token, int position, int steps, int advance, uint32_t* tokens_host) {
+    if (!loaded_) throw Error(Q4K_EINVAL, "weights are not loaded");
+    if (token >= (uint32_t)c_.vocab) throw Error(Q4K_ERANGE, "Token ID out of range");
+    if (steps < 0 || steps > c_.capacity) throw Error(Q4K_ERANGE, "too many steps");
+    const long long last = (long long)position + (advance ? (long long)steps - 1 : 0);
+    if (position < 0 || last >= c_.capacity) throw Error(Q4K_ERANGE, "KV cache capacity exceeded");
+    if (steps == 0) return;
+    ensure_graph();
+    host_io_[0] = token;
+    host_io_[1] = (uint32_t)position;
+    host_io_[2] = advance ? 1u : 0u;
+    cuda_check(cudaMemcpyAsync(token_, &host_io_[0], 4, cudaMemcpyHostToDevice, stream_), "h2d");
+    cuda_check(cudaMemcpyAsync(pos_, &host_io_[1], 4, cudaMemcpyHostToDevice, stream_), "h2d");
+    cuda_check(cudaMemcpyAsync(advance_, &host_io_[2], 4, cudaMemcpyHostToDevice, stream_), "h2d");
+    cuda_check(cudaMemsetAsync(history_n_, 0, 4, stream_), "memset");
+    for (int s = 0; s < steps; ++s) cuda_check(cudaGraphLaunch(exec_, stream_), "graph launch");
+    if (tokens_host)
+        cuda_check(cudaMemcpyAsync(tokens_host, history_, sizeof(uint32_t) * steps, cudaMemcpyDeviceToHost, stream_),
+                   "d2h tokens");
+    check_device_error();
+}
+
+}  // namespace q4k

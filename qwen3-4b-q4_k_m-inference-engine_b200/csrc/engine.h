@@ -1,0 +1,111 @@
+// Decode engine: resident weights, fp16 KV cache, one CUDA graph per step,
+// optional tensor parallelism over NCCL (one process per GPU).
+#pragma once
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/q4k_b200.h"
+
+namespace q4k {
+
+// Errors carry the C-ABI status they map to.
+struct Error : std::runtime_error {
+    int status;
+    Error(int s, const std::string& m) : std::runtime_error(m), status(s) {}
+};
+
+void cuda_check(cudaError_t e, const char* what);
+
+struct TensorSpec {
+    std::string name;
+    int type = 0;
+    int64_t ne0 = 0, ne1 = 0;
+    int layer = -1;  // -1: global tensor
+    int slot = 0;    // 0..10 per layer; 0: output_norm, 1: token_embd for globals
+};
+
+// The synthetic Q4_K_M model's tensor list (q4k_model_tensor).
+std::vector<TensorSpec> model_tensors(const q4k_engine_config& c);
+
+// Part of a GGUF tensor that tensor-parallel rank `rank` of `world` holds:
+// rows [n0, n1) and super-blocks [b0, b1) of every row.
+struct TensorSlice {
+    int64_t n0, n1, b0, b1;
+};
+TensorSlice tp_slice(const q4k_engine_config& c, const TensorSpec& t, int rank, int world);
+
+class Engine {
+public:
+    Engine(const q4k_engine_config& cfg, const void* nccl_id);
+    ~Engine();
+    Engine(const Engine&) = delete;
+    Engine& operator=(const Engine&) = delete;
+
+    void load_synthetic(uint64_t seed);
+    void set_tensor(const std::string& name, int type, int64_t ne0, int64_t ne1, const void* host_gguf);
+    void fill_kv_synthetic(uint64_t seed, int n);
+    void read_kv(int layer, uint16_t* k_host, uint16_t* v_host);
+    uint32_t decode(uint32_t token, int position, float* logits_host, float* hidden_host);
+    void generate(uint32_t token, int position, int steps, int advance, uint32_t* tokens_host);
+    cudaStream_t stream() const { return stream_; }
+
+private:
+    struct Layer {
+        float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *ffn_norm = nullptr;
+        uint8_t *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr, *gate = nullptr, *up = nullptr, *down = nullptr;
+        int tq = 0, tk = 0, tv = 0, to = 0, tgate = 0, tup = 0, tdown = 0;
+    };
+    using Slice = TensorSlice;
+
+    void* alloc(size_t bytes);
+    Slice shard_of(const TensorSpec& t) const;
+    void** tensor_slot(const TensorSpec& t, int** type_slot);
+    void place(const TensorSpec& t, const void* raw_device);
+    void enqueue_step(bool record_hidden);
+    void check_device_error();
+    void ensure_graph();
+
+    q4k_engine_config c_;
+    int rank_ = 0, world_ = 1;
+    int Hl_ = 0, KVHl_ = 0, qd_ = 0, kvd_ = 0;
+    int64_t ffn_b0_ = 0, ffn_b1_ = 0;
+    int ffn_l_ = 0;
+    int64_t vocab0_ = 0, vocab1_ = 0;
+    int splits_ = 1;
+    bool loaded_ = false;
+    std::vector<bool> have_;
+
+    cudaStream_t stream_ = nullptr;
+    ncclComm_t comm_ = nullptr;
+    std::vector<void*> allocations_;
+    std::vector<Layer> layers_;
+    float* output_norm_ = nullptr;
+    uint8_t* token_embd_ = nullptr;
+    int t_embd_ = 0;
+
+    float *x_ = nullptr, *qkv_ = nullptr, *att_ = nullptr, *act_ = nullptr, *partial_ = nullptr,
+          *logits_ = nullptr, *hidden_ = nullptr;
+    uint32_t* token_ = nullptr;     // device: token to embed (and the step's result)
+    int* pos_ = nullptr;            // device: position of the token
+    int* advance_ = nullptr;        // device: position increment per step
+    uint32_t* history_ = nullptr;   // device: generated tokens
+    unsigned* history_n_ = nullptr; // device: count
+    int* err_ = nullptr;
+    uint16_t *kcache_ = nullptr, *vcache_ = nullptr;
+    float *attn_part_o_ = nullptr, *attn_part_ml_ = nullptr;
+    unsigned* attn_counters_ = nullptr;
+    float* am_score_ = nullptr;
+    uint32_t* am_index_ = nullptr;
+    unsigned* am_counter_ = nullptr;
+    float* tp_cand_local_ = nullptr;  // [2] score, index (as float bits)
+    float* tp_cand_all_ = nullptr;    // [2 * world]
+    uint32_t* host_io_ = nullptr;     // pinned: token, position, result
+
+    cudaGraphExec_t exec_ = nullptr;
+};
+
+}  // namespace q4k

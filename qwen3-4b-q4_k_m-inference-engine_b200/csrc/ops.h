@@ -1,0 +1,59 @@
+// Launchers for the non-GEMV kernels (ops.cu, attention_decode.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "q4k_internal.h"
+
+namespace q4k {
+
+cudaError_t rms_norm(const float* x, const float* gamma, float* y, size_t rows, size_t width, float eps,
+                     cudaStream_t s);
+cudaError_t rope(float* x, size_t tokens, size_t heads, size_t head_dim, size_t pos, float base, cudaStream_t s);
+cudaError_t attention_f32(const float* q, const float* k, const float* v, float* out, size_t tokens, size_t heads,
+                          size_t kv_heads, size_t head_dim, size_t offset, cudaStream_t s);
+cudaError_t residual_add(float* state, const float* branch, size_t count, cudaStream_t s);
+cudaError_t silu_multiply(const float* gate, const float* up, float* out, size_t count, cudaStream_t s);
+cudaError_t dequantize_raw(const void* packed, float* out, size_t rows, size_t width, size_t row_bytes, int type,
+                           cudaStream_t s);
+cudaError_t embed_rows(const void* table, int type, size_t width, size_t vocab, const uint32_t* tokens, size_t count,
+                       float* out, int* err, cudaStream_t s, bool pdl);
+size_t argmax_scratch_bytes();
+cudaError_t argmax(const float* logits, size_t count, uint32_t* result, void* scratch, cudaStream_t s);
+// Rows [n0, n1), super-blocks [b0, b1) of a GGUF-layout matrix with K_full
+// inputs into the device layout (Q4_K verbatim, Q6_K planar).
+cudaError_t relayout(const void* raw, int type, size_t K_full, size_t n0, size_t n1, size_t b0, size_t b1,
+                     void* out, cudaStream_t s);
+// Synthetic quantised matrix in GGUF layout (q4k_format.h generator).
+cudaError_t synth_raw(uint64_t key, int type, size_t K, size_t N, void* out, cudaStream_t s);
+cudaError_t synth_gamma(uint64_t key, float* out, size_t n, cudaStream_t s);
+cudaError_t synth_f32(uint64_t key, float* out, size_t n, cudaStream_t s);
+cudaError_t synth_f16(uint64_t key, uint16_t* out, size_t n, size_t index_base, cudaStream_t s);
+
+// Split-K flash-decode attention over an fp16 KV cache for one new token,
+// with the per-head QK RMSNorm and RoPE of that token fused in, and the new
+// K/V row written into the cache (attention_decode.cu).
+struct DecodeAttnArgs {
+    const float* qkv;          // [H*D | KVH*D | KVH*D] raw projections of the new token
+    const float* q_gamma;      // [D]
+    const float* k_gamma;      // [D]
+    uint16_t* k_cache;         // [KVH][capacity][D] fp16 (this layer)
+    uint16_t* v_cache;         // [KVH][capacity][D] fp16
+    int capacity;
+    const int* position;       // device scalar: index of the new token
+    int heads, kv_heads;       // head_dim is 128
+    float eps, rope_base;
+    float* partial_o;          // [KVH][splits][G][D]
+    float* partial_ml;         // [KVH][splits][G][2]
+    unsigned* counters;        // [KVH], zero before the first launch; reset by the kernel
+    float* out;                // [H*D] attended output
+    int* err;
+    int splits;                // CTAs per KV head
+};
+constexpr int kDecodeHeadDim = 128;
+int decode_attention_splits(int kv_heads);
+size_t decode_attention_scratch_floats(int heads, int kv_heads, int splits);
+cudaError_t decode_attention(const DecodeAttnArgs& a, cudaStream_t s, bool pdl);
+
+}  // namespace q4k

@@ -1,0 +1,60 @@
+// Internal launch interfaces shared by the library's translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace q4k {
+
+// ---------------------------------------------------------------------------
+// Quantised matrix-vector / small-batch matrix product.
+// ---------------------------------------------------------------------------
+enum Epilogue : int {
+    EPI_STORE = 0,   // y[m][n] = dot
+    EPI_ADD = 1,     // y[m][n] += dot            (residual stream update)
+    EPI_SWIGLU = 2,  // y[m][n] = silu(gate) * up (segments 0 and 1 paired row by row)
+    EPI_ARGMAX = 3,  // greedy token over all rows (M == 1), optional logits in y
+};
+
+constexpr int kMaxSegments = 4;
+
+struct GemvSegment {
+    const uint8_t* w = nullptr;  // rows in the device layout (q4k_format.h)
+    float* y = nullptr;          // output of this segment: y[m * ldy + n]
+    int type = 0;                // Q4K_TYPE_Q4_K or Q4K_TYPE_Q6_K
+    int rows = 0;                // N of this segment
+};
+
+struct ArgmaxTarget {
+    float* cand_score = nullptr;     // [grid] per-CTA best logit
+    uint32_t* cand_index = nullptr;  // [grid] per-CTA best row
+    unsigned* counter = nullptr;     // zero before the first launch; reset by the kernel
+    uint32_t* token = nullptr;       // result: best row + index_base
+    uint32_t index_base = 0;         // global index of row 0 (sharded heads)
+    float* score = nullptr;          // optional: best logit
+};
+
+struct GemvRequest {
+    GemvSegment seg[kMaxSegments];
+    int nseg = 0;
+    int K = 0;                     // inputs per row (multiple of 256)
+    int M = 1;                     // activation rows
+    int ldx = 0;                   // floats between activation rows (0: K)
+    int ldy = 0;                   // floats between output rows (0: segment rows)
+    const float* x = nullptr;      // fp32 activations [M][ldx]
+    const float* gamma = nullptr;  // optional RMSNorm weight applied to x first
+    float eps = 1e-6f;
+    int epilogue = EPI_STORE;
+    ArgmaxTarget argmax;
+    int* err = nullptr;  // optional device error word (bits of q4k_device.cuh)
+    int ctas = 0;        // 0: one CTA per SM
+    bool pdl = false;    // launch with programmatic stream serialisation
+};
+
+// Plans and launches one product. Returns cudaErrorInvalidValue for shapes it
+// does not support (the caller validates user-facing arguments first).
+cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream);
+
+int sm_count();
+
+}  // namespace q4k

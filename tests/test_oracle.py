@@ -1,0 +1,200 @@
+"""The CPU oracle, pinned: against the gguf package's dequantisation (ggml's
+own restatement of the reference test oracle's to_float) and against the
+reference engine's own kernels' outputs (tests/golden/ref_kernels.npz, made by
+tests/golden/make_ref_golden.py on a B200), plus internal consistency."""
+import os
+
+import numpy as np
+import pytest
+
+import oracle as o
+from conftest import GOLDEN, rel_l2
+from tiny_model import TINY, tiny_tensors
+
+REF_GOLDEN = os.path.join(GOLDEN, "ref_kernels.npz")
+
+
+def approx_ok(actual, expected, margin, eps=1e-4):
+    """Catch::Approx(expected).margin(m).epsilon(eps) (MatmulReference.hpp:71-79)."""
+    a = np.asarray(actual, np.float64)
+    e = np.asarray(expected, np.float64)
+    tol = np.maximum(margin, eps * np.maximum(np.abs(e), np.abs(e)))
+    return np.abs(a - e) <= tol + 1e-300
+
+
+@pytest.fixture(scope="module")
+def gg():
+    return np.load(os.path.join(GOLDEN, "dequant_gguf.npz"))
+
+
+@pytest.fixture(scope="module")
+def ref():
+    if not os.path.exists(REF_GOLDEN):
+        pytest.fail("tests/golden/ref_kernels.npz is missing (run tests/golden/make_ref_golden.py on a GPU)")
+    return np.load(REF_GOLDEN)
+
+
+@pytest.mark.parametrize("tag,qt", [("q4k", o.Q4_K), ("q6k", o.Q6_K)])
+def test_dequant_matches_gguf_bit_exact(gg, tag, qt):
+    blocks, want = gg[f"{tag}_blocks"], gg[f"{tag}_values"]
+    got = o.dequantize_rows(blocks.ravel(), qt, blocks.shape[0], 256, blocks.shape[1])
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("tag,qt", [("q4k", o.Q4_K), ("q6k", o.Q6_K)])
+def test_dequant_matches_reference_kernel_bit_exact(ref, tag, qt):
+    raw, want = ref[f"dequant_{tag}_raw"], ref[f"dequant_{tag}_out"]
+    got = o.dequantize_rows(raw, qt, 4, 2560)
+    assert np.array_equal(got.ravel().view(np.uint32), want.view(np.uint32))
+
+
+def test_dequant_rejects_other_types():
+    with pytest.raises(ValueError):
+        o.dequantize_rows(np.zeros(144, np.uint8), o.F32, 1, 256)
+
+
+def test_quantize_q8_properties():
+    rng = np.random.default_rng(1)
+    x = rng.normal(size=4096).astype(np.float32)
+    x[64:96] = 0.0  # an all-zero group quantises to zeros with scale 0
+    codes, scales = o.quantize_q8(x)
+    g = x.reshape(-1, 32)
+    assert np.array_equal(scales, (np.abs(g).max(1) / np.float32(127)).astype(np.float32))
+    assert np.all(codes.reshape(-1, 32)[2] == 0) and scales[2] == 0
+    assert np.abs(codes).max() <= 127
+    rec = codes.reshape(-1, 32) * scales[:, None]
+    assert np.all(np.abs(rec - g) <= scales[:, None] * 0.5 + 1e-7)
+    # the group maximum maps to +-127 exactly
+    idx = np.abs(g).argmax(1)
+    assert np.all(np.abs(codes.reshape(-1, 32)[np.arange(g.shape[0]), idx])[scales > 0] == 127)
+
+
+@pytest.mark.parametrize("case", ["q4k_K2560", "q6k_K2560", "q4k_K9728", "q6k_K9728"])
+def test_matmul_matches_reference_kernel(ref, case):
+    qt = o.Q4_K if case.startswith("q4k") else o.Q6_K
+    K = int(case.split("_K")[1])
+    w = ref[f"mm_{case}_w"]
+    N = w.size // o.row_bytes(qt, K)
+    rows_seen = 0
+    for key in ref.files:
+        if not key.startswith(f"mm_{case}_r") or not key.endswith("_x"):
+            continue
+        rows = int(key[len(f"mm_{case}_r"):-2])
+        x = ref[key]
+        want = ref[f"mm_{case}_r{rows}_y"]
+        got = o.matmul(x, w, qt, K, N)
+        assert approx_ok(want, got.ravel(), 3e-5).all(), case
+        assert rel_l2(want, got) < 1e-5
+        rows_seen += 1
+    assert rows_seen >= 2
+
+
+def test_matmul_against_numpy_double(gg):
+    # independent product: gguf-decoded rows x oracle-quantised input, numpy double
+    blocks = gg["q4k_blocks"][:40]  # 4 rows of 10 blocks
+    w = blocks.ravel()
+    deq = gg["q4k_values"][:40].reshape(4, 2560).astype(np.float64)
+    rng = np.random.default_rng(3)
+    x = rng.normal(size=(2, 2560)).astype(np.float32)
+    codes, scales = o.quantize_q8(x)
+    xq = (codes.astype(np.float32) * np.repeat(scales, 32)).astype(np.float32).reshape(2, 2560)
+    want = xq.astype(np.float64) @ deq.T
+    got = o.matmul(x, w, o.Q4_K, 2560, 4)
+    assert np.allclose(got, want, rtol=1e-12, atol=1e-9)
+
+
+def test_attention_matches_reference_kernel(ref):
+    for i in range(5):
+        queries, prefix, heads, kvh, dim = (int(v) for v in ref[f"attn_{i}_shape"])
+        got = o.attention(ref[f"attn_{i}_q"], ref[f"attn_{i}_k"], ref[f"attn_{i}_v"], queries, heads, kvh, dim, prefix)
+        # AttentionTests.cpp:68: margin 3e-5 against its CPU reference
+        assert np.abs(got - ref[f"attn_{i}_out"]).max() <= 3e-5, i
+
+
+def test_attention_against_numpy():
+    rng = np.random.default_rng(4)
+    T, P, H, KVH, D = 3, 7, 4, 2, 16
+    q = rng.normal(size=(T, H, D)).astype(np.float32)
+    k = rng.normal(size=(P + T, KVH, D)).astype(np.float32)
+    v = rng.normal(size=(P + T, KVH, D)).astype(np.float32)
+    got = o.attention(q, k, v, T, H, KVH, D, P).reshape(T, H, D)
+    for t in range(T):
+        for h in range(H):
+            kv = h // (H // KVH)
+            s = k[: P + t + 1, kv].astype(np.float64) @ q[t, h] / np.sqrt(D)
+            p = np.exp(s - s.max())
+            p /= p.sum()
+            assert np.allclose(got[t, h], p @ v[: P + t + 1, kv], atol=1e-6)
+
+
+def test_rope_rms_silu_match_reference_kernels(ref):
+    got = o.rope(ref["rope_x"], 3, 4, 128, 4090, 1e6)
+    assert rel_l2(got, ref["rope_out"]) < 1e-6
+    got = o.rms_norm(ref["rms_x"], ref["rms_g"], 2560, 1e-6)
+    assert rel_l2(got, ref["rms_out"]) < 1e-6
+    got = o.silu_multiply(ref["silu_g"], ref["silu_u"])
+    assert rel_l2(got, ref["silu_out"]) < 1e-6
+
+
+def test_argmax_matches_reference_kernel(ref):
+    assert o.argmax(ref["argmax_logits"]) == int(ref["argmax_out"][0]) == 777
+
+
+def test_argmax_ties_nan_and_empty():
+    x = np.array([1.0, 5.0, np.nan, 5.0, -np.inf], np.float32)
+    assert o.argmax(x) == 1
+    assert o.argmax(np.array([np.nan, np.nan], np.float32)) == 0xFFFFFFFF
+    assert o.argmax(np.array([-np.inf], np.float32)) == 0xFFFFFFFF
+
+
+def _tiny():
+    return TINY, tiny_tensors(TINY)
+
+
+def test_forward_matches_reference_replay(ref):
+    cfg, tensors = _tiny()
+    model = o.Model(cfg, {n: (t, d) for n, (t, a, b, d) in tensors.items()})
+    cap = 16
+    kvw = cfg["kv_heads"] * cfg["head_dim"]
+    kc = np.zeros(cfg["layers"] * cap * kvw, np.float32)
+    vc = np.zeros_like(kc)
+    step = 0
+    while f"fwd_{step}_tokens" in ref.files:
+        toks = ref[f"fwd_{step}_tokens"]
+        pos = int(ref[f"fwd_{step}_pos"][0])
+        nxt, logits, hidden = model.forward(kc, vc, cap, toks, pos, kv_round_f16=True)
+        assert rel_l2(hidden.ravel(), ref[f"fwd_{step}_hidden"]) < 1e-4, step
+        assert rel_l2(logits, ref[f"fwd_{step}_logits"]) < 1e-4, step
+        assert nxt == int(ref[f"fwd_{step}_next"][0]), step
+        step += 1
+    assert step >= 2
+    assert rel_l2(kc, ref["fwd_kcache"]) < 1e-4
+
+
+def test_forward_prefill_equals_sequential_decode():
+    cfg, tensors = _tiny()
+    model = o.Model(cfg, {n: (t, d) for n, (t, a, b, d) in tensors.items()})
+    cap = 8
+    kvw = cfg["kv_heads"] * cfg["head_dim"]
+    toks = [5, 17, 300, 999]
+    ka = np.zeros(cfg["layers"] * cap * kvw, np.float32)
+    va = np.zeros_like(ka)
+    na, la, _ = model.forward(ka, va, cap, toks, 0, kv_round_f16=False)
+    kb = np.zeros_like(ka)
+    vb = np.zeros_like(ka)
+    for i, t in enumerate(toks):
+        nb, lb, _ = model.forward(kb, vb, cap, [t], i, kv_round_f16=False)
+    assert na == nb
+    assert rel_l2(lb, la) < 1e-5
+    assert rel_l2(kb, ka) < 1e-5
+
+
+def test_forward_capacity_checks():
+    cfg, tensors = _tiny()
+    model = o.Model(cfg, {n: (t, d) for n, (t, a, b, d) in tensors.items()})
+    kvw = cfg["kv_heads"] * cfg["head_dim"]
+    kc = np.zeros(cfg["layers"] * 2 * kvw, np.float32)
+    with pytest.raises(RuntimeError):
+        model.forward(kc, kc.copy(), 2, [1, 2, 3], 0)
+    with pytest.raises(RuntimeError):
+        model.forward(kc, kc.copy(), 2, [cfg["vocab"]], 0)

@@ -174,7 +174,8 @@ def time_gemv(q, torch, qtype: int, K: int, N: int, copies: int, reps: int, swig
     q.check(q.lib().q4k_synth_f32_device(SEED, b"bench.x", K, x.data_ptr(), None))
     gamma = torch.ones(K, device="cuda")
     y = torch.empty(N, device="cuda")
-    stream = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()  # a capturable (non-default) stream
     sp = stream.cuda_stream
     L = q.lib()
 
@@ -191,16 +192,74 @@ def time_gemv(q, torch, qtype: int, K: int, N: int, copies: int, reps: int, swig
     for i in range(3 * copies):
         launch(i % copies)
     torch.cuda.synchronize()
+    # The launches are captured in a CUDA graph so that host-side call
+    # overhead (ctypes, planning) does not starve the device between launches.
+    per_graph = max(copies, min(reps, 4 * copies))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        sp = stream.cuda_stream
+        for i in range(per_graph):
+            launch(i % copies)
+    replays = max(1, reps // per_graph)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for i in range(reps):
-        launch(i % copies)
-    ev1.record(stream)
+    with torch.cuda.stream(stream):  # replay() launches on the current stream
+        graph.replay()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(replays):
+            graph.replay()
+        ev1.record(stream)
     torch.cuda.synchronize()
-    secs = ev0.elapsed_time(ev1) / 1e3 / reps
+    secs = ev0.elapsed_time(ev1) / 1e3 / (replays * per_graph)
+    del graph
     del weights
     torch.cuda.empty_cache()
     return secs
+
+
+def time_attention(q, torch, kv_heads: int = 8, ctx: int = CTX, layers: int = 8, reps: int = 200):
+    """Average device time (s) of one decode-attention launch at position
+    ctx-1 over `layers` distinct fp16 KV caches in rotation (graph-timed)."""
+    import ctypes as C
+
+    H, D = 4 * kv_heads, 128
+    k = torch.empty((layers, kv_heads * ctx * D), dtype=torch.int16, device="cuda").random_(0, 15000)
+    v = torch.empty_like(k).random_(0, 15000)
+    qkv = torch.randn((H + 2 * kv_heads) * D, device="cuda")
+    g = torch.ones(D, device="cuda")
+    pos = torch.tensor([ctx - 1], dtype=torch.int32, device="cuda")
+    out = torch.empty(H * D, device="cuda")
+    scratch = torch.zeros(q.lib().q4k_attention_decode_scratch_bytes(H, kv_heads), dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.Stream()
+    L = q.lib()
+
+    def launch(i):
+        q.check(L.q4k_attention_decode_f16(qkv.data_ptr(), g.data_ptr(), g.data_ptr(), k[i].data_ptr(), v[i].data_ptr(),
+                                           ctx, pos.data_ptr(), H, kv_heads, D, 1e-6, 1e6, out.data_ptr(),
+                                           scratch.data_ptr(), stream.cuda_stream))
+
+    torch.cuda.synchronize()
+    for i in range(layers):
+        launch(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(layers):
+            launch(i)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    replays = max(1, reps // layers)
+    with torch.cuda.stream(stream):
+        graph.replay()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(replays):
+            graph.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    secs = ev0.elapsed_time(ev1) / 1e3 / (replays * layers)
+    del graph, k, v
+    torch.cuda.empty_cache()
+    return secs, 2 * kv_heads * ctx * D * 2
 
 
 def gemv_bytes(q, qtype, K, N, nmat=1, norm=False):
@@ -300,6 +359,9 @@ def run_decode(args, world, rank, local):
             t = time_gemv(q, torch, qt, kk, nn, copies=copies, reps=100 if copies > 2 else 20)
             gemv[tag] = {"us": round(t * 1e6, 3), "gbs": round(gemv_bytes(q, qt, kk, nn) / t / 1e9, 1),
                          "frac": round(gemv_bytes(q, qt, kk, nn) / t / 1e9 / peaks["hbm_gbs"], 4)}
+        t_att, att_bytes = time_attention(q, torch, kv_heads=8 // world)
+        gemv["attention_decode_ctx4096"] = {"us": round(t_att * 1e6, 3), "gbs": round(att_bytes / t_att / 1e9, 1),
+                                            "frac": round(att_bytes / t_att / 1e9 / peaks["hbm_gbs"], 4)}
         step_bytes = (2503489024 + 36 * 2 * CTX * 8 * 128 * 2) / world
         value = args.steps / secs
         kernels_per_step = 1 + 36 * 5 + 2 + (72 if world > 1 else 0)
@@ -371,6 +433,28 @@ def run_gemv(args, world, rank, local):
             "gpu_launches": args.steps, "clocks": clk}
 
 
+def run_attention(args, world, rank, local):
+    """Decode attention alone (one layer's 8 KV heads at context 4096,
+    8 caches in rotation): the profiling target for the attention kernel."""
+    import torch
+
+    import q4kb200 as q
+
+    torch.cuda.set_device(local)
+    peaks = load_peaks()
+    t, b = time_attention(q, torch, kv_heads=8, reps=args.steps)
+    gbs = b / t / 1e9
+    return {"metric": "decode attention HBM GB/s (ctx 4096, 8 KV heads, fp16 KV)", "value": round(gbs, 1),
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": 8, "ms_per_step": round(t * 1e3, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16 KV, fp32 softmax",
+            "data": "synthetic", "config": {"workload": "attention decode, one layer", "model": MODEL,
+                                            "global_batch": 1, "seq_len": CTX, "parallelism": "replica",
+                                            "l2": "8 distinct caches (134 MB) in rotation"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": None, "algorithmic_bytes": b},
+            "gpu_launches": args.steps}
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return None
@@ -400,7 +484,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("decode", "gemv"), default="decode")
+    ap.add_argument("--workload", choices=("decode", "gemv", "attention"), default="decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     world, rank, local = dist_init()
@@ -411,7 +495,12 @@ def main() -> None:
             print(json.dumps(out), flush=True)
         return
 
-    out = run_decode(args, world, rank, local) if args.workload == "decode" else run_gemv(args, world, rank, local)
+    if args.workload == "decode":
+        out = run_decode(args, world, rank, local)
+    elif args.workload == "attention":
+        out = run_attention(args, world, rank, local)
+    else:
+        out = run_gemv(args, world, rank, local)
     if rank == 0 and out is not None:
         if world == 1 and args.workload == "decode" and not args.no_cpu_baseline:
             model, kc, vc = cpu_decode_model()

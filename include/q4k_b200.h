@@ -202,6 +202,9 @@ int q4k_engine_set_tensor(q4k_engine* engine, const char* name, int type, int64_
  * layer's [kv_heads/tp_world][capacity][128] K and V back to the host. */
 int q4k_engine_fill_kv_synthetic(q4k_engine* engine, uint64_t seed, int n);
 int q4k_engine_read_kv(q4k_engine* engine, int layer, uint16_t* k_host, uint16_t* v_host);
+/* Replaces one layer's K/V (same layout as read_kv; either may be NULL),
+ * e.g. to resume a saved session (ChatSession's cache, ChatSession.hpp:30-44). */
+int q4k_engine_write_kv(q4k_engine* engine, int layer, const uint16_t* k_host, const uint16_t* v_host);
 
 /* One decode step (Engine::inference for one new token, src/Engine.cpp:37-114):
  * embeds `token` at `position`, runs every layer and the output head, and
@@ -219,6 +222,12 @@ int q4k_engine_decode(q4k_engine* engine, uint32_t token, int position, uint32_t
  * the `steps` generated tokens (may be NULL). Synchronous at the end. */
 int q4k_engine_generate(q4k_engine* engine, uint32_t token, int position, int steps, int advance,
                         uint32_t* tokens_host);
+
+/* One transformer block (src/Engine.cpp:71-103) applied to a given residual
+ * stream x_host (hidden floats) for a token at `position`, result in
+ * x_out_host; writes that layer's K/V row at `position`. For checking a
+ * layer against another implementation on identical inputs. Synchronous. */
+int q4k_engine_layer(q4k_engine* engine, int layer, const float* x_host, int position, float* x_out_host);
 
 /* Stream the engine launches on (cudaStream_t), e.g. to time with events. */
 void* q4k_engine_stream(q4k_engine* engine);

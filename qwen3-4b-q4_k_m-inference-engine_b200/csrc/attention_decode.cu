@@ -8,18 +8,26 @@
 // [0, pos] with scale 1/sqrt(d) and a softmax.
 //
 // B200 structure: grid (splits, kv_heads). The CTA for (split, kv head)
-// takes a contiguous range of positions and serves all G = heads/kv_heads
-// query heads of its group, so each K/V row is read from HBM once per
-// group (the reference re-reads it per query head). A producer warp streams
-// 64-position K and V tiles (16 KB each, contiguous in the head-major cache
-// layout) into a two-stage shared-memory ring with cp.async.bulk, starting
-// before griddepcontrol.wait. Eight compute warps do the scores, an online
-// softmax and the weighted V sum in fp32. Each CTA writes an unnormalised
-// partial (o, max, sum); the last CTA of a KV head to finish merges the
-// partials (log-sum-exp) and writes the attended output.
+// takes a contiguous range of positions and serves all G = 4 query heads of
+// its group, so each K/V row is read from HBM once per group. A producer
+// warp streams 64-position K and V tiles into a shared-memory ring with 2-D
+// TMA loads (cp.async.bulk.tensor, 128-byte swizzle), starting before
+// griddepcontrol.wait. Each of the eight compute warps owns 8 positions of
+// every tile and runs its own online softmax with tensor-core MMAs:
+//   scores  S[4 x 8] = Q[4 x 128] K^T         (mma.m16n8k16, rows 4..15 zero)
+//   output  O[4 x 128] += P[4 x 8] V[8 x 128]  (mma.m16n8k8)
+// Q and P are fp32 values split into fp16 hi + lo parts (two MMAs each), and
+// K/V are exact fp16, so the products carry ~22 bits like the reference's
+// fp32 arithmetic. The warps' (max, sum, O) are merged in shared memory, each
+// CTA writes an unnormalised partial, and the last CTA of a KV head to finish
+// merges the partials (log-sum-exp) and writes the attended output.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <math_constants.h>
+
+#include <cstring>
+#include <mutex>
 
 #include "ops.h"
 #include "q4k_device.cuh"
@@ -30,22 +38,29 @@ namespace {
 constexpr int D = kDecodeHeadDim;  // 128
 constexpr int G = 4;               // query heads per KV head
 constexpr int T = 64;              // positions per tile
-constexpr int kStages = 2;
 constexpr int kComputeWarps = 8;
 constexpr int kComputeThreads = kComputeWarps * 32;
+constexpr int kBox = T * 64 * 2;       // one 64-position x 64-dim fp16 box: 8 KB
+constexpr int kTileBytes = 2 * kBox;   // K or V tile: 16 KB
+constexpr int kStageBytes = 2 * kTileBytes;  // K + V
 
-struct Smem {
-    uint16_t k[kStages][T * D];
-    uint16_t v[kStages][T * D];
-    float q[G][D];
-    float w[G][T];
-    uint16_t k_new[D];
-    uint16_t v_new[D];
-    float red[kComputeWarps][2];
-    uint64_t full[kStages];
-    uint64_t empty[kStages];
-    int last;
-    int abort;
+struct Args {
+    const float* qkv;
+    const float* q_gamma;
+    const float* k_gamma;
+    uint16_t* k_cache;  // this layer: [kv_heads][capacity][128]
+    uint16_t* v_cache;
+    int row_base;       // row of this layer's head 0, position 0 in the tensor maps
+    int capacity;
+    const int* position;
+    int heads, kv_heads;
+    float eps, rope_base;
+    float* partial_o;
+    float* partial_ml;
+    unsigned* counters;
+    float* out;
+    int* err;
+    int stages;
 };
 
 __device__ __forceinline__ float rope_angle(int pos, int j, float base) {
@@ -53,9 +68,77 @@ __device__ __forceinline__ float rope_angle(int pos, int j, float base) {
     return (float)pos * powf(base, -2.0f * (float)j / (float)D);
 }
 
-__global__ void __launch_bounds__(kComputeThreads + 32, 1) decode_attention_kernel(const __grid_constant__ DecodeAttnArgs a) {
-    extern __shared__ __align__(128) uint8_t smem_raw[];
-    Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Byte offset of (row r, 16-byte chunk c of the 128-dim row) inside a tile
+// loaded as two 64-dim boxes with the 128-byte swizzle.
+__device__ __forceinline__ uint32_t tile_off(int r, int c) {
+    return (uint32_t)((c >> 3) * kBox + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+    // rows 8..15 of A are zero (a1 = a3 = 0)
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void mma1688(float& c0, float& c1, uint32_t a0, uint32_t b0) {
+    float c2 = 0.0f, c3 = 0.0f;  // rows 8..15: zero A rows, results unused
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%0, %1, %2, %3};"
+        : "+f"(c0), "+f"(c1), "+f"(c2), "+f"(c3)
+        : "r"(a0), "r"(0u), "r"(b0));
+}
+
+// fp32 pair -> packed fp16 (hi) and the fp16 residual (lo).
+__device__ __forceinline__ void split2(float x, float y, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x, y);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(x - hf.x, y - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+struct SmemTail {
+    float q[G][D];
+    uint16_t k_new[D];
+    uint16_t v_new[D];
+    float red[kComputeWarps][2];
+    uint64_t full[8];
+    uint64_t empty[8];
+    int last;
+    int abort[2];  // per tile parity: a fast warp's next tile never clears the current flag
+};
+
+__global__ void __launch_bounds__(kComputeThreads + 32, 1)
+    decode_attention_kernel(const __grid_constant__ Args a, const __grid_constant__ CUtensorMap kmap,
+                            const __grid_constant__ CUtensorMap vmap) {
+    // the 128-byte TMA swizzle is keyed to 1024-byte smem address blocks
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    const int S = a.stages;
+    SmemTail& sm = *reinterpret_cast<SmemTail*>(smem + S * kStageBytes);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x, kvh = blockIdx.y, splits = gridDim.x;
 
@@ -68,32 +151,32 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1) decode_attention_kern
     const int chunk = (n_keys + splits - 1) / splits;
     const int p0 = min(split * chunk, n_keys), p1 = min(p0 + chunk, n_keys);
     const int tiles = (p1 - p0 + T - 1) / T;
-    const size_t head_base = (size_t)kvh * a.capacity * D;
+    const int row0 = a.row_base + kvh * a.capacity;  // tensor-map row of (kvh, position 0)
 
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < S; ++s) {
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], 1);
         }
+        sm.abort[0] = sm.abort[1] = 0;
         mbar_fence_init();
     }
     __syncthreads();
     pdl_launch_dependents();
 
     if (warp == kComputeWarps) {
-        // ---------------- producer: cached rows [p0, min(p1, pos)) ----------------
+        // ---------------- producer: K and V tiles (rows past p1 are masked) ----------------
         if (lane == 0) {
             for (int t = 0; t < tiles; ++t) {
-                const int s = t % kStages, use = t / kStages;
+                const int s = t % S, use = t / S;
                 if (use > 0 && !mbar_wait_bounded(&sm.empty[s], (use - 1) & 1, a.err, ERR_WAIT_TIMEOUT_EMPTY)) break;
-                const int lo = p0 + t * T;
-                const int hi = min(min(lo + T, p1), pos);
-                const int rows = max(hi - lo, 0);
-                mbar_arrive_expect_tx(&sm.full[s], (uint32_t)(2 * rows * D * 2));
-                if (rows > 0) {
-                    bulk_g2s(sm.k[s], a.k_cache + head_base + (size_t)lo * D, (uint32_t)(rows * D * 2), &sm.full[s]);
-                    bulk_g2s(sm.v[s], a.v_cache + head_base + (size_t)lo * D, (uint32_t)(rows * D * 2), &sm.full[s]);
-                }
+                const int y = row0 + p0 + t * T;
+                uint8_t* st = smem + s * kStageBytes;
+                mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
+                tma_load_2d(st, &kmap, 0, y, &sm.full[s]);
+                tma_load_2d(st + kBox, &kmap, 64, y, &sm.full[s]);
+                tma_load_2d(st + kTileBytes, &vmap, 0, y, &sm.full[s]);
+                tma_load_2d(st + kTileBytes + kBox, &vmap, 64, y, &sm.full[s]);
             }
         }
         return;
@@ -101,6 +184,7 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1) decode_attention_kern
 
     // ---------------- compute warps: q (and the new k/v) of this token ----------------
     pdl_wait();
+    const size_t head_base = (size_t)kvh * a.capacity * D;
     const float* q_raw = a.qkv + (size_t)kvh * G * D;
     const float* k_raw = a.qkv + (size_t)a.heads * D + (size_t)kvh * D;
     const float* v_raw = a.qkv + (size_t)a.heads * D + (size_t)a.kv_heads * D + (size_t)kvh * D;
@@ -109,7 +193,7 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1) decode_attention_kern
         // Thread t handles pair (j, j + 64) of head h = t / 64 (4 heads x 64 pairs).
         const int h = tid >> 6, j = tid & 63;
         float x0 = q_raw[h * D + j], x1 = q_raw[h * D + j + 64];
-        float ss = warp_sum(x0 * x0 + x1 * x1);
+        const float ss = warp_sum(x0 * x0 + x1 * x1);
         float kx0 = 0.0f, kx1 = 0.0f, kss = 0.0f;
         if (owner && h == 0) {
             kx0 = k_raw[j];
@@ -149,80 +233,151 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1) decode_attention_kern
         named_barrier(1, kComputeThreads);
     }
 
-    // ---------------- tiles ----------------
+    // Q as MMA A-fragments (rows = heads, only rows 0..3 live): lane (g, t)
+    // holds q[g][16s + 2t, +1] (a0) and q[g][16s + 8 + 2t, +1] (a2).
+    const int g = lane >> 2, tq = lane & 3;
+    uint32_t qa0h[8], qa0l[8], qa2h[8], qa2l[8];
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        if (g < G) {
+            split2(sm.q[g][16 * s + 2 * tq], sm.q[g][16 * s + 2 * tq + 1], qa0h[s], qa0l[s]);
+            split2(sm.q[g][16 * s + 8 + 2 * tq], sm.q[g][16 * s + 8 + 2 * tq + 1], qa2h[s], qa2l[s]);
+        } else {
+            qa0h[s] = qa0l[s] = qa2h[s] = qa2l[s] = 0u;
+        }
+    }
+
+    // ---------------- tiles: this warp owns tile rows [8w, 8w + 8) ----------------
     const float scale = rsqrtf((float)D);  // attention.cu:40
-    const int h = tid >> 6;                // head of this thread (score and PV phases)
-    const int pp = tid & 63;               // position slot in the tile (score phase)
-    const int d0 = 2 * (tid & 63);         // dims d0, d0+1 (PV phase)
-    float m_run = -CUDART_INF_F, l_run = 0.0f, o0 = 0.0f, o1 = 0.0f;
-    if (tid == 0) sm.abort = 0;
-    named_barrier(1, kComputeThreads);
+    const int r_lane = 8 * warp + (lane & 7);  // tile row this lane addresses for ldmatrix
+    float m_run = -CUDART_INF_F, l_run = 0.0f;  // per head g (lanes with g < 4)
+    float o[16][2];                             // O[g][8j + 2tq, +1]
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = 0.0f;
+
     for (int t = 0; t < tiles; ++t) {
-        const int s = t % kStages, use = t / kStages;
-        // A thread that gives up flags the CTA; all compute threads leave
-        // together after the next barrier, so none is left waiting at it.
+        const int s = t % S, use = t / S;
+        // A warp whose wait gave up flags the CTA; every warp still reaches the
+        // end-of-tile barrier, after which all leave together.
         const bool landed = mbar_wait_bounded(&sm.full[s], use & 1, a.err, ERR_WAIT_TIMEOUT_FULL);
-        if (!landed) sm.abort = 1;
+        if (!__all_sync(0xffffffffu, landed) && lane == 0) sm.abort[t & 1] = 1;
         const int lo = p0 + t * T;
         const int n = min(T, p1 - lo);
-        // scores
-        float score = -CUDART_INF_F;
-        if (landed && pp < n) {
-            const uint16_t* krow = (lo + pp == pos) ? sm.k_new : sm.k[s] + pp * D;
-            float dot = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int c = (i + pp) & 15;
-                const uint4 kv = *reinterpret_cast<const uint4*>(krow + c * 8);
-                const float4 qa = *reinterpret_cast<const float4*>(&sm.q[h][c * 8]);
-                const float4 qb = *reinterpret_cast<const float4*>(&sm.q[h][c * 8 + 4]);
-                const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&kv.x));
-                const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&kv.y));
-                const float2 k45 = __half22float2(*reinterpret_cast<const __half2*>(&kv.z));
-                const float2 k67 = __half22float2(*reinterpret_cast<const __half2*>(&kv.w));
-                dot += qa.x * k01.x + qa.y * k01.y + qa.z * k23.x + qa.w * k23.y;
-                dot += qb.x * k45.x + qb.y * k45.y + qb.z * k67.x + qb.w * k67.y;
+        uint8_t* kt = smem + s * kStageBytes;
+        uint8_t* vt = kt + kTileBytes;
+        // the new token's row: this warp's slab holds it in the owner CTA
+        const int prow = pos - lo;
+        if (owner && prow >= 8 * warp && prow < 8 * warp + 8) {
+            if (lane < 16) {
+                *reinterpret_cast<uint4*>(kt + tile_off(prow, lane)) = *reinterpret_cast<const uint4*>(sm.k_new + 8 * lane);
+                *reinterpret_cast<uint4*>(vt + tile_off(prow, lane)) = *reinterpret_cast<const uint4*>(sm.v_new + 8 * lane);
             }
-            score = dot * scale;
+            __syncwarp();
         }
-        // online softmax over this tile, per head (64 threads = warps 2h, 2h+1)
-        float tmax = warp_max(score);
-        if (lane == 0) sm.red[warp][0] = tmax;
-        named_barrier(1, kComputeThreads);
-        if (sm.abort) break;
-        tmax = fmaxf(sm.red[2 * h][0], sm.red[2 * h + 1][0]);
+        // scores for 8 positions x 4 heads
+        float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const uint32_t kbase = smem_addr(kt);
+#pragma unroll
+        for (int s2 = 0; s2 < 8; s2 += 2) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(kbase + tile_off(r_lane, 2 * s2 + (lane >> 3)), b0, b1, b2, b3);
+            mma16816(sc, qa0h[s2], qa2h[s2], b0, b1);
+            mma16816(sc, qa0l[s2], qa2l[s2], b0, b1);
+            mma16816(sc, qa0h[s2 + 1], qa2h[s2 + 1], b2, b3);
+            mma16816(sc, qa0l[s2 + 1], qa2l[s2 + 1], b2, b3);
+        }
+        // online softmax over this warp's 8 positions (lane (g, tq): positions 2tq, 2tq+1)
+        const int c0 = 8 * warp + 2 * tq;
+        const float s0 = c0 < n ? sc[0] * scale : -CUDART_INF_F;
+        const float s1 = c0 + 1 < n ? sc[1] * scale : -CUDART_INF_F;
+        float tmax = fmaxf(s0, s1);
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
         const float m_new = fmaxf(m_run, tmax);
-        const float wgt = pp < n ? expf(score - m_new) : 0.0f;
-        sm.w[h][pp] = wgt;
-        float tsum = warp_sum(wgt);
-        if (lane == 0) sm.red[warp][1] = tsum;
-        named_barrier(1, kComputeThreads);
-        tsum = sm.red[2 * h][1] + sm.red[2 * h + 1][1];
-        const float rescale = expf(m_run - m_new);
-        l_run = l_run * rescale + tsum;
-        m_run = m_new;
-        // weighted V
-        o0 *= rescale;
-        o1 *= rescale;
-        for (int r = 0; r < n; ++r) {
-            const uint16_t* vrow = (lo + r == pos) ? sm.v_new : sm.v[s] + r * D;
-            const float2 vv = __half22float2(*reinterpret_cast<const __half2*>(vrow + d0));
-            const float wr = sm.w[h][r];
-            o0 += wr * vv.x;
-            o1 += wr * vv.y;
+        float p0v = 0.0f, p1v = 0.0f, rescale = 1.0f;
+        if (m_new != -CUDART_INF_F) {
+            p0v = expf(s0 - m_new);
+            p1v = expf(s1 - m_new);
+            rescale = expf(m_run - m_new);
         }
+        float psum = p0v + p1v;
+        psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+        psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+        l_run = l_run * rescale + psum;
+        m_run = m_new;
+        uint32_t pa_h, pa_l;
+        split2(p0v, p1v, pa_h, pa_l);
+        if (g >= G) pa_h = pa_l = 0u;
+        // O += P V over this warp's 8 positions, 128 dims in 16 column tiles
+        const uint32_t vbase = smem_addr(vt);
+#pragma unroll
+        for (int j4 = 0; j4 < 16; j4 += 4) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(vbase + tile_off(r_lane, j4 + (lane >> 3)), b0, b1, b2, b3);
+            const uint32_t bb[4] = {b0, b1, b2, b3};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                float c0f = o[j4 + q][0] * rescale, c1f = o[j4 + q][1] * rescale;
+                mma1688(c0f, c1f, pa_h, bb[q]);
+                mma1688(c0f, c1f, pa_l, bb[q]);
+                o[j4 + q][0] = c0f;
+                o[j4 + q][1] = c1f;
+            }
+        }
+        if (owner && prow >= 8 * warp && prow < 8 * warp + 8)
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes before the next TMA
+        __syncwarp();
+        // the slot is free once all eight warps are done with it
         named_barrier(1, kComputeThreads);
         if (tid == 0) mbar_arrive(&sm.empty[s]);
+        if (sm.abort[t & 1]) break;
+    }
+    named_barrier(1, kComputeThreads);
+
+    // ---------------- merge the 8 warps (stage buffers reused as scratch) ----------------
+    float* wm = reinterpret_cast<float*>(smem);            // [warps][G]
+    float* wl = wm + kComputeWarps * G;                    // [warps][G]
+    float* wo = wl + kComputeWarps * G;                    // [warps][G][D]
+    const bool aborted = sm.abort[0] | sm.abort[1];
+    if (!aborted) {
+        if (g < G) {
+            if (tq == 0) {
+                wm[warp * G + g] = m_run;
+                wl[warp * G + g] = l_run;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                wo[(warp * G + g) * D + 8 * j + 2 * tq] = o[j][0];
+                wo[(warp * G + g) * D + 8 * j + 2 * tq + 1] = o[j][1];
+            }
+        }
+    }
+    named_barrier(1, kComputeThreads);
+    const int hq = tid >> 6;          // query head within the group
+    const int d0 = 2 * (tid & 63);    // dims d0, d0+1
+    float M = -CUDART_INF_F;
+    for (int w = 0; w < kComputeWarps; ++w) M = fmaxf(M, wm[w * G + hq]);
+    float L = 0.0f, acc0 = 0.0f, acc1 = 0.0f;
+    for (int w = 0; w < kComputeWarps; ++w) {
+        const float l = wl[w * G + hq];
+        if (!(l > 0.0f)) continue;
+        const float f = expf(wm[w * G + hq] - M);
+        L += l * f;
+        acc0 += wo[(w * G + hq) * D + d0] * f;
+        acc1 += wo[(w * G + hq) * D + d0 + 1] * f;
+    }
+    if (aborted) {
+        M = -CUDART_INF_F;
+        L = acc0 = acc1 = 0.0f;
     }
 
     // ---------------- partials and the cross-split merge ----------------
-    const int hq = h;  // query head within the group
     const size_t pidx = ((size_t)kvh * splits + split) * G + hq;
-    a.partial_o[pidx * D + d0] = o0;
-    a.partial_o[pidx * D + d0 + 1] = o1;
+    a.partial_o[pidx * D + d0] = acc0;
+    a.partial_o[pidx * D + d0 + 1] = acc1;
     if ((tid & 63) == 0) {
-        a.partial_ml[pidx * 2 + 0] = m_run;
-        a.partial_ml[pidx * 2 + 1] = l_run;
+        a.partial_ml[pidx * 2 + 0] = M;
+        a.partial_ml[pidx * 2 + 1] = L;
     }
     __threadfence();
     named_barrier(1, kComputeThreads);
@@ -230,28 +385,65 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1) decode_attention_kern
     named_barrier(1, kComputeThreads);
     if (!sm.last) return;
     __threadfence();
-    float M = -CUDART_INF_F;
+    float MM = -CUDART_INF_F;
     for (int sp = 0; sp < splits; ++sp) {
         const size_t q = ((size_t)kvh * splits + sp) * G + hq;
-        if (__ldcg(a.partial_ml + q * 2 + 1) > 0.0f) M = fmaxf(M, __ldcg(a.partial_ml + q * 2));
+        if (__ldcg(a.partial_ml + q * 2 + 1) > 0.0f) MM = fmaxf(MM, __ldcg(a.partial_ml + q * 2));
     }
-    float L = 0.0f, acc0 = 0.0f, acc1 = 0.0f;
+    float LL = 0.0f, o0 = 0.0f, o1 = 0.0f;
     for (int sp = 0; sp < splits; ++sp) {
         const size_t q = ((size_t)kvh * splits + sp) * G + hq;
         const float l = __ldcg(a.partial_ml + q * 2 + 1);
         if (!(l > 0.0f)) continue;
-        const float f = expf(__ldcg(a.partial_ml + q * 2) - M);
-        L += l * f;
-        acc0 += __ldcg(a.partial_o + q * D + d0) * f;
-        acc1 += __ldcg(a.partial_o + q * D + d0 + 1) * f;
+        const float f = expf(__ldcg(a.partial_ml + q * 2) - MM);
+        LL += l * f;
+        o0 += __ldcg(a.partial_o + q * D + d0) * f;
+        o1 += __ldcg(a.partial_o + q * D + d0 + 1) * f;
     }
     float* out = a.out + ((size_t)kvh * G + hq) * D;
-    out[d0] = acc0 / L;
-    out[d0 + 1] = acc1 / L;
+    out[d0] = o0 / LL;
+    out[d0 + 1] = o1 / LL;
     if (tid == 0) a.counters[kvh] = 0u;
 }
 
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
+
+size_t smem_bytes(int stages) { return (size_t)stages * kStageBytes + sizeof(SmemTail) + 1024; }
+
 }  // namespace
+
+cudaError_t make_kv_tensor_map(const uint16_t* base, long long rows, KvTensorMap* out) {
+    static_assert(sizeof(KvTensorMap) == sizeof(CUtensorMap), "tensor map storage size");
+    EncodeTiled enc = encoder();
+    if (!enc) return cudaErrorNotSupported;
+    if (reinterpret_cast<uintptr_t>(base) % 16 || rows <= 0) return cudaErrorInvalidValue;
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)T};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(base), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    std::memcpy(out, &map, sizeof map);
+    return cudaSuccess;
+}
 
 int decode_attention_splits(int kv_heads) {
     const int s = sm_count() / (kv_heads > 0 ? kv_heads : 1);
@@ -263,26 +455,51 @@ size_t decode_attention_scratch_floats(int heads, int kv_heads, int splits) {
     return (size_t)heads * splits * (D + 2);
 }
 
-cudaError_t decode_attention(const DecodeAttnArgs& a, cudaStream_t s, bool pdl) {
-    if (a.kv_heads <= 0 || a.heads != a.kv_heads * G || a.splits <= 0 || a.capacity <= 0) return cudaErrorInvalidValue;
-    static bool attr_done = false;
-    if (!attr_done) {
-        const cudaError_t e = cudaFuncSetAttribute(decode_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   (int)sizeof(Smem));
-        if (e != cudaSuccess) return e;
-        attr_done = true;
-    }
+cudaError_t decode_attention(const DecodeAttnArgs& in, const KvTensorMap& kmap, const KvTensorMap& vmap,
+                             cudaStream_t s, bool pdl) {
+    if (in.kv_heads <= 0 || in.heads != in.kv_heads * G || in.splits <= 0 || in.capacity <= 0)
+        return cudaErrorInvalidValue;
+    Args a;
+    a.qkv = in.qkv;
+    a.q_gamma = in.q_gamma;
+    a.k_gamma = in.k_gamma;
+    a.k_cache = in.k_cache;
+    a.v_cache = in.v_cache;
+    a.row_base = in.row_base;
+    a.capacity = in.capacity;
+    a.position = in.position;
+    a.heads = in.heads;
+    a.kv_heads = in.kv_heads;
+    a.eps = in.eps;
+    a.rope_base = in.rope_base;
+    a.partial_o = in.partial_o;
+    a.partial_ml = in.partial_ml;
+    a.counters = in.counters;
+    a.out = in.out;
+    a.err = in.err;
+    a.stages = 4;
+    const size_t smem = smem_bytes(a.stages);
+    static std::once_flag once;
+    static cudaError_t attr = cudaSuccess;
+    std::call_once(once, [] {
+        attr = cudaFuncSetAttribute(decode_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)smem_bytes(4));
+    });
+    if (attr != cudaSuccess) return attr;
+    CUtensorMap km, vm;
+    std::memcpy(&km, &kmap, sizeof km);
+    std::memcpy(&vm, &vmap, sizeof vm);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.splits, a.kv_heads);
+    cfg.gridDim = dim3(in.splits, in.kv_heads);
     cfg.blockDim = dim3(kComputeThreads + 32);
-    cfg.dynamicSmemBytes = sizeof(Smem);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, decode_attention_kernel, a);
+    return cudaLaunchKernelEx(&cfg, decode_attention_kernel, a, km, vm);
 }
 
 }  // namespace q4k

@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "engine.h"
+#include "nccl_api.h"
 #include "ops.h"
 #include "q4k_format.h"
 #include "q4k_internal.h"
@@ -37,6 +38,17 @@ int guarded(F&& f) {
     }
 }
 
+// Entry points that touch the device: a launch error left by an earlier,
+// unrelated call is not this call's error, so clear it first (sticky
+// context errors persist regardless and surface on the next CUDA call).
+template <class F>
+int guarded_cuda(F&& f) {
+    return guarded([&] {
+        (void)cudaGetLastError();
+        f();
+    });
+}
+
 [[noreturn]] void invalid(const char* msg) { throw q4k::Error(Q4K_EINVAL, msg); }
 
 void launched(cudaError_t e) { q4k::cuda_check(e, "CUDA kernel launch failed"); }
@@ -48,8 +60,9 @@ bool quantised(int type) { return type == Q4K_TYPE_Q4_K || type == Q4K_TYPE_Q6_K
 void check_matrix(int type, int64_t ne0, int64_t ne1) {
     // matmul.cu:132-136
     if (!quantised(type)) invalid("matmul supports Q4_K and Q6_K weights only");
-    if (ne0 <= 0 || ne0 % 256 != 0 || ne1 <= 0 || ne0 > (1 << 24) || ne1 > (1 << 30))
+    if (ne0 <= 0 || ne0 % 256 != 0 || ne1 <= 0 || ne1 > (1 << 30))
         invalid("Invalid matmul weight dimensions");
+    if (ne0 > 12288) invalid("matmul supports up to 12288 inputs per row (K)");
 }
 
 }  // namespace
@@ -65,7 +78,7 @@ Q4K_API size_t q4k_weight_device_bytes(int type, int64_t ne0, int64_t ne1) {
 }
 
 Q4K_API int q4k_weight_upload(int type, int64_t ne0, int64_t ne1, const void* host_gguf, void* device, void* stream) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         if (type == Q4K_TYPE_F32) {
             if (ne0 <= 0 || ne1 <= 0 || !host_gguf || !device) invalid("invalid F32 tensor");
             q4k::cuda_check(cudaMemcpyAsync(device, host_gguf, sizeof(float) * ne0 * ne1, cudaMemcpyHostToDevice,
@@ -115,7 +128,7 @@ Q4K_API int q4k_synth_tensor_host(uint64_t seed, const char* name, int type, int
 
 Q4K_API int q4k_synth_tensor_device(uint64_t seed, const char* name, int type, int64_t ne0, int64_t ne1, void* device,
                                     void* stream) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         if (!name || !device || ne0 <= 0 || ne1 <= 0) invalid("invalid synthetic tensor request");
         const uint64_t key = q4k_tensor_key(seed, name);
         cudaStream_t s = as_stream(stream);
@@ -153,7 +166,7 @@ Q4K_API int q4k_synth_f32_host(uint64_t seed, const char* name, size_t n, float*
 }
 
 Q4K_API int q4k_synth_f32_device(uint64_t seed, const char* name, size_t n, float* out, void* stream) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         if (!name || (!out && n)) invalid("invalid synthetic request");
         if (n) launched(q4k::synth_f32(q4k_tensor_key(seed, name), out, n, as_stream(stream)));
     });
@@ -161,7 +174,7 @@ Q4K_API int q4k_synth_f32_device(uint64_t seed, const char* name, size_t n, floa
 
 Q4K_API int q4k_rms_norm(const float* input, const float* scale, float* output, size_t rows, size_t width,
                          float epsilon, void* stream) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         if (rows == 0) return;
         // rms_norm.cu:34-36
         if (width == 0 || !(epsilon > 0.0f) || !scale || !input || !output)
@@ -172,7 +185,7 @@ Q4K_API int q4k_rms_norm(const float* input, const float* scale, float* output, 
 
 Q4K_API int q4k_matmul(const float* input, const void* weight, int type, int64_t ne0, int64_t ne1, float* output,
                        size_t rows, void* stream) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         check_matrix(type, ne0, ne1);
         if (rows == 0) return;
         if (!input || !weight || !output) invalid("matmul requires device buffers");
@@ -193,7 +206,7 @@ Q4K_API int q4k_matmul(const float* input, const void* weight, int type, int64_t
 
 Q4K_API int q4k_rope(float* input, size_t tokens, size_t heads, size_t head_dim, size_t position_offset,
                      float frequency_base, void* stream) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         if (tokens == 0) return;
         // rope.cu:34-35
         if (heads == 0 || head_dim == 0 || head_dim % 2 != 0 || !(frequency_base > 0.0f))
@@ -205,7 +218,7 @@ Q4K_API int q4k_rope(float* input, size_t tokens, size_t heads, size_t head_dim,
 
 Q4K_API int q4k_attention(const float* q, const float* k, const float* v, float* output, size_t tokens,
                           size_t query_heads, size_t kv_heads, size_t head_dim, size_t query_offset, void* stream) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         if (tokens == 0) return;
         // attention.cu:98-105
         if (!q || !k || !v || !output || kv_heads == 0 || query_heads == 0 || query_heads % kv_heads != 0 ||
@@ -221,7 +234,7 @@ Q4K_API int q4k_attention(const float* q, const float* k, const float* v, float*
 }
 
 Q4K_API int q4k_residual_add(float* state, const float* branch, size_t count, void* stream) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         if (count == 0) return;
         if (!state || !branch) invalid("residual_add requires buffers");
         launched(q4k::residual_add(state, branch, count, as_stream(stream)));
@@ -229,7 +242,7 @@ Q4K_API int q4k_residual_add(float* state, const float* branch, size_t count, vo
 }
 
 Q4K_API int q4k_silu_multiply(const float* gate, const float* up, float* output, size_t count, void* stream) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         if (count == 0) return;
         if (!gate || !up || !output) invalid("silu_multiply requires buffers");
         launched(q4k::silu_multiply(gate, up, output, count, as_stream(stream)));
@@ -238,7 +251,7 @@ Q4K_API int q4k_silu_multiply(const float* gate, const float* up, float* output,
 
 Q4K_API int q4k_dequantize_embeddings(const void* packed, float* output, size_t rows, size_t width, size_t row_bytes,
                                       int type, void* stream) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         if (rows == 0) return;
         // embedding.cu:69-70
         if (!quantised(type)) invalid("Unsupported embedding storage type");
@@ -250,7 +263,7 @@ Q4K_API int q4k_dequantize_embeddings(const void* packed, float* output, size_t 
 }
 
 Q4K_API int q4k_argmax(const float* logits, size_t vocabulary_size, uint32_t* result, void* stream) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         // argmax.cu:73-74
         if (!logits || vocabulary_size == 0 || vocabulary_size > UINT32_MAX || !result)
             invalid("Invalid argmax input");
@@ -276,7 +289,7 @@ Q4K_API int q4k_matmul_ex(const float* input, const float* norm_gamma, float eps
                           const void* const* weights, const int* types, const int64_t* out_rows, float* const* outputs,
                           int64_t ne0, size_t rows, int epilogue, uint32_t* token_device, void* scratch,
                           void* stream) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         if (count < 1 || count > q4k::kMaxSegments || !weights || !types || !out_rows || !outputs)
             invalid("matmul_ex needs 1..4 weights");
         if (epilogue < Q4K_EPI_STORE || epilogue > Q4K_EPI_ARGMAX) invalid("unknown epilogue");
@@ -327,7 +340,7 @@ Q4K_API int q4k_attention_decode_f16(const float* qkv, const float* q_gamma, con
                                      uint16_t* v_cache, int capacity, const int* position_device, int query_heads,
                                      int kv_heads, int head_dim, float epsilon, float rope_base, float* output,
                                      void* scratch, void* stream) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         if (!qkv || !q_gamma || !k_gamma || !k_cache || !v_cache || !position_device || !output || !scratch)
             invalid("decode attention requires device buffers");
         if (head_dim != q4k::kDecodeHeadDim || kv_heads <= 0 || query_heads != 4 * kv_heads || capacity <= 0)
@@ -355,7 +368,11 @@ Q4K_API int q4k_attention_decode_f16(const float* qkv, const float* q_gamma, con
         a.out = output;
         a.err = nullptr;
         a.splits = splits;
-        launched(q4k::decode_attention(a, as_stream(stream), false));
+        a.row_base = 0;
+        q4k::KvTensorMap km, vm;
+        q4k::cuda_check(q4k::make_kv_tensor_map(k_cache, (long long)kv_heads * capacity, &km), "K tensor map");
+        q4k::cuda_check(q4k::make_kv_tensor_map(v_cache, (long long)kv_heads * capacity, &vm), "V tensor map");
+        launched(q4k::decode_attention(a, km, vm, as_stream(stream), false));
     });
 }
 
@@ -419,15 +436,16 @@ Q4K_API int q4k_nccl_unique_id(void* id128) {
     return guarded([&] {
         if (!id128) invalid("buffer required");
         ncclUniqueId id;
-        const ncclResult_t r = ncclGetUniqueId(&id);
-        if (r != ncclSuccess) throw q4k::Error(Q4K_ECUDA, std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+        const auto& api = q4k::nccl();
+        const ncclResult_t r = api.GetUniqueId(&id);
+        if (r != ncclSuccess) throw q4k::Error(Q4K_ECUDA, std::string("ncclGetUniqueId: ") + api.GetErrorString(r));
         static_assert(sizeof id == 128, "NCCL unique id is 128 bytes");
         std::memcpy(id128, &id, sizeof id);
     });
 }
 
 Q4K_API int q4k_engine_create(const q4k_engine_config* cfg, const void* nccl_id, q4k_engine** out) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         if (!cfg || !out) invalid("config and output required");
         *out = nullptr;
         *out = new q4k_engine(*cfg, nccl_id);
@@ -435,11 +453,11 @@ Q4K_API int q4k_engine_create(const q4k_engine_config* cfg, const void* nccl_id,
 }
 
 Q4K_API int q4k_engine_destroy(q4k_engine* e) {
-    return guarded([&] { delete e; });
+    return guarded_cuda([&] { delete e; });
 }
 
 Q4K_API int q4k_engine_load_synthetic(q4k_engine* e, uint64_t seed) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         if (!e) invalid("engine required");
         e->impl.load_synthetic(seed);
     });
@@ -447,29 +465,36 @@ Q4K_API int q4k_engine_load_synthetic(q4k_engine* e, uint64_t seed) {
 
 Q4K_API int q4k_engine_set_tensor(q4k_engine* e, const char* name, int type, int64_t ne0, int64_t ne1,
                                   const void* host_gguf) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         if (!e || !name || !host_gguf) invalid("engine, name and data required");
         e->impl.set_tensor(name, type, ne0, ne1, host_gguf);
     });
 }
 
 Q4K_API int q4k_engine_fill_kv_synthetic(q4k_engine* e, uint64_t seed, int n) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         if (!e) invalid("engine required");
         e->impl.fill_kv_synthetic(seed, n);
     });
 }
 
 Q4K_API int q4k_engine_read_kv(q4k_engine* e, int layer, uint16_t* k_host, uint16_t* v_host) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         if (!e) invalid("engine required");
         e->impl.read_kv(layer, k_host, v_host);
     });
 }
 
+Q4K_API int q4k_engine_write_kv(q4k_engine* e, int layer, const uint16_t* k_host, const uint16_t* v_host) {
+    return guarded_cuda([&] {
+        if (!e) invalid("engine required");
+        e->impl.write_kv(layer, k_host, v_host);
+    });
+}
+
 Q4K_API int q4k_engine_decode(q4k_engine* e, uint32_t token, int position, uint32_t* next_token, float* logits_host,
                               float* hidden_host) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         if (!e || !next_token) invalid("engine and output required");
         *next_token = e->impl.decode(token, position, logits_host, hidden_host);
     });
@@ -477,9 +502,16 @@ Q4K_API int q4k_engine_decode(q4k_engine* e, uint32_t token, int position, uint3
 
 Q4K_API int q4k_engine_generate(q4k_engine* e, uint32_t token, int position, int steps, int advance,
                                 uint32_t* tokens_host) {
-    return guarded([&] {
+    return guarded_cuda([&] {
         if (!e) invalid("engine required");
         e->impl.generate(token, position, steps, advance, tokens_host);
+    });
+}
+
+Q4K_API int q4k_engine_layer(q4k_engine* e, int layer, const float* x_host, int position, float* x_out_host) {
+    return guarded_cuda([&] {
+        if (!e || !x_host || !x_out_host) invalid("engine and buffers required");
+        e->impl.layer_step(layer, x_host, position, x_out_host);
     });
 }
 

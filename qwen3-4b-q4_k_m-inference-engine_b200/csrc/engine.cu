@@ -20,9 +20,14 @@
 
 #include <cuda_runtime.h>
 
+#include <dlfcn.h>
+
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
+
+#include "nccl_api.h"
 
 #include "ops.h"
 #include "q4k_device.cuh"
@@ -35,7 +40,32 @@ void cuda_check(cudaError_t e, const char* what) {
 }
 
 static void nccl_check(ncclResult_t r, const char* what) {
-    if (r != ncclSuccess) throw Error(Q4K_ECUDA, std::string(what) + ": " + ncclGetErrorString(r));
+    if (r != ncclSuccess) throw Error(Q4K_ECUDA, std::string(what) + ": " + nccl().GetErrorString(r));
+}
+
+const NcclApi& nccl() {
+    static NcclApi api;
+    static std::once_flag once;
+    static std::string failure;
+    std::call_once(once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) {
+            failure = std::string("NCCL is not available: ") + dlerror();
+            return;
+        }
+        api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
+        api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(dlsym(h, "ncclCommInitRank"));
+        api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
+        api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(dlsym(h, "ncclAllReduce"));
+        api.AllGather = reinterpret_cast<decltype(api.AllGather)>(dlsym(h, "ncclAllGather"));
+        api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
+        if (!api.GetUniqueId || !api.CommInitRank || !api.CommDestroy || !api.AllReduce || !api.AllGather ||
+            !api.GetErrorString)
+            failure = "NCCL library lacks a required symbol";
+    });
+    if (!failure.empty()) throw Error(Q4K_ECUDA, failure);
+    return api;
 }
 
 namespace {
@@ -161,7 +191,7 @@ Engine::Engine(const q4k_engine_config& cfg, const void* nccl_id) : c_(cfg) {
         if (!nccl_id) throw Error(Q4K_EINVAL, "tp_world > 1 needs an NCCL unique id");
         ncclUniqueId id;
         std::memcpy(&id, nccl_id, sizeof id);
-        nccl_check(ncclCommInitRank(&comm_, world_, id, rank_), "ncclCommInitRank");
+        nccl_check(nccl().CommInitRank(&comm_, world_, id, rank_), "ncclCommInitRank");
     }
 
     layers_.resize(c.layers);
@@ -184,6 +214,9 @@ Engine::Engine(const q4k_engine_config& cfg, const void* nccl_id) : c_(cfg) {
     const size_t kv_elems = (size_t)c.layers * KVHl_ * c.capacity * c.head_dim;
     kcache_ = static_cast<uint16_t*>(alloc(kv_elems * 2));
     vcache_ = static_cast<uint16_t*>(alloc(kv_elems * 2));
+    // TMA views of the whole cache: rows = layers * kv_heads * capacity
+    cuda_check(make_kv_tensor_map(kcache_, (long long)c.layers * KVHl_ * c.capacity, &kmap_), "K tensor map");
+    cuda_check(make_kv_tensor_map(vcache_, (long long)c.layers * KVHl_ * c.capacity, &vmap_), "V tensor map");
     attn_part_o_ = static_cast<float*>(alloc(sizeof(float) * (size_t)Hl_ * splits_ * c.head_dim));
     attn_part_ml_ = static_cast<float*>(alloc(sizeof(float) * (size_t)Hl_ * splits_ * 2));
     attn_counters_ = static_cast<unsigned*>(alloc(sizeof(unsigned) * KVHl_));
@@ -199,7 +232,7 @@ Engine::Engine(const q4k_engine_config& cfg, const void* nccl_id) : c_(cfg) {
 Engine::~Engine() {
     if (exec_) cudaGraphExecDestroy(exec_);
     if (stream_) cudaStreamSynchronize(stream_);
-    if (comm_) ncclCommDestroy(comm_);
+    if (comm_) nccl().CommDestroy(comm_);
     for (void* p : allocations_) cudaFree(p);
     if (host_io_) cudaFreeHost(host_io_);
     if (stream_) cudaStreamDestroy(stream_);
@@ -350,6 +383,105 @@ void Engine::read_kv(int layer, uint16_t* k_host, uint16_t* v_host) {
     cuda_check(cudaStreamSynchronize(stream_), "read_kv");
 }
 
+void Engine::write_kv(int layer, const uint16_t* k_host, const uint16_t* v_host) {
+    if (layer < 0 || layer >= c_.layers) throw Error(Q4K_ERANGE, "layer out of range");
+    const size_t n = (size_t)KVHl_ * c_.capacity * c_.head_dim;
+    if (k_host)
+        cuda_check(cudaMemcpyAsync(kcache_ + (size_t)layer * n, k_host, n * 2, cudaMemcpyHostToDevice, stream_), "write");
+    if (v_host)
+        cuda_check(cudaMemcpyAsync(vcache_ + (size_t)layer * n, v_host, n * 2, cudaMemcpyHostToDevice, stream_), "write");
+    cuda_check(cudaStreamSynchronize(stream_), "write_kv");
+}
+
+// One transformer block (Engine.cpp:71-103) on the device buffers: x is
+// updated in place, layer i's K/V rows at *pos_ are written.
+void Engine::enqueue_layer(int i) {
+    const auto& c = c_;
+    const int H = c.hidden;
+    auto gemv = [&](GemvRequest& r) { cuda_check(launch_gemv(r, stream_), "gemv launch"); };
+    auto all_reduce_into_x = [&]() {
+        nccl_check(nccl().AllReduce(partial_, partial_, H, ncclFloat, ncclSum, comm_, stream_), "ncclAllReduce");
+        cuda_check(residual_add(x_, partial_, H, stream_), "residual_add");
+    };
+    const Layer& L = layers_[i];
+    const size_t kv_layer = (size_t)i * KVHl_ * c.capacity * c.head_dim;
+    {
+        GemvRequest r;
+        r.nseg = 3;
+        r.seg[0] = {L.q, qkv_, L.tq, qd_};
+        r.seg[1] = {L.k, qkv_ + qd_, L.tk, kvd_};
+        r.seg[2] = {L.v, qkv_ + qd_ + kvd_, L.tv, kvd_};
+        r.K = H;
+        r.x = x_;
+        r.gamma = L.attn_norm;
+        r.eps = c.eps;
+        r.epilogue = EPI_STORE;
+        r.err = err_;
+        r.pdl = true;
+        gemv(r);
+    }
+    {
+        DecodeAttnArgs a;
+        a.qkv = qkv_;
+        a.q_gamma = L.q_norm;
+        a.k_gamma = L.k_norm;
+        a.k_cache = kcache_ + kv_layer;
+        a.v_cache = vcache_ + kv_layer;
+        a.capacity = c.capacity;
+        a.position = pos_;
+        a.heads = Hl_;
+        a.kv_heads = KVHl_;
+        a.eps = c.eps;
+        a.rope_base = c.rope_base;
+        a.partial_o = attn_part_o_;
+        a.partial_ml = attn_part_ml_;
+        a.counters = attn_counters_;
+        a.out = att_;
+        a.err = err_;
+        a.splits = splits_;
+        a.row_base = i * KVHl_ * c.capacity;
+        cuda_check(decode_attention(a, kmap_, vmap_, stream_, true), "attention launch");
+    }
+    {
+        GemvRequest r;
+        r.nseg = 1;
+        r.seg[0] = {L.o, world_ > 1 ? partial_ : x_, L.to, H};
+        r.K = qd_;
+        r.x = att_;
+        r.epilogue = world_ > 1 ? EPI_STORE : EPI_ADD;
+        r.err = err_;
+        r.pdl = true;
+        gemv(r);
+        if (world_ > 1) all_reduce_into_x();
+    }
+    {
+        GemvRequest r;
+        r.nseg = 2;
+        r.seg[0] = {L.gate, act_, L.tgate, ffn_l_};
+        r.seg[1] = {L.up, act_, L.tup, ffn_l_};
+        r.K = H;
+        r.x = x_;
+        r.gamma = L.ffn_norm;
+        r.eps = c.eps;
+        r.epilogue = EPI_SWIGLU;
+        r.err = err_;
+        r.pdl = true;
+        gemv(r);
+    }
+    {
+        GemvRequest r;
+        r.nseg = 1;
+        r.seg[0] = {L.down, world_ > 1 ? partial_ : x_, L.tdown, H};
+        r.K = ffn_l_;
+        r.x = act_;
+        r.epilogue = world_ > 1 ? EPI_STORE : EPI_ADD;
+        r.err = err_;
+        r.pdl = true;
+        gemv(r);
+        if (world_ > 1) all_reduce_into_x();
+    }
+}
+
 void Engine::enqueue_step(bool record_hidden) {
     const auto& c = c_;
     const int H = c.hidden;
@@ -360,90 +492,11 @@ void Engine::enqueue_step(bool record_hidden) {
                                        stream_),
                        "snapshot");
     };
-    auto all_reduce_into_x = [&]() {
-        nccl_check(ncclAllReduce(partial_, partial_, H, ncclFloat, ncclSum, comm_, stream_), "ncclAllReduce");
-        cuda_check(residual_add(x_, partial_, H, stream_), "residual_add");
-    };
 
     cuda_check(embed_rows(token_embd_, t_embd_, H, c.vocab, token_, 1, x_, err_, stream_, false), "embed");
     snapshot(0);
     for (int i = 0; i < c.layers; ++i) {
-        const Layer& L = layers_[i];
-        const size_t kv_layer = (size_t)i * KVHl_ * c.capacity * c.head_dim;
-        {
-            GemvRequest r;
-            r.nseg = 3;
-            r.seg[0] = {L.q, qkv_, L.tq, qd_};
-            r.seg[1] = {L.k, qkv_ + qd_, L.tk, kvd_};
-            r.seg[2] = {L.v, qkv_ + qd_ + kvd_, L.tv, kvd_};
-            r.K = H;
-            r.x = x_;
-            r.gamma = L.attn_norm;
-            r.eps = c.eps;
-            r.epilogue = EPI_STORE;
-            r.err = err_;
-            r.pdl = true;
-            gemv(r);
-        }
-        {
-            DecodeAttnArgs a;
-            a.qkv = qkv_;
-            a.q_gamma = L.q_norm;
-            a.k_gamma = L.k_norm;
-            a.k_cache = kcache_ + kv_layer;
-            a.v_cache = vcache_ + kv_layer;
-            a.capacity = c.capacity;
-            a.position = pos_;
-            a.heads = Hl_;
-            a.kv_heads = KVHl_;
-            a.eps = c.eps;
-            a.rope_base = c.rope_base;
-            a.partial_o = attn_part_o_;
-            a.partial_ml = attn_part_ml_;
-            a.counters = attn_counters_;
-            a.out = att_;
-            a.err = err_;
-            a.splits = splits_;
-            cuda_check(decode_attention(a, stream_, true), "attention launch");
-        }
-        {
-            GemvRequest r;
-            r.nseg = 1;
-            r.seg[0] = {L.o, world_ > 1 ? partial_ : x_, L.to, H};
-            r.K = qd_;
-            r.x = att_;
-            r.epilogue = world_ > 1 ? EPI_STORE : EPI_ADD;
-            r.err = err_;
-            r.pdl = true;
-            gemv(r);
-            if (world_ > 1) all_reduce_into_x();
-        }
-        {
-            GemvRequest r;
-            r.nseg = 2;
-            r.seg[0] = {L.gate, act_, L.tgate, ffn_l_};
-            r.seg[1] = {L.up, act_, L.tup, ffn_l_};
-            r.K = H;
-            r.x = x_;
-            r.gamma = L.ffn_norm;
-            r.eps = c.eps;
-            r.epilogue = EPI_SWIGLU;
-            r.err = err_;
-            r.pdl = true;
-            gemv(r);
-        }
-        {
-            GemvRequest r;
-            r.nseg = 1;
-            r.seg[0] = {L.down, world_ > 1 ? partial_ : x_, L.tdown, H};
-            r.K = ffn_l_;
-            r.x = act_;
-            r.epilogue = world_ > 1 ? EPI_STORE : EPI_ADD;
-            r.err = err_;
-            r.pdl = true;
-            gemv(r);
-            if (world_ > 1) all_reduce_into_x();
-        }
+        enqueue_layer(i);
         snapshot(i + 1);
     }
     {
@@ -471,7 +524,7 @@ void Engine::enqueue_step(bool record_hidden) {
         gemv(r);
     }
     if (world_ > 1)
-        nccl_check(ncclAllGather(tp_cand_local_, tp_cand_all_, 2, ncclUint32, comm_, stream_), "ncclAllGather");
+        nccl_check(nccl().AllGather(tp_cand_local_, tp_cand_all_, 2, ncclUint32, comm_, stream_), "ncclAllGather");
     {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(1);
@@ -570,6 +623,18 @@ void Engine::generate(uint32_t token, int position, int steps, int advance, uint
     if (tokens_host)
         cuda_check(cudaMemcpyAsync(tokens_host, history_, sizeof(uint32_t) * steps, cudaMemcpyDeviceToHost, stream_),
                    "d2h tokens");
+    check_device_error();
+}
+
+void Engine::layer_step(int layer, const float* x_host, int position, float* x_out_host) {
+    if (!loaded_) throw Error(Q4K_EINVAL, "weights are not loaded");
+    if (layer < 0 || layer >= c_.layers) throw Error(Q4K_ERANGE, "layer out of range");
+    if (position < 0 || position >= c_.capacity) throw Error(Q4K_ERANGE, "KV cache capacity exceeded");
+    host_io_[1] = (uint32_t)position;
+    cuda_check(cudaMemcpyAsync(pos_, &host_io_[1], 4, cudaMemcpyHostToDevice, stream_), "h2d");
+    cuda_check(cudaMemcpyAsync(x_, x_host, sizeof(float) * c_.hidden, cudaMemcpyHostToDevice, stream_), "h2d x");
+    enqueue_layer(layer);
+    cuda_check(cudaMemcpyAsync(x_out_host, x_, sizeof(float) * c_.hidden, cudaMemcpyDeviceToHost, stream_), "d2h x");
     check_device_error();
 }
 

@@ -9,6 +9,7 @@
 #include <vector>
 
 #include "../../include/q4k_b200.h"
+#include "ops.h"
 
 namespace q4k {
 
@@ -49,8 +50,11 @@ public:
     void set_tensor(const std::string& name, int type, int64_t ne0, int64_t ne1, const void* host_gguf);
     void fill_kv_synthetic(uint64_t seed, int n);
     void read_kv(int layer, uint16_t* k_host, uint16_t* v_host);
+    void write_kv(int layer, const uint16_t* k_host, const uint16_t* v_host);
     uint32_t decode(uint32_t token, int position, float* logits_host, float* hidden_host);
     void generate(uint32_t token, int position, int steps, int advance, uint32_t* tokens_host);
+    // One block on a given residual-stream input (tp_world == 1 or all ranks).
+    void layer_step(int layer, const float* x_host, int position, float* x_out_host);
     cudaStream_t stream() const { return stream_; }
 
 private:
@@ -66,6 +70,7 @@ private:
     void** tensor_slot(const TensorSpec& t, int** type_slot);
     void place(const TensorSpec& t, const void* raw_device);
     void enqueue_step(bool record_hidden);
+    void enqueue_layer(int i);
     void check_device_error();
     void ensure_graph();
 
@@ -96,6 +101,7 @@ private:
     unsigned* history_n_ = nullptr; // device: count
     int* err_ = nullptr;
     uint16_t *kcache_ = nullptr, *vcache_ = nullptr;
+    KvTensorMap kmap_{}, vmap_{};
     float *attn_part_o_ = nullptr, *attn_part_ml_ = nullptr;
     unsigned* attn_counters_ = nullptr;
     float* am_score_ = nullptr;

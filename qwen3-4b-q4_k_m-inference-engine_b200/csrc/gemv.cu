@@ -4,27 +4,34 @@
 // (src/cuda/matmul.cu:24-125): the fp32 activation is first quantised to
 // int8 with one fp32 scale per 32 values (matmul.cu:8-22), then every
 // 32-value group contributes  xs[g] * (d*sc*sum(q*xq) - dmin*m*sum(xq))
-// for Q4_K and  xs[g] * (d*sc*sum((q-32)*xq))  for Q6_K, with the integer
-// dot products done by dp4a.
+// for Q4_K and every 16-value run  xs[g] * (d*sc*sum((q-32)*xq))  for Q6_K,
+// with the integer dot products done by dp4a.
 //
-// B200 structure (one CTA per SM, HBM-bound):
-//   * warp W (the last one) is a producer: one lane streams whole weight rows
-//     from HBM into shared memory with cp.async.bulk (TMA bulk copies)
-//     completing on mbarriers. It starts before griddepcontrol.wait, so under
-//     programmatic dependent launch the weights of this product stream in
-//     while the previous kernel is still finishing.
-//   * warps 0..W-1 are consumers. They quantise the activation into shared
-//     memory (optionally applying RMSNorm first, which fuses
-//     rms_norm.cu:6-24 into the product), then each warp owns a private ring
-//     of S row buffers: row i of the CTA's range goes to warp i % W. A warp
-//     reduces its row with shuffles and lane 0 writes the result, so the main
-//     loop has no CTA-wide barrier.
-//   * activation codes are stored in a permuted order per block so that the
-//     16-byte shared loads of the 8 lanes working on one super-block hit 32
+// B200 structure (HBM-bound; one or two CTAs per SM):
+//   * warp W (the last one) is a producer: one lane streams "stages" of R
+//     consecutive weight rows (20-35 KB, one cp.async.bulk per matrix) into a
+//     ring of S shared-memory buffers, completing on mbarriers. The bulk-copy
+//     engine reaches full HBM bandwidth only with copies of >= 16 KB and
+//     >= 64 KB in flight per SM, hence the large stages. The producer starts
+//     before griddepcontrol.wait, so under programmatic dependent launch a
+//     product's weights stream in while the previous kernel drains.
+//   * warps 0..W-1 are consumers in T teams of TW warps; team k consumes the
+//     stages k, k+T, ... . Within a team, LPR lanes work on one row (so a
+//     team covers R = TW*32/LPR rows per stage); lane f of a row takes the
+//     16-byte chunks f, f+LPR, ... . Rows are reduced with xor-shuffles in a
+//     fixed order, so results are deterministic.
+//   * before the rows, the consumers quantise the activation into shared
+//     memory (optionally RMSNorm-ing it first, which fuses rms_norm.cu:6-24
+//     into the product). Codes are stored in a per-block permuted order so
+//     that the 16-byte loads of the 8 lanes on one super-block hit 32
 //     distinct banks.
+//   * Q4_K: the two lanes on one 32-byte group pair each dot both nibble
+//     planes of their 16 bytes, swap one partial with a shuffle, and then
+//     each finishes one whole group (one 6-bit scale/min decode per lane).
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "q4k_device.cuh"
@@ -33,23 +40,36 @@
 namespace q4k {
 namespace {
 
+constexpr int kTeamWarps = 4;  // warps per consumer team
+constexpr int kAllConsumersBarrier = 8;
+
 struct GemvPlan {
     GemvSegment seg[kMaxSegments];
-    int seg_start[kMaxSegments + 1];
+    int stage_start[kMaxSegments + 1];  // first stage index of each segment
     int nseg;
     int K, nb, M, ldx, ldy;
     const float* x;
     const float* gamma;
     float eps;
     int epilogue;
-    int total_rows;
-    int stages;      // S: buffers per consumer warp
-    int slot_bytes;  // bytes per buffer (one job: 1 row, or 2 rows when paired)
+    int total_stages;
+    int rows_per_stage;  // R: output rows per stage
+    int lpr;             // lanes per row
+    int S;               // ring depth
+    int stage_bytes;
     int row_bytes[kMaxSegments];
-    int off_xq4, off_xq6, off_xs, off_xsum, off_bufs, off_bars, off_red;  // shared-memory offsets
+    int off_xq4, off_xq6, off_xs, off_xsum16, off_xsum32, off_bufs, off_bars, off_misc;
     ArgmaxTarget argmax;
     int* err;
 };
+
+// Segment, first local row and row count of stage i.
+__device__ __forceinline__ void stage_rows(const GemvPlan& p, int i, int& seg, int& r0, int& nr) {
+    seg = 0;
+    while (seg + 1 < p.nseg && i >= p.stage_start[seg + 1]) ++seg;
+    r0 = (i - p.stage_start[seg]) * p.rows_per_stage;
+    nr = min(p.rows_per_stage, p.seg[seg].rows - r0);
+}
 
 // 6-bit scale and min of 32-value group g of a Q4_K block, from the three
 // header words holding bytes 4..15 (matmul.cu:40-48).
@@ -65,15 +85,17 @@ __device__ __forceinline__ void q4_scale_min(uint32_t w0, uint32_t w1, uint32_t 
     }
 }
 
-// Lane chunk f of a Q4_K row: block b = f/8, c = f%8 covers bytes
-// 16 + 32*(c/2) + 16*(c%2) .. +16 of the block, i.e. positions 16*(c%2)..+15
-// of groups 2*(c/2) (low nibbles) and 2*(c/2)+1 (high nibbles).
-template <int MT, int JR>
-__device__ __forceinline__ void q4_chunk(const uint8_t* const (&rows)[JR], int f, const uint8_t* xq, const float* xs,
-                                         const int* xsum, int K, int mcount, float (&acc)[JR][MT]) {
+// Q4_K chunk f of a row: block b = f/8, c = f%8, j = c/2, h = c%2 covers the
+// 16 bytes at 16 + 32*j + 16*h of the block: positions 16h..16h+15 of group
+// 2j (low nibbles) and of group 2j+1 (high nibbles). The pair of lanes
+// (h = 0, 1) exchanges one partial dot so that the h = 0 lane completes group
+// 2j and the h = 1 lane group 2j+1. `live` is false for a padding iteration
+// (the lane still takes part in the shuffle, its term is dropped).
+template <int MT, int NR>
+__device__ __forceinline__ void q4_chunk(const uint8_t* const (&rows)[NR], int f, bool live, const uint8_t* xq,
+                                         const float* xs, const int* xsum32, int K, int mcount, float (&acc)[NR][MT]) {
     const int b = f >> 3, c = f & 7, j = c >> 1, h = c & 1;
-    const int g0 = 2 * j;
-    const int r_lo = b * 16 + 4 * j + h, r_hi = r_lo + 2;
+    const int g = 2 * j + h;
     uint4 xlo[MT], xhi[MT];
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
@@ -83,16 +105,14 @@ __device__ __forceinline__ void q4_chunk(const uint8_t* const (&rows)[JR], int f
         }
     }
 #pragma unroll
-    for (int r = 0; r < JR; ++r) {
+    for (int r = 0; r < NR; ++r) {
         const uint8_t* blk = rows[r] + b * 144;
         const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
         const uint4 q = *reinterpret_cast<const uint4*>(blk + 16 + 32 * j + 16 * h);
-        const float d = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
-        int sc0, m0, sc1, m1;
-        q4_scale_min(hdr.y, hdr.z, hdr.w, g0, sc0, m0);
-        q4_scale_min(hdr.y, hdr.z, hdr.w, g0 + 1, sc1, m1);
-        const float ds0 = d * (float)sc0, dm0 = dmin * (float)m0;
-        const float ds1 = d * (float)sc1, dm1 = dmin * (float)m1;
+        int sc, mn;
+        q4_scale_min(hdr.y, hdr.z, hdr.w, g, sc, mn);
+        const float ds = half_bits_to_float(hdr.x) * (float)sc;
+        const float dm = half_bits_to_float(hdr.x >> 16) * (float)mn;
         const uint32_t l0 = q.x & 0x0f0f0f0fu, l1 = q.y & 0x0f0f0f0fu, l2 = q.z & 0x0f0f0f0fu, l3 = q.w & 0x0f0f0f0fu;
         const uint32_t h0 = (q.x >> 4) & 0x0f0f0f0fu, h1 = (q.y >> 4) & 0x0f0f0f0fu;
         const uint32_t h2 = (q.z >> 4) & 0x0f0f0f0fu, h3 = (q.w >> 4) & 0x0f0f0f0fu;
@@ -107,24 +127,26 @@ __device__ __forceinline__ void q4_chunk(const uint8_t* const (&rows)[JR], int f
                 dhi = __dp4a((int)h1, (int)xhi[m].y, dhi);
                 dhi = __dp4a((int)h2, (int)xhi[m].z, dhi);
                 dhi = __dp4a((int)h3, (int)xhi[m].w, dhi);
-                const float* xsm = xs + m * (K / 32) + b * 8;
-                const int* sum = xsum + m * (K / 16);
-                acc[r][m] += xsm[g0] * (ds0 * (float)dlo - dm0 * (float)sum[r_lo]) +
-                             xsm[g0 + 1] * (ds1 * (float)dhi - dm1 * (float)sum[r_hi]);
+                const int mine = h ? dhi : dlo;
+                const int theirs = __shfl_xor_sync(0xffffffffu, h ? dlo : dhi, 1);
+                const int dot = mine + theirs;
+                const int gi = m * (K / 32) + b * 8 + g;
+                const float term = xs[gi] * (ds * (float)dot - dm * (float)xsum32[gi]);
+                if (live) acc[r][m] += term;
             }
         }
     }
 }
 
-// Lane chunk f of a Q6_K planar row: block b = f/8, c = f%8 -> half = c/4,
+// Q6_K chunk f of a planar row: block b = f/8, c = f%8 -> half = c/4,
 // s = (c/2)%2, t = c%2. The 16 ql bytes at half*64 + s*32 + t*16 carry the
 // low nibbles of 16-value runs A (32-group 4*half+s) and B (4*half+s+2);
 // the 16 qh bytes at half*32 + t*16 carry their top two bits
 // (matmul.cu:68-83, embedding.cu:42-58).
-template <int MT, int JR>
-__device__ __forceinline__ void q6_chunk(const uint8_t* const (&rows)[JR], int nb, int f, const uint8_t* xq,
-                                         const float* xs, const int* xsum, int K, int mcount,
-                                         float (&acc)[JR][MT]) {
+template <int MT, int NR>
+__device__ __forceinline__ void q6_chunk(const uint8_t* const (&rows)[NR], int nb, int f, bool live,
+                                         const uint8_t* xq, const float* xs, const int* xsum16, int K, int mcount,
+                                         float (&acc)[NR][MT]) {
     const int b = f >> 3, c = f & 7, half = c >> 2, s = (c >> 1) & 1, t = c & 1;
     const int rA = 8 * half + 2 * s + t, rB = rA + 4;
     const int gA = 4 * half + s, gB = gA + 2;
@@ -138,7 +160,7 @@ __device__ __forceinline__ void q6_chunk(const uint8_t* const (&rows)[JR], int n
         }
     }
 #pragma unroll
-    for (int r = 0; r < JR; ++r) {
+    for (int r = 0; r < NR; ++r) {
         const uint8_t* row = rows[r];
         const uint4 ql = *reinterpret_cast<const uint4*>(row + b * 128 + half * 64 + s * 32 + t * 16);
         const uint4 qh = *reinterpret_cast<const uint4*>(row + nb * 128 + b * 64 + half * 32 + t * 16);
@@ -156,9 +178,9 @@ __device__ __forceinline__ void q6_chunk(const uint8_t* const (&rows)[JR], int n
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
             if (m < mcount) {
-                const int* sum = xsum + m * (K / 16) + b * 16;
+                const int* sum = xsum16 + m * (K / 16) + b * 16;
                 // codes are in [0, 63], so signed dp4a is exact; (q - 32) is
-                // applied through the run sums.
+                // applied through the run sums
                 int da = __dp4a((int)a0, (int)xa[m].x, 0);
                 da = __dp4a((int)a1, (int)xa[m].y, da);
                 da = __dp4a((int)a2, (int)xa[m].z, da);
@@ -170,7 +192,8 @@ __device__ __forceinline__ void q6_chunk(const uint8_t* const (&rows)[JR], int n
                 db = __dp4a((int)b3, (int)xb[m].w, db);
                 db -= 32 * sum[rB];
                 const float* xsm = xs + m * (K / 32) + b * 8;
-                acc[r][m] += xsm[gA] * (dA * (float)da) + xsm[gB] * (dB * (float)db);
+                const float term = xsm[gA] * (dA * (float)da) + xsm[gB] * (dB * (float)db);
+                if (live) acc[r][m] += term;
             }
         }
     }
@@ -192,91 +215,57 @@ __device__ __forceinline__ int8_t q8_code(float v, float amax) {
     return amax == 0.0f ? 0 : static_cast<int8_t>(roundf(__fmul_rn(__fdiv_rn(v, amax), 127.0f)));
 }
 
-template <int MT, int JR>
-__global__ void __launch_bounds__(288, MT <= 2 ? 2 : 1) gemv_kernel(const __grid_constant__ GemvPlan p) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int W = (int)(blockDim.x >> 5) - 1;  // consumer warps
-    const int S = p.stages;
+// Quantise MT activation rows into shared memory: codes (in the Q4_K and/or
+// Q6_K permuted order), one fp32 scale per 32 values, code sums per 16 and
+// per 32 values. Called by all W*32 consumer threads.
+__device__ __forceinline__ void quantise_activation(const GemvPlan& p, int m0, int mcount, uint8_t* smem, int tid,
+                                                    int lane, int warp, int nthreads) {
     const int K = p.K;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bars);
-    uint64_t* empty = full + W * S;
-    uint8_t* bufs = smem + p.off_bufs;
-
-    const int G = gridDim.x;
-    const int r_begin = (int)((long long)p.total_rows * blockIdx.x / G);
-    const int r_end = (int)((long long)p.total_rows * (blockIdx.x + 1) / G);
-    const int m0 = blockIdx.y * MT;
-    const int mcount = min(MT, p.M - m0);
-
-    if (tid == 0) {
-        for (int i = 0; i < W * S; ++i) {
-            mbar_init(full + i, 1);
-            mbar_init(empty + i, 1);
-        }
-        mbar_fence_init();
-    }
-    __syncthreads();
-    pdl_launch_dependents();
-
-    if (warp == W) {
-        // ---------------- producer ----------------
-        if (lane == 0) {
-            const uint64_t policy = policy_evict_first();
-            int seg = 0;
-            for (int i = 0, row = r_begin; row < r_end; ++i, ++row) {
-                const int w = i % W, slot = (i / W) % S, use = i / (W * S);
-                uint64_t* fb = full + w * S + slot;
-                if (use > 0 && !mbar_wait_bounded(empty + w * S + slot, (use - 1) & 1, p.err, ERR_WAIT_TIMEOUT_EMPTY))
-                    break;
-                while (seg + 1 < p.nseg && row >= p.seg_start[seg + 1]) ++seg;
-                const int local = row - p.seg_start[seg];
-                uint8_t* dst = bufs + (size_t)(w * S + slot) * p.slot_bytes;
-                if (JR == 2) {
-                    const int rb = p.row_bytes[0];
-                    mbar_arrive_expect_tx(fb, 2 * rb);
-                    bulk_g2s_hint(dst, p.seg[0].w + (size_t)local * rb, rb, fb, policy);
-                    bulk_g2s_hint(dst + rb, p.seg[1].w + (size_t)local * rb, rb, fb, policy);
-                } else {
-                    const int rb = p.row_bytes[seg];
-                    mbar_arrive_expect_tx(fb, rb);
-                    bulk_g2s_hint(dst, p.seg[seg].w + (size_t)local * rb, rb, fb, policy);
-                }
-            }
-        }
-        return;
-    }
-
-    // ---------------- consumers: quantise the activation ----------------
-    pdl_wait();
     uint8_t* xq4 = p.off_xq4 >= 0 ? smem + p.off_xq4 : nullptr;
     uint8_t* xq6 = p.off_xq6 >= 0 ? smem + p.off_xq6 : nullptr;
     float* xs = reinterpret_cast<float*>(smem + p.off_xs);
-    int* xsum = reinterpret_cast<int*>(smem + p.off_xsum);
-    float* red = reinterpret_cast<float*>(smem + p.off_red);
-    const int nthreads = W * 32;
+    int* xsum16 = reinterpret_cast<int*>(smem + p.off_xsum16);
+    int* xsum32 = reinterpret_cast<int*>(smem + p.off_xsum32);
+    float* red = reinterpret_cast<float*>(smem + p.off_misc);
+    const int nvec = K / 4;
+    constexpr int kHeld = 12;  // float4s of the row a thread keeps in registers (K <= 12 * 4 * nthreads)
     for (int m = 0; m < mcount; ++m) {
-        const float* xr = p.x + (size_t)(m0 + m) * p.ldx;
+        const float4* xr = reinterpret_cast<const float4*>(p.x + (size_t)(m0 + m) * p.ldx);
+        // one pass over the row: every load in flight at once, kept for both uses
+        float4 held[kHeld];
+#pragma unroll
+        for (int k = 0; k < kHeld; ++k) {
+            const int i = tid + k * nthreads;
+            if (i < nvec) held[k] = xr[i];
+        }
         float inv = 1.0f;
         if (p.gamma) {
             float ss = 0.0f;
-            for (int i = tid * 4; i < K; i += nthreads * 4) {
-                const float4 v = *reinterpret_cast<const float4*>(xr + i);
-                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+#pragma unroll
+            for (int k = 0; k < kHeld; ++k) {
+                const int i = tid + k * nthreads;
+                if (i < nvec) {
+                    const float4 v = held[k];
+                    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                }
             }
             ss = warp_sum(ss);
             if (lane == 0) red[warp] = ss;
-            named_barrier(1, nthreads);
+            named_barrier(kAllConsumersBarrier, nthreads);
             float total = 0.0f;
-            for (int i = 0; i < W; ++i) total += red[i];
+            for (int i = 0; i < nthreads / 32; ++i) total += red[i];
             inv = rsqrtf(total / (float)K + p.eps);  // rms_norm.cu:17
-            named_barrier(1, nthreads);
+            named_barrier(kAllConsumersBarrier, nthreads);
         }
-        for (int g = warp * 4 + (lane >> 3); g < K / 32; g += W * 4) {
-            const int e = g * 32 + (lane & 7) * 4;
-            float4 v = *reinterpret_cast<const float4*>(xr + e);
+        // element e = 4*i of the row; the 8 lanes i..i+7 hold one 32-group
+#pragma unroll
+        for (int k = 0; k < kHeld; ++k) {
+            const int i = tid + k * nthreads;
+            if (i >= nvec) break;
+            const int e = 4 * i;
+            float4 v = held[k];
             if (p.gamma) {
-                const float4 gm = *reinterpret_cast<const float4*>(p.gamma + e);
+                const float4 gm = reinterpret_cast<const float4*>(p.gamma)[i];
                 v.x = (v.x * inv) * gm.x;  // rms_norm.cu:19: input * inverse_rms * scale
                 v.y = (v.y * inv) * gm.y;
                 v.z = (v.z * inv) * gm.z;
@@ -293,68 +282,157 @@ __global__ void __launch_bounds__(288, MT <= 2 ? 2 : 1) gemv_kernel(const __grid
             int run = (int)c0 + (int)c1 + (int)c2 + (int)c3;
             run += __shfl_xor_sync(0xffffffffu, run, 1);
             run += __shfl_xor_sync(0xffffffffu, run, 2);
+            const int group = run + __shfl_xor_sync(0xffffffffu, run, 4);
             const int b = e >> 8, r16 = (e & 255) >> 4, o = e & 15;
             if (xq4) *reinterpret_cast<uint32_t*>(xq4 + m * K + b * 256 + perm_q4(r16) + o) = word;
             if (xq6) *reinterpret_cast<uint32_t*>(xq6 + m * K + b * 256 + perm_q6(r16) + o) = word;
-            if ((lane & 3) == 0) xsum[m * (K / 16) + (e >> 4)] = run;
-            if ((lane & 7) == 0) xs[m * (K / 32) + g] = amax / 127.0f;  // matmul.cu:18
+            if ((lane & 3) == 0) xsum16[m * (K / 16) + (e >> 4)] = run;
+            if ((lane & 7) == 0) {
+                xsum32[m * (K / 32) + (e >> 5)] = group;
+                xs[m * (K / 32) + (e >> 5)] = amax / 127.0f;  // matmul.cu:18
+            }
         }
     }
-    named_barrier(1, nthreads);
+    named_barrier(kAllConsumersBarrier, nthreads);
+}
 
-    // ---------------- consumers: rows ----------------
+template <int MT, int NR>
+__global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant__ GemvPlan p) {
+    constexpr bool PAIR = NR == 2;  // gate and up rows worked together (SwiGLU)
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int W = (int)(blockDim.x >> 5) - 1;  // consumer warps
+    const int T = W / kTeamWarps;             // teams
+    const int S = p.S;
+    const int K = p.K;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bars);
+    uint64_t* empty = full + S;
+    uint8_t* bufs = smem + p.off_bufs;
+    int* team_abort = reinterpret_cast<int*>(smem + p.off_misc) + 64;
+
+    const int G = gridDim.x;
+    const int s_begin = (int)((long long)p.total_stages * blockIdx.x / G);
+    const int s_end = (int)((long long)p.total_stages * (blockIdx.x + 1) / G);
+    const int m0 = blockIdx.y * MT;
+    const int mcount = min(MT, p.M - m0);
+
+    if (tid == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, 1);
+        }
+        for (int k = 0; k < 4; ++k) team_abort[k] = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+
+    if (warp == W) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            const uint64_t policy = policy_evict_first();
+            for (int i = 0, st = s_begin; st < s_end; ++i, ++st) {
+                const int slot = i % S, use = i / S;
+                uint64_t* fb = full + slot;
+                if (use > 0 && !mbar_wait_bounded(empty + slot, (use - 1) & 1, p.err, ERR_WAIT_TIMEOUT_EMPTY)) break;
+                int seg, r0, nr;
+                stage_rows(p, st, seg, r0, nr);
+                const int rb = p.row_bytes[seg];
+                uint8_t* dst = bufs + (size_t)slot * p.stage_bytes;
+                if (PAIR) {
+                    mbar_arrive_expect_tx(fb, 2 * nr * rb);
+                    bulk_g2s_hint(dst, p.seg[0].w + (size_t)r0 * rb, nr * rb, fb, policy);
+                    bulk_g2s_hint(dst + p.rows_per_stage * rb, p.seg[1].w + (size_t)r0 * rb, nr * rb, fb, policy);
+                } else {
+                    mbar_arrive_expect_tx(fb, nr * rb);
+                    bulk_g2s_hint(dst, p.seg[seg].w + (size_t)r0 * rb, nr * rb, fb, policy);
+                }
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers ----------------
+    pdl_wait();
+    const int nthreads = W * 32;
+    quantise_activation(p, m0, mcount, smem, tid, lane, warp, nthreads);
+    const uint8_t* xq4 = p.off_xq4 >= 0 ? smem + p.off_xq4 : nullptr;
+    const uint8_t* xq6 = p.off_xq6 >= 0 ? smem + p.off_xq6 : nullptr;
+    const float* xs = reinterpret_cast<const float*>(smem + p.off_xs);
+    const int* xsum16 = reinterpret_cast<const int*>(smem + p.off_xsum16);
+    const int* xsum32 = reinterpret_cast<const int*>(smem + p.off_xsum32);
+
+    const int team = warp / kTeamWarps;
+    const int team_threads = kTeamWarps * 32;
+    const int LPR = p.lpr;
+    const int sub = lane % LPR;                                        // lane within the row's lanes
+    const int slot_row = (warp % kTeamWarps) * (32 / LPR) + lane / LPR;  // row of the stage
+    const int chunks = p.nb * 8;
+    const int iters = (chunks + LPR - 1) / LPR;
     float best_score = -__int_as_float(0x7f800000);
     uint32_t best_index = 0xffffffffu;
-    int seg = 0;
-    for (int i = warp, row = r_begin + warp; row < r_end; i += W, row += W) {
-        const int slot = (i / W) % S, use = i / (W * S);
-        // every lane waits; the warp leaves together if any lane gave up
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(full + warp * S + slot, use & 1, p.err, ERR_WAIT_TIMEOUT_FULL)))
-            break;
-        while (seg + 1 < p.nseg && row >= p.seg_start[seg + 1]) ++seg;
-        const int jseg = JR == 2 ? 0 : seg;
-        const int local = row - p.seg_start[jseg];
-        const uint8_t* buf = bufs + (size_t)(warp * S + slot) * p.slot_bytes;
-        const uint8_t* rows[JR];
+
+    for (int i = team, st = s_begin + team; st < s_end; i += T, st += T) {
+        const int slot = i % S, use = i / S;
+        if (!mbar_wait_bounded(full + slot, use & 1, p.err, ERR_WAIT_TIMEOUT_FULL)) team_abort[team] = 1;
+        int seg, r0, nr;
+        stage_rows(p, st, seg, r0, nr);
+        const int rb = p.row_bytes[seg];
+        const uint8_t* buf = bufs + (size_t)slot * p.stage_bytes;
+        const int rr = slot_row < nr ? slot_row : 0;  // idle rows alias row 0; dropped below
+        const uint8_t* rows[NR];
+        rows[0] = buf + rr * rb;
+        if (PAIR) rows[NR - 1] = buf + (p.rows_per_stage + rr) * rb;
+        float acc[NR][MT];
 #pragma unroll
-        for (int r = 0; r < JR; ++r) rows[r] = buf + r * p.row_bytes[jseg];
-        float acc[JR][MT];
-#pragma unroll
-        for (int r = 0; r < JR; ++r)
+        for (int r = 0; r < NR; ++r)
 #pragma unroll
             for (int m = 0; m < MT; ++m) acc[r][m] = 0.0f;
-        const int chunks = p.nb * 8;
-        if (p.seg[jseg].type == Q4K_TYPE_Q4_K) {
-#pragma unroll(MT <= 2 ? 2 : 1)
-            for (int f = lane; f < chunks; f += 32) q4_chunk<MT, JR>(rows, f, xq4, xs, xsum, K, mcount, acc);
+        if (p.seg[seg].type == Q4K_TYPE_Q4_K) {
+#pragma unroll 2
+            for (int k = 0; k < iters; ++k) {
+                const int f = sub + LPR * k;
+                const bool live = f < chunks;
+                q4_chunk<MT, NR>(rows, live ? f : (f & 1), live, xq4, xs, xsum32, K, mcount, acc);
+            }
         } else {
-#pragma unroll(MT <= 2 ? 2 : 1)
-            for (int f = lane; f < chunks; f += 32) q6_chunk<MT, JR>(rows, p.nb, f, xq6, xs, xsum, K, mcount, acc);
+#pragma unroll 2
+            for (int k = 0; k < iters; ++k) {
+                const int f = sub + LPR * k;
+                const bool live = f < chunks;
+                q6_chunk<MT, NR>(rows, p.nb, live ? f : (f & 1), live, xq6, xs, xsum16, K, mcount, acc);
+            }
         }
+        // all of this team's reads of the stage are done: release it
+        named_barrier(1 + team, team_threads);
+        if (warp % kTeamWarps == 0 && lane == 0) mbar_arrive(empty + slot);
+        const bool abort_now = team_abort[team] != 0;
+        // reduce each row over its LPR lanes (fixed xor order)
 #pragma unroll
-        for (int r = 0; r < JR; ++r)
+        for (int r = 0; r < NR; ++r)
 #pragma unroll
-            for (int m = 0; m < MT; ++m) acc[r][m] = warp_sum(acc[r][m]);
-        __syncwarp();
-        if (lane == 0) {
-            mbar_arrive(empty + warp * S + slot);
-            float* y = p.seg[jseg].y;
+            for (int m = 0; m < MT; ++m)
+                for (int o = LPR >> 1; o > 0; o >>= 1) acc[r][m] += __shfl_xor_sync(0xffffffffu, acc[r][m], o);
+        if (abort_now) break;
+        if (sub == 0 && slot_row < nr) {
+            float* y = p.seg[seg].y;
+            const int row = r0 + slot_row;
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
                 if (m >= mcount) break;
-                float* out = y ? y + (size_t)(m0 + m) * p.ldy + local : nullptr;
+                float* out = y ? y + (size_t)(m0 + m) * p.ldy + row : nullptr;
                 if (p.epilogue == EPI_STORE) {
                     *out = acc[0][m];
                 } else if (p.epilogue == EPI_ADD) {
                     *out += acc[0][m];
                 } else if (p.epilogue == EPI_SWIGLU) {
-                    const float g = acc[0][m], u = acc[JR - 1][m];
+                    const float g = acc[0][m], u = acc[NR - 1][m];
                     *out = (g / (1.0f + expf(-g))) * u;  // silu_multiply.cu:9-10
                 } else {
                     if (out) *out = acc[0][m];
-                    if (candidate_better(acc[0][m], (uint32_t)local, best_score, best_index)) {
+                    if (candidate_better(acc[0][m], (uint32_t)row, best_score, best_index)) {
                         best_score = acc[0][m];
-                        best_index = (uint32_t)local;
+                        best_index = (uint32_t)row;
                     }
                 }
             }
@@ -367,11 +445,20 @@ __global__ void __launch_bounds__(288, MT <= 2 ? 2 : 1) gemv_kernel(const __grid
         __shared__ float s_score[32];
         __shared__ uint32_t s_index[32];
         __shared__ bool s_last;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float os = __shfl_xor_sync(0xffffffffu, best_score, o);
+            const uint32_t oi = __shfl_xor_sync(0xffffffffu, best_index, o);
+            if (candidate_better(os, oi, best_score, best_index)) {
+                best_score = os;
+                best_index = oi;
+            }
+        }
         if (lane == 0) {
             s_score[warp] = best_score;
             s_index[warp] = best_index;
         }
-        named_barrier(1, nthreads);
+        named_barrier(kAllConsumersBarrier, nthreads);
         if (tid == 0) {
             float bs = s_score[0];
             uint32_t bi = s_index[0];
@@ -386,7 +473,7 @@ __global__ void __launch_bounds__(288, MT <= 2 ? 2 : 1) gemv_kernel(const __grid
             const unsigned done = atomicAdd(p.argmax.counter, 1u);
             s_last = done == (unsigned)(G - 1);
         }
-        named_barrier(1, nthreads);
+        named_barrier(kAllConsumersBarrier, nthreads);
         if (s_last && warp == 0) {
             __threadfence();
             float bs = -__int_as_float(0x7f800000);
@@ -417,15 +504,22 @@ __global__ void __launch_bounds__(288, MT <= 2 ? 2 : 1) gemv_kernel(const __grid
     }
 }
 
-template <int MT, int JR>
+template <int MT, int NR>
 cudaError_t launch_instance(const GemvPlan& plan, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl) {
     static std::once_flag once;
     static cudaError_t attr_status = cudaSuccess;
+    static size_t max_dynamic = 0;
     std::call_once(once, [] {
-        attr_status = cudaFuncSetAttribute(gemv_kernel<MT, JR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           227 * 1024);
+        // static + dynamic shared memory must fit the 227 KB per-block limit
+        cudaFuncAttributes fa{};
+        attr_status = cudaFuncGetAttributes(&fa, gemv_kernel<MT, NR>);
+        if (attr_status != cudaSuccess) return;
+        max_dynamic = 227 * 1024 - fa.sharedSizeBytes;
+        attr_status = cudaFuncSetAttribute(gemv_kernel<MT, NR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)max_dynamic);
     });
     if (attr_status != cudaSuccess) return attr_status;
+    if (smem > max_dynamic) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -436,10 +530,15 @@ cudaError_t launch_instance(const GemvPlan& plan, dim3 grid, dim3 block, size_t 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<MT, JR>, plan);
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<MT, NR>, plan);
 }
 
 int align_up(int v, int a) { return (v + a - 1) / a * a; }
+
+int env_int(const char* name, int fallback) {
+    const char* v = std::getenv(name);
+    return v && *v ? std::atoi(v) : fallback;
+}
 
 }  // namespace
 
@@ -462,7 +561,6 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
         return cudaErrorInvalidValue;
 
     GemvPlan p = {};
-    p.nseg = rq.nseg;
     p.K = rq.K;
     p.nb = rq.K / 256;
     p.M = rq.M;
@@ -474,7 +572,7 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     p.argmax = rq.argmax;
     p.err = rq.err;
     bool need_q4 = false, need_q6 = false;
-    int max_row = 0, total = 0;
+    int max_row = 0;
     for (int s = 0; s < rq.nseg; ++s) {
         const GemvSegment& g = rq.seg[s];
         if ((g.type != Q4K_TYPE_Q4_K && g.type != Q4K_TYPE_Q6_K) || g.rows <= 0 || !g.w ||
@@ -486,16 +584,11 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
         max_row = std::max(max_row, p.row_bytes[s]);
         need_q4 |= g.type == Q4K_TYPE_Q4_K;
         need_q6 |= g.type == Q4K_TYPE_Q6_K;
-        p.seg_start[s] = total;
-        if (!pair || s == 0) total += g.rows;
     }
-    p.seg_start[rq.nseg] = total;
-    if (pair) p.seg_start[1] = total;  // both segments index the same rows
-    p.total_rows = total;
     p.ldy = rq.ldy ? rq.ldy : rq.seg[0].rows;
 
     // Batch tile: as many activation rows as fit in ~48 KB of shared memory.
-    const int per_row_x = (need_q4 ? rq.K : 0) + (need_q6 ? rq.K : 0) + rq.K / 32 * 4 + rq.K / 16 * 4;
+    const int per_row_x = (need_q4 ? rq.K : 0) + (need_q6 ? rq.K : 0) + rq.K / 32 * 8 + rq.K / 16 * 4;
     int MT = 1;
     while (MT < rq.M && MT < 8) MT <<= 1;
     while (MT > 1 && MT * per_row_x > 48 * 1024) MT >>= 1;
@@ -514,39 +607,58 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     }
     p.off_xs = off;
     off += MT * (rq.K / 32) * 4;
-    p.off_xsum = off;
+    p.off_xsum16 = off;
     off += MT * (rq.K / 16) * 4;
-    p.off_red = off;
-    off += 64 * 4;
+    p.off_xsum32 = off;
+    off += MT * (rq.K / 32) * 4;
+    p.off_misc = off;
+    off += 128 * 4;
     off = align_up(off, 128);
 
-    const int JR = pair ? 2 : 1;
-    p.slot_bytes = align_up(max_row * JR, 128);
-    // Consumer warps and per-warp ring depth within ~110 KB (so that two
-    // products can be resident on one SM while one drains and the next
-    // prefetches), never fewer than 2 buffers per warp.
-    const int budget = std::max(110 * 1024 - off, 0);
-    int W = 8, S = budget / (W * p.slot_bytes);
-    while (S < 2 && W > 2) {
-        W >>= 1;
-        S = budget / (W * p.slot_bytes);
-    }
-    S = std::min(S, 4);
-    if (S < 1) S = 1;
-    if (off + W * S * p.slot_bytes + 2 * W * S * 8 > 227 * 1024) return cudaErrorInvalidValue;
-    p.stages = S;
+    // Lanes per row: about ten 16-byte chunks per lane per stage.
+    const int chunks = p.nb * 8;
+    int lpr = env_int("Q4K_GEMV_LPR", chunks <= 96 ? 8 : chunks <= 160 ? 16 : 32);
+    if (lpr != 8 && lpr != 16 && lpr != 32) lpr = 32;
+    // consumer warps: teams of four (8 by default); K/4 float4s of the
+    // activation row must fit the prologue's registers (12 per thread)
+    int W = env_int("Q4K_GEMV_WARPS", 16);
+    if (W != 8 && W != 12 && W != 16) W = 16;
+    if (rq.K / 4 > 12 * W * 32) return cudaErrorInvalidValue;
+    const int R = kTeamWarps * 32 / lpr;
+    const int rows_in_stage = pair ? 2 * R : R;
+    const int stage_bytes = align_up(rows_in_stage * max_row, 128);
+    const int budget = std::max(env_int("Q4K_GEMV_SMEM_KB", 200) * 1024 - off, stage_bytes);
+    int S = std::min(budget / stage_bytes, 8);
+    if (S < 2) S = 2;
+    if (off + S * stage_bytes + 2 * S * 8 > 220 * 1024) return cudaErrorInvalidValue;
+    p.lpr = lpr;
+    p.rows_per_stage = R;
+    p.stage_bytes = stage_bytes;
+    p.S = S;
     p.off_bufs = off;
-    off += W * S * p.slot_bytes;
+    off += S * stage_bytes;
     p.off_bars = off;
-    off += 2 * W * S * 8;
+    off += 2 * S * 8;
     const size_t smem = (size_t)off;
 
-    int ctas = rq.ctas > 0 ? rq.ctas : sm_count();
-    ctas = std::min(ctas, total);
+    // stages of R output rows, never crossing a segment
+    int stages = 0;
+    const int stage_segs = pair ? 1 : rq.nseg;
+    for (int s = 0; s < stage_segs; ++s) {
+        p.stage_start[s] = stages;
+        stages += (rq.seg[s].rows + R - 1) / R;
+    }
+    for (int s = stage_segs; s <= kMaxSegments; ++s) p.stage_start[s] = stages;
+    p.nseg = stage_segs;
+    p.total_stages = stages;
+
+    int ctas = rq.ctas > 0 ? rq.ctas : env_int("Q4K_GEMV_CTAS_PER_SM", 1) * sm_count();
+    ctas = std::min(ctas, stages);
     if (rq.epilogue == EPI_ARGMAX) ctas = std::min(ctas, 1024);
     const dim3 grid(ctas, (rq.M + MT - 1) / MT), block((W + 1) * 32);
 
-    switch (MT * 4 + JR) {
+    const int NR = pair ? 2 : 1;
+    switch (MT * 4 + NR) {
         case 1 * 4 + 1: return launch_instance<1, 1>(p, grid, block, smem, stream, rq.pdl);
         case 2 * 4 + 1: return launch_instance<2, 1>(p, grid, block, smem, stream, rq.pdl);
         case 4 * 4 + 1: return launch_instance<4, 1>(p, grid, block, smem, stream, rq.pdl);

@@ -314,7 +314,10 @@ __global__ void relayout_kernel(const uint8_t* raw, int type, size_t nb_full, si
         uint4* dst = reinterpret_cast<uint4*>(out + (r * nb + b) * Q4K_Q4_BLOCK);
         for (int k = 0; k < Q4K_Q4_BLOCK / 16; ++k) dst[k] = src[k];
     } else {
-        q4k_q6_to_planar(raw + ((n0 + r) * nb_full + b0 + b) * Q4K_Q6_BLOCK, out + r * q4k_q6p_row_bytes(nb), nb, b);
+        uint8_t* row = out + r * q4k_q6p_row_bytes(nb);
+        q4k_q6_to_planar(raw + ((n0 + r) * nb_full + b0 + b) * Q4K_Q6_BLOCK, row, nb, b);
+        if (b == nb - 1)  // zero the d plane's padding so the layout is deterministic
+            for (size_t i = nb * 210; i < q4k_q6p_row_bytes(nb); ++i) row[i] = 0;
     }
 }
 

@@ -40,6 +40,7 @@ struct DecodeAttnArgs {
     const float* k_gamma;      // [D]
     uint16_t* k_cache;         // [KVH][capacity][D] fp16 (this layer)
     uint16_t* v_cache;         // [KVH][capacity][D] fp16
+    int row_base;              // row of (this layer, head 0, position 0) in the tensor maps
     int capacity;
     const int* position;       // device scalar: index of the new token
     int heads, kv_heads;       // head_dim is 128
@@ -52,8 +53,15 @@ struct DecodeAttnArgs {
     int splits;                // CTAs per KV head
 };
 constexpr int kDecodeHeadDim = 128;
+// Opaque storage of a TMA tensor map (CUtensorMap) over an fp16 KV cache
+// viewed as [rows][128]: 64-row x 64-dim boxes, 128-byte swizzle.
+struct alignas(64) KvTensorMap {
+    unsigned char bytes[128];
+};
+cudaError_t make_kv_tensor_map(const uint16_t* base, long long rows, KvTensorMap* out);
 int decode_attention_splits(int kv_heads);
 size_t decode_attention_scratch_floats(int heads, int kv_heads, int splits);
-cudaError_t decode_attention(const DecodeAttnArgs& a, cudaStream_t s, bool pdl);
+cudaError_t decode_attention(const DecodeAttnArgs& a, const KvTensorMap& kmap, const KvTensorMap& vmap,
+                             cudaStream_t s, bool pdl);
 
 }  // namespace q4k

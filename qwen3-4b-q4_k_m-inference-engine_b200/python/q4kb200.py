@@ -29,7 +29,7 @@ EXPORTS = (
     "q4k_attention_decode_scratch_bytes", "q4k_engine_config_qwen3_4b", "q4k_model_tensor", "q4k_nccl_unique_id",
     "q4k_engine_create", "q4k_engine_destroy", "q4k_engine_load_synthetic", "q4k_engine_set_tensor",
     "q4k_engine_fill_kv_synthetic", "q4k_engine_read_kv", "q4k_engine_decode", "q4k_engine_generate",
-    "q4k_engine_stream", "q4k_tp_shard",
+    "q4k_engine_stream", "q4k_tp_shard", "q4k_engine_layer", "q4k_engine_write_kv",
 )
 
 
@@ -102,6 +102,8 @@ def lib():
             "q4k_engine_decode": ([P, C.c_uint32, I, C.POINTER(C.c_uint32), P, P], I),
             "q4k_engine_generate": ([P, C.c_uint32, I, I, I, P], I),
             "q4k_engine_stream": ([P], P),
+            "q4k_engine_layer": ([P, I, P, I, P], I),
+            "q4k_engine_write_kv": ([P, I, P, P], I),
             "q4k_tp_shard": ([C.POINTER(EngineConfig), I, I, I, C.POINTER(I64), C.POINTER(I64), C.POINTER(I64),
                               C.POINTER(I64)], I),
         }
@@ -248,6 +250,11 @@ class Engine:
         check(lib().q4k_engine_read_kv(self.h, layer, hptr(k), hptr(v)))
         return k, v
 
+    def write_kv(self, layer: int, k: np.ndarray | None, v: np.ndarray | None):
+        k = None if k is None else np.ascontiguousarray(k, np.uint16)
+        v = None if v is None else np.ascontiguousarray(v, np.uint16)
+        check(lib().q4k_engine_write_kv(self.h, layer, hptr(k), hptr(v)))
+
     def decode(self, token: int, position: int, want_logits=False, want_hidden=False):
         c = self.cfg
         world = max(c.tp_world, 1)
@@ -263,6 +270,13 @@ class Engine:
         out = np.empty(max(steps, 1), np.uint32) if want_tokens else None
         check(lib().q4k_engine_generate(self.h, token, position, steps, int(advance), hptr(out)))
         return out[:steps] if want_tokens else None
+
+    def layer(self, layer: int, x: np.ndarray, position: int) -> np.ndarray:
+        """One block applied to residual stream x (q4k_engine_layer)."""
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty_like(x)
+        check(lib().q4k_engine_layer(self.h, layer, hptr(x), position, hptr(out)))
+        return out
 
     @property
     def stream(self) -> int:

@@ -38,8 +38,15 @@ sys.path.insert(0, HERE)
 from tiny_model import SEED, TINY, tiny_tensors  # noqa: E402
 
 
+_KEEP = []
+
+
 def dev(a: np.ndarray) -> torch.Tensor:
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    # kept alive for the whole run: a raw data_ptr() of a temporary could be
+    # handed to the next allocation before the kernel reads it
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    _KEEP.append(t)
+    return t
 
 
 def main() -> None:
@@ -80,7 +87,8 @@ def main() -> None:
         kk = (np.cos(np.arange(cached * kvh * dim, dtype=np.float32) * np.float32(0.07)) * 9).astype(np.float32)
         vv = np.sin(np.arange(cached * kvh * dim, dtype=np.float32) * np.float32(0.11)).astype(np.float32)
         y = torch.empty(queries * heads * dim, device="cuda")
-        o.ref_check(R.ref_attention(dev(qv).data_ptr(), dev(kk).data_ptr(), dev(vv).data_ptr(), y.data_ptr(),
+        qd, kd, vd = dev(qv), dev(kk), dev(vv)  # keep the device copies alive across the call
+        o.ref_check(R.ref_attention(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), y.data_ptr(),
                                     queries, heads, kvh, dim, prefix))
         torch.cuda.synchronize()
         out[f"attn_{i}_shape"] = np.array([queries, prefix, heads, kvh, dim], np.int64)
@@ -107,7 +115,8 @@ def main() -> None:
     g = q.synth_f32_host(SEED, "golden.silu.g", 1000) * 4
     u = q.synth_f32_host(SEED, "golden.silu.u", 1000)
     y = torch.empty(1000, device="cuda")
-    o.ref_check(R.ref_silu_multiply(dev(g).data_ptr(), dev(u).data_ptr(), y.data_ptr(), 1000))
+    gd, ud = dev(g), dev(u)
+    o.ref_check(R.ref_silu_multiply(gd.data_ptr(), ud.data_ptr(), y.data_ptr(), 1000))
     torch.cuda.synchronize()
     out["silu_g"], out["silu_u"], out["silu_out"] = g, u, y.cpu().numpy()
 

@@ -30,8 +30,22 @@ def approx_ok(actual, expected, margin=3e-5, eps=1e-4):
     return np.abs(a - e) <= np.maximum(margin * scale, eps * np.abs(e))
 
 
+_KEEP = []
+
+
+@pytest.fixture(autouse=True)
+def _release_device_copies():
+    yield
+    _KEEP.clear()
+
+
 def dev(cuda, a):
-    return cuda.from_numpy(np.ascontiguousarray(a)).cuda()
+    """Device copy of a host array, kept alive until the test ends: a raw
+    data_ptr() of a temporary would let the caching allocator hand the same
+    memory to the next copy before the kernel reads it."""
+    t = cuda.from_numpy(np.ascontiguousarray(a)).cuda()
+    _KEEP.append(t)
+    return t
 
 
 def upload(cuda, qt, K, N, raw):
@@ -233,7 +247,10 @@ def test_rms_norm_rope_silu_residual(cuda):
         r = q.synth_f32_host(1, "e.r", 3 * 32 * 128)
         t = dev(cuda, r)
         q.check(L.q4k_rope(t.data_ptr(), 3, 32, 128, pos, 1e6, None))
-        assert rel_l2(t.cpu().numpy(), o.rope(r, 3, 32, 128, pos, 1e6)) < 1e-5
+        # the angle float(pos) * powf(base, -2j/d) is rounded to fp32 (as the
+        # reference forms it), so the device and host libm differ by a few ulp
+        # of an angle of up to 4095 rad: ~3e-5 relative at the last position
+        assert rel_l2(t.cpu().numpy(), o.rope(r, 3, 32, 128, pos, 1e6)) < 1e-4
         if o.ref_available():
             t2 = dev(cuda, r)
             o.ref_check(o.ref().ref_rope(t2.data_ptr(), 3, 32, 128, pos, 1e6))

@@ -141,7 +141,7 @@ size_t q4k_matmul_argmax_scratch_bytes(void);
  * the token; caches are [kv_heads][capacity][128] fp16 for one layer;
  * *position_device is the token's position. head_dim must be 128 and
  * query_heads == 4 * kv_heads. scratch: q4k_attention_decode_scratch_bytes
- * bytes, zeroed once before first use. */
+ * bytes, 16-byte aligned, zeroed once before first use. */
 int q4k_attention_decode_f16(const float* qkv, const float* q_gamma, const float* k_gamma, uint16_t* k_cache,
                              uint16_t* v_cache, int capacity, const int* position_device, int query_heads,
                              int kv_heads, int head_dim, float epsilon, float rope_base, float* output,
@@ -231,6 +231,15 @@ int q4k_engine_layer(q4k_engine* engine, int layer, const float* x_host, int pos
 
 /* Stream the engine launches on (cudaStream_t), e.g. to time with events. */
 void* q4k_engine_stream(q4k_engine* engine);
+
+/* Diagnostics, no counterpart in the reference: one decode step (like
+ * q4k_engine_decode) whose kernels record, per CTA, four words
+ * {tag, block, start_ns, end_ns} of the %globaltimer clock. Tags are
+ * kind * 10000 + layer (1 QKV, 2 attention (+500 for the CTA that merges a
+ * head), 3 O, 4 gate/up, 5 down, 6 output head). Up to max_records records
+ * go to records_host; *count receives how many were written. */
+int q4k_engine_trace(q4k_engine* engine, uint32_t token, int position, unsigned long long* records_host,
+                     size_t max_records, size_t* count);
 
 #ifdef __cplusplus
 }

@@ -26,6 +26,7 @@
 
 #include <math_constants.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -61,6 +62,8 @@ struct Args {
     float* out;
     int* err;
     int stages;
+    unsigned long long* trace;
+    int trace_tag;
 };
 
 __device__ __forceinline__ float rope_angle(int pos, int j, float base) {
@@ -121,6 +124,7 @@ __device__ __forceinline__ void split2(float x, float y, uint32_t& hi, uint32_t&
 }
 
 struct SmemTail {
+    uint4 qf[8][32];
     float q[G][D];
     uint16_t k_new[D];
     uint16_t v_new[D];
@@ -131,7 +135,7 @@ struct SmemTail {
     int abort[2];  // per tile parity: a fast warp's next tile never clears the current flag
 };
 
-__global__ void __launch_bounds__(kComputeThreads + 32, 1)
+__global__ void __launch_bounds__(kComputeThreads + 32, 2)
     decode_attention_kernel(const __grid_constant__ Args a, const __grid_constant__ CUtensorMap kmap,
                             const __grid_constant__ CUtensorMap vmap) {
     // the 128-byte TMA swizzle is keyed to 1024-byte smem address blocks
@@ -141,6 +145,7 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
     SmemTail& sm = *reinterpret_cast<SmemTail*>(smem + S * kStageBytes);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x, kvh = blockIdx.y, splits = gridDim.x;
+    const uint64_t t_start = a.trace ? global_timer_ns() : 0;
 
     const int pos = *a.position;
     if (pos < 0 || pos >= a.capacity) {
@@ -183,7 +188,6 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
     }
 
     // ---------------- compute warps: q (and the new k/v) of this token ----------------
-    pdl_wait();
     const size_t head_base = (size_t)kvh * a.capacity * D;
     const float* q_raw = a.qkv + (size_t)kvh * G * D;
     const float* k_raw = a.qkv + (size_t)a.heads * D + (size_t)kvh * D;
@@ -192,14 +196,22 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
     {
         // Thread t handles pair (j, j + 64) of head h = t / 64 (4 heads x 64 pairs).
         const int h = tid >> 6, j = tid & 63;
+        // weights and the rotation angle do not depend on the previous kernel
+        const float gq0 = a.q_gamma[j], gq1 = a.q_gamma[j + 64];
+        const float gk0 = a.k_gamma[j], gk1 = a.k_gamma[j + 64];
+        float sn, cs;
+        sincosf(rope_angle(pos, j, a.rope_base), &sn, &cs);
+        pdl_wait();
         float x0 = q_raw[h * D + j], x1 = q_raw[h * D + j + 64];
-        const float ss = warp_sum(x0 * x0 + x1 * x1);
-        float kx0 = 0.0f, kx1 = 0.0f, kss = 0.0f;
+        float kx0 = 0.0f, kx1 = 0.0f, vx0 = 0.0f, vx1 = 0.0f;
         if (owner && h == 0) {
             kx0 = k_raw[j];
             kx1 = k_raw[j + 64];
-            kss = warp_sum(kx0 * kx0 + kx1 * kx1);
+            vx0 = v_raw[j];
+            vx1 = v_raw[j + 64];
         }
+        const float ss = warp_sum(x0 * x0 + x1 * x1);
+        const float kss = (owner && h == 0) ? warp_sum(kx0 * kx0 + kx1 * kx1) : 0.0f;
         if (lane == 0) {
             sm.red[warp][0] = ss;
             sm.red[warp][1] = kss;
@@ -207,19 +219,17 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
         named_barrier(1, kComputeThreads);
         const float qsum = sm.red[2 * h][0] + sm.red[2 * h + 1][0];
         const float inv = rsqrtf(qsum / (float)D + a.eps);  // rms_norm.cu:17
-        x0 = (x0 * inv) * a.q_gamma[j];
-        x1 = (x1 * inv) * a.q_gamma[j + 64];
-        float sn, cs;
-        sincosf(rope_angle(pos, j, a.rope_base), &sn, &cs);
+        x0 = (x0 * inv) * gq0;
+        x1 = (x1 * inv) * gq1;
         sm.q[h][j] = x0 * cs - x1 * sn;  // rope.cu:21-22
         sm.q[h][j + 64] = x0 * sn + x1 * cs;
         if (owner && h == 0) {
             const float kinv = rsqrtf((sm.red[0][1] + sm.red[1][1]) / (float)D + a.eps);
-            kx0 = (kx0 * kinv) * a.k_gamma[j];
-            kx1 = (kx1 * kinv) * a.k_gamma[j + 64];
+            kx0 = (kx0 * kinv) * gk0;
+            kx1 = (kx1 * kinv) * gk1;
             const uint16_t k0 = q4k_f32_to_f16(kx0 * cs - kx1 * sn);
             const uint16_t k1 = q4k_f32_to_f16(kx0 * sn + kx1 * cs);
-            const uint16_t v0 = q4k_f32_to_f16(v_raw[j]), v1 = q4k_f32_to_f16(v_raw[j + 64]);
+            const uint16_t v0 = q4k_f32_to_f16(vx0), v1 = q4k_f32_to_f16(vx1);
             sm.k_new[j] = k0;
             sm.k_new[j + 64] = k1;
             sm.v_new[j] = v0;
@@ -233,19 +243,20 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
         named_barrier(1, kComputeThreads);
     }
 
-    // Q as MMA A-fragments (rows = heads, only rows 0..3 live): lane (g, t)
-    // holds q[g][16s + 2t, +1] (a0) and q[g][16s + 8 + 2t, +1] (a2).
+    // Q as MMA A-fragments (rows = heads, only rows 0..3 live), shared by all
+    // warps: for k-step s, lane (g, t) = (l / 4, l % 4) holds q[g][16s + 2t, +1]
+    // (a0) and q[g][16s + 8 + 2t, +1] (a2), each as fp16 hi and lo parts.
     const int g = lane >> 2, tq = lane & 3;
-    uint32_t qa0h[8], qa0l[8], qa2h[8], qa2l[8];
-#pragma unroll
-    for (int s = 0; s < 8; ++s) {
-        if (g < G) {
-            split2(sm.q[g][16 * s + 2 * tq], sm.q[g][16 * s + 2 * tq + 1], qa0h[s], qa0l[s]);
-            split2(sm.q[g][16 * s + 8 + 2 * tq], sm.q[g][16 * s + 8 + 2 * tq + 1], qa2h[s], qa2l[s]);
-        } else {
-            qa0h[s] = qa0l[s] = qa2h[s] = qa2l[s] = 0u;
+    {
+        const int s = tid >> 5, l = tid & 31, gg = l >> 2, tt = l & 3;  // 256 threads: 8 k-steps x 32 lanes
+        uint4 f = make_uint4(0u, 0u, 0u, 0u);
+        if (gg < G) {
+            split2(sm.q[gg][16 * s + 2 * tt], sm.q[gg][16 * s + 2 * tt + 1], f.x, f.y);
+            split2(sm.q[gg][16 * s + 8 + 2 * tt], sm.q[gg][16 * s + 8 + 2 * tt + 1], f.z, f.w);
         }
+        sm.qf[s][l] = f;
     }
+    named_barrier(1, kComputeThreads);
 
     // ---------------- tiles: this warp owns tile rows [8w, 8w + 8) ----------------
     const float scale = rsqrtf((float)D);  // attention.cu:40
@@ -281,10 +292,11 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
         for (int s2 = 0; s2 < 8; s2 += 2) {
             uint32_t b0, b1, b2, b3;
             ldsm_x4(kbase + tile_off(r_lane, 2 * s2 + (lane >> 3)), b0, b1, b2, b3);
-            mma16816(sc, qa0h[s2], qa2h[s2], b0, b1);
-            mma16816(sc, qa0l[s2], qa2l[s2], b0, b1);
-            mma16816(sc, qa0h[s2 + 1], qa2h[s2 + 1], b2, b3);
-            mma16816(sc, qa0l[s2 + 1], qa2l[s2 + 1], b2, b3);
+            const uint4 fa = sm.qf[s2][lane], fb = sm.qf[s2 + 1][lane];
+            mma16816(sc, fa.x, fa.z, b0, b1);  // hi parts
+            mma16816(sc, fa.y, fa.w, b0, b1);  // lo parts
+            mma16816(sc, fb.x, fb.z, b2, b3);
+            mma16816(sc, fb.y, fb.w, b2, b3);
         }
         // online softmax over this warp's 8 positions (lane (g, tq): positions 2tq, 2tq+1)
         const int c0 = 8 * warp + 2 * tq;
@@ -327,10 +339,13 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
         if (owner && prow >= 8 * warp && prow < 8 * warp + 8)
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes before the next TMA
         __syncwarp();
-        // the slot is free once all eight warps are done with it
-        named_barrier(1, kComputeThreads);
-        if (tid == 0) mbar_arrive(&sm.empty[s]);
-        if (sm.abort[t & 1]) break;
+        // the slot is reused only when the ring wraps; then it is free once
+        // all eight warps are done with it
+        if (t + S < tiles) {
+            named_barrier(1, kComputeThreads);
+            if (tid == 0) mbar_arrive(&sm.empty[s]);
+            if (sm.abort[t & 1]) break;
+        }
     }
     named_barrier(1, kComputeThreads);
 
@@ -383,27 +398,50 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
     named_barrier(1, kComputeThreads);
     if (tid == 0) sm.last = atomicAdd(a.counters + kvh, 1u) == (unsigned)(splits - 1);
     named_barrier(1, kComputeThreads);
-    if (!sm.last) return;
-    __threadfence();
-    float MM = -CUDART_INF_F;
-    for (int sp = 0; sp < splits; ++sp) {
-        const size_t q = ((size_t)kvh * splits + sp) * G + hq;
-        if (__ldcg(a.partial_ml + q * 2 + 1) > 0.0f) MM = fmaxf(MM, __ldcg(a.partial_ml + q * 2));
+    if (!sm.last) {
+        if (tid == 0) trace_record(a.trace, a.trace_tag, t_start);
+        return;
     }
+    __threadfence();
+    // (m, l) of every split into shared memory (the stage buffers are free),
+    // then the o partials with many loads in flight per thread: the merge is
+    // on the critical path of the step, so it must not be one L2 round trip
+    // per split.
+    float* mls = reinterpret_cast<float*>(smem);  // [splits][G][2]
+    const float* ml_head = a.partial_ml + (size_t)kvh * splits * G * 2;
+    for (int i = tid; i < splits * G * 2; i += kComputeThreads) mls[i] = __ldcg(ml_head + i);
+    named_barrier(1, kComputeThreads);
+    float MM = -CUDART_INF_F;
+    for (int sp = 0; sp < splits; ++sp)
+        if (mls[(sp * G + hq) * 2 + 1] > 0.0f) MM = fmaxf(MM, mls[(sp * G + hq) * 2]);
     float LL = 0.0f, o0 = 0.0f, o1 = 0.0f;
-    for (int sp = 0; sp < splits; ++sp) {
-        const size_t q = ((size_t)kvh * splits + sp) * G + hq;
-        const float l = __ldcg(a.partial_ml + q * 2 + 1);
-        if (!(l > 0.0f)) continue;
-        const float f = expf(__ldcg(a.partial_ml + q * 2) - MM);
-        LL += l * f;
-        o0 += __ldcg(a.partial_o + q * D + d0) * f;
-        o1 += __ldcg(a.partial_o + q * D + d0 + 1) * f;
+    const float2* po = reinterpret_cast<const float2*>(a.partial_o + ((size_t)kvh * splits * G + hq) * D + d0);
+    constexpr int kBatch = 16;
+    for (int sp0 = 0; sp0 < splits; sp0 += kBatch) {
+        float2 v[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+            v[u] = sp0 + u < splits ? __ldcg(po + (size_t)(sp0 + u) * (G * D / 2)) : make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            if (sp0 + u < splits) {
+                const float l = mls[((sp0 + u) * G + hq) * 2 + 1];
+                if (l > 0.0f) {
+                    const float f = expf(mls[((sp0 + u) * G + hq) * 2] - MM);
+                    LL += l * f;
+                    o0 += v[u].x * f;
+                    o1 += v[u].y * f;
+                }
+            }
+        }
     }
     float* out = a.out + ((size_t)kvh * G + hq) * D;
     out[d0] = o0 / LL;
     out[d0 + 1] = o1 / LL;
-    if (tid == 0) a.counters[kvh] = 0u;
+    if (tid == 0) {
+        a.counters[kvh] = 0u;
+        trace_record(a.trace, a.trace_tag + 500, t_start);  // the merging CTA
+    }
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -445,8 +483,13 @@ cudaError_t make_kv_tensor_map(const uint16_t* base, long long rows, KvTensorMap
     return cudaSuccess;
 }
 
+// One CTA per SM and KV head share by default (Q4K_ATTN_CTAS_PER_SM raises
+// it; the kernel fits two per SM): more splits shorten each CTA's KV stream
+// but lengthen the cross-split merge, and one per SM measured faster.
 int decode_attention_splits(int kv_heads) {
-    const int s = sm_count() / (kv_heads > 0 ? kv_heads : 1);
+    const char* env = std::getenv("Q4K_ATTN_CTAS_PER_SM");
+    const int per_sm = env && *env ? std::atoi(env) : 1;
+    const int s = per_sm * sm_count() / (kv_heads > 0 ? kv_heads : 1);
     return s < 1 ? 1 : s;
 }
 
@@ -477,13 +520,15 @@ cudaError_t decode_attention(const DecodeAttnArgs& in, const KvTensorMap& kmap, 
     a.counters = in.counters;
     a.out = in.out;
     a.err = in.err;
-    a.stages = 4;
+    a.trace = in.trace;
+    a.trace_tag = in.trace_tag;
+    a.stages = 3;
     const size_t smem = smem_bytes(a.stages);
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
     std::call_once(once, [] {
         attr = cudaFuncSetAttribute(decode_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)smem_bytes(4));
+                                    (int)smem_bytes(3));
     });
     if (attr != cudaSuccess) return attr;
     CUtensorMap km, vm;

@@ -348,6 +348,7 @@ Q4K_API int q4k_attention_decode_f16(const float* qkv, const float* q_gamma, con
         if (!(epsilon > 0.0f) || !(rope_base > 0.0f)) invalid("epsilon and rope base must be positive");
         if (reinterpret_cast<uintptr_t>(k_cache) % 16 || reinterpret_cast<uintptr_t>(v_cache) % 16)
             invalid("KV caches must be 16-byte aligned");
+        if (reinterpret_cast<uintptr_t>(scratch) % 16) invalid("scratch must be 16-byte aligned");
         const int splits = q4k::decode_attention_splits(kv_heads);
         uint8_t* sb = static_cast<uint8_t*>(scratch);
         q4k::DecodeAttnArgs a;
@@ -512,6 +513,14 @@ Q4K_API int q4k_engine_layer(q4k_engine* e, int layer, const float* x_host, int 
     return guarded_cuda([&] {
         if (!e || !x_host || !x_out_host) invalid("engine and buffers required");
         e->impl.layer_step(layer, x_host, position, x_out_host);
+    });
+}
+
+Q4K_API int q4k_engine_trace(q4k_engine* e, uint32_t token, int position, unsigned long long* records_host,
+                             size_t max_records, size_t* count) {
+    return guarded_cuda([&] {
+        if (!e || !count) invalid("engine and count required");
+        *count = e->impl.trace_step(token, position, records_host, max_records);
     });
 }
 

@@ -418,6 +418,8 @@ void Engine::enqueue_layer(int i) {
         r.epilogue = EPI_STORE;
         r.err = err_;
         r.pdl = true;
+        r.trace = trace_;
+        r.trace_tag = 10000 + i;
         gemv(r);
     }
     {
@@ -440,6 +442,8 @@ void Engine::enqueue_layer(int i) {
         a.err = err_;
         a.splits = splits_;
         a.row_base = i * KVHl_ * c.capacity;
+        a.trace = trace_;
+        a.trace_tag = 20000 + i;
         cuda_check(decode_attention(a, kmap_, vmap_, stream_, true), "attention launch");
     }
     {
@@ -451,6 +455,8 @@ void Engine::enqueue_layer(int i) {
         r.epilogue = world_ > 1 ? EPI_STORE : EPI_ADD;
         r.err = err_;
         r.pdl = true;
+        r.trace = trace_;
+        r.trace_tag = 30000 + i;
         gemv(r);
         if (world_ > 1) all_reduce_into_x();
     }
@@ -466,6 +472,8 @@ void Engine::enqueue_layer(int i) {
         r.epilogue = EPI_SWIGLU;
         r.err = err_;
         r.pdl = true;
+        r.trace = trace_;
+        r.trace_tag = 40000 + i;
         gemv(r);
     }
     {
@@ -477,6 +485,8 @@ void Engine::enqueue_layer(int i) {
         r.epilogue = world_ > 1 ? EPI_STORE : EPI_ADD;
         r.err = err_;
         r.pdl = true;
+        r.trace = trace_;
+        r.trace_tag = 50000 + i;
         gemv(r);
         if (world_ > 1) all_reduce_into_x();
     }
@@ -513,6 +523,8 @@ void Engine::enqueue_step(bool record_hidden) {
         r.argmax.cand_index = am_index_;
         r.argmax.counter = am_counter_;
         r.argmax.index_base = (uint32_t)vocab0_;
+        r.trace = trace_;
+        r.trace_tag = 60000;
         if (world_ > 1) {
             r.argmax.token = reinterpret_cast<uint32_t*>(tp_cand_local_) + 1;
             r.argmax.score = tp_cand_local_;
@@ -624,6 +636,46 @@ void Engine::generate(uint32_t token, int position, int steps, int advance, uint
         cuda_check(cudaMemcpyAsync(tokens_host, history_, sizeof(uint32_t) * steps, cudaMemcpyDeviceToHost, stream_),
                    "d2h tokens");
     check_device_error();
+}
+
+size_t Engine::trace_step(uint32_t token, int position, unsigned long long* records_host, size_t max_records) {
+    if (!loaded_) throw Error(Q4K_EINVAL, "weights are not loaded");
+    if (token >= (uint32_t)c_.vocab) throw Error(Q4K_ERANGE, "Token ID out of range");
+    if (position < 0 || position >= c_.capacity) throw Error(Q4K_ERANGE, "KV cache capacity exceeded");
+    const size_t words = 1 + 4 * (size_t)kTraceRecords;
+    if (!trace_buf_) trace_buf_ = static_cast<unsigned long long*>(alloc(words * 8));
+    cuda_check(cudaMemsetAsync(trace_buf_, 0, words * 8, stream_), "memset trace");
+    // a traced graph of its own; the normal graph stays untraced
+    cudaGraphExec_t saved = exec_;
+    exec_ = nullptr;
+    trace_ = trace_buf_;
+    size_t n = 0;
+    try {
+        ensure_graph();
+        host_io_[0] = token;
+        host_io_[1] = (uint32_t)position;
+        host_io_[2] = 0;
+        cuda_check(cudaMemcpyAsync(token_, &host_io_[0], 4, cudaMemcpyHostToDevice, stream_), "h2d");
+        cuda_check(cudaMemcpyAsync(pos_, &host_io_[1], 4, cudaMemcpyHostToDevice, stream_), "h2d");
+        cuda_check(cudaMemcpyAsync(advance_, &host_io_[2], 4, cudaMemcpyHostToDevice, stream_), "h2d");
+        cuda_check(cudaGraphLaunch(exec_, stream_), "graph launch");
+        unsigned long long count = 0;
+        cuda_check(cudaMemcpyAsync(&count, trace_buf_, 8, cudaMemcpyDeviceToHost, stream_), "d2h");
+        cuda_check(cudaStreamSynchronize(stream_), "trace step");
+        n = std::min<size_t>((size_t)count, std::min<size_t>(max_records, kTraceRecords));
+        if (records_host && n)
+            cuda_check(cudaMemcpy(records_host, trace_buf_ + 1, n * 4 * 8, cudaMemcpyDeviceToHost), "d2h trace");
+    } catch (...) {
+        if (exec_) cudaGraphExecDestroy(exec_);
+        exec_ = saved;
+        trace_ = nullptr;
+        throw;
+    }
+    cudaGraphExecDestroy(exec_);
+    exec_ = saved;
+    trace_ = nullptr;
+    check_device_error();
+    return n;
 }
 
 void Engine::layer_step(int layer, const float* x_host, int position, float* x_out_host) {

@@ -55,6 +55,8 @@ public:
     void generate(uint32_t token, int position, int steps, int advance, uint32_t* tokens_host);
     // One block on a given residual-stream input (tp_world == 1 or all ranks).
     void layer_step(int layer, const float* x_host, int position, float* x_out_host);
+    // One step with every kernel CTA's %globaltimer start/end recorded.
+    size_t trace_step(uint32_t token, int position, unsigned long long* records_host, size_t max_records);
     cudaStream_t stream() const { return stream_; }
 
 private:
@@ -112,6 +114,8 @@ private:
     uint32_t* host_io_ = nullptr;     // pinned: token, position, result
 
     cudaGraphExec_t exec_ = nullptr;
+    unsigned long long* trace_ = nullptr;      // set only while a traced graph is captured
+    unsigned long long* trace_buf_ = nullptr;
 };
 
 }  // namespace q4k

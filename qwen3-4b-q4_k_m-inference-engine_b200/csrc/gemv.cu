@@ -16,7 +16,10 @@
 //     before griddepcontrol.wait, so under programmatic dependent launch a
 //     product's weights stream in while the previous kernel drains.
 //   * warps 0..W-1 are consumers in T teams of TW warps; team k consumes the
-//     stages k, k+T, ... . Within a team, LPR lanes work on one row (so a
+//     stages k, k+T, ... . T divides the ring depth S, so every ring slot
+//     is only ever taken by one team and its mbarrier phases are waited on
+//     in order (a team waiting on a slot another team has not yet released
+//     could match a parity two phases old). Within a team, LPR lanes work on one row (so a
 //     team covers R = TW*32/LPR rows per stage); lane f of a row takes the
 //     16-byte chunks f, f+LPR, ... . Rows are reduced with xor-shuffles in a
 //     fixed order, so results are deterministic.
@@ -55,12 +58,15 @@ struct GemvPlan {
     int total_stages;
     int rows_per_stage;  // R: output rows per stage
     int lpr;             // lanes per row
-    int S;               // ring depth
+    int S;               // ring depth (a multiple of teams)
+    int teams;           // consumer teams that take stages (slot i % S always belongs to team i % teams)
     int stage_bytes;
     int row_bytes[kMaxSegments];
     int off_xq4, off_xq6, off_xs, off_xsum16, off_xsum32, off_bufs, off_bars, off_misc;
     ArgmaxTarget argmax;
     int* err;
+    unsigned long long* trace;
+    int trace_tag;
 };
 
 // Segment, first local row and row count of stage i.
@@ -301,8 +307,9 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     constexpr bool PAIR = NR == 2;  // gate and up rows worked together (SwiGLU)
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint64_t t_start = p.trace ? global_timer_ns() : 0;
     const int W = (int)(blockDim.x >> 5) - 1;  // consumer warps
-    const int T = W / kTeamWarps;             // teams
+    const int T = p.teams;                     // teams taking stages (<= W / kTeamWarps)
     const int S = p.S;
     const int K = p.K;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bars);
@@ -372,7 +379,10 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     float best_score = -__int_as_float(0x7f800000);
     uint32_t best_index = 0xffffffffu;
 
-    for (int i = team, st = s_begin + team; st < s_end; i += T, st += T) {
+    // Stage i always lands in slot i % S and is taken by team i % T; as T
+    // divides S, each slot is only ever waited on by one team, in order, so
+    // a parity wait can never see a phase two uses old.
+    for (int i = team, st = s_begin + team; team < T && st < s_end; i += T, st += T) {
         const int slot = i % S, use = i / S;
         if (!mbar_wait_bounded(full + slot, use & 1, p.err, ERR_WAIT_TIMEOUT_FULL)) team_abort[team] = 1;
         int seg, r0, nr;
@@ -502,6 +512,7 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
             }
         }
     }
+    if (tid == 0) trace_record(p.trace, p.trace_tag, t_start);
 }
 
 template <int MT, int NR>
@@ -571,6 +582,8 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     p.epilogue = rq.epilogue;
     p.argmax = rq.argmax;
     p.err = rq.err;
+    p.trace = rq.trace;
+    p.trace_tag = rq.trace_tag;
     bool need_q4 = false, need_q6 = false;
     int max_row = 0;
     for (int s = 0; s < rq.nseg; ++s) {
@@ -630,11 +643,15 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     const int budget = std::max(env_int("Q4K_GEMV_SMEM_KB", 200) * 1024 - off, stage_bytes);
     int S = std::min(budget / stage_bytes, 8);
     if (S < 2) S = 2;
+    // every ring slot belongs to one team: teams <= S and S a multiple of it
+    const int teams = std::min(W / kTeamWarps, S);
+    S -= S % teams;
     if (off + S * stage_bytes + 2 * S * 8 > 220 * 1024) return cudaErrorInvalidValue;
     p.lpr = lpr;
     p.rows_per_stage = R;
     p.stage_bytes = stage_bytes;
     p.S = S;
+    p.teams = teams;
     p.off_bufs = off;
     off += S * stage_bytes;
     p.off_bars = off;

@@ -51,6 +51,8 @@ struct DecodeAttnArgs {
     float* out;                // [H*D] attended output
     int* err;
     int splits;                // CTAs per KV head
+    unsigned long long* trace = nullptr;  // optional timeline records
+    int trace_tag = 0;
 };
 constexpr int kDecodeHeadDim = 128;
 // Opaque storage of a TMA tensor map (CUtensorMap) over an fp16 KV cache

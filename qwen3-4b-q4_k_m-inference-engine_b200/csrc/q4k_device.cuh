@@ -128,6 +128,21 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// Optional timeline records: trace[0] counts records, record i occupies
+// trace[1 + 4i .. 4 + 4i] = {tag, block, start ns, end ns} (%globaltimer).
+// Kernels write one record per CTA when given a trace buffer.
+constexpr int kTraceRecords = 1 << 16;
+__device__ __forceinline__ void trace_record(unsigned long long* trace, int tag, uint64_t start) {
+    if (!trace) return;
+    const unsigned long long i = atomicAdd(trace, 1ull);
+    if (i >= (unsigned long long)kTraceRecords) return;
+    unsigned long long* r = trace + 1 + 4 * i;
+    r[0] = (unsigned long long)tag;
+    r[1] = (unsigned long long)(blockIdx.x + gridDim.x * blockIdx.y);
+    r[2] = start;
+    r[3] = global_timer_ns();
+}
+
 // Argmax candidate order of the reference (src/cuda/argmax.cu:19-23): larger
 // score wins, ties go to the lower index; NaN never wins.
 __device__ __forceinline__ bool candidate_better(float s, uint32_t i, float bs, uint32_t bi) {

@@ -47,6 +47,8 @@ struct GemvRequest {
     int epilogue = EPI_STORE;
     ArgmaxTarget argmax;
     int* err = nullptr;  // optional device error word (bits of q4k_device.cuh)
+    unsigned long long* trace = nullptr;  // optional timeline records (q4k_device.cuh)
+    int trace_tag = 0;
     int ctas = 0;        // 0: one CTA per SM
     bool pdl = false;    // launch with programmatic stream serialisation
 };

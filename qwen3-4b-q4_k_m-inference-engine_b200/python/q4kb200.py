@@ -30,6 +30,7 @@ EXPORTS = (
     "q4k_engine_create", "q4k_engine_destroy", "q4k_engine_load_synthetic", "q4k_engine_set_tensor",
     "q4k_engine_fill_kv_synthetic", "q4k_engine_read_kv", "q4k_engine_decode", "q4k_engine_generate",
     "q4k_engine_stream", "q4k_tp_shard", "q4k_engine_layer", "q4k_engine_write_kv",
+    "q4k_engine_trace",
 )
 
 
@@ -104,6 +105,7 @@ def lib():
             "q4k_engine_stream": ([P], P),
             "q4k_engine_layer": ([P, I, P, I, P], I),
             "q4k_engine_write_kv": ([P, I, P, P], I),
+            "q4k_engine_trace": ([P, C.c_uint32, I, P, C.c_size_t, C.POINTER(C.c_size_t)], I),
             "q4k_tp_shard": ([C.POINTER(EngineConfig), I, I, I, C.POINTER(I64), C.POINTER(I64), C.POINTER(I64),
                               C.POINTER(I64)], I),
         }
@@ -281,6 +283,13 @@ class Engine:
     @property
     def stream(self) -> int:
         return lib().q4k_engine_stream(self.h)
+
+    def trace(self, token: int, position: int, max_records: int = 1 << 16) -> np.ndarray:
+        """One traced decode step: rows of (tag, block, start_ns, end_ns)."""
+        rec = np.zeros((max_records, 4), np.uint64)
+        n = C.c_size_t(0)
+        check(lib().q4k_engine_trace(self.h, token, position, hptr(rec), max_records, C.byref(n)))
+        return rec[: n.value]
 
 
 def nccl_unique_id() -> bytes:

@@ -208,6 +208,41 @@ def test_matmul_ex_swiglu_and_add(cuda):
     assert rel_l2(resid.cpu().numpy(), want) < 1e-5
 
 
+@pytest.mark.parametrize("qt", [q.Q4_K, q.Q6_K])
+def test_gemv_ring_shapes_agree(cuda, monkeypatch, qt):
+    """Every ring size the planner accepts gives the same bits for a given
+    number of consumer warps (per-row arithmetic does not depend on which
+    team takes a stage; the warp count changes the RMSNorm sum's order), and
+    every (warps, ring) shape matches the oracle.
+    The small rings put fewer slots than teams (2-3 slots of ~46-67 KB
+    SwiGLU stages for 3-4 teams), where each slot must still belong to a
+    single team."""
+    K, N = 2560, 1000
+    rg = q.synth_tensor_host(6, "ring.gate", qt, K, N)
+    ru = q.synth_tensor_host(6, "ring.up", qt, K, N)
+    Wg, Wu = upload(cuda, qt, K, N, rg), upload(cuda, qt, K, N, ru)
+    x = dev(cuda, q.synth_f32_host(6, "ring.x", K))
+    gamma = dev(cuda, q.synth_tensor_host(6, "ring.g", q.F32, K, 1))
+    n = o.rms_norm(x.cpu().numpy(), gamma.cpu().numpy(), K, 1e-6)
+    want = o.silu_multiply(o.matmul(n, rg, qt, K, N).astype(np.float32),
+                           o.matmul(n, ru, qt, K, N).astype(np.float32))
+    results = {}
+    for warps, kb in [(16, 200), (16, 96), (16, 64), (12, 200), (12, 96), (8, 96), (8, 40)]:
+        monkeypatch.setenv("Q4K_GEMV_WARPS", str(warps))
+        monkeypatch.setenv("Q4K_GEMV_SMEM_KB", str(kb))
+        out = cuda.full((N,), float("nan"), device="cuda")
+        q.check(q.lib().q4k_matmul_ex(x.data_ptr(), gamma.data_ptr(), 1e-6, 2,
+                                      (C.c_void_p * 2)(Wg.data_ptr(), Wu.data_ptr()), (C.c_int * 2)(qt, qt),
+                                      (C.c_int64 * 2)(N, N), (C.c_void_p * 2)(out.data_ptr(), out.data_ptr()), K, 1,
+                                      q.EPI_SWIGLU, None, None, None))
+        cuda.cuda.synchronize()
+        results[(warps, kb)] = out.cpu().numpy()
+        assert rel_l2(results[(warps, kb)], want) < 1e-4, (warps, kb)
+    for (warps, kb), got in results.items():
+        first = next(v for (w, _), v in results.items() if w == warps)
+        assert np.array_equal(got, first), (warps, kb)
+
+
 def test_matmul_ex_argmax_head(cuda):
     K, N = 2560, 151936
     raw = q.synth_tensor_host(0x5EED, "token_embd.weight", q.Q6_K, K, N)

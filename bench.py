@@ -11,6 +11,8 @@ whole job (strong scaling: the same model and token stream at every N).
 
 gemv (BASELINE configs[0]/[1]): the Q4_K 9728x2560 matrix-vector product,
 value in GB/s of algorithmic bytes, 20 distinct weight copies in rotation.
+swiglu / attention: the decode step's fused gate/up product and its decode
+attention alone (profiling targets).
 
 --impl reference: the reference's hot path on this host's CPU cores (the
 C restatement in oracle/, OpenMP over output rows; the reference has no CPU
@@ -433,6 +435,32 @@ def run_gemv(args, world, rank, local):
             "gpu_launches": args.steps, "clocks": clk}
 
 
+def run_swiglu(args, world, rank, local):
+    """The decode step's dominant kernel alone: RMSNorm + ffn_gate/ffn_up
+    Q4_K 2560x9728 + SiLU*up in one launch, 8 distinct weight pairs
+    (224 MB) in rotation: the profiling target behind the decode line's
+    roofline object."""
+    import torch
+
+    import q4kb200 as q
+
+    torch.cuda.set_device(local)
+    peaks = load_peaks()
+    t = time_gemv(q, torch, q.Q4_K, 2560, 9728, copies=8, reps=args.steps, swiglu=True)
+    b = gemv_bytes(q, q.Q4_K, 2560, 9728, nmat=2, norm=True)
+    gbs = b / t / 1e9
+    return {"metric": "fused RMSNorm+gate/up+SiLU Q4_K 2x9728x2560 HBM GB/s", "value": round(gbs, 1),
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": 24, "ms_per_step": round(t * 1e3, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "q4k weights, int8 activations (dp4a), fp32 accumulate", "data": "synthetic (seeded)",
+            "config": {"workload": "gate/up SwiGLU product, batch 1", "model": MODEL, "global_batch": 1,
+                       "seq_len": 1, "parallelism": "replica", "l2": "8 distinct weight pairs (224 MB) in rotation"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / peaks["hbm_gbs"], 4),
+                         "traffic": read_traffic("gemv_swiglu_q4k_2560x9728.md"), "algorithmic_bytes": b},
+            "gpu_launches": args.steps}
+
+
 def run_attention(args, world, rank, local):
     """Decode attention alone (one layer's 8 KV heads at context 4096,
     8 caches in rotation): the profiling target for the attention kernel."""
@@ -484,7 +512,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("decode", "gemv", "attention"), default="decode")
+    ap.add_argument("--workload", choices=("decode", "gemv", "swiglu", "attention"), default="decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     world, rank, local = dist_init()
@@ -499,6 +527,8 @@ def main() -> None:
         out = run_decode(args, world, rank, local)
     elif args.workload == "attention":
         out = run_attention(args, world, rank, local)
+    elif args.workload == "swiglu":
+        out = run_swiglu(args, world, rank, local)
     else:
         out = run_gemv(args, world, rank, local)
     if rank == 0 and out is not None:

@@ -148,6 +148,21 @@ int q4k_attention_decode_f16(const float* qkv, const float* q_gamma, const float
                              void* scratch, void* stream);
 size_t q4k_attention_decode_scratch_bytes(int query_heads, int kv_heads);
 
+/* No counterpart in the reference. q4k_attention_decode_f16 without a
+ * scratch argument, for callers that may not allocate device memory: the
+ * scratch is a fixed 1 MiB array in the library's device memory (one per
+ * device), so nothing is allocated. Limit: 256 + 520 * query_heads * splits
+ * bytes must fit in 1 MiB (2016 head-splits; with the default one CTA per SM
+ * a B200 needs 592), else Q4K_ERANGE; at most 64 KV heads. The first call on
+ * a device (with it current) looks up the array's address and should come
+ * before any stream capture. Every call clears the per-head counters on
+ * `stream` before launching. Calls on one device share the array: calls that
+ * can overlap in time race and must be ordered by the caller. */
+int q4k_attention_decode_f16_static(const float* qkv, const float* q_gamma, const float* k_gamma, uint16_t* k_cache,
+                                    uint16_t* v_cache, int capacity, const int* position_device, int query_heads,
+                                    int kv_heads, int head_dim, float epsilon, float rope_base, float* output,
+                                    void* stream);
+
 /* ------------------------------------------------------- decode engine */
 
 /* Replaces Engine / ChatSession (src/Engine.cpp:14-114,

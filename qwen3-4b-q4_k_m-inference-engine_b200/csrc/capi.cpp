@@ -336,6 +336,28 @@ Q4K_API size_t q4k_attention_decode_scratch_bytes(int query_heads, int kv_heads)
     return 256 + sizeof(float) * (size_t)query_heads * splits * (q4k::kDecodeHeadDim + 2);
 }
 
+// Allocation-free variant: the scratch is the library's fixed device array
+// (attention_static_scratch.cu); the launch itself is the regular entry
+// point's. Nothing is allocated: only the counters are cleared.
+Q4K_API int q4k_attention_decode_f16_static(const float* qkv, const float* q_gamma, const float* k_gamma,
+                                            uint16_t* k_cache, uint16_t* v_cache, int capacity,
+                                            const int* position_device, int query_heads, int kv_heads, int head_dim,
+                                            float epsilon, float rope_base, float* output, void* stream) {
+    void* scratch = nullptr;
+    const int rc = guarded_cuda([&] {
+        if (head_dim != q4k::kDecodeHeadDim || kv_heads <= 0 || kv_heads > 64 || query_heads != 4 * kv_heads)
+            invalid("decode attention supports head_dim 128 with 4 query heads per KV head (at most 64 KV heads)");
+        const size_t need = 256 + sizeof(float) * (size_t)query_heads *
+                                      q4k::decode_attention_splits(kv_heads) * (q4k::kDecodeHeadDim + 2);
+        scratch = q4k::attention_static_scratch(need);
+        q4k::cuda_check(cudaMemsetAsync(scratch, 0, 256, as_stream(stream)), "clear attention counters");
+    });
+    if (rc != Q4K_OK) return rc;
+    return q4k_attention_decode_f16(qkv, q_gamma, k_gamma, k_cache, v_cache, capacity, position_device, query_heads,
+                                    kv_heads, head_dim, epsilon, rope_base, output, scratch, stream);
+}
+
+
 Q4K_API int q4k_attention_decode_f16(const float* qkv, const float* q_gamma, const float* k_gamma, uint16_t* k_cache,
                                      uint16_t* v_cache, int capacity, const int* position_device, int query_heads,
                                      int kv_heads, int head_dim, float epsilon, float rope_base, float* output,

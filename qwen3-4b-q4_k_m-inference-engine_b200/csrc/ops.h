@@ -65,5 +65,9 @@ int decode_attention_splits(int kv_heads);
 size_t decode_attention_scratch_floats(int heads, int kv_heads, int splits);
 cudaError_t decode_attention(const DecodeAttnArgs& a, const KvTensorMap& kmap, const KvTensorMap& vmap,
                              cudaStream_t s, bool pdl);
+// This device's fixed scratch for q4k_attention_decode_f16_static
+// (attention_static_scratch.cu); throws q4k::Error if `need` does not fit.
+void* attention_static_scratch(size_t need);
+size_t attention_static_scratch_capacity();
 
 }  // namespace q4k

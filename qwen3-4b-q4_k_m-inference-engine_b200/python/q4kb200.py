@@ -30,7 +30,7 @@ EXPORTS = (
     "q4k_engine_create", "q4k_engine_destroy", "q4k_engine_load_synthetic", "q4k_engine_set_tensor",
     "q4k_engine_fill_kv_synthetic", "q4k_engine_read_kv", "q4k_engine_decode", "q4k_engine_generate",
     "q4k_engine_stream", "q4k_tp_shard", "q4k_engine_layer", "q4k_engine_write_kv",
-    "q4k_engine_trace",
+    "q4k_engine_trace", "q4k_attention_decode_f16_static",
 )
 
 
@@ -89,6 +89,7 @@ def lib():
             "q4k_matmul_ex": ([P, P, C.c_float, I, P, P, P, P, I64, S, I, P, P, P], I),
             "q4k_matmul_argmax_scratch_bytes": ([], S),
             "q4k_attention_decode_f16": ([P, P, P, P, P, I, P, I, I, I, C.c_float, C.c_float, P, P, P], I),
+            "q4k_attention_decode_f16_static": ([P, P, P, P, P, I, P, I, I, I, C.c_float, C.c_float, P, P], I),
             "q4k_attention_decode_scratch_bytes": ([I, I], S),
             "q4k_engine_config_qwen3_4b": ([C.POINTER(EngineConfig), I], None),
             "q4k_model_tensor": ([C.POINTER(EngineConfig), I, C.c_char_p, S, C.POINTER(I), C.POINTER(I64),

@@ -139,8 +139,9 @@ size_t q4k_matmul_argmax_scratch_bytes(void);
  * per-head q/k RMSNorm (src/Engine.cpp:87-88), RoPE (:89-90), the K/V cache
  * write and split-K attention (:92). qkv = [q | k | v] raw projections of
  * the token; caches are [kv_heads][capacity][128] fp16 for one layer;
- * *position_device is the token's position. head_dim must be 128 and
- * query_heads == 4 * kv_heads. scratch: q4k_attention_decode_scratch_bytes
+ * *position_device is the token's position. head_dim must be 128,
+ * query_heads == 4 * kv_heads and kv_heads <= 64 (the scratch's 256-byte
+ * counter block). scratch: q4k_attention_decode_scratch_bytes
  * bytes, 16-byte aligned, zeroed once before first use. */
 int q4k_attention_decode_f16(const float* qkv, const float* q_gamma, const float* k_gamma, uint16_t* k_cache,
                              uint16_t* v_cache, int capacity, const int* position_device, int query_heads,

@@ -365,8 +365,9 @@ Q4K_API int q4k_attention_decode_f16(const float* qkv, const float* q_gamma, con
     return guarded_cuda([&] {
         if (!qkv || !q_gamma || !k_gamma || !k_cache || !v_cache || !position_device || !output || !scratch)
             invalid("decode attention requires device buffers");
-        if (head_dim != q4k::kDecodeHeadDim || kv_heads <= 0 || query_heads != 4 * kv_heads || capacity <= 0)
-            invalid("decode attention supports head_dim 128 with 4 query heads per KV head");
+        if (head_dim != q4k::kDecodeHeadDim || kv_heads <= 0 || kv_heads > 64 || query_heads != 4 * kv_heads ||
+            capacity <= 0)
+            invalid("decode attention supports head_dim 128 with 4 query heads per KV head (at most 64 KV heads)");
         if (!(epsilon > 0.0f) || !(rope_base > 0.0f)) invalid("epsilon and rope base must be positive");
         if (reinterpret_cast<uintptr_t>(k_cache) % 16 || reinterpret_cast<uintptr_t>(v_cache) % 16)
             invalid("KV caches must be 16-byte aligned");

@@ -21,16 +21,16 @@
 //     in order (a team waiting on a slot another team has not yet released
 //     could match a parity two phases old). Within a team, LPR lanes work on one row (so a
 //     team covers R = TW*32/LPR rows per stage); lane f of a row takes the
-//     16-byte chunks f, f+LPR, ... . Rows are reduced with xor-shuffles in a
+//     64-value chunks f, f+LPR, ... . Rows are reduced with xor-shuffles in a
 //     fixed order, so results are deterministic.
 //   * before the rows, the consumers quantise the activation into shared
 //     memory (optionally RMSNorm-ing it first, which fuses rms_norm.cu:6-24
 //     into the product). Codes are stored in a per-block permuted order so
-//     that the 16-byte loads of the 8 lanes on one super-block hit 32
-//     distinct banks.
-//   * Q4_K: the two lanes on one 32-byte group pair each dot both nibble
-//     planes of their 16 bytes, swap one partial with a shuffle, and then
-//     each finishes one whole group (one 6-bit scale/min decode per lane).
+//     that the 16-byte code loads of the lanes on one row are conflict free.
+//   * a lane's 64-value chunk is two whole 32-value groups for Q4_K (the
+//     low and high nibbles of 32 bytes) and four 16-value runs for Q6_K, so
+//     each scale is decoded once per chunk and no partial crosses lanes
+//     before the row reduction.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -77,143 +77,151 @@ __device__ __forceinline__ void stage_rows(const GemvPlan& p, int i, int& seg, i
     nr = min(p.rows_per_stage, p.seg[seg].rows - r0);
 }
 
-// 6-bit scale and min of 32-value group g of a Q4_K block, from the three
-// header words holding bytes 4..15 (matmul.cu:40-48).
-__device__ __forceinline__ void q4_scale_min(uint32_t w0, uint32_t w1, uint32_t w2, int g, int& sc, int& mn) {
-    const int u = (g & 3) * 8;
-    const int b0 = (w0 >> u) & 0xff, b1 = (w1 >> u) & 0xff, b2 = (w2 >> u) & 0xff;
-    if (g < 4) {
-        sc = b0 & 63;
-        mn = b1 & 63;
-    } else {
-        sc = (b2 & 15) | ((b0 >> 6) << 4);
-        mn = (b2 >> 4) | ((b1 >> 6) << 4);
-    }
+// dp4a with unsigned bytes in a and signed bytes in b.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
 }
 
-// Q4_K chunk f of a row: block b = f/8, c = f%8, j = c/2, h = c%2 covers the
-// 16 bytes at 16 + 32*j + 16*h of the block: positions 16h..16h+15 of group
-// 2j (low nibbles) and of group 2j+1 (high nibbles). The pair of lanes
-// (h = 0, 1) exchanges one partial dot so that the h = 0 lane completes group
-// 2j and the h = 1 lane group 2j+1. `live` is false for a padding iteration
-// (the lane still takes part in the shuffle, its term is dropped).
+// 16-byte unit, within its 256-code block, where the activation codes of
+// piece s (codes 16s..16s+15 of the block) are stored for the Q4_K and Q6_K
+// lane mappings below. For the pieces that the lanes of one row read at the
+// same time, consecutive blocks land on disjoint halves of the 8 bank
+// groups, so a row's 16-byte loads are conflict free.
+__device__ __forceinline__ int perm_q4(int s, int b) {
+    // s = 4j + q: pair-chunk j, piece q of it
+    const int j = s >> 2, q = s & 3;
+    return 8 * (q >> 1) + 4 * ((q & 1) ^ (b & 1)) + j;
+}
+__device__ __forceinline__ int perm_q6(int s, int b) {
+    // s = 8h + 2g + l: half h, 32-group g of it, 16-run l of the group
+    const int h = s >> 3, g = (s >> 1) & 3, l = s & 1;
+    return 8 * (g >> 1) + 4 * ((g & 1) ^ (b & 1)) + 2 * h + l;
+}
+
+// Q4_K pair-chunk p of a row: block b = p/4, j = p%4 covers the 32 nibble
+// bytes at 16 + 32j of the block, i.e. the whole 32-value groups 2j (low
+// nibbles) and 2j+1 (high nibbles) (matmul.cu:24-54). A lane's j is fixed
+// (LPR is a multiple of 4), so its scale/min bytes come from fixed places.
+// The high nibbles are dotted in place (16x) with an unsigned-byte dp4a.
 template <int MT, int NR>
-__device__ __forceinline__ void q4_chunk(const uint8_t* const (&rows)[NR], int f, bool live, const uint8_t* xq,
-                                         const float* xs, const int* xsum32, int K, int mcount, float (&acc)[NR][MT]) {
-    const int b = f >> 3, c = f & 7, j = c >> 1, h = c & 1;
-    const int g = 2 * j + h;
-    uint4 xlo[MT], xhi[MT];
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-        if (m < mcount) {
-            xlo[m] = *reinterpret_cast<const uint4*>(xq + m * K + b * 256 + 16 * c);
-            xhi[m] = *reinterpret_cast<const uint4*>(xq + m * K + b * 256 + 128 + 16 * c);
-        }
-    }
+__device__ __forceinline__ void q4_pair(const uint8_t* const (&rows)[NR], int p, int j, const uint8_t* xq,
+                                        const float* xs, const float* xsumf, int K, int mcount,
+                                        float (&acc)[NR][MT]) {
+    const int b = p >> 2;
+    const int sh = (j & 1) * 16;
+    uint32_t lo[NR][8], hi[NR][8];
+    float ds0[NR], ds1[NR], dm0[NR], dm1[NR];
 #pragma unroll
     for (int r = 0; r < NR; ++r) {
         const uint8_t* blk = rows[r] + b * 144;
         const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-        const uint4 q = *reinterpret_cast<const uint4*>(blk + 16 + 32 * j + 16 * h);
-        int sc, mn;
-        q4_scale_min(hdr.y, hdr.z, hdr.w, g, sc, mn);
-        const float ds = half_bits_to_float(hdr.x) * (float)sc;
-        const float dm = half_bits_to_float(hdr.x >> 16) * (float)mn;
-        const uint32_t l0 = q.x & 0x0f0f0f0fu, l1 = q.y & 0x0f0f0f0fu, l2 = q.z & 0x0f0f0f0fu, l3 = q.w & 0x0f0f0f0fu;
-        const uint32_t h0 = (q.x >> 4) & 0x0f0f0f0fu, h1 = (q.y >> 4) & 0x0f0f0f0fu;
-        const uint32_t h2 = (q.z >> 4) & 0x0f0f0f0fu, h3 = (q.w >> 4) & 0x0f0f0f0fu;
+        const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * j);
+        const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * j);
+        // the 6-bit scales (SC) and mins (MN) of groups 0..3 or 4..7 as bytes
+        const uint32_t SC = j < 2 ? (hdr.y & 0x3f3f3f3fu) : ((hdr.w & 0x0f0f0f0fu) | ((hdr.y >> 2) & 0x30303030u));
+        const uint32_t MN =
+            j < 2 ? (hdr.z & 0x3f3f3f3fu) : (((hdr.w >> 4) & 0x0f0f0f0fu) | ((hdr.z >> 2) & 0x30303030u));
+        const float d = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
+        ds0[r] = d * (float)((SC >> sh) & 0xffu);
+        ds1[r] = d * (float)((SC >> (sh + 8)) & 0xffu);
+        dm0[r] = dmin * (float)((MN >> sh) & 0xffu);
+        dm1[r] = dmin * (float)((MN >> (sh + 8)) & 0xffu);
+        const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-        for (int m = 0; m < MT; ++m) {
-            if (m < mcount) {
-                int dlo = __dp4a((int)l0, (int)xlo[m].x, 0);
-                dlo = __dp4a((int)l1, (int)xlo[m].y, dlo);
-                dlo = __dp4a((int)l2, (int)xlo[m].z, dlo);
-                dlo = __dp4a((int)l3, (int)xlo[m].w, dlo);
-                int dhi = __dp4a((int)h0, (int)xhi[m].x, 0);
-                dhi = __dp4a((int)h1, (int)xhi[m].y, dhi);
-                dhi = __dp4a((int)h2, (int)xhi[m].z, dhi);
-                dhi = __dp4a((int)h3, (int)xhi[m].w, dhi);
-                const int mine = h ? dhi : dlo;
-                const int theirs = __shfl_xor_sync(0xffffffffu, h ? dlo : dhi, 1);
-                const int dot = mine + theirs;
-                const int gi = m * (K / 32) + b * 8 + g;
-                const float term = xs[gi] * (ds * (float)dot - dm * (float)xsum32[gi]);
-                if (live) acc[r][m] += term;
-            }
+        for (int k = 0; k < 8; ++k) {
+            lo[r][k] = w[k] & 0x0f0f0f0fu;
+            hi[r][k] = w[k] & 0xf0f0f0f0u;
         }
     }
-}
-
-// Q6_K chunk f of a planar row: block b = f/8, c = f%8 -> half = c/4,
-// s = (c/2)%2, t = c%2. The 16 ql bytes at half*64 + s*32 + t*16 carry the
-// low nibbles of 16-value runs A (32-group 4*half+s) and B (4*half+s+2);
-// the 16 qh bytes at half*32 + t*16 carry their top two bits
-// (matmul.cu:68-83, embedding.cu:42-58).
-template <int MT, int NR>
-__device__ __forceinline__ void q6_chunk(const uint8_t* const (&rows)[NR], int nb, int f, bool live,
-                                         const uint8_t* xq, const float* xs, const int* xsum16, int K, int mcount,
-                                         float (&acc)[NR][MT]) {
-    const int b = f >> 3, c = f & 7, half = c >> 2, s = (c >> 1) & 1, t = c & 1;
-    const int rA = 8 * half + 2 * s + t, rB = rA + 4;
-    const int gA = 4 * half + s, gB = gA + 2;
-    const int shA = 2 * s, shB = 2 * s + 4;
-    uint4 xa[MT], xb[MT];
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
         if (m < mcount) {
-            xa[m] = *reinterpret_cast<const uint4*>(xq + m * K + b * 256 + 16 * c);
-            xb[m] = *reinterpret_cast<const uint4*>(xq + m * K + b * 256 + 128 + 16 * c);
-        }
-    }
+            const uint8_t* xb = xq + m * K + b * 256;
+            uint4 xv[4];
 #pragma unroll
-    for (int r = 0; r < NR; ++r) {
-        const uint8_t* row = rows[r];
-        const uint4 ql = *reinterpret_cast<const uint4*>(row + b * 128 + half * 64 + s * 32 + t * 16);
-        const uint4 qh = *reinterpret_cast<const uint4*>(row + nb * 128 + b * 64 + half * 32 + t * 16);
-        const int8_t* sc = reinterpret_cast<const int8_t*>(row + nb * 192 + b * 16);
-        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(row + nb * 208 + b * 2));
-        const float dA = d * (float)sc[rA], dB = d * (float)sc[rB];
-        const uint32_t a0 = (ql.x & 0x0f0f0f0fu) | (((qh.x >> shA) & 0x03030303u) << 4);
-        const uint32_t a1 = (ql.y & 0x0f0f0f0fu) | (((qh.y >> shA) & 0x03030303u) << 4);
-        const uint32_t a2 = (ql.z & 0x0f0f0f0fu) | (((qh.z >> shA) & 0x03030303u) << 4);
-        const uint32_t a3 = (ql.w & 0x0f0f0f0fu) | (((qh.w >> shA) & 0x03030303u) << 4);
-        const uint32_t b0 = ((ql.x >> 4) & 0x0f0f0f0fu) | (((qh.x >> shB) & 0x03030303u) << 4);
-        const uint32_t b1 = ((ql.y >> 4) & 0x0f0f0f0fu) | (((qh.y >> shB) & 0x03030303u) << 4);
-        const uint32_t b2 = ((ql.z >> 4) & 0x0f0f0f0fu) | (((qh.z >> shB) & 0x03030303u) << 4);
-        const uint32_t b3 = ((ql.w >> 4) & 0x0f0f0f0fu) | (((qh.w >> shB) & 0x03030303u) << 4);
+            for (int q = 0; q < 4; ++q) xv[q] = *reinterpret_cast<const uint4*>(xb + 16 * perm_q4(4 * j + q, b));
+            const float2 s2 = *reinterpret_cast<const float2*>(xs + m * (K / 32) + b * 8 + 2 * j);
+            const float2 t2 = *reinterpret_cast<const float2*>(xsumf + m * (K / 32) + b * 8 + 2 * j);
+            const uint32_t xl[8] = {xv[0].x, xv[0].y, xv[0].z, xv[0].w, xv[1].x, xv[1].y, xv[1].z, xv[1].w};
+            const uint32_t xh[8] = {xv[2].x, xv[2].y, xv[2].z, xv[2].w, xv[3].x, xv[3].y, xv[3].z, xv[3].w};
 #pragma unroll
-        for (int m = 0; m < MT; ++m) {
-            if (m < mcount) {
-                const int* sum = xsum16 + m * (K / 16) + b * 16;
-                // codes are in [0, 63], so signed dp4a is exact; (q - 32) is
-                // applied through the run sums
-                int da = __dp4a((int)a0, (int)xa[m].x, 0);
-                da = __dp4a((int)a1, (int)xa[m].y, da);
-                da = __dp4a((int)a2, (int)xa[m].z, da);
-                da = __dp4a((int)a3, (int)xa[m].w, da);
-                da -= 32 * sum[rA];
-                int db = __dp4a((int)b0, (int)xb[m].x, 0);
-                db = __dp4a((int)b1, (int)xb[m].y, db);
-                db = __dp4a((int)b2, (int)xb[m].z, db);
-                db = __dp4a((int)b3, (int)xb[m].w, db);
-                db -= 32 * sum[rB];
-                const float* xsm = xs + m * (K / 32) + b * 8;
-                const float term = xsm[gA] * (dA * (float)da) + xsm[gB] * (dB * (float)db);
-                if (live) acc[r][m] += term;
+            for (int r = 0; r < NR; ++r) {
+                int dl = 0, dh = 0;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    dl = __dp4a((int)lo[r][k], (int)xl[k], dl);
+                    dh = dp4a_us(hi[r][k], xh[k], dh);
+                }
+                dh >>= 4;  // exact: every term is a multiple of 16
+                acc[r][m] += s2.x * (ds0[r] * (float)dl - dm0[r] * t2.x);
+                acc[r][m] += s2.y * (ds1[r] * (float)dh - dm1[r] * t2.y);
             }
         }
     }
 }
 
-// Permuted byte offset, inside its 256-value block, of the 16-value run r16
-// for the Q4_K and Q6_K lane mappings above.
-__device__ __forceinline__ int perm_q4(int r16) {
-    const int j = r16 >> 2, lohi = (r16 >> 1) & 1, h = r16 & 1;
-    return (lohi * 8 + 2 * j + h) * 16;
-}
-__device__ __forceinline__ int perm_q6(int r16) {
-    const int half = r16 >> 3, ab = (r16 >> 2) & 1, s = (r16 >> 1) & 1, t = r16 & 1;
-    return (ab * 8 + 4 * half + 2 * s + t) * 16;
+// Q6_K quarter p of a planar row: block b = p/4, i = p%4 -> half h = i/2,
+// l = i%2 covers positions 16l..16l+15 of every 32-group g = 0..3 of half h,
+// i.e. the 16-value runs 8h + 2g + l. The 16 ql bytes at 64h + 16l (groups
+// 0, 2) and 64h + 32 + 16l (groups 1, 3) carry the low nibbles, the 16 qh
+// bytes at 32h + 16l the top two bits (matmul.cu:56-84, embedding.cu:42-58).
+// A lane's i is fixed. xs16 holds 32 * (code sum) of each run, ordered so
+// that a quarter's four runs are adjacent.
+template <int MT, int NR>
+__device__ __forceinline__ void q6_quarter(const uint8_t* const (&rows)[NR], int nb, int p, int i,
+                                           const uint8_t* xq, const float* xs, const int* xs16, int K, int mcount,
+                                           float (&acc)[NR][MT]) {
+    const int b = p >> 2, h = i >> 1, l = i & 1;
+    uint32_t q[NR][4][4];  // [row][group g][word]
+    float dsc[NR][4];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+        const uint8_t* row = rows[r];
+        const uint4 A = *reinterpret_cast<const uint4*>(row + b * 128 + 64 * h + 16 * l);
+        const uint4 B = *reinterpret_cast<const uint4*>(row + b * 128 + 64 * h + 32 + 16 * l);
+        const uint4 Q = *reinterpret_cast<const uint4*>(row + nb * 128 + b * 64 + 32 * h + 16 * l);
+        const uint2 scw = *reinterpret_cast<const uint2*>(row + nb * 192 + b * 16 + 8 * h);
+        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(row + nb * 208 + b * 2));
+        // run 8h + 2g + l: scale byte l + 2g of the 8 at 8h
+        dsc[r][0] = d * (float)(int8_t)(scw.x >> (8 * l));
+        dsc[r][1] = d * (float)(int8_t)(scw.x >> (8 * l + 16));
+        dsc[r][2] = d * (float)(int8_t)(scw.y >> (8 * l));
+        dsc[r][3] = d * (float)(int8_t)(scw.y >> (8 * l + 16));
+        const uint32_t a[4] = {A.x, A.y, A.z, A.w}, bb[4] = {B.x, B.y, B.z, B.w}, qh[4] = {Q.x, Q.y, Q.z, Q.w};
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            q[r][0][w] = (a[w] & 0x0f0f0f0fu) | ((qh[w] << 4) & 0x30303030u);
+            q[r][1][w] = (bb[w] & 0x0f0f0f0fu) | ((qh[w] << 2) & 0x30303030u);
+            q[r][2][w] = ((a[w] >> 4) & 0x0f0f0f0fu) | (qh[w] & 0x30303030u);
+            q[r][3][w] = ((bb[w] >> 4) & 0x0f0f0f0fu) | ((qh[w] >> 2) & 0x30303030u);
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+        if (m < mcount) {
+            const uint8_t* xb = xq + m * K + b * 256;
+            const float4 s4 = *reinterpret_cast<const float4*>(xs + m * (K / 32) + b * 8 + 4 * h);
+            const int4 c4 = *reinterpret_cast<const int4*>(xs16 + m * (K / 16) + b * 16 + 4 * i);
+            const float sg[4] = {s4.x, s4.y, s4.z, s4.w};
+            const int cg[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                const uint4 xv = *reinterpret_cast<const uint4*>(xb + 16 * perm_q6(8 * h + 2 * g + l, b));
+#pragma unroll
+                for (int r = 0; r < NR; ++r) {
+                    // codes are in [0, 63], so signed dp4a is exact; the -32
+                    // is applied through the run sums
+                    int dd = __dp4a((int)q[r][g][0], (int)xv.x, 0);
+                    dd = __dp4a((int)q[r][g][1], (int)xv.y, dd);
+                    dd = __dp4a((int)q[r][g][2], (int)xv.z, dd);
+                    dd = __dp4a((int)q[r][g][3], (int)xv.w, dd);
+                    acc[r][m] += sg[g] * (dsc[r][g] * (float)(dd - cg[g]));
+                }
+            }
+        }
+    }
 }
 
 __device__ __forceinline__ int8_t q8_code(float v, float amax) {
@@ -231,7 +239,7 @@ __device__ __forceinline__ void quantise_activation(const GemvPlan& p, int m0, i
     uint8_t* xq6 = p.off_xq6 >= 0 ? smem + p.off_xq6 : nullptr;
     float* xs = reinterpret_cast<float*>(smem + p.off_xs);
     int* xsum16 = reinterpret_cast<int*>(smem + p.off_xsum16);
-    int* xsum32 = reinterpret_cast<int*>(smem + p.off_xsum32);
+    float* xsum32 = reinterpret_cast<float*>(smem + p.off_xsum32);
     float* red = reinterpret_cast<float*>(smem + p.off_misc);
     const int nvec = K / 4;
     constexpr int kHeld = 12;  // float4s of the row a thread keeps in registers (K <= 12 * 4 * nthreads)
@@ -290,11 +298,13 @@ __device__ __forceinline__ void quantise_activation(const GemvPlan& p, int m0, i
             run += __shfl_xor_sync(0xffffffffu, run, 2);
             const int group = run + __shfl_xor_sync(0xffffffffu, run, 4);
             const int b = e >> 8, r16 = (e & 255) >> 4, o = e & 15;
-            if (xq4) *reinterpret_cast<uint32_t*>(xq4 + m * K + b * 256 + perm_q4(r16) + o) = word;
-            if (xq6) *reinterpret_cast<uint32_t*>(xq6 + m * K + b * 256 + perm_q6(r16) + o) = word;
-            if ((lane & 3) == 0) xsum16[m * (K / 16) + (e >> 4)] = run;
+            if (xq4) *reinterpret_cast<uint32_t*>(xq4 + m * K + b * 256 + 16 * perm_q4(r16, b) + o) = word;
+            if (xq6) *reinterpret_cast<uint32_t*>(xq6 + m * K + b * 256 + 16 * perm_q6(r16, b) + o) = word;
+            // run r16 = 8h + 2g + l is stored at quarter (2h + l), slot g
+            if ((lane & 3) == 0)
+                xsum16[m * (K / 16) + b * 16 + 4 * (2 * (r16 >> 3) + (r16 & 1)) + ((r16 >> 1) & 3)] = 32 * run;
             if ((lane & 7) == 0) {
-                xsum32[m * (K / 32) + (e >> 5)] = group;
+                xsum32[m * (K / 32) + (e >> 5)] = (float)group;
                 xs[m * (K / 32) + (e >> 5)] = amax / 127.0f;  // matmul.cu:18
             }
         }
@@ -367,15 +377,16 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     const uint8_t* xq6 = p.off_xq6 >= 0 ? smem + p.off_xq6 : nullptr;
     const float* xs = reinterpret_cast<const float*>(smem + p.off_xs);
     const int* xsum16 = reinterpret_cast<const int*>(smem + p.off_xsum16);
-    const int* xsum32 = reinterpret_cast<const int*>(smem + p.off_xsum32);
+    const float* xsum32 = reinterpret_cast<const float*>(smem + p.off_xsum32);
 
     const int team = warp / kTeamWarps;
     const int team_threads = kTeamWarps * 32;
     const int LPR = p.lpr;
     const int sub = lane % LPR;                                        // lane within the row's lanes
     const int slot_row = (warp % kTeamWarps) * (32 / LPR) + lane / LPR;  // row of the stage
-    const int chunks = p.nb * 8;
+    const int chunks = p.nb * 4;  // 64-value pair-chunks (Q4_K) or quarters (Q6_K) per row
     const int iters = (chunks + LPR - 1) / LPR;
+    const int lane_part = sub & 3;  // the lane's chunk within a block (LPR is a multiple of 4)
     float best_score = -__int_as_float(0x7f800000);
     uint32_t best_index = 0xffffffffu;
 
@@ -402,15 +413,13 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
 #pragma unroll 2
             for (int k = 0; k < iters; ++k) {
                 const int f = sub + LPR * k;
-                const bool live = f < chunks;
-                q4_chunk<MT, NR>(rows, live ? f : (f & 1), live, xq4, xs, xsum32, K, mcount, acc);
+                if (f < chunks) q4_pair<MT, NR>(rows, f, lane_part, xq4, xs, xsum32, K, mcount, acc);
             }
         } else {
 #pragma unroll 2
             for (int k = 0; k < iters; ++k) {
                 const int f = sub + LPR * k;
-                const bool live = f < chunks;
-                q6_chunk<MT, NR>(rows, p.nb, live ? f : (f & 1), live, xq6, xs, xsum16, K, mcount, acc);
+                if (f < chunks) q6_quarter<MT, NR>(rows, p.nb, f, lane_part, xq6, xs, xsum16, K, mcount, acc);
             }
         }
         // all of this team's reads of the stage are done: release it
@@ -628,9 +637,9 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     off += 128 * 4;
     off = align_up(off, 128);
 
-    // Lanes per row: about ten 16-byte chunks per lane per stage.
-    const int chunks = p.nb * 8;
-    int lpr = env_int("Q4K_GEMV_LPR", chunks <= 96 ? 8 : chunks <= 160 ? 16 : 32);
+    // Lanes per row: about five 64-value chunks per lane per stage.
+    const int chunks = p.nb * 4;
+    int lpr = env_int("Q4K_GEMV_LPR", chunks <= 48 ? 8 : chunks <= 80 ? 16 : 32);
     if (lpr != 8 && lpr != 16 && lpr != 32) lpr = 32;
     // consumer warps: teams of four (8 by default); K/4 float4s of the
     // activation row must fit the prologue's registers (12 per thread)

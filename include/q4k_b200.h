@@ -249,11 +249,12 @@ int q4k_engine_layer(q4k_engine* engine, int layer, const float* x_host, int pos
 void* q4k_engine_stream(q4k_engine* engine);
 
 /* Diagnostics, no counterpart in the reference: one decode step (like
- * q4k_engine_decode) whose kernels record, per CTA, four words
- * {tag, block, start_ns, end_ns} of the %globaltimer clock. Tags are
- * kind * 10000 + layer (1 QKV, 2 attention (+500 for the CTA that merges a
- * head), 3 O, 4 gate/up, 5 down, 6 output head). Up to max_records records
- * go to records_host; *count receives how many were written. */
+ * q4k_engine_decode) whose kernels store %globaltimer nanoseconds into a
+ * [256 launches][1024 CTAs][8 slots] array of words: launch 5*layer + k
+ * (k: 0 QKV, 1 attention, 2 O, 3 gate/up, 4 down), 5*layers the output
+ * head; slot 0 a CTA's start, 7 its end, 1..6 kernel checkpoints (6 marks the
+ * attention CTA that merged a head); 0 where nothing was recorded. Up to
+ * max_records words go to records_host; *count receives how many. */
 int q4k_engine_trace(q4k_engine* engine, uint32_t token, int position, unsigned long long* records_host,
                      size_t max_records, size_t* count);
 

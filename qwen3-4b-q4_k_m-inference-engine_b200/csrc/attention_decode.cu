@@ -32,17 +32,15 @@
 
 #include "ops.h"
 #include "q4k_device.cuh"
+#include "attention_device.cuh"
 
 namespace q4k {
 namespace {
 
-constexpr int D = kDecodeHeadDim;  // 128
-constexpr int G = 4;               // query heads per KV head
-constexpr int T = 64;              // positions per tile
+using namespace attn_dev;
+constexpr int T = kAttnTile;  // positions per tile
 constexpr int kComputeWarps = 8;
 constexpr int kComputeThreads = kComputeWarps * 32;
-constexpr int kBox = T * 64 * 2;       // one 64-position x 64-dim fp16 box: 8 KB
-constexpr int kTileBytes = 2 * kBox;   // K or V tile: 16 KB
 constexpr int kStageBytes = 2 * kTileBytes;  // K + V
 
 struct Args {
@@ -66,63 +64,6 @@ struct Args {
     int trace_tag;
 };
 
-__device__ __forceinline__ float rope_angle(int pos, int j, float base) {
-    // rope.cu:19-20
-    return (float)pos * powf(base, -2.0f * (float)j / (float)D);
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_addr(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
-        : "memory");
-}
-
-// Byte offset of (row r, 16-byte chunk c of the 128-dim row) inside a tile
-// loaded as two 64-dim boxes with the 128-byte swizzle.
-__device__ __forceinline__ uint32_t tile_off(int r, int c) {
-    return (uint32_t)((c >> 3) * kBox + r * 128 + (((c & 7) ^ (r & 7)) << 4));
-}
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(addr));
-}
-
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(addr));
-}
-
-__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-    // rows 8..15 of A are zero (a1 = a3 = 0)
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-        "{%0, %1, %2, %3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ void mma1688(float& c0, float& c1, uint32_t a0, uint32_t b0) {
-    float c2 = 0.0f, c3 = 0.0f;  // rows 8..15: zero A rows, results unused
-    asm volatile(
-        "mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%0, %1, %2, %3};"
-        : "+f"(c0), "+f"(c1), "+f"(c2), "+f"(c3)
-        : "r"(a0), "r"(0u), "r"(b0));
-}
-
-// fp32 pair -> packed fp16 (hi) and the fp16 residual (lo).
-__device__ __forceinline__ void split2(float x, float y, uint32_t& hi, uint32_t& lo) {
-    const __half2 h = __floats2half2_rn(x, y);
-    const float2 hf = __half22float2(h);
-    const __half2 l = __floats2half2_rn(x - hf.x, y - hf.y);
-    hi = *reinterpret_cast<const uint32_t*>(&h);
-    lo = *reinterpret_cast<const uint32_t*>(&l);
-}
-
 struct SmemTail {
     uint4 qf[8][32];
     float q[G][D];
@@ -145,7 +86,7 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 2)
     SmemTail& sm = *reinterpret_cast<SmemTail*>(smem + S * kStageBytes);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x, kvh = blockIdx.y, splits = gridDim.x;
-    const uint64_t t_start = a.trace ? global_timer_ns() : 0;
+    if (threadIdx.x == 0) trace_at(a.trace, a.trace_tag, 0);
 
     const int pos = *a.position;
     if (pos < 0 || pos >= a.capacity) {
@@ -257,6 +198,7 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 2)
         sm.qf[s][l] = f;
     }
     named_barrier(1, kComputeThreads);
+    if (tid == 0) trace_at(a.trace, a.trace_tag, 1);
 
     // ---------------- tiles: this warp owns tile rows [8w, 8w + 8) ----------------
     const float scale = rsqrtf((float)D);  // attention.cu:40
@@ -271,6 +213,7 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 2)
         // A warp whose wait gave up flags the CTA; every warp still reaches the
         // end-of-tile barrier, after which all leave together.
         const bool landed = mbar_wait_bounded(&sm.full[s], use & 1, a.err, ERR_WAIT_TIMEOUT_FULL);
+        if (tid == 0 && (t == 0 || t == tiles - 1)) trace_at(a.trace, a.trace_tag, t == 0 ? 2 : 3);
         if (!__all_sync(0xffffffffu, landed) && lane == 0) sm.abort[t & 1] = 1;
         const int lo = p0 + t * T;
         const int n = min(T, p1 - lo);
@@ -396,10 +339,11 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 2)
     }
     __threadfence();
     named_barrier(1, kComputeThreads);
+    if (tid == 0) trace_at(a.trace, a.trace_tag, 4);
     if (tid == 0) sm.last = atomicAdd(a.counters + kvh, 1u) == (unsigned)(splits - 1);
     named_barrier(1, kComputeThreads);
     if (!sm.last) {
-        if (tid == 0) trace_record(a.trace, a.trace_tag, t_start);
+        if (tid == 0) trace_at(a.trace, a.trace_tag, 7);
         return;
     }
     __threadfence();
@@ -440,7 +384,8 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 2)
     out[d0 + 1] = o1 / LL;
     if (tid == 0) {
         a.counters[kvh] = 0u;
-        trace_record(a.trace, a.trace_tag + 500, t_start);  // the merging CTA
+        trace_at(a.trace, a.trace_tag, 6);  // slot 6 marks the merging CTA
+        trace_at(a.trace, a.trace_tag, 7);
     }
 }
 

@@ -23,6 +23,7 @@
 #include <dlfcn.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -226,6 +227,26 @@ Engine::Engine(const q4k_engine_config& cfg, const void* nccl_id) : c_(cfg) {
     tp_cand_local_ = static_cast<float*>(alloc(64));
     tp_cand_all_ = static_cast<float*>(alloc(sizeof(float) * 2 * world_ + 64));
     cuda_check(cudaMallocHost(&host_io_, 64), "cudaMallocHost");
+    {
+        // Q4K_STEP_KERNEL=1: decode with the persistent decode-step kernel
+        // (or fail saying why it cannot run); otherwise the launch sequence,
+        // which measures faster today
+        const char* env = std::getenv("Q4K_STEP_KERNEL");
+        const bool wanted = env && env[0] == '1';
+        std::string why;
+        step_ctas_ = step_ctas(&why);
+        step_splits_ = step_ctas_ > 0 ? step_ctas_ / KVHl_ : 0;
+        if (world_ != 1) why = "tensor parallelism uses the launch sequence";
+        else if (step_ctas_ > 0 && (step_splits_ < 1 || step_splits_ > splits_)) why = "attention split count";
+        step_kernel_ = wanted && why.empty();
+        if (wanted && !step_kernel_)
+            throw Error(Q4K_EINVAL, "decode-step kernel unavailable: " + why);
+        if (step_kernel_) {
+            step_nphases_ = 2 + 5 * c.layers;
+            step_phases_ = static_cast<StepPhase*>(alloc(sizeof(StepPhase) * step_nphases_));
+            step_sync_ = static_cast<unsigned*>(alloc(sizeof(unsigned) * (step_nphases_ + 1)));
+        }
+    }
     cuda_check(cudaStreamSynchronize(stream_), "init");
 }
 
@@ -316,6 +337,7 @@ void Engine::load_synthetic(uint64_t seed) {
     }
     cudaFree(tmp);
     loaded_ = true;
+    step_ready_ = false;
 }
 
 void Engine::set_tensor(const std::string& name, int type, int64_t ne0, int64_t ne1, const void* host_gguf) {
@@ -348,6 +370,7 @@ void Engine::set_tensor(const std::string& name, int type, int64_t ne0, int64_t 
     cuda_check(e, "set_tensor");
     have_[idx] = true;
     loaded_ = std::all_of(have_.begin(), have_.end(), [](bool b) { return b; });
+    step_ready_ = false;
     if (exec_) {
         cudaGraphExecDestroy(exec_);
         exec_ = nullptr;
@@ -419,7 +442,7 @@ void Engine::enqueue_layer(int i) {
         r.err = err_;
         r.pdl = true;
         r.trace = trace_;
-        r.trace_tag = 10000 + i;
+        r.trace_tag = 5 * i;
         gemv(r);
     }
     {
@@ -443,7 +466,7 @@ void Engine::enqueue_layer(int i) {
         a.splits = splits_;
         a.row_base = i * KVHl_ * c.capacity;
         a.trace = trace_;
-        a.trace_tag = 20000 + i;
+        a.trace_tag = 5 * i + 1;
         cuda_check(decode_attention(a, kmap_, vmap_, stream_, true), "attention launch");
     }
     {
@@ -456,7 +479,7 @@ void Engine::enqueue_layer(int i) {
         r.err = err_;
         r.pdl = true;
         r.trace = trace_;
-        r.trace_tag = 30000 + i;
+        r.trace_tag = 5 * i + 2;
         gemv(r);
         if (world_ > 1) all_reduce_into_x();
     }
@@ -473,7 +496,7 @@ void Engine::enqueue_layer(int i) {
         r.err = err_;
         r.pdl = true;
         r.trace = trace_;
-        r.trace_tag = 40000 + i;
+        r.trace_tag = 5 * i + 3;
         gemv(r);
     }
     {
@@ -486,7 +509,7 @@ void Engine::enqueue_layer(int i) {
         r.err = err_;
         r.pdl = true;
         r.trace = trace_;
-        r.trace_tag = 50000 + i;
+        r.trace_tag = 5 * i + 4;
         gemv(r);
         if (world_ > 1) all_reduce_into_x();
     }
@@ -524,7 +547,7 @@ void Engine::enqueue_step(bool record_hidden) {
         r.argmax.counter = am_counter_;
         r.argmax.index_base = (uint32_t)vocab0_;
         r.trace = trace_;
-        r.trace_tag = 60000;
+        r.trace_tag = 5 * c_.layers;
         if (world_ > 1) {
             r.argmax.token = reinterpret_cast<uint32_t*>(tp_cand_local_) + 1;
             r.argmax.score = tp_cand_local_;
@@ -552,6 +575,121 @@ void Engine::enqueue_step(bool record_hidden) {
                                       world_ > 1 ? reinterpret_cast<const uint32_t*>(tp_cand_all_) : nullptr, world_),
                    "finish launch");
     }
+}
+
+void Engine::ensure_step_plan() {
+    if (step_ready_) return;
+    const auto& c = c_;
+    const int H = c.hidden;
+    std::vector<StepPhase> ph;
+    auto gemv_phase = [&](int dep, int layer, int epilogue, int K, const float* x, const float* gamma,
+                          std::initializer_list<GemvSegment> segs, bool pair) {
+        StepPhase p;
+        p.kind = kStepGemv;
+        p.dep = dep;
+        p.layer = layer;
+        p.epilogue = epilogue;
+        p.K = K;
+        p.nb = K / 256;
+        p.pair = pair ? 1 : 0;
+        p.x = x;
+        p.gamma = gamma;
+        int n = 0, max_row = 0;
+        for (const GemvSegment& g : segs) {
+            p.w[n] = g.w;
+            p.y[n] = g.y;
+            p.type[n] = g.type;
+            p.rows[n] = g.rows;
+            p.row_bytes[n] = (int)q4k_device_row_bytes(g.type, (size_t)K);
+            max_row = std::max(max_row, p.row_bytes[n]);
+            (g.type == Q4K_TYPE_Q4_K ? p.q4 : p.q6) = 1;
+            ++n;
+        }
+        // the step kernel stages the fp32 activation (and gamma) in 40 KB of shared memory
+        if (K * 4 * (gamma ? 2 : 1) > 40 * 1024 || !step_gemv_geometry(K, max_row, pair, p.q4, p.q6, p.lpr, p.R))
+            throw Error(Q4K_EINVAL, "decode-step kernel: no stage geometry for this product");
+        p.nseg = pair ? 1 : n;
+        int stages = 0;
+        for (int s = 0; s < p.nseg; ++s) {
+            p.stage_start[s] = stages;
+            stages += (p.rows[s] + p.R - 1) / p.R;
+        }
+        for (int s = p.nseg; s <= kMaxSegments; ++s) p.stage_start[s] = stages;
+        p.total_stages = stages;
+        ph.push_back(p);
+        return (int)ph.size() - 1;
+    };
+    StepPhase embed;
+    embed.kind = kStepEmbed;
+    ph.push_back(embed);
+    int prev = 0;
+    for (int i = 0; i < c.layers; ++i) {
+        const Layer& L = layers_[i];
+        const int qkv = gemv_phase(prev, i, EPI_STORE, H, x_, L.attn_norm,
+                                   {{L.q, qkv_, L.tq, qd_}, {L.k, qkv_ + qd_, L.tk, kvd_},
+                                    {L.v, qkv_ + qd_ + kvd_, L.tv, kvd_}},
+                                   false);
+        StepPhase at;
+        at.kind = kStepAttention;
+        at.dep = qkv;
+        at.layer = i;
+        at.gamma = L.q_norm;
+        at.gamma2 = L.k_norm;
+        ph.push_back(at);
+        const int att = (int)ph.size() - 1;
+        const int o = gemv_phase(att, i, EPI_ADD, qd_, att_, nullptr, {{L.o, x_, L.to, H}}, false);
+        const int gu = gemv_phase(o, i, EPI_SWIGLU, H, x_, L.ffn_norm,
+                                  {{L.gate, act_, L.tgate, ffn_l_}, {L.up, act_, L.tup, ffn_l_}}, true);
+        prev = gemv_phase(gu, i, EPI_ADD, ffn_l_, act_, nullptr, {{L.down, x_, L.tdown, H}}, false);
+    }
+    gemv_phase(prev, c.layers, EPI_ARGMAX, H, x_, output_norm_, {{token_embd_, logits_, t_embd_, c.vocab}}, false);
+    if ((int)ph.size() != step_nphases_) throw Error(Q4K_ECUDA, "decode-step plan size");
+    cuda_check(cudaMemcpyAsync(step_phases_, ph.data(), sizeof(StepPhase) * ph.size(), cudaMemcpyHostToDevice,
+                               stream_),
+               "upload step plan");
+    cuda_check(cudaStreamSynchronize(stream_), "upload step plan");
+    step_ready_ = true;
+}
+
+void Engine::enqueue_step_kernel() {
+    const auto& c = c_;
+    StepArgs a;
+    a.phases = step_phases_;
+    a.nphases = step_nphases_;
+    a.sync = step_sync_;
+    a.err = err_;
+    a.token = token_;
+    a.pos = pos_;
+    a.advance = advance_;
+    a.history = history_;
+    a.history_n = history_n_;
+    a.history_cap = (unsigned)c.capacity;
+    a.embd = token_embd_;
+    a.embd_type = t_embd_;
+    a.hidden = c.hidden;
+    a.vocab = c.vocab;
+    a.x = x_;
+    a.qkv = qkv_;
+    a.att = att_;
+    a.kcache = kcache_;
+    a.vcache = vcache_;
+    a.capacity = c.capacity;
+    a.heads = Hl_;
+    a.kv_heads = KVHl_;
+    a.splits = step_splits_;
+    a.eps = c.eps;
+    a.rope_base = c.rope_base;
+    a.partial_o = attn_part_o_;
+    a.partial_ml = attn_part_ml_;
+    a.counters = attn_counters_;
+    a.argmax.cand_score = am_score_;
+    a.argmax.cand_index = am_index_;
+    a.argmax.counter = am_counter_;
+    a.argmax.token = token_;
+    a.argmax.index_base = 0;
+    a.trace = trace_;
+    if (const char* env = std::getenv("Q4K_STEP_INFLIGHT")) a.inflight = std::max(1, std::atoi(env));
+    cuda_check(launch_decode_step(a, kmap_, vmap_, step_ctas_, stream_), "decode-step launch");
 }
 
 void Engine::ensure_graph() {
@@ -599,6 +737,9 @@ uint32_t Engine::decode(uint32_t token, int position, float* logits_host, float*
     cuda_check(cudaMemsetAsync(history_n_, 0, 4, stream_), "memset");
     if (hidden_host) {
         enqueue_step(true);
+    } else if (step_kernel_) {
+        ensure_step_plan();
+        enqueue_step_kernel();
     } else {
         ensure_graph();
         cuda_check(cudaGraphLaunch(exec_, stream_), "graph launch");
@@ -623,7 +764,10 @@ void Engine::generate(uint32_t token, int position, int steps, int advance, uint
     const long long last = (long long)position + (advance ? (long long)steps - 1 : 0);
     if (position < 0 || last >= c_.capacity) throw Error(Q4K_ERANGE, "KV cache capacity exceeded");
     if (steps == 0) return;
-    ensure_graph();
+    if (step_kernel_)
+        ensure_step_plan();
+    else
+        ensure_graph();
     host_io_[0] = token;
     host_io_[1] = (uint32_t)position;
     host_io_[2] = advance ? 1u : 0u;
@@ -631,7 +775,12 @@ void Engine::generate(uint32_t token, int position, int steps, int advance, uint
     cuda_check(cudaMemcpyAsync(pos_, &host_io_[1], 4, cudaMemcpyHostToDevice, stream_), "h2d");
     cuda_check(cudaMemcpyAsync(advance_, &host_io_[2], 4, cudaMemcpyHostToDevice, stream_), "h2d");
     cuda_check(cudaMemsetAsync(history_n_, 0, 4, stream_), "memset");
-    for (int s = 0; s < steps; ++s) cuda_check(cudaGraphLaunch(exec_, stream_), "graph launch");
+    for (int s = 0; s < steps; ++s) {
+        if (step_kernel_)
+            enqueue_step_kernel();
+        else
+            cuda_check(cudaGraphLaunch(exec_, stream_), "graph launch");
+    }
     if (tokens_host)
         cuda_check(cudaMemcpyAsync(tokens_host, history_, sizeof(uint32_t) * steps, cudaMemcpyDeviceToHost, stream_),
                    "d2h tokens");
@@ -642,36 +791,40 @@ size_t Engine::trace_step(uint32_t token, int position, unsigned long long* reco
     if (!loaded_) throw Error(Q4K_EINVAL, "weights are not loaded");
     if (token >= (uint32_t)c_.vocab) throw Error(Q4K_ERANGE, "Token ID out of range");
     if (position < 0 || position >= c_.capacity) throw Error(Q4K_ERANGE, "KV cache capacity exceeded");
-    const size_t words = 1 + 4 * (size_t)kTraceRecords;
+    if (5 * c_.layers + 1 > kTraceLaunches) throw Error(Q4K_ERANGE, "too many layers to trace");
+    const size_t words = (size_t)kTraceLaunches * kTraceCtas * kTraceSlots;
     if (!trace_buf_) trace_buf_ = static_cast<unsigned long long*>(alloc(words * 8));
     cuda_check(cudaMemsetAsync(trace_buf_, 0, words * 8, stream_), "memset trace");
     // a traced graph of its own; the normal graph stays untraced
     cudaGraphExec_t saved = exec_;
     exec_ = nullptr;
     trace_ = trace_buf_;
-    size_t n = 0;
+    const size_t n = std::min(words, max_records);
     try {
-        ensure_graph();
+        if (step_kernel_)
+            ensure_step_plan();
+        else
+            ensure_graph();
         host_io_[0] = token;
         host_io_[1] = (uint32_t)position;
         host_io_[2] = 0;
         cuda_check(cudaMemcpyAsync(token_, &host_io_[0], 4, cudaMemcpyHostToDevice, stream_), "h2d");
         cuda_check(cudaMemcpyAsync(pos_, &host_io_[1], 4, cudaMemcpyHostToDevice, stream_), "h2d");
         cuda_check(cudaMemcpyAsync(advance_, &host_io_[2], 4, cudaMemcpyHostToDevice, stream_), "h2d");
-        cuda_check(cudaGraphLaunch(exec_, stream_), "graph launch");
-        unsigned long long count = 0;
-        cuda_check(cudaMemcpyAsync(&count, trace_buf_, 8, cudaMemcpyDeviceToHost, stream_), "d2h");
+        if (step_kernel_)
+            enqueue_step_kernel();
+        else
+            cuda_check(cudaGraphLaunch(exec_, stream_), "graph launch");
         cuda_check(cudaStreamSynchronize(stream_), "trace step");
-        n = std::min<size_t>((size_t)count, std::min<size_t>(max_records, kTraceRecords));
         if (records_host && n)
-            cuda_check(cudaMemcpy(records_host, trace_buf_ + 1, n * 4 * 8, cudaMemcpyDeviceToHost), "d2h trace");
+            cuda_check(cudaMemcpy(records_host, trace_buf_, n * 8, cudaMemcpyDeviceToHost), "d2h trace");
     } catch (...) {
         if (exec_) cudaGraphExecDestroy(exec_);
         exec_ = saved;
         trace_ = nullptr;
         throw;
     }
-    cudaGraphExecDestroy(exec_);
+    if (exec_) cudaGraphExecDestroy(exec_);
     exec_ = saved;
     trace_ = nullptr;
     check_device_error();

@@ -9,6 +9,7 @@
 #include <vector>
 
 #include "../../include/q4k_b200.h"
+#include "decode_step.h"
 #include "ops.h"
 
 namespace q4k {
@@ -75,6 +76,9 @@ private:
     void enqueue_layer(int i);
     void check_device_error();
     void ensure_graph();
+    // Persistent decode-step kernel (tp_world == 1): one launch per token.
+    void ensure_step_plan();
+    void enqueue_step_kernel();
 
     q4k_engine_config c_;
     int rank_ = 0, world_ = 1;
@@ -114,6 +118,13 @@ private:
     uint32_t* host_io_ = nullptr;     // pinned: token, position, result
 
     cudaGraphExec_t exec_ = nullptr;
+    bool step_kernel_ = false;       // decode with decode_step.cu instead of the launch sequence
+    bool step_ready_ = false;        // step_phases_ matches the placed tensors
+    int step_ctas_ = 0;
+    int step_splits_ = 0;
+    int step_nphases_ = 0;
+    StepPhase* step_phases_ = nullptr;  // device
+    unsigned* step_sync_ = nullptr;     // device, [nphases + 1]
     unsigned long long* trace_ = nullptr;      // set only while a traced graph is captured
     unsigned long long* trace_buf_ = nullptr;
 };

@@ -39,9 +39,12 @@
 
 #include "q4k_device.cuh"
 #include "q4k_internal.h"
+#include "gemv_device.cuh"
 
 namespace q4k {
 namespace {
+
+using namespace gemv_dev;
 
 constexpr int kTeamWarps = 4;  // warps per consumer team
 constexpr int kAllConsumersBarrier = 8;
@@ -77,239 +80,12 @@ __device__ __forceinline__ void stage_rows(const GemvPlan& p, int i, int& seg, i
     nr = min(p.rows_per_stage, p.seg[seg].rows - r0);
 }
 
-// dp4a with unsigned bytes in a and signed bytes in b.
-__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
-    int d;
-    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
-
-// 16-byte unit, within its 256-code block, where the activation codes of
-// piece s (codes 16s..16s+15 of the block) are stored for the Q4_K and Q6_K
-// lane mappings below. For the pieces that the lanes of one row read at the
-// same time, consecutive blocks land on disjoint halves of the 8 bank
-// groups, so a row's 16-byte loads are conflict free.
-__device__ __forceinline__ int perm_q4(int s, int b) {
-    // s = 4j + q: pair-chunk j, piece q of it
-    const int j = s >> 2, q = s & 3;
-    return 8 * (q >> 1) + 4 * ((q & 1) ^ (b & 1)) + j;
-}
-__device__ __forceinline__ int perm_q6(int s, int b) {
-    // s = 8h + 2g + l: half h, 32-group g of it, 16-run l of the group
-    const int h = s >> 3, g = (s >> 1) & 3, l = s & 1;
-    return 8 * (g >> 1) + 4 * ((g & 1) ^ (b & 1)) + 2 * h + l;
-}
-
-// Q4_K pair-chunk p of a row: block b = p/4, j = p%4 covers the 32 nibble
-// bytes at 16 + 32j of the block, i.e. the whole 32-value groups 2j (low
-// nibbles) and 2j+1 (high nibbles) (matmul.cu:24-54). A lane's j is fixed
-// (LPR is a multiple of 4), so its scale/min bytes come from fixed places.
-// The high nibbles are dotted in place (16x) with an unsigned-byte dp4a.
-template <int MT, int NR>
-__device__ __forceinline__ void q4_pair(const uint8_t* const (&rows)[NR], int p, int j, const uint8_t* xq,
-                                        const float* xs, const float* xsumf, int K, int mcount,
-                                        float (&acc)[NR][MT]) {
-    const int b = p >> 2;
-    const int sh = (j & 1) * 16;
-    uint32_t lo[NR][8], hi[NR][8];
-    float ds0[NR], ds1[NR], dm0[NR], dm1[NR];
-#pragma unroll
-    for (int r = 0; r < NR; ++r) {
-        const uint8_t* blk = rows[r] + b * 144;
-        const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-        const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * j);
-        const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * j);
-        // the 6-bit scales (SC) and mins (MN) of groups 0..3 or 4..7 as bytes
-        const uint32_t SC = j < 2 ? (hdr.y & 0x3f3f3f3fu) : ((hdr.w & 0x0f0f0f0fu) | ((hdr.y >> 2) & 0x30303030u));
-        const uint32_t MN =
-            j < 2 ? (hdr.z & 0x3f3f3f3fu) : (((hdr.w >> 4) & 0x0f0f0f0fu) | ((hdr.z >> 2) & 0x30303030u));
-        const float d = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
-        ds0[r] = d * (float)((SC >> sh) & 0xffu);
-        ds1[r] = d * (float)((SC >> (sh + 8)) & 0xffu);
-        dm0[r] = dmin * (float)((MN >> sh) & 0xffu);
-        dm1[r] = dmin * (float)((MN >> (sh + 8)) & 0xffu);
-        const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            lo[r][k] = w[k] & 0x0f0f0f0fu;
-            hi[r][k] = w[k] & 0xf0f0f0f0u;
-        }
-    }
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-        if (m < mcount) {
-            const uint8_t* xb = xq + m * K + b * 256;
-            uint4 xv[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) xv[q] = *reinterpret_cast<const uint4*>(xb + 16 * perm_q4(4 * j + q, b));
-            const float2 s2 = *reinterpret_cast<const float2*>(xs + m * (K / 32) + b * 8 + 2 * j);
-            const float2 t2 = *reinterpret_cast<const float2*>(xsumf + m * (K / 32) + b * 8 + 2 * j);
-            const uint32_t xl[8] = {xv[0].x, xv[0].y, xv[0].z, xv[0].w, xv[1].x, xv[1].y, xv[1].z, xv[1].w};
-            const uint32_t xh[8] = {xv[2].x, xv[2].y, xv[2].z, xv[2].w, xv[3].x, xv[3].y, xv[3].z, xv[3].w};
-#pragma unroll
-            for (int r = 0; r < NR; ++r) {
-                int dl = 0, dh = 0;
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    dl = __dp4a((int)lo[r][k], (int)xl[k], dl);
-                    dh = dp4a_us(hi[r][k], xh[k], dh);
-                }
-                dh >>= 4;  // exact: every term is a multiple of 16
-                acc[r][m] += s2.x * (ds0[r] * (float)dl - dm0[r] * t2.x);
-                acc[r][m] += s2.y * (ds1[r] * (float)dh - dm1[r] * t2.y);
-            }
-        }
-    }
-}
-
-// Q6_K quarter p of a planar row: block b = p/4, i = p%4 -> half h = i/2,
-// l = i%2 covers positions 16l..16l+15 of every 32-group g = 0..3 of half h,
-// i.e. the 16-value runs 8h + 2g + l. The 16 ql bytes at 64h + 16l (groups
-// 0, 2) and 64h + 32 + 16l (groups 1, 3) carry the low nibbles, the 16 qh
-// bytes at 32h + 16l the top two bits (matmul.cu:56-84, embedding.cu:42-58).
-// A lane's i is fixed. xs16 holds 32 * (code sum) of each run, ordered so
-// that a quarter's four runs are adjacent.
-template <int MT, int NR>
-__device__ __forceinline__ void q6_quarter(const uint8_t* const (&rows)[NR], int nb, int p, int i,
-                                           const uint8_t* xq, const float* xs, const int* xs16, int K, int mcount,
-                                           float (&acc)[NR][MT]) {
-    const int b = p >> 2, h = i >> 1, l = i & 1;
-    uint32_t q[NR][4][4];  // [row][group g][word]
-    float dsc[NR][4];
-#pragma unroll
-    for (int r = 0; r < NR; ++r) {
-        const uint8_t* row = rows[r];
-        const uint4 A = *reinterpret_cast<const uint4*>(row + b * 128 + 64 * h + 16 * l);
-        const uint4 B = *reinterpret_cast<const uint4*>(row + b * 128 + 64 * h + 32 + 16 * l);
-        const uint4 Q = *reinterpret_cast<const uint4*>(row + nb * 128 + b * 64 + 32 * h + 16 * l);
-        const uint2 scw = *reinterpret_cast<const uint2*>(row + nb * 192 + b * 16 + 8 * h);
-        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(row + nb * 208 + b * 2));
-        // run 8h + 2g + l: scale byte l + 2g of the 8 at 8h
-        dsc[r][0] = d * (float)(int8_t)(scw.x >> (8 * l));
-        dsc[r][1] = d * (float)(int8_t)(scw.x >> (8 * l + 16));
-        dsc[r][2] = d * (float)(int8_t)(scw.y >> (8 * l));
-        dsc[r][3] = d * (float)(int8_t)(scw.y >> (8 * l + 16));
-        const uint32_t a[4] = {A.x, A.y, A.z, A.w}, bb[4] = {B.x, B.y, B.z, B.w}, qh[4] = {Q.x, Q.y, Q.z, Q.w};
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-            q[r][0][w] = (a[w] & 0x0f0f0f0fu) | ((qh[w] << 4) & 0x30303030u);
-            q[r][1][w] = (bb[w] & 0x0f0f0f0fu) | ((qh[w] << 2) & 0x30303030u);
-            q[r][2][w] = ((a[w] >> 4) & 0x0f0f0f0fu) | (qh[w] & 0x30303030u);
-            q[r][3][w] = ((bb[w] >> 4) & 0x0f0f0f0fu) | ((qh[w] >> 2) & 0x30303030u);
-        }
-    }
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-        if (m < mcount) {
-            const uint8_t* xb = xq + m * K + b * 256;
-            const float4 s4 = *reinterpret_cast<const float4*>(xs + m * (K / 32) + b * 8 + 4 * h);
-            const int4 c4 = *reinterpret_cast<const int4*>(xs16 + m * (K / 16) + b * 16 + 4 * i);
-            const float sg[4] = {s4.x, s4.y, s4.z, s4.w};
-            const int cg[4] = {c4.x, c4.y, c4.z, c4.w};
-#pragma unroll
-            for (int g = 0; g < 4; ++g) {
-                const uint4 xv = *reinterpret_cast<const uint4*>(xb + 16 * perm_q6(8 * h + 2 * g + l, b));
-#pragma unroll
-                for (int r = 0; r < NR; ++r) {
-                    // codes are in [0, 63], so signed dp4a is exact; the -32
-                    // is applied through the run sums
-                    int dd = __dp4a((int)q[r][g][0], (int)xv.x, 0);
-                    dd = __dp4a((int)q[r][g][1], (int)xv.y, dd);
-                    dd = __dp4a((int)q[r][g][2], (int)xv.z, dd);
-                    dd = __dp4a((int)q[r][g][3], (int)xv.w, dd);
-                    acc[r][m] += sg[g] * (dsc[r][g] * (float)(dd - cg[g]));
-                }
-            }
-        }
-    }
-}
-
-__device__ __forceinline__ int8_t q8_code(float v, float amax) {
-    // matmul.cu:19: roundf((value / maximum) * 127), IEEE division.
-    return amax == 0.0f ? 0 : static_cast<int8_t>(roundf(__fmul_rn(__fdiv_rn(v, amax), 127.0f)));
-}
-
-// Quantise MT activation rows into shared memory: codes (in the Q4_K and/or
-// Q6_K permuted order), one fp32 scale per 32 values, code sums per 16 and
-// per 32 values. Called by all W*32 consumer threads.
 __device__ __forceinline__ void quantise_activation(const GemvPlan& p, int m0, int mcount, uint8_t* smem, int tid,
                                                     int lane, int warp, int nthreads) {
-    const int K = p.K;
-    uint8_t* xq4 = p.off_xq4 >= 0 ? smem + p.off_xq4 : nullptr;
-    uint8_t* xq6 = p.off_xq6 >= 0 ? smem + p.off_xq6 : nullptr;
-    float* xs = reinterpret_cast<float*>(smem + p.off_xs);
-    int* xsum16 = reinterpret_cast<int*>(smem + p.off_xsum16);
-    float* xsum32 = reinterpret_cast<float*>(smem + p.off_xsum32);
-    float* red = reinterpret_cast<float*>(smem + p.off_misc);
-    const int nvec = K / 4;
-    constexpr int kHeld = 12;  // float4s of the row a thread keeps in registers (K <= 12 * 4 * nthreads)
-    for (int m = 0; m < mcount; ++m) {
-        const float4* xr = reinterpret_cast<const float4*>(p.x + (size_t)(m0 + m) * p.ldx);
-        // one pass over the row: every load in flight at once, kept for both uses
-        float4 held[kHeld];
-#pragma unroll
-        for (int k = 0; k < kHeld; ++k) {
-            const int i = tid + k * nthreads;
-            if (i < nvec) held[k] = xr[i];
-        }
-        float inv = 1.0f;
-        if (p.gamma) {
-            float ss = 0.0f;
-#pragma unroll
-            for (int k = 0; k < kHeld; ++k) {
-                const int i = tid + k * nthreads;
-                if (i < nvec) {
-                    const float4 v = held[k];
-                    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-                }
-            }
-            ss = warp_sum(ss);
-            if (lane == 0) red[warp] = ss;
-            named_barrier(kAllConsumersBarrier, nthreads);
-            float total = 0.0f;
-            for (int i = 0; i < nthreads / 32; ++i) total += red[i];
-            inv = rsqrtf(total / (float)K + p.eps);  // rms_norm.cu:17
-            named_barrier(kAllConsumersBarrier, nthreads);
-        }
-        // element e = 4*i of the row; the 8 lanes i..i+7 hold one 32-group
-#pragma unroll
-        for (int k = 0; k < kHeld; ++k) {
-            const int i = tid + k * nthreads;
-            if (i >= nvec) break;
-            const int e = 4 * i;
-            float4 v = held[k];
-            if (p.gamma) {
-                const float4 gm = reinterpret_cast<const float4*>(p.gamma)[i];
-                v.x = (v.x * inv) * gm.x;  // rms_norm.cu:19: input * inverse_rms * scale
-                v.y = (v.y * inv) * gm.y;
-                v.z = (v.z * inv) * gm.z;
-                v.w = (v.w * inv) * gm.w;
-            }
-            float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-            const int8_t c0 = q8_code(v.x, amax), c1 = q8_code(v.y, amax);
-            const int8_t c2 = q8_code(v.z, amax), c3 = q8_code(v.w, amax);
-            const uint32_t word = (uint32_t)(uint8_t)c0 | ((uint32_t)(uint8_t)c1 << 8) |
-                                  ((uint32_t)(uint8_t)c2 << 16) | ((uint32_t)(uint8_t)c3 << 24);
-            int run = (int)c0 + (int)c1 + (int)c2 + (int)c3;
-            run += __shfl_xor_sync(0xffffffffu, run, 1);
-            run += __shfl_xor_sync(0xffffffffu, run, 2);
-            const int group = run + __shfl_xor_sync(0xffffffffu, run, 4);
-            const int b = e >> 8, r16 = (e & 255) >> 4, o = e & 15;
-            if (xq4) *reinterpret_cast<uint32_t*>(xq4 + m * K + b * 256 + 16 * perm_q4(r16, b) + o) = word;
-            if (xq6) *reinterpret_cast<uint32_t*>(xq6 + m * K + b * 256 + 16 * perm_q6(r16, b) + o) = word;
-            // run r16 = 8h + 2g + l is stored at quarter (2h + l), slot g
-            if ((lane & 3) == 0)
-                xsum16[m * (K / 16) + b * 16 + 4 * (2 * (r16 >> 3) + (r16 & 1)) + ((r16 >> 1) & 3)] = 32 * run;
-            if ((lane & 7) == 0) {
-                xsum32[m * (K / 32) + (e >> 5)] = (float)group;
-                xs[m * (K / 32) + (e >> 5)] = amax / 127.0f;  // matmul.cu:18
-            }
-        }
-    }
-    named_barrier(kAllConsumersBarrier, nthreads);
+    quantise_rows<12>(p.x, p.ldx, m0, mcount, p.gamma, p.eps, p.K, p.off_xq4 >= 0 ? smem + p.off_xq4 : nullptr,
+                  p.off_xq6 >= 0 ? smem + p.off_xq6 : nullptr, reinterpret_cast<float*>(smem + p.off_xs),
+                  reinterpret_cast<int*>(smem + p.off_xsum16), reinterpret_cast<float*>(smem + p.off_xsum32),
+                  reinterpret_cast<float*>(smem + p.off_misc), tid, lane, warp, nthreads, kAllConsumersBarrier);
 }
 
 template <int MT, int NR>
@@ -317,7 +93,7 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     constexpr bool PAIR = NR == 2;  // gate and up rows worked together (SwiGLU)
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint64_t t_start = p.trace ? global_timer_ns() : 0;
+    if (threadIdx.x == 0) trace_at(p.trace, p.trace_tag, 0);
     const int W = (int)(blockDim.x >> 5) - 1;  // consumer warps
     const int T = p.teams;                     // teams taking stages (<= W / kTeamWarps)
     const int S = p.S;
@@ -371,8 +147,10 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
 
     // ---------------- consumers ----------------
     pdl_wait();
+    if (tid == 0) trace_at(p.trace, p.trace_tag, 1);
     const int nthreads = W * 32;
     quantise_activation(p, m0, mcount, smem, tid, lane, warp, nthreads);
+    if (tid == 0) trace_at(p.trace, p.trace_tag, 2);
     const uint8_t* xq4 = p.off_xq4 >= 0 ? smem + p.off_xq4 : nullptr;
     const uint8_t* xq6 = p.off_xq6 >= 0 ? smem + p.off_xq6 : nullptr;
     const float* xs = reinterpret_cast<const float*>(smem + p.off_xs);
@@ -396,6 +174,7 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     for (int i = team, st = s_begin + team; team < T && st < s_end; i += T, st += T) {
         const int slot = i % S, use = i / S;
         if (!mbar_wait_bounded(full + slot, use & 1, p.err, ERR_WAIT_TIMEOUT_FULL)) team_abort[team] = 1;
+        if (tid == 0 && i == 0) trace_at(p.trace, p.trace_tag, 3);
         int seg, r0, nr;
         stage_rows(p, st, seg, r0, nr);
         const int rb = p.row_bytes[seg];
@@ -458,6 +237,7 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
         }
     }
 
+    if (tid == 0) trace_at(p.trace, p.trace_tag, 4);
     if (p.epilogue == EPI_ARGMAX) {
         // CTA best, then the last CTA to finish reduces all CTAs in index
         // order (argmax.cu:25-61, :89-97).
@@ -521,7 +301,7 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
             }
         }
     }
-    if (tid == 0) trace_record(p.trace, p.trace_tag, t_start);
+    if (tid == 0) trace_at(p.trace, p.trace_tag, 7);
 }
 
 template <int MT, int NR>

@@ -16,6 +16,7 @@ enum : int {
     ERR_WAIT_TIMEOUT_EMPTY = 2,  // the producer gave up waiting for a buffer to drain
     ERR_BAD_POSITION = 4,        // a position read from device memory was out of range
     ERR_BAD_TOKEN = 8,           // a token id read from device memory was out of range
+    ERR_WAIT_TIMEOUT_DEP = 16,   // a CTA gave up waiting for the other CTAs to finish a phase
 };
 
 // A waiting thread gives up after this many nanoseconds of %globaltimer.
@@ -112,6 +113,21 @@ __device__ __forceinline__ void named_barrier(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// Named barrier that also ORs a predicate over its participants: every
+// thread gets the same answer.
+__device__ __forceinline__ bool named_barrier_or(int id, int threads, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.or.pred p, %2, %3, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(id), "r"(threads)
+        : "memory");
+    return r != 0;
+}
+
 __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xffffu)));
 }
@@ -131,20 +147,20 @@ __device__ __forceinline__ float warp_max(float v) {
 // Optional timeline records: trace[0] counts records, record i occupies
 // trace[1 + 4i .. 4 + 4i] = {tag, block, start ns, end ns} (%globaltimer).
 // Kernels write one record per CTA when given a trace buffer.
-constexpr int kTraceRecords = 1 << 16;
-__device__ __forceinline__ void trace_record(unsigned long long* trace, int tag, uint64_t start) {
+// Optional timeline: trace[(launch * kTraceCtas + cta) * kTraceSlots + slot]
+// receives %globaltimer at checkpoint `slot` of CTA `cta` of kernel launch
+// `launch` (plain stores, no atomics, so tracing barely perturbs timing).
+// Slot 0 is the CTA's start and slot 7 its end.
+constexpr int kTraceLaunches = 256;
+constexpr int kTraceCtas = 1024;
+constexpr int kTraceSlots = 8;
+__device__ __forceinline__ void trace_at(unsigned long long* trace, int launch, int slot) {
     if (!trace) return;
-    const unsigned long long i = atomicAdd(trace, 1ull);
-    if (i >= (unsigned long long)kTraceRecords) return;
-    unsigned long long* r = trace + 1 + 4 * i;
-    r[0] = (unsigned long long)tag;
-    r[1] = (unsigned long long)(blockIdx.x + gridDim.x * blockIdx.y);
-    r[2] = start;
-    r[3] = global_timer_ns();
+    const unsigned cta = blockIdx.x + gridDim.x * blockIdx.y;
+    if (launch < 0 || launch >= kTraceLaunches || cta >= (unsigned)kTraceCtas) return;
+    trace[((size_t)launch * kTraceCtas + cta) * kTraceSlots + slot] = global_timer_ns();
 }
 
-// Argmax candidate order of the reference (src/cuda/argmax.cu:19-23): larger
-// score wins, ties go to the lower index; NaN never wins.
 __device__ __forceinline__ bool candidate_better(float s, uint32_t i, float bs, uint32_t bi) {
     return s > bs || (s == bs && i < bi);
 }

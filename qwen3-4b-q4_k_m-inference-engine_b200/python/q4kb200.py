@@ -285,12 +285,13 @@ class Engine:
     def stream(self) -> int:
         return lib().q4k_engine_stream(self.h)
 
-    def trace(self, token: int, position: int, max_records: int = 1 << 16) -> np.ndarray:
-        """One traced decode step: rows of (tag, block, start_ns, end_ns)."""
-        rec = np.zeros((max_records, 4), np.uint64)
+    def trace(self, token: int, position: int) -> np.ndarray:
+        """One traced decode step: [256 launches][1024 CTAs][8 slots] of
+        %globaltimer ns (0 = not recorded)."""
+        rec = np.zeros((256, 1024, 8), np.uint64)
         n = C.c_size_t(0)
-        check(lib().q4k_engine_trace(self.h, token, position, hptr(rec), max_records, C.byref(n)))
-        return rec[: n.value]
+        check(lib().q4k_engine_trace(self.h, token, position, hptr(rec), rec.size, C.byref(n)))
+        return rec
 
 
 def nccl_unique_id() -> bytes:

@@ -271,3 +271,68 @@ def test_greedy_128_steps_teacher_forced_vs_reference_kernels(cuda, full_model):
           f"{len(mismatches)} mismatches; worst logits rel-L2 {worst:.2e}; free-running first divergence "
           f"{int(div[0]) if div.size else None}")
     assert not mismatches, mismatches
+
+
+def _step_kernel_engine(monkeypatch, cfg):
+    monkeypatch.setenv("Q4K_STEP_KERNEL", "1")
+    eng = q.Engine(cfg)
+    monkeypatch.delenv("Q4K_STEP_KERNEL")
+    return eng
+
+
+def test_tiny_step_kernel_matches_oracle(cuda, monkeypatch):
+    """The persistent decode-step kernel (one launch per token) against the
+    CPU oracle on the tiny model: same logits and greedy token, step after
+    step, with the cache it writes itself."""
+    tensors = tiny_tensors()
+    cap = 16
+    eng = _step_kernel_engine(monkeypatch, engine_config(TINY, capacity=cap))
+    for n, (t, a, b, d) in tensors.items():
+        eng.set_tensor(n, t, a, b, d)
+    model = oracle_model(TINY, tensors)
+    L, KVH = TINY["layers"], TINY["kv_heads"]
+    kc = np.zeros(L * cap * KVH * 128, np.float32)
+    vc = np.zeros_like(kc)
+    tok = 3
+    for pos in range(8):
+        want_next, want_logits, _ = model.forward(kc, vc, cap, [tok], pos, kv_round_f16=True)
+        got_next, got_logits, _ = eng.decode(tok, pos, want_logits=True)
+        assert np.isfinite(got_logits).all(), pos
+        assert rel_l2(got_logits, want_logits) < 1e-2, pos
+        assert greedy_ok(got_next, want_next, want_logits, got_logits), pos
+        tok = want_next
+    eng.close()
+
+
+def test_full_model_step_kernel_matches_launch_sequence(cuda, full_model, monkeypatch):
+    """Both decode paths of the engine on the same weights and cache: the
+    decode-step kernel and the per-product launch sequence agree on every
+    greedy token of a teacher-forced run and on the logits (they differ only
+    in fp32 summation order, which 36 random-init layers amplify, hence the
+    whole-step bar of the other full-model tests), and generate() agrees
+    with decode()."""
+    cfg, c, eng, tensors, handles = full_model
+    step = _step_kernel_engine(monkeypatch, cfg)
+    step.load_synthetic(SEED)
+    start = 4096 - 16
+    eng.fill_kv_synthetic(SEED, start)
+    step.fill_kv_synthetic(SEED, start)
+    tok, worst = 4242, 0.0
+    for s in range(16):
+        a_next, a_logits, _ = eng.decode(tok, start + s, want_logits=True)
+        b_next, b_logits, _ = step.decode(tok, start + s, want_logits=True)
+        worst = max(worst, rel_l2(b_logits, a_logits))
+        assert greedy_ok(b_next, a_next, a_logits, b_logits), s
+        tok = a_next
+    print(f"decode-step kernel vs launch sequence, worst logits rel-L2 over 16 steps: {worst:.2e}")
+    assert worst < 5e-2
+    # generate() on the step kernel: same tokens as its own decode() loop
+    step.fill_kv_synthetic(SEED, start)
+    gen = step.generate(4242, start, 8)
+    step.fill_kv_synthetic(SEED, start)
+    tok, seq = 4242, []
+    for s in range(8):
+        tok, _, _ = step.decode(tok, start + s)
+        seq.append(tok)
+    assert list(gen) == seq
+    step.close()

@@ -61,6 +61,7 @@ constexpr int kPrologueThreads = 256;
 constexpr int kKvStage = 2 * kTileBytes;  // K + V tile
 static_assert(kKvStage <= kSlot, "a K/V tile must fit a ring slot");
 static_assert(kS % kTeams == 0, "every ring slot belongs to one team");
+static_assert(sizeof(StepPhase) % 4 == 0, "phase descriptors are copied as words");
 static_assert(kSlot % 1024 == 0, "slots keep the 1024-byte alignment of the TMA swizzle");
 
 struct Tail {
@@ -74,6 +75,12 @@ struct Tail {
     uint64_t full[kS];
     uint64_t empty[kS];
     uint64_t xbar;  // the activation's bulk copy into the staging buffer
+    float mred[kTeams][2][kTeamWarps][16];  // cross-warp partials of tensor-core stages
+    // the current phase's descriptor for the consumers and, separately, for
+    // the producer (which runs ahead): read from shared memory on every stage
+    // instead of from global memory
+    StepPhase phase_c;
+    StepPhase phase_p;
     int team_abort[kTeams];
     int abort_local;
     int last;
@@ -170,7 +177,12 @@ __device__ __forceinline__ void producer(const StepArgs& a, const CUtensorMap* k
     const int cta = blockIdx.x, ctas = gridDim.x;
     int i = 0;
     for (int ph = 0; ph < a.nphases; ++ph) {
-        const StepPhase& P = a.phases[ph];
+        {
+            const uint32_t* src = reinterpret_cast<const uint32_t*>(a.phases + ph);
+            uint32_t* dst = reinterpret_cast<uint32_t*>(&tl.phase_p);
+            for (int w = 0; w < (int)(sizeof(StepPhase) / 4); ++w) dst[w] = __ldg(src + w);
+        }
+        const StepPhase& P = tl.phase_p;
         int n = 0, s_begin = 0;
         AttnUnit u{};
         if (P.kind == kStepGemv) {
@@ -321,6 +333,10 @@ __device__ __forceinline__ void gemv_phase(const StepArgs& a, const StepPhase& P
         const uint64_t w0 = a.trace ? global_timer_ns() : 0;
         const bool landed = slot_wait(&tl.full[slot], use & 1, a, ERR_WAIT_TIMEOUT_FULL);
         if (a.trace) waited += global_timer_ns() - w0;
+        // trace only: per-stage times of team 0 in layer 5's phases (launch 255)
+        const int dk = (k - k0) / kTeams;
+        if (a.trace && tid == 0 && dk < 4 && ph >= 26 && ph <= 30)
+            a.trace[((size_t)(255 - (30 - ph)) * kTraceCtas + blockIdx.x) * kTraceSlots + 2 * dk] = global_timer_ns();
         if (tid == 0 && k == k0) trace_at(a.trace, ph, 2);
         int seg, r0, nr;
         stage_rows(P, s_begin + k, seg, r0, nr);
@@ -333,7 +349,24 @@ __device__ __forceinline__ void gemv_phase(const StepArgs& a, const StepPhase& P
         float acc[NR][1];
 #pragma unroll
         for (int r = 0; r < NR; ++r) acc[r][0] = 0.0f;
-        if (P.type[seg] == Q4K_TYPE_Q4_K) {
+        const bool mma = P.mma && P.type[seg] == Q4K_TYPE_Q4_K;
+        float* mred = &tl.mred[team][(k / kTeams) & 1][0][0];
+        if (mma) {
+            const int gq = lane >> 2, tq = lane & 3, wt = warp % kTeamWarps;
+            const int rg = gq < nr ? gq : 0;
+            const uint8_t* row_g = buf + rg * rb;
+            const uint8_t* row_h = NR == 2 ? buf + (P.R + rg) * rb : buf + (gq + 8 < nr ? gq + 8 : 0) * rb;
+            float ag = 0.0f, ah = 0.0f;
+            q4_rows_mma<3>(row_g, row_h, wt, kTeamWarps, P.nb, xa.xq4, xa.xs, xa.xsum32, gq, tq, ag, ah);
+            ag += __shfl_xor_sync(0xffffffffu, ag, 1);
+            ag += __shfl_xor_sync(0xffffffffu, ag, 2);
+            ah += __shfl_xor_sync(0xffffffffu, ah, 1);
+            ah += __shfl_xor_sync(0xffffffffu, ah, 2);
+            if (tq == 0) {
+                mred[wt * 16 + gq] = ag;
+                mred[wt * 16 + gq + 8] = ah;
+            }
+        } else if (P.type[seg] == Q4K_TYPE_Q4_K) {
 #pragma unroll 4
             for (int it = 0; it < iters; ++it) {
                 const int f = sub + LPR * it;
@@ -352,12 +385,34 @@ __device__ __forceinline__ void gemv_phase(const StepArgs& a, const StepPhase& P
             mbar_arrive(&tl.empty[slot]);
             if (abort_now) tl.team_abort[team] = 1;
         }
+        if (a.trace && tid == 0 && dk < 4 && ph >= 26 && ph <= 30)
+            a.trace[((size_t)(255 - (30 - ph)) * kTraceCtas + blockIdx.x) * kTraceSlots + 2 * dk + 1] = global_timer_ns();
+        bool owner;
+        int out_row;
+        if (mma) {
+            // warp 0 of the team: lane r sums the four warps' partials of row r
+            owner = warp % kTeamWarps == 0 && lane < (NR == 2 ? 8 : 16);
+            out_row = lane;
+            if (owner) {
+                float v0 = 0.0f, v1 = 0.0f;
 #pragma unroll
-        for (int r = 0; r < NR; ++r)
-            for (int o = LPR >> 1; o > 0; o >>= 1) acc[r][0] += __shfl_xor_sync(0xffffffffu, acc[r][0], o);
+                for (int w = 0; w < kTeamWarps; ++w) {
+                    v0 += mred[w * 16 + lane];
+                    if (NR == 2) v1 += mred[w * 16 + lane + 8];
+                }
+                acc[0][0] = v0;
+                acc[NR - 1][0] = NR == 2 ? v1 : v0;
+            }
+        } else {
+#pragma unroll
+            for (int r = 0; r < NR; ++r)
+                for (int o = LPR >> 1; o > 0; o >>= 1) acc[r][0] += __shfl_xor_sync(0xffffffffu, acc[r][0], o);
+            owner = sub == 0;
+            out_row = slot_row;
+        }
         if (abort_now) break;
-        if (sub == 0 && slot_row < nr) {
-            const int row = r0 + slot_row;
+        if (owner && out_row < nr) {
+            const int row = r0 + out_row;
             float* y = P.y[seg];
             if (epilogue == EPI_STORE) {
                 y[row] = acc[0][0];
@@ -737,10 +792,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     int i = 0;     // ring sequence index of the next stage this CTA consumes
     int xuse = 0;  // activation copies so far (parity of tl.xbar)
     for (int ph = 0; ph < a.nphases; ++ph) {
-        const StepPhase& P = a.phases[ph];
+        // the previous phase's readers of tl.phase_c passed the phase-end barriers
+        if (tid < (int)(sizeof(StepPhase) / 4))
+            reinterpret_cast<uint32_t*>(&tl.phase_c)[tid] = __ldg(reinterpret_cast<const uint32_t*>(a.phases + ph) + tid);
+        const StepPhase& P = tl.phase_c;
         bool failed = false;
         if (tid == 0) {
-            failed = P.dep >= 0 && !dep_wait(a, P.dep, gridDim.x);
+            const int dep = __ldg(&a.phases[ph].dep);  // tl.phase_c is complete only after the barrier below
+            failed = dep >= 0 && !dep_wait(a, dep, gridDim.x);
             trace_at(a.trace, ph, 0);
         }
         if (named_barrier_or(kBarConsumers, kConsumerThreads, failed)) {

@@ -27,6 +27,7 @@ struct StepPhase {
     int nseg = 1, pair = 0;         // segments; pair: SwiGLU gate (w[0]) / up (w[1]) rows together
     int total_stages = 0;
     int q4 = 0, q6 = 0;             // which code layouts the activation needs
+    int mma = 0;                    // Q4_K stages on the tensor cores (16 rows, or 8 gate + 8 up rows)
     int stage_start[kMaxSegments + 1] = {};
     int row_bytes[kMaxSegments] = {};
     int type[kMaxSegments] = {};

@@ -609,6 +609,11 @@ void Engine::ensure_step_plan() {
         if (K * 4 * (gamma ? 2 : 1) > 40 * 1024 || !step_gemv_geometry(K, max_row, pair, p.q4, p.q6, p.lpr, p.R))
             throw Error(Q4K_EINVAL, "decode-step kernel: no stage geometry for this product");
         p.nseg = pair ? 1 : n;
+        // Q4_K stages on the tensor cores where the stage is 16 rows (8 + 8 for
+        // SwiGLU) and the row stride keeps the fragment loads bank-friendly
+        // (opt-in with Q4K_GEMV_MMA=1, as in the per-product kernel)
+        const char* mma_env = std::getenv("Q4K_GEMV_MMA");
+        p.mma = mma_env && mma_env[0] == '1' && K <= 3072 && p.R == (pair ? 8 : 16) ? 1 : 0;
         int stages = 0;
         for (int s = 0; s < p.nseg; ++s) {
             p.stage_start[s] = stages;

@@ -65,7 +65,8 @@ struct GemvPlan {
     int teams;           // consumer teams that take stages (slot i % S always belongs to team i % teams)
     int stage_bytes;
     int row_bytes[kMaxSegments];
-    int off_xq4, off_xq6, off_xs, off_xsum16, off_xsum32, off_bufs, off_bars, off_misc;
+    int off_xq4, off_xq6, off_xs, off_xsum16, off_xsum32, off_bufs, off_bars, off_misc, off_mred;
+    int mma;  // Q4_K stages run on the tensor cores (M == 1, 16 rows or 8 + 8 SwiGLU rows per stage)
     ArgmaxTarget argmax;
     int* err;
     unsigned long long* trace;
@@ -188,7 +189,27 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
         for (int r = 0; r < NR; ++r)
 #pragma unroll
             for (int m = 0; m < MT; ++m) acc[r][m] = 0.0f;
-        if (p.seg[seg].type == Q4K_TYPE_Q4_K) {
+        // tensor-core stages: 16 rows (8 gate + 8 up rows for SwiGLU), the
+        // team's 4 warps take every 4th super-block
+        const bool mma = MT == 1 && p.mma && p.seg[seg].type == Q4K_TYPE_Q4_K;
+        const int par = (i / T) & 1;  // double buffer of the cross-warp partials
+        float* mred = reinterpret_cast<float*>(smem + p.off_mred) + (team * 2 + par) * kTeamWarps * 16;
+        if (mma) {
+            const int gq = lane >> 2, tq = lane & 3, wt = warp % kTeamWarps;
+            const int rg = gq < nr ? gq : 0;
+            const uint8_t* row_g = buf + rg * rb;
+            const uint8_t* row_h = PAIR ? buf + (p.rows_per_stage + rg) * rb : buf + (gq + 8 < nr ? gq + 8 : 0) * rb;
+            float ag = 0.0f, ah = 0.0f;
+            q4_rows_mma<2>(row_g, row_h, wt, kTeamWarps, p.nb, xq4, xs, xsum32, gq, tq, ag, ah);
+            ag += __shfl_xor_sync(0xffffffffu, ag, 1);
+            ag += __shfl_xor_sync(0xffffffffu, ag, 2);
+            ah += __shfl_xor_sync(0xffffffffu, ah, 1);
+            ah += __shfl_xor_sync(0xffffffffu, ah, 2);
+            if (tq == 0) {
+                mred[wt * 16 + gq] = ag;
+                mred[wt * 16 + gq + 8] = ah;
+            }
+        } else if (p.seg[seg].type == Q4K_TYPE_Q4_K) {
 #pragma unroll 2
             for (int k = 0; k < iters; ++k) {
                 const int f = sub + LPR * k;
@@ -205,16 +226,36 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
         named_barrier(1 + team, team_threads);
         if (warp % kTeamWarps == 0 && lane == 0) mbar_arrive(empty + slot);
         const bool abort_now = team_abort[team] != 0;
-        // reduce each row over its LPR lanes (fixed xor order)
+        bool owner;
+        int out_row;
+        if (mma) {
+            // warp 0 of the team: lane r sums the four warps' partials of row r
+            owner = warp % kTeamWarps == 0 && lane < (PAIR ? 8 : 16);
+            out_row = lane;
+            if (owner) {
+                float v0 = 0.0f, v1 = 0.0f;
 #pragma unroll
-        for (int r = 0; r < NR; ++r)
+                for (int w = 0; w < kTeamWarps; ++w) {
+                    v0 += mred[w * 16 + lane];
+                    if (PAIR) v1 += mred[w * 16 + lane + 8];
+                }
+                acc[0][0] = v0;
+                acc[NR - 1][0] = PAIR ? v1 : v0;
+            }
+        } else {
+            // reduce each row over its LPR lanes (fixed xor order)
 #pragma unroll
-            for (int m = 0; m < MT; ++m)
-                for (int o = LPR >> 1; o > 0; o >>= 1) acc[r][m] += __shfl_xor_sync(0xffffffffu, acc[r][m], o);
+            for (int r = 0; r < NR; ++r)
+#pragma unroll
+                for (int m = 0; m < MT; ++m)
+                    for (int o = LPR >> 1; o > 0; o >>= 1) acc[r][m] += __shfl_xor_sync(0xffffffffu, acc[r][m], o);
+            owner = sub == 0;
+            out_row = slot_row;
+        }
         if (abort_now) break;
-        if (sub == 0 && slot_row < nr) {
+        if (owner && out_row < nr) {
             float* y = p.seg[seg].y;
-            const int row = r0 + slot_row;
+            const int row = r0 + out_row;
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
                 if (m >= mcount) break;
@@ -415,12 +456,21 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     off += MT * (rq.K / 32) * 4;
     p.off_misc = off;
     off += 128 * 4;
+    p.off_mred = off;
+    off += 4 * 2 * kTeamWarps * 16 * 4;  // [team][2][warp][16 rows] partials of tensor-core stages
     off = align_up(off, 128);
 
     // Lanes per row: about five 64-value chunks per lane per stage.
     const int chunks = p.nb * 4;
     int lpr = env_int("Q4K_GEMV_LPR", chunks <= 48 ? 8 : chunks <= 80 ? 16 : 32);
     if (lpr != 8 && lpr != 16 && lpr != 32) lpr = 32;
+    // Tensor-core stages need 16 rows (8 gate + 8 up for SwiGLU): for a
+    // batch of one with Q4_K rows of up to 3072 inputs (bank-friendly row
+    // strides), pick the lane split that gives that stage height.
+    const bool any_q4 = need_q4;
+    // Opt-in (Q4K_GEMV_MMA=1): measured no faster than the dp4a path here.
+    const bool mma = rq.M == 1 && any_q4 && rq.K <= 3072 && env_int("Q4K_GEMV_MMA", 0) != 0;
+    if (mma) lpr = pair ? 16 : 8;
     // consumer warps: teams of four (8 by default); K/4 float4s of the
     // activation row must fit the prologue's registers (12 per thread)
     int W = env_int("Q4K_GEMV_WARPS", 16);
@@ -437,6 +487,7 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     S -= S % teams;
     if (off + S * stage_bytes + 2 * S * 8 > 220 * 1024) return cudaErrorInvalidValue;
     p.lpr = lpr;
+    p.mma = mma ? 1 : 0;
     p.rows_per_stage = R;
     p.stage_bytes = stage_bytes;
     p.S = S;

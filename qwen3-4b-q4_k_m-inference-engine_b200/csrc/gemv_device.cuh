@@ -95,6 +95,78 @@ __device__ __forceinline__ void q4_pair(const uint8_t* const (&rows)[NR], int p,
     }
 }
 
+// Tensor-core integer product: D = A (16x32 u8) * B (32x8 s8), zero C.
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%10, %10, %10, %10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// Q4_K dot products of two rows (row_g, row_h: the A rows g and g+8 of lane
+// (g, t) = (lane / 4, lane % 4)) over super-blocks b_begin, b_begin + b_step,
+// ... < nb, on the tensor cores. For block b, MMA (j, h) takes nibble plane
+// h of 32-byte chunk j of the warp's 16 rows as A (u8; the high plane as
+// 16x its value) and the codes of the block's 8 groups as the 8 columns of
+// B, so column 2j + h, the diagonal, is group 2j + h's dot product. Lane
+// (g, t) keeps chunk t's two columns for its rows and applies the group
+// scales exactly as q4_pair does (matmul.cu:24-54).
+template <int UNROLL>
+__device__ __forceinline__ void q4_rows_mma(const uint8_t* row_g, const uint8_t* row_h, int b_begin, int b_step,
+                                            int nb, const uint8_t* xq, const float* xs, const float* xsumf, int g,
+                                            int t, float& acc_g, float& acc_h) {
+    const int sh = (t & 1) * 16;
+    // UNROLL blocks in flight per warp: each block is a chain of shared
+    // loads, MMAs and scale arithmetic, so independent blocks hide latency
+#pragma unroll UNROLL
+    for (int b = b_begin; b < nb; b += b_step) {
+        const uint8_t* pg = row_g + b * 144;
+        const uint8_t* ph = row_h + b * 144;
+        const uint8_t* xb = xq + b * 256;
+        // B: codes of group g at positions 4t.. (piece 2g) and 4t + 16.. (piece 2g + 1)
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(xb + 16 * perm_q4(2 * g, b) + 4 * t);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(xb + 16 * perm_q4(2 * g + 1, b) + 4 * t);
+        int dlg = 0, dlh = 0, dhg = 0, dhh = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t g0 = *reinterpret_cast<const uint32_t*>(pg + 16 + 32 * j + 4 * t);
+            const uint32_t g1 = *reinterpret_cast<const uint32_t*>(pg + 32 + 32 * j + 4 * t);
+            const uint32_t h0 = *reinterpret_cast<const uint32_t*>(ph + 16 + 32 * j + 4 * t);
+            const uint32_t h1 = *reinterpret_cast<const uint32_t*>(ph + 32 + 32 * j + 4 * t);
+            int c[4];
+            mma_u8s8(c, g0 & 0x0f0f0f0fu, h0 & 0x0f0f0f0fu, g1 & 0x0f0f0f0fu, h1 & 0x0f0f0f0fu, b0, b1);
+            if (j == t) {
+                dlg = c[0];
+                dlh = c[2];
+            }
+            mma_u8s8(c, g0 & 0xf0f0f0f0u, h0 & 0xf0f0f0f0u, g1 & 0xf0f0f0f0u, h1 & 0xf0f0f0f0u, b0, b1);
+            if (j == t) {
+                dhg = c[1] >> 4;  // exact: every term is a multiple of 16
+                dhh = c[3] >> 4;
+            }
+        }
+        const float2 s2 = *reinterpret_cast<const float2*>(xs + b * 8 + 2 * t);
+        const float2 t2 = *reinterpret_cast<const float2*>(xsumf + b * 8 + 2 * t);
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const uint4 hdr = *reinterpret_cast<const uint4*>(r == 0 ? pg : ph);
+            const uint32_t SC =
+                t < 2 ? (hdr.y & 0x3f3f3f3fu) : ((hdr.w & 0x0f0f0f0fu) | ((hdr.y >> 2) & 0x30303030u));
+            const uint32_t MN =
+                t < 2 ? (hdr.z & 0x3f3f3f3fu) : (((hdr.w >> 4) & 0x0f0f0f0fu) | ((hdr.z >> 2) & 0x30303030u));
+            const float d = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
+            const float ds0 = d * (float)((SC >> sh) & 0xffu), ds1 = d * (float)((SC >> (sh + 8)) & 0xffu);
+            const float dm0 = dmin * (float)((MN >> sh) & 0xffu), dm1 = dmin * (float)((MN >> (sh + 8)) & 0xffu);
+            const int dl = r == 0 ? dlg : dlh, dh = r == 0 ? dhg : dhh;
+            float& acc = r == 0 ? acc_g : acc_h;
+            acc += s2.x * (ds0 * (float)dl - dm0 * t2.x);
+            acc += s2.y * (ds1 * (float)dh - dm1 * t2.y);
+        }
+    }
+}
+
 // Q6_K quarter p of a planar row: block b = p/4, i = p%4 -> half h = i/2,
 // l = i%2 covers positions 16l..16l+15 of every 32-group g = 0..3 of half h,
 // i.e. the 16-value runs 8h + 2g + l. The 16 ql bytes at 64h + 16l (groups

@@ -243,6 +243,38 @@ def test_gemv_ring_shapes_agree(cuda, monkeypatch, qt):
         assert np.array_equal(got, first), (warps, kb)
 
 
+@pytest.mark.parametrize("epilogue", ["store", "swiglu"])
+def test_gemv_tensor_core_stages(cuda, monkeypatch, epilogue):
+    """Q4K_GEMV_MMA=1: Q4_K stages of K <= 3072 run their integer dot
+    products on the tensor cores (mma m16n8k32, u8 x s8); they must match
+    the oracle like the dp4a path, including partial last stages."""
+    monkeypatch.setenv("Q4K_GEMV_MMA", "1")
+    K, N = 2560, 1000
+    rg = q.synth_tensor_host(8, "mma.gate", q.Q4_K, K, N)
+    ru = q.synth_tensor_host(8, "mma.up", q.Q4_K, K, N)
+    Wg, Wu = upload(cuda, q.Q4_K, K, N, rg), upload(cuda, q.Q4_K, K, N, ru)
+    x = dev(cuda, q.synth_f32_host(8, "mma.x", K))
+    gamma = dev(cuda, q.synth_tensor_host(8, "mma.g", q.F32, K, 1))
+    n = o.rms_norm(x.cpu().numpy(), gamma.cpu().numpy(), K, 1e-6)
+    out = cuda.full((N,), float("nan"), device="cuda")
+    if epilogue == "swiglu":
+        q.check(q.lib().q4k_matmul_ex(x.data_ptr(), gamma.data_ptr(), 1e-6, 2,
+                                      (C.c_void_p * 2)(Wg.data_ptr(), Wu.data_ptr()), (C.c_int * 2)(q.Q4_K, q.Q4_K),
+                                      (C.c_int64 * 2)(N, N), (C.c_void_p * 2)(out.data_ptr(), out.data_ptr()), K, 1,
+                                      q.EPI_SWIGLU, None, None, None))
+        want = o.silu_multiply(o.matmul(n, rg, q.Q4_K, K, N).astype(np.float32),
+                               o.matmul(n, ru, q.Q4_K, K, N).astype(np.float32))
+    else:
+        q.check(q.lib().q4k_matmul_ex(x.data_ptr(), gamma.data_ptr(), 1e-6, 1, (C.c_void_p * 1)(Wg.data_ptr()),
+                                      (C.c_int * 1)(q.Q4_K), (C.c_int64 * 1)(N), (C.c_void_p * 1)(out.data_ptr()),
+                                      K, 1, q.EPI_STORE, None, None, None))
+        want = o.matmul(n, rg, q.Q4_K, K, N).ravel()
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert rel_l2(got, want) < 1e-4
+    assert np.mean(approx_ok(got, want, 3e-5, 1e-3)) > 0.999
+
+
 def test_matmul_ex_argmax_head(cuda):
     K, N = 2560, 151936
     raw = q.synth_tensor_host(0x5EED, "token_embd.weight", q.Q6_K, K, N)

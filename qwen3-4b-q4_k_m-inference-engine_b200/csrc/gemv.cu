@@ -47,6 +47,7 @@ namespace {
 using namespace gemv_dev;
 
 constexpr int kTeamWarps = 4;  // warps per consumer team
+constexpr int kHeldVec4 = 6;   // activation float4s a consumer thread holds while quantising
 constexpr int kAllConsumersBarrier = 8;
 
 struct GemvPlan {
@@ -66,6 +67,7 @@ struct GemvPlan {
     int stage_bytes;
     int row_bytes[kMaxSegments];
     int off_xq4, off_xq6, off_xs, off_xsum16, off_xsum32, off_bufs, off_bars, off_misc, off_mred;
+    int off_gamma;  // RMSNorm gamma staged in shared memory (-1: no norm)
     int mma;  // Q4_K stages run on the tensor cores (M == 1, 16 rows or 8 + 8 SwiGLU rows per stage)
     ArgmaxTarget argmax;
     int* err;
@@ -83,14 +85,18 @@ __device__ __forceinline__ void stage_rows(const GemvPlan& p, int i, int& seg, i
 
 __device__ __forceinline__ void quantise_activation(const GemvPlan& p, int m0, int mcount, uint8_t* smem, int tid,
                                                     int lane, int warp, int nthreads) {
-    quantise_rows<12>(p.x, p.ldx, m0, mcount, p.gamma, p.eps, p.K, p.off_xq4 >= 0 ? smem + p.off_xq4 : nullptr,
+    const float* gamma = p.gamma ? reinterpret_cast<const float*>(smem + p.off_gamma) : nullptr;
+    quantise_rows<kHeldVec4>(p.x, p.ldx, m0, mcount, gamma, p.eps, p.K, p.off_xq4 >= 0 ? smem + p.off_xq4 : nullptr,
                   p.off_xq6 >= 0 ? smem + p.off_xq6 : nullptr, reinterpret_cast<float*>(smem + p.off_xs),
                   reinterpret_cast<int*>(smem + p.off_xsum16), reinterpret_cast<float*>(smem + p.off_xsum32),
                   reinterpret_cast<float*>(smem + p.off_misc), tid, lane, warp, nthreads, kAllConsumersBarrier);
 }
 
-template <int MT, int NR>
+// MMA: the tensor-core stage path is compiled in (a separate instance, so
+// that the default instances keep their registers for the dp4a loop).
+template <int MT, int NR, bool MMA>
 __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant__ GemvPlan p) {
+    static_assert(!MMA || MT == 1, "tensor-core stages take a batch of one");
     constexpr bool PAIR = NR == 2;  // gate and up rows worked together (SwiGLU)
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -147,6 +153,12 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     }
 
     // ---------------- consumers ----------------
+    if (p.gamma) {
+        // a weight: independent of the preceding kernel, so it is staged
+        // before the wait and the quantisation needs one global round trip
+        float4* g4 = reinterpret_cast<float4*>(smem + p.off_gamma);
+        for (int i = tid; i < K / 4; i += W * 32) g4[i] = __ldg(reinterpret_cast<const float4*>(p.gamma) + i);
+    }
     pdl_wait();
     if (tid == 0) trace_at(p.trace, p.trace_tag, 1);
     const int nthreads = W * 32;
@@ -191,7 +203,7 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
             for (int m = 0; m < MT; ++m) acc[r][m] = 0.0f;
         // tensor-core stages: 16 rows (8 gate + 8 up rows for SwiGLU), the
         // team's 4 warps take every 4th super-block
-        const bool mma = MT == 1 && p.mma && p.seg[seg].type == Q4K_TYPE_Q4_K;
+        const bool mma = MMA && p.seg[seg].type == Q4K_TYPE_Q4_K;
         const int par = (i / T) & 1;  // double buffer of the cross-warp partials
         float* mred = reinterpret_cast<float*>(smem + p.off_mred) + (team * 2 + par) * kTeamWarps * 16;
         if (mma) {
@@ -345,7 +357,7 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     if (tid == 0) trace_at(p.trace, p.trace_tag, 7);
 }
 
-template <int MT, int NR>
+template <int MT, int NR, bool MMA = false>
 cudaError_t launch_instance(const GemvPlan& plan, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl) {
     static std::once_flag once;
     static cudaError_t attr_status = cudaSuccess;
@@ -353,10 +365,10 @@ cudaError_t launch_instance(const GemvPlan& plan, dim3 grid, dim3 block, size_t 
     std::call_once(once, [] {
         // static + dynamic shared memory must fit the 227 KB per-block limit
         cudaFuncAttributes fa{};
-        attr_status = cudaFuncGetAttributes(&fa, gemv_kernel<MT, NR>);
+        attr_status = cudaFuncGetAttributes(&fa, gemv_kernel<MT, NR, MMA>);
         if (attr_status != cudaSuccess) return;
         max_dynamic = 227 * 1024 - fa.sharedSizeBytes;
-        attr_status = cudaFuncSetAttribute(gemv_kernel<MT, NR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        attr_status = cudaFuncSetAttribute(gemv_kernel<MT, NR, MMA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)max_dynamic);
     });
     if (attr_status != cudaSuccess) return attr_status;
@@ -371,7 +383,7 @@ cudaError_t launch_instance(const GemvPlan& plan, dim3 grid, dim3 block, size_t 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<MT, NR>, plan);
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<MT, NR, MMA>, plan);
 }
 
 int align_up(int v, int a) { return (v + a - 1) / a * a; }
@@ -456,6 +468,11 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     off += MT * (rq.K / 32) * 4;
     p.off_misc = off;
     off += 128 * 4;
+    p.off_gamma = -1;
+    if (rq.gamma) {
+        p.off_gamma = off;
+        off += rq.K * 4;
+    }
     p.off_mred = off;
     off += 4 * 2 * kTeamWarps * 16 * 4;  // [team][2][warp][16 rows] partials of tensor-core stages
     off = align_up(off, 128);
@@ -471,11 +488,11 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     // Opt-in (Q4K_GEMV_MMA=1): measured no faster than the dp4a path here.
     const bool mma = rq.M == 1 && any_q4 && rq.K <= 3072 && env_int("Q4K_GEMV_MMA", 0) != 0;
     if (mma) lpr = pair ? 16 : 8;
-    // consumer warps: teams of four (8 by default); K/4 float4s of the
-    // activation row must fit the prologue's registers (12 per thread)
+    // consumer warps: teams of four (16 by default); K/4 float4s of the
+    // activation row must fit the prologue's registers (kHeldVec4 per thread)
     int W = env_int("Q4K_GEMV_WARPS", 16);
     if (W != 8 && W != 12 && W != 16) W = 16;
-    if (rq.K / 4 > 12 * W * 32) return cudaErrorInvalidValue;
+    if (rq.K / 4 > kHeldVec4 * W * 32) return cudaErrorInvalidValue;
     const int R = kTeamWarps * 32 / lpr;
     const int rows_in_stage = pair ? 2 * R : R;
     const int stage_bytes = align_up(rows_in_stage * max_row, 128);
@@ -516,11 +533,15 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
 
     const int NR = pair ? 2 : 1;
     switch (MT * 4 + NR) {
-        case 1 * 4 + 1: return launch_instance<1, 1>(p, grid, block, smem, stream, rq.pdl);
+        case 1 * 4 + 1:
+            return mma ? launch_instance<1, 1, true>(p, grid, block, smem, stream, rq.pdl)
+                       : launch_instance<1, 1>(p, grid, block, smem, stream, rq.pdl);
         case 2 * 4 + 1: return launch_instance<2, 1>(p, grid, block, smem, stream, rq.pdl);
         case 4 * 4 + 1: return launch_instance<4, 1>(p, grid, block, smem, stream, rq.pdl);
         case 8 * 4 + 1: return launch_instance<8, 1>(p, grid, block, smem, stream, rq.pdl);
-        case 1 * 4 + 2: return launch_instance<1, 2>(p, grid, block, smem, stream, rq.pdl);
+        case 1 * 4 + 2:
+            return mma ? launch_instance<1, 2, true>(p, grid, block, smem, stream, rq.pdl)
+                       : launch_instance<1, 2>(p, grid, block, smem, stream, rq.pdl);
         case 2 * 4 + 2: return launch_instance<2, 2>(p, grid, block, smem, stream, rq.pdl);
         case 4 * 4 + 2: return launch_instance<4, 2>(p, grid, block, smem, stream, rq.pdl);
         case 8 * 4 + 2: return launch_instance<8, 2>(p, grid, block, smem, stream, rq.pdl);

@@ -234,6 +234,24 @@ __device__ __forceinline__ int8_t q8_code(float v, float amax) {
     return amax == 0.0f ? 0 : static_cast<int8_t>(roundf(__fmul_rn(__fdiv_rn(v, amax), 127.0f)));
 }
 
+// The same code, bit for bit, without a division per value. c127 is
+// 127 / amax from __fdividef (at most 2 ulp, i.e. 4 * 2^-24 relative, off
+// for amax in [2^-126, 2^126]), so q = v * c127 is within 5 * 2^-24
+// (relative) of the true 127 v / amax, and the reference's
+// fl(fl(v / amax) * 127) within 2 * 2^-24: as |q| <= 127 the two differ by
+// less than 7 * 2^-24 * 127 < 6e-5. When q is more than 2e-4 from
+// a rounding boundary k + 0.5, both therefore round to the same integer, and
+// there round-to-nearest-even (__float2int_rn) equals roundf; closer to a
+// boundary the exact form above is evaluated.
+__device__ __forceinline__ int8_t q8_code_fast(float v, float amax, float c127, bool fast_ok) {
+    const float q = v * c127;
+    const float f = fabsf(q - truncf(q));  // distance above the integer towards zero
+    if (fast_ok && fabsf(f - 0.5f) > 2e-4f) return static_cast<int8_t>(__float2int_rn(q));
+    return q8_code(v, amax);
+}
+// Whether the fast path's error bound holds for this group maximum.
+__device__ __forceinline__ bool q8_fast_ok(float amax) { return amax >= 1.2e-38f && amax <= 8.0e37f; }
+
 // Quantise MT activation rows into shared memory: codes (in the Q4_K and/or
 // Q6_K permuted order), one fp32 scale per 32 values, code sums per 16 and
 // per 32 values. Called by all W*32 consumer threads.
@@ -247,8 +265,10 @@ __device__ __forceinline__ void quantise_vec4(float4 v, int e, int K, int m, uin
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-    const int8_t c0 = q8_code(v.x, amax), c1 = q8_code(v.y, amax);
-    const int8_t c2 = q8_code(v.z, amax), c3 = q8_code(v.w, amax);
+    const bool fast_ok = q8_fast_ok(amax);
+    const float c127 = __fdividef(127.0f, amax);
+    const int8_t c0 = q8_code_fast(v.x, amax, c127, fast_ok), c1 = q8_code_fast(v.y, amax, c127, fast_ok);
+    const int8_t c2 = q8_code_fast(v.z, amax, c127, fast_ok), c3 = q8_code_fast(v.w, amax, c127, fast_ok);
     const uint32_t word = (uint32_t)(uint8_t)c0 | ((uint32_t)(uint8_t)c1 << 8) |
                           ((uint32_t)(uint8_t)c2 << 16) | ((uint32_t)(uint8_t)c3 << 24);
     int run = (int)c0 + (int)c1 + (int)c2 + (int)c3;

@@ -117,6 +117,57 @@ def test_matmul_matches_oracle(cuda, qt, K, N, rows):
     assert np.all(got[1:-1] == 0.0) and got[0] == 123.0 and got[-1] == 123.0
 
 
+def _one_hot_q4k(K):
+    """K Q4_K rows of K inputs; row r has d = 1, every 6-bit scale 1, every
+    min 0 and a single code 1 at input r, so y[r] = xs[r / 32] * xq[r]
+    exactly: the product exposes the activation's Q8 codes."""
+    nb = K // 256
+    blk = np.zeros((K, nb, 144), np.uint8)
+    blk[:, :, 0:2] = np.frombuffer(np.float16(1.0).tobytes(), np.uint8)  # d; dmin stays 0
+    blk[:, :, 4:8] = 1      # scales of groups 0-3 (6 bits), top bits 0
+    blk[:, :, 12:16] = 1    # groups 4-7: low nibble scale 1, high nibble min 0
+    r = np.arange(K)
+    b, t = r // 256, r % 256
+    g, i = t // 32, t % 32
+    byte = 16 + 32 * (g // 2) + i
+    blk[r, b, byte] = np.where(g % 2 == 0, 0x01, 0x10)
+    return blk.reshape(-1)
+
+
+def test_activation_codes_bit_exact(cuda):
+    """The Q8 codes and scales of the activation (matmul.cu:8-22) match the
+    oracle bit for bit, including values at and next to the rounding
+    boundaries k + 0.5, where the kernel switches from its multiply-by-
+    reciprocal path to the IEEE-division form, and groups whose maximum is
+    0, subnormal or near the float range."""
+    K = 2560
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal(K).astype(np.float32)
+    groups = x.reshape(-1, 32)
+    deltas = [0.0, 1e-7, -1e-7, 1e-6, -1e-6, 3e-5, -3e-5, 1e-4, -1e-4, 1.9e-4, -1.9e-4, 2.1e-4, -2.1e-4, 5e-4]
+    for gi in range(0, 48):
+        amax = np.float32(rng.uniform(0.01, 40.0))
+        ks = rng.integers(-126, 126, 31)
+        d = np.array([deltas[(gi + j) % len(deltas)] for j in range(31)], np.float64)
+        vals = ((ks + 0.5 + d) * float(amax) / 127.0).astype(np.float32)
+        groups[gi, :31] = np.clip(vals, -amax, amax)
+        groups[gi, 31] = amax if gi % 2 else -amax
+    groups[50] = 0.0
+    groups[51] = np.float32(1e-39) * np.sign(groups[51] + 0.5)                         # subnormal maximum
+    groups[52] = (rng.uniform(-1, 1, 32) * 2e38).astype(np.float32)                     # past the fast-path range
+    groups[53] = (rng.uniform(-1, 1, 32) * 3e37).astype(np.float32)                     # just inside it
+    groups[54] = (rng.uniform(-1, 1, 32) * 1e-37).astype(np.float32)
+    x = groups.reshape(-1)
+    codes, scales = o.quantize_q8(x)
+    want = (codes.astype(np.float32) * scales[np.arange(K) // 32]).astype(np.float32)
+    W = upload(cuda, q.Q4_K, K, K, _one_hot_q4k(K))
+    out = cuda.empty(K, device="cuda")
+    q.check(q.lib().q4k_matmul(dev(cuda, x).data_ptr(), W.data_ptr(), q.Q4_K, K, K, out.data_ptr(), 1, None))
+    got = out.cpu().numpy()
+    bad = np.nonzero(got.view(np.uint32) != want.view(np.uint32))[0]
+    assert bad.size == 0, (bad[:8], got[bad[:8]], want[bad[:8]])
+
+
 def test_matmul_concurrent_streams(cuda):
     qt, K, N, rows = q.Q4_K, 2560, 1024, 3
     raw = q.synth_tensor_host(5, "mm.streams", qt, K, N)

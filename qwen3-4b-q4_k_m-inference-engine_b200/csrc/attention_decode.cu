@@ -62,6 +62,7 @@ struct Args {
     int stages;
     unsigned long long* trace;
     int trace_tag;
+    L2Prefetch prefetch[kMaxPrefetch];  // the next kernel's operands, after this CTA's first tiles
 };
 
 struct SmemTail {
@@ -76,7 +77,7 @@ struct SmemTail {
     int abort[2];  // per tile parity: a fast warp's next tile never clears the current flag
 };
 
-__global__ void __launch_bounds__(kComputeThreads + 32, 2)
+__global__ void __launch_bounds__(kComputeThreads + 32, 1)
     decode_attention_kernel(const __grid_constant__ Args a, const __grid_constant__ CUtensorMap kmap,
                             const __grid_constant__ CUtensorMap vmap) {
     // the 128-byte TMA swizzle is keyed to 1024-byte smem address blocks
@@ -123,7 +124,10 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 2)
                 tma_load_2d(st + kBox, &kmap, 64, y, &sm.full[s]);
                 tma_load_2d(st + kTileBytes, &vmap, 0, y, &sm.full[s]);
                 tma_load_2d(st + kTileBytes + kBox, &vmap, 64, y, &sm.full[s]);
+                if (t == min(S, tiles) - 1)
+                    issue_l2_prefetch(a.prefetch, split + splits * kvh, splits * gridDim.y);
             }
+            if (tiles == 0) issue_l2_prefetch(a.prefetch, split + splits * kvh, splits * gridDim.y);
         }
         return;
     }
@@ -347,25 +351,31 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 2)
         return;
     }
     __threadfence();
-    // (m, l) of every split into shared memory (the stage buffers are free),
-    // then the o partials with many loads in flight per thread: the merge is
-    // on the critical path of the step, so it must not be one L2 round trip
-    // per split.
+    if (tid == 0) trace_at(a.trace, a.trace_tag, 3);  // the merging CTA: last arrival seen
+    // The merge is on the critical path of the step: the o partials of the
+    // first kBatch splits are loaded in the same round trip as every
+    // split's (m, l) (into shared memory; the stage buffers are free).
+    constexpr int kBatch = 24;
+    const float2* po = reinterpret_cast<const float2*>(a.partial_o + ((size_t)kvh * splits * G + hq) * D + d0);
+    float2 v[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+        v[u] = u < splits ? __ldcg(po + (size_t)u * (G * D / 2)) : make_float2(0.0f, 0.0f);
     float* mls = reinterpret_cast<float*>(smem);  // [splits][G][2]
     const float* ml_head = a.partial_ml + (size_t)kvh * splits * G * 2;
     for (int i = tid; i < splits * G * 2; i += kComputeThreads) mls[i] = __ldcg(ml_head + i);
     named_barrier(1, kComputeThreads);
+    if (tid == 0) trace_at(a.trace, a.trace_tag, 5);
     float MM = -CUDART_INF_F;
     for (int sp = 0; sp < splits; ++sp)
         if (mls[(sp * G + hq) * 2 + 1] > 0.0f) MM = fmaxf(MM, mls[(sp * G + hq) * 2]);
     float LL = 0.0f, o0 = 0.0f, o1 = 0.0f;
-    const float2* po = reinterpret_cast<const float2*>(a.partial_o + ((size_t)kvh * splits * G + hq) * D + d0);
-    constexpr int kBatch = 16;
     for (int sp0 = 0; sp0 < splits; sp0 += kBatch) {
-        float2 v[kBatch];
+        if (sp0 > 0) {
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u)
-            v[u] = sp0 + u < splits ? __ldcg(po + (size_t)(sp0 + u) * (G * D / 2)) : make_float2(0.0f, 0.0f);
+            for (int u = 0; u < kBatch; ++u)
+                v[u] = sp0 + u < splits ? __ldcg(po + (size_t)(sp0 + u) * (G * D / 2)) : make_float2(0.0f, 0.0f);
+        }
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
             if (sp0 + u < splits) {
@@ -429,8 +439,9 @@ cudaError_t make_kv_tensor_map(const uint16_t* base, long long rows, KvTensorMap
 }
 
 // One CTA per SM and KV head share by default (Q4K_ATTN_CTAS_PER_SM raises
-// it; the kernel fits two per SM): more splits shorten each CTA's KV stream
-// but lengthen the cross-split merge, and one per SM measured faster.
+// it; the CTAs then run in waves, one per SM at a time, as the kernel keeps
+// all its registers for the tile loop): more splits shorten each CTA's KV
+// stream but lengthen the cross-split merge, and one per SM measured faster.
 int decode_attention_splits(int kv_heads) {
     const char* env = std::getenv("Q4K_ATTN_CTAS_PER_SM");
     const int per_sm = env && *env ? std::atoi(env) : 1;
@@ -467,6 +478,7 @@ cudaError_t decode_attention(const DecodeAttnArgs& in, const KvTensorMap& kmap, 
     a.err = in.err;
     a.trace = in.trace;
     a.trace_tag = in.trace_tag;
+    for (int e = 0; e < kMaxPrefetch; ++e) a.prefetch[e] = in.prefetch[e];
     a.stages = 3;
     const size_t smem = smem_bytes(a.stages);
     static std::once_flag once;

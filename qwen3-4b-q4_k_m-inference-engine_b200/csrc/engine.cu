@@ -231,6 +231,7 @@ Engine::Engine(const q4k_engine_config& cfg, const void* nccl_id) : c_(cfg) {
         // Q4K_STEP_KERNEL=1: decode with the persistent decode-step kernel
         // (or fail saying why it cannot run); otherwise the launch sequence,
         // which measures faster today
+        if (const char* pf = std::getenv("Q4K_L2_PREFETCH")) l2_prefetch_ = pf[0] != '0';
         const char* env = std::getenv("Q4K_STEP_KERNEL");
         const bool wanted = env && env[0] == '1';
         std::string why;
@@ -417,6 +418,16 @@ void Engine::write_kv(int layer, const uint16_t* k_host, const uint16_t* v_host)
 }
 
 // One transformer block (Engine.cpp:71-103) on the device buffers: x is
+L2Prefetch Engine::weight_prefetch(const uint8_t* w, int type, int K, int rows) const {
+    L2Prefetch f;
+    if (!l2_prefetch_ || !w) return f;
+    f.base = w;
+    f.bytes = (unsigned long long)q4k_device_row_bytes(type, K) * (unsigned long long)rows;
+    f.stride = f.bytes;
+    f.count = 1;
+    return f;
+}
+
 // updated in place, layer i's K/V rows at *pos_ are written.
 void Engine::enqueue_layer(int i) {
     const auto& c = c_;
@@ -443,6 +454,17 @@ void Engine::enqueue_layer(int i) {
         r.pdl = true;
         r.trace = trace_;
         r.trace_tag = 5 * i;
+        if (l2_prefetch_) {
+            // the attention's K and V rows 0..*pos_ of every KV head
+            for (int e = 0; e < 2; ++e) {
+                L2Prefetch& f = r.prefetch[e];
+                f.base = (e == 0 ? kcache_ : vcache_) + kv_layer;
+                f.bytes = (unsigned long long)c.head_dim * 2;
+                f.stride = (unsigned long long)c.capacity * c.head_dim * 2;
+                f.count = KVHl_;
+                f.position = pos_;
+            }
+        }
         gemv(r);
     }
     {
@@ -467,6 +489,7 @@ void Engine::enqueue_layer(int i) {
         a.row_base = i * KVHl_ * c.capacity;
         a.trace = trace_;
         a.trace_tag = 5 * i + 1;
+        a.prefetch[0] = weight_prefetch(L.o, L.to, qd_, H);
         cuda_check(decode_attention(a, kmap_, vmap_, stream_, true), "attention launch");
     }
     {
@@ -480,6 +503,8 @@ void Engine::enqueue_layer(int i) {
         r.pdl = true;
         r.trace = trace_;
         r.trace_tag = 5 * i + 2;
+        r.prefetch[0] = weight_prefetch(L.gate, L.tgate, H, ffn_l_);
+        r.prefetch[1] = weight_prefetch(L.up, L.tup, H, ffn_l_);
         gemv(r);
         if (world_ > 1) all_reduce_into_x();
     }
@@ -497,6 +522,7 @@ void Engine::enqueue_layer(int i) {
         r.pdl = true;
         r.trace = trace_;
         r.trace_tag = 5 * i + 3;
+        r.prefetch[0] = weight_prefetch(L.down, L.tdown, ffn_l_, H);
         gemv(r);
     }
     {
@@ -510,6 +536,12 @@ void Engine::enqueue_layer(int i) {
         r.pdl = true;
         r.trace = trace_;
         r.trace_tag = 5 * i + 4;
+        if (i + 1 < c.layers) {
+            const Layer& N = layers_[i + 1];
+            r.prefetch[0] = weight_prefetch(N.q, N.tq, H, qd_);
+            r.prefetch[1] = weight_prefetch(N.k, N.tk, H, kvd_);
+            r.prefetch[2] = weight_prefetch(N.v, N.tv, H, kvd_);
+        }
         gemv(r);
         if (world_ > 1) all_reduce_into_x();
     }
@@ -548,6 +580,10 @@ void Engine::enqueue_step(bool record_hidden) {
         r.argmax.index_base = (uint32_t)vocab0_;
         r.trace = trace_;
         r.trace_tag = 5 * c_.layers;
+        // the next token's first product
+        r.prefetch[0] = weight_prefetch(layers_[0].q, layers_[0].tq, H, qd_);
+        r.prefetch[1] = weight_prefetch(layers_[0].k, layers_[0].tk, H, kvd_);
+        r.prefetch[2] = weight_prefetch(layers_[0].v, layers_[0].tv, H, kvd_);
         if (world_ > 1) {
             r.argmax.token = reinterpret_cast<uint32_t*>(tp_cand_local_) + 1;
             r.argmax.score = tp_cand_local_;

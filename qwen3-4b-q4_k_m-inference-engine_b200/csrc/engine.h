@@ -74,6 +74,8 @@ private:
     void place(const TensorSpec& t, const void* raw_device);
     void enqueue_step(bool record_hidden);
     void enqueue_layer(int i);
+    // L2 prefetch descriptors of layer i's weights (q, k, v; o; gate, up; down).
+    L2Prefetch weight_prefetch(const uint8_t* w, int type, int K, int rows) const;
     void check_device_error();
     void ensure_graph();
     // Persistent decode-step kernel (tp_world == 1): one launch per token.
@@ -118,6 +120,7 @@ private:
     uint32_t* host_io_ = nullptr;     // pinned: token, position, result
 
     cudaGraphExec_t exec_ = nullptr;
+    bool l2_prefetch_ = true;        // each launch prefetches the next one's operands into L2
     bool step_kernel_ = false;       // decode with decode_step.cu instead of the launch sequence
     bool step_ready_ = false;        // step_phases_ matches the placed tensors
     int step_ctas_ = 0;

@@ -73,6 +73,7 @@ struct GemvPlan {
     int* err;
     unsigned long long* trace;
     int trace_tag;
+    L2Prefetch prefetch[kMaxPrefetch];  // the next kernel's operands, after this CTA's first S stages
 };
 
 // Segment, first local row and row count of stage i.
@@ -89,7 +90,8 @@ __device__ __forceinline__ void quantise_activation(const GemvPlan& p, int m0, i
     quantise_rows<kHeldVec4>(p.x, p.ldx, m0, mcount, gamma, p.eps, p.K, p.off_xq4 >= 0 ? smem + p.off_xq4 : nullptr,
                   p.off_xq6 >= 0 ? smem + p.off_xq6 : nullptr, reinterpret_cast<float*>(smem + p.off_xs),
                   reinterpret_cast<int*>(smem + p.off_xsum16), reinterpret_cast<float*>(smem + p.off_xsum32),
-                  reinterpret_cast<float*>(smem + p.off_misc), tid, lane, warp, nthreads, kAllConsumersBarrier);
+                  reinterpret_cast<float*>(smem + p.off_misc), tid, lane, warp, nthreads, kAllConsumersBarrier,
+                  p.trace, p.trace_tag);
 }
 
 // MMA: the tensor-core stage path is compiled in (a separate instance, so
@@ -147,6 +149,9 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
                     mbar_arrive_expect_tx(fb, nr * rb);
                     bulk_g2s_hint(dst, p.seg[seg].w + (size_t)r0 * rb, nr * rb, fb, policy);
                 }
+                // the ring is full (or this CTA's stages are all issued):
+                // let HBM go on with the next kernel's operands
+                if ((i == S - 1 || st == s_end - 1) && blockIdx.y == 0) issue_l2_prefetch(p.prefetch, blockIdx.x, G);
             }
         }
         return;
@@ -426,6 +431,7 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     p.err = rq.err;
     p.trace = rq.trace;
     p.trace_tag = rq.trace_tag;
+    for (int e = 0; e < kMaxPrefetch; ++e) p.prefetch[e] = rq.prefetch[e];
     bool need_q4 = false, need_q6 = false;
     int max_row = 0;
     for (int s = 0; s < rq.nseg; ++s) {

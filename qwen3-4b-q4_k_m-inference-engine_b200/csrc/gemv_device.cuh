@@ -291,7 +291,8 @@ template <int kHeld>
 __device__ __forceinline__ void quantise_rows(const float* x, int ldx, int m0, int mcount, const float* gamma,
                                               float eps, int K, uint8_t* xq4, uint8_t* xq6, float* xs, int* xsum16,
                                               float* xsum32, float* red, int tid, int lane, int warp, int nthreads,
-                                              int barrier_id) {
+                                              int barrier_id, unsigned long long* trace = nullptr,
+                                              int trace_tag = 0) {
     const int nvec = K / 4;
     // kHeld: float4s of the row a thread keeps in registers (K <= kHeld * 4 * nthreads)
     for (int m = 0; m < mcount; ++m) {
@@ -302,6 +303,13 @@ __device__ __forceinline__ void quantise_rows(const float* x, int ldx, int m0, i
         for (int k = 0; k < kHeld; ++k) {
             const int i = tid + k * nthreads;
             if (i < nvec) held[k] = __ldcg(xr + i);  // may have been written by other SMs in this launch
+        }
+        if (trace && tid == 0 && m == 0) {
+            // timeline: when thread 0's first activation load has landed
+            float landed;
+            asm volatile("mov.b32 %0, %1;" : "=f"(landed) : "f"(held[0].x));
+            asm volatile("" ::"f"(landed));
+            trace_at(trace, trace_tag, 5);
         }
         float inv = 1.0f;
         if (gamma) {

@@ -53,6 +53,7 @@ struct DecodeAttnArgs {
     int splits;                // CTAs per KV head
     unsigned long long* trace = nullptr;  // optional timeline records
     int trace_tag = 0;
+    L2Prefetch prefetch[kMaxPrefetch];    // the next kernel's operands (optional)
 };
 constexpr int kDecodeHeadDim = 128;
 // Opaque storage of a TMA tensor map (CUtensorMap) over an fp16 KV cache

@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include "q4k_format.h"
+#include "q4k_internal.h"
 
 namespace q4k {
 
@@ -101,6 +102,55 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
     return p;
+}
+
+// Asks L2 to fetch [p, p + bytes) from HBM; nothing completes or waits on it.
+// p and bytes must be multiples of 16.
+__device__ __forceinline__ void l2_prefetch_bulk(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Issues this CTA's share (CTA `cta` of `ctas`, cut at 256-byte boundaries
+// of the concatenated ranges) of the prefetch list as bulk L2 prefetches of
+// at most 32 KB each. Addresses are kept in bounds of every range.
+static __device__ __noinline__ void issue_l2_prefetch(const L2Prefetch* pf, int cta, int ctas) {
+    unsigned long long len[kMaxPrefetch];
+    unsigned long long total = 0;
+    for (int e = 0; e < kMaxPrefetch; ++e) {
+        unsigned long long l = 0;
+        if (pf[e].base && pf[e].count > 0) {
+            l = pf[e].bytes;
+            if (pf[e].position) {
+                int pos = *reinterpret_cast<const volatile int*>(pf[e].position);
+                if (pos < 0) pos = 0;
+                l = (unsigned long long)(pos + 1) * pf[e].bytes;
+                if (l > pf[e].stride) l = pf[e].stride;
+            }
+            total += l * (unsigned long long)pf[e].count;
+        }
+        len[e] = l;
+    }
+    if (total == 0 || ctas <= 0) return;
+    const unsigned long long lo = (total * (unsigned long long)cta / ctas) & ~255ull;
+    const unsigned long long hi =
+        cta + 1 >= ctas ? total : (total * (unsigned long long)(cta + 1) / ctas) & ~255ull;
+    unsigned long long at = 0;  // start of the current range in the concatenation
+    for (int e = 0; e < kMaxPrefetch && at < hi; ++e) {
+        if (!len[e]) continue;
+        for (int k = 0; k < pf[e].count && at < hi; ++k, at += len[e]) {
+            const unsigned long long a = at > lo ? at : lo;
+            const unsigned long long b = at + len[e] < hi ? at + len[e] : hi;
+            if (a >= b) continue;
+            const uintptr_t range = reinterpret_cast<uintptr_t>(pf[e].base) + (uintptr_t)k * pf[e].stride;
+            uintptr_t p = (range + (a - at) + 15) & ~(uintptr_t)15;
+            const uintptr_t end = (range + (b - at)) & ~(uintptr_t)15;
+            while (p < end) {
+                const uint32_t piece = end - p < 32768 ? (uint32_t)(end - p) : 32768u;
+                l2_prefetch_bulk(reinterpret_cast<const void*>(p), piece);
+                p += piece;
+            }
+        }
+    }
 }
 
 // Programmatic dependent launch: wait for the preceding kernel's results /

@@ -25,6 +25,21 @@ struct GemvSegment {
     int rows = 0;                // N of this segment
 };
 
+// Bytes that a kernel's producer asks L2 to fetch for the kernel after it,
+// once its own copies are issued, so that HBM keeps streaming while the
+// current kernel computes and the next one finds its operands in L2:
+// `count` ranges of `bytes` each, `stride` bytes apart from `base`. With
+// `position` set, a range is (*position + 1) * bytes long, clamped to
+// `stride` (a KV cache up to the new token). Only a hint: nothing waits on it.
+struct L2Prefetch {
+    const void* base = nullptr;
+    unsigned long long bytes = 0;
+    unsigned long long stride = 0;
+    int count = 0;
+    const int* position = nullptr;
+};
+constexpr int kMaxPrefetch = 3;
+
 struct ArgmaxTarget {
     float* cand_score = nullptr;     // [grid] per-CTA best logit
     uint32_t* cand_index = nullptr;  // [grid] per-CTA best row
@@ -51,6 +66,7 @@ struct GemvRequest {
     int trace_tag = 0;
     int ctas = 0;        // 0: one CTA per SM
     bool pdl = false;    // launch with programmatic stream serialisation
+    L2Prefetch prefetch[kMaxPrefetch];  // the next kernel's operands (optional)
 };
 
 // Plans and launches one product. Returns cudaErrorInvalidValue for shapes it

@@ -33,6 +33,7 @@
 #include "ops.h"
 #include "q4k_device.cuh"
 #include "attention_device.cuh"
+#include "gemv_device.cuh"
 
 namespace q4k {
 namespace {
@@ -63,6 +64,7 @@ struct Args {
     unsigned long long* trace;
     int trace_tag;
     L2Prefetch prefetch[kMaxPrefetch];  // the next kernel's operands, after this CTA's first tiles
+    ActImage out_image;                 // optional: the output quantised for the O product
 };
 
 struct SmemTail {
@@ -392,6 +394,14 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
     float* out = a.out + ((size_t)kvh * G + hq) * D;
     out[d0] = o0 / LL;
     out[d0 + 1] = o1 / LL;
+    if (a.out_image.base) {
+        // this KV head's G x 128 outputs are 16 whole 32-value groups of the
+        // O product's activation, each held by a half-warp two values per
+        // lane: quantise them from registers
+        const gemv_dev::ImageParts img = gemv_dev::image_parts(a.out_image.base, a.out_image.K);
+        gemv_dev::quantise_pair(o0 / LL, o1 / LL, ((kvh * G + hq) * D) + d0, a.out_image.K, img.q4, img.q6, img.xs,
+                                img.xsum16, img.xsum32, lane);
+    }
     if (tid == 0) {
         a.counters[kvh] = 0u;
         trace_at(a.trace, a.trace_tag, 6);  // slot 6 marks the merging CTA
@@ -479,6 +489,8 @@ cudaError_t decode_attention(const DecodeAttnArgs& in, const KvTensorMap& kmap, 
     a.trace = in.trace;
     a.trace_tag = in.trace_tag;
     for (int e = 0; e < kMaxPrefetch; ++e) a.prefetch[e] = in.prefetch[e];
+    a.out_image = in.out_image;
+    if (a.out_image.base && (a.out_image.K != in.heads * D || a.out_image.K % 256 != 0)) return cudaErrorInvalidValue;
     a.stages = 3;
     const size_t smem = smem_bytes(a.stages);
     static std::once_flag once;

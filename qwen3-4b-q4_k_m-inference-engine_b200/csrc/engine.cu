@@ -203,6 +203,13 @@ Engine::Engine(const q4k_engine_config& cfg, const void* nccl_id) : c_(cfg) {
     qkv_ = static_cast<float*>(alloc(sizeof(float) * (qd_ + 2 * kvd_)));
     att_ = static_cast<float*>(alloc(sizeof(float) * qd_));
     act_ = static_cast<float*>(alloc(sizeof(float) * ffn_l_));
+    if (const char* ai = std::getenv("Q4K_ACT_IMAGE")) act_images_ = ai[0] != '0';
+    if (act_images_ && ffn_l_ % 256 == 0 && qd_ % 256 == 0) {
+        act_img_ = {static_cast<uint8_t*>(alloc(act_image_bytes(ffn_l_))), ffn_l_};
+        att_img_ = {static_cast<uint8_t*>(alloc(act_image_bytes(qd_))), qd_};
+    } else {
+        act_images_ = false;
+    }
     partial_ = static_cast<float*>(alloc(sizeof(float) * H));
     logits_ = static_cast<float*>(alloc(sizeof(float) * (vocab1_ - vocab0_)));
     hidden_ = static_cast<float*>(alloc(sizeof(float) * H * (c.layers + 1)));
@@ -490,6 +497,7 @@ void Engine::enqueue_layer(int i) {
         a.trace = trace_;
         a.trace_tag = 5 * i + 1;
         a.prefetch[0] = weight_prefetch(L.o, L.to, qd_, H);
+        if (act_images_) a.out_image = att_img_;
         cuda_check(decode_attention(a, kmap_, vmap_, stream_, true), "attention launch");
     }
     {
@@ -505,6 +513,7 @@ void Engine::enqueue_layer(int i) {
         r.trace_tag = 5 * i + 2;
         r.prefetch[0] = weight_prefetch(L.gate, L.tgate, H, ffn_l_);
         r.prefetch[1] = weight_prefetch(L.up, L.tup, H, ffn_l_);
+        if (act_images_) r.in_image = att_img_;
         gemv(r);
         if (world_ > 1) all_reduce_into_x();
     }
@@ -523,6 +532,7 @@ void Engine::enqueue_layer(int i) {
         r.trace = trace_;
         r.trace_tag = 5 * i + 3;
         r.prefetch[0] = weight_prefetch(L.down, L.tdown, ffn_l_, H);
+        if (act_images_) r.out_image = act_img_;
         gemv(r);
     }
     {
@@ -536,6 +546,7 @@ void Engine::enqueue_layer(int i) {
         r.pdl = true;
         r.trace = trace_;
         r.trace_tag = 5 * i + 4;
+        if (act_images_) r.in_image = act_img_;
         if (i + 1 < c.layers) {
             const Layer& N = layers_[i + 1];
             r.prefetch[0] = weight_prefetch(N.q, N.tq, H, qd_);

@@ -121,6 +121,8 @@ private:
 
     cudaGraphExec_t exec_ = nullptr;
     bool l2_prefetch_ = true;        // each launch prefetches the next one's operands into L2
+    bool act_images_ = true;         // SwiGLU and attention hand the next product a quantised activation
+    ActImage act_img_, att_img_;     // quantised act_ (for ffn_down) and att_ (for attn_output)
     bool step_kernel_ = false;       // decode with decode_step.cu instead of the launch sequence
     bool step_ready_ = false;        // step_phases_ matches the placed tensors
     int step_ctas_ = 0;

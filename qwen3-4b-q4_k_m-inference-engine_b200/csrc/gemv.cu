@@ -74,6 +74,10 @@ struct GemvPlan {
     unsigned long long* trace;
     int trace_tag;
     L2Prefetch prefetch[kMaxPrefetch];  // the next kernel's operands, after this CTA's first S stages
+    ActImage in_image;   // copy this quantised activation instead of quantising x (M == 1)
+    ActImage out_image;  // SwiGLU: quantise this CTA's output rows into it (M == 1)
+    int group_stages;    // stages per 32-row group: CTA shares start on group boundaries (out_image)
+    int off_ostage;      // this CTA's output rows (out_image)
 };
 
 // Segment, first local row and row count of stage i.
@@ -92,6 +96,88 @@ __device__ __forceinline__ void quantise_activation(const GemvPlan& p, int m0, i
                   reinterpret_cast<int*>(smem + p.off_xsum16), reinterpret_cast<float*>(smem + p.off_xsum32),
                   reinterpret_cast<float*>(smem + p.off_misc), tid, lane, warp, nthreads, kAllConsumersBarrier,
                   p.trace, p.trace_tag);
+}
+
+// Batch of one whose activation the preceding kernel already quantised:
+// copy the image's parts this product uses into shared memory, all loads
+// of a thread in flight at once (16-byte units; at most 4 per thread).
+__device__ __forceinline__ void copy_image(const GemvPlan& p, uint8_t* smem, int tid, int nthreads) {
+    const int K = p.K;
+    const ImageParts src = image_parts(p.in_image.base, K);
+    const int n4 = p.off_xq4 >= 0 ? K / 16 : 0, n6 = p.off_xq6 >= 0 ? K / 16 : 0;
+    const int ns = K / 128, n16 = K / 64;
+    const int total = n4 + n6 + ns + n16 + ns;
+    auto unit = [&](int u, const uint4*& from, uint4*& to) {
+        if (u < n4) {
+            from = reinterpret_cast<const uint4*>(src.q4) + u;
+            to = reinterpret_cast<uint4*>(smem + p.off_xq4) + u;
+            return;
+        }
+        u -= n4;
+        if (u < n6) {
+            from = reinterpret_cast<const uint4*>(src.q6) + u;
+            to = reinterpret_cast<uint4*>(smem + p.off_xq6) + u;
+            return;
+        }
+        u -= n6;
+        if (u < ns) {
+            from = reinterpret_cast<const uint4*>(src.xs) + u;
+            to = reinterpret_cast<uint4*>(smem + p.off_xs) + u;
+            return;
+        }
+        u -= ns;
+        if (u < n16) {
+            from = reinterpret_cast<const uint4*>(src.xsum16) + u;
+            to = reinterpret_cast<uint4*>(smem + p.off_xsum16) + u;
+            return;
+        }
+        u -= n16;
+        from = reinterpret_cast<const uint4*>(src.xsum32) + u;
+        to = reinterpret_cast<uint4*>(smem + p.off_xsum32) + u;
+    };
+    uint4 v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int u = tid + k * nthreads;
+        if (u < total) {
+            const uint4* from;
+            uint4* to;
+            unit(u, from, to);
+            v[k] = __ldcg(from);  // written by the preceding kernel
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int u = tid + k * nthreads;
+        if (u < total) {
+            const uint4* from;
+            uint4* to;
+            unit(u, from, to);
+            *to = v[k];
+        }
+    }
+    named_barrier(kAllConsumersBarrier, nthreads);
+}
+
+// SwiGLU with an output image: this CTA's rows [lo, hi) of the output are
+// whole 32-value groups (its stages start on a group boundary), and their
+// values were also kept in shared memory (off_ostage) by the epilogue.
+// Each warp quantises 4 groups per pass, 8 lanes each; lanes past the last
+// group only take part in their warp's shuffles. Called by all consumer
+// threads after a barrier that follows the last output row.
+__device__ __forceinline__ void quantise_output_groups(const GemvPlan& p, int lo, int hi, const uint8_t* smem, int lane,
+                                                       int warp, int nthreads) {
+    const ActImage& im = p.out_image;
+    const ImageParts img = image_parts(im.base, im.K);
+    const float* ostage = reinterpret_cast<const float*>(smem + p.off_ostage);
+    const int ng = (hi - lo) / 32;
+    for (int j0 = 0; j0 < ng; j0 += 4 * (nthreads / 32)) {
+        const int j = j0 + warp * 4 + lane / 8;
+        const bool valid = j < ng;
+        const int local = 32 * (valid ? j : 0) + 4 * (lane & 7);
+        const float4 v = *reinterpret_cast<const float4*>(ostage + local);
+        quantise_vec4(v, lo + local, im.K, 0, img.q4, img.q6, img.xs, img.xsum16, img.xsum32, lane, valid);
+    }
 }
 
 // MMA: the tensor-core stage path is compiled in (a separate instance, so
@@ -113,8 +199,11 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     int* team_abort = reinterpret_cast<int*>(smem + p.off_misc) + 64;
 
     const int G = gridDim.x;
-    const int s_begin = (int)((long long)p.total_stages * blockIdx.x / G);
-    const int s_end = (int)((long long)p.total_stages * (blockIdx.x + 1) / G);
+    // shares in units of group_stages stages (1 unless an output image is written)
+    const int u = p.group_stages;
+    const int units = (p.total_stages + u - 1) / u;
+    const int s_begin = u * (int)((long long)units * blockIdx.x / G);
+    const int s_end = min(u * (int)((long long)units * (blockIdx.x + 1) / G), p.total_stages);
     const int m0 = blockIdx.y * MT;
     const int mcount = min(MT, p.M - m0);
 
@@ -167,7 +256,10 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     pdl_wait();
     if (tid == 0) trace_at(p.trace, p.trace_tag, 1);
     const int nthreads = W * 32;
-    quantise_activation(p, m0, mcount, smem, tid, lane, warp, nthreads);
+    if (p.in_image.base)
+        copy_image(p, smem, tid, nthreads);
+    else
+        quantise_activation(p, m0, mcount, smem, tid, lane, warp, nthreads);
     if (tid == 0) trace_at(p.trace, p.trace_tag, 2);
     const uint8_t* xq4 = p.off_xq4 >= 0 ? smem + p.off_xq4 : nullptr;
     const uint8_t* xq6 = p.off_xq6 >= 0 ? smem + p.off_xq6 : nullptr;
@@ -282,8 +374,11 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
                 } else if (p.epilogue == EPI_ADD) {
                     *out += acc[0][m];
                 } else if (p.epilogue == EPI_SWIGLU) {
-                    const float g = acc[0][m], u = acc[NR - 1][m];
-                    *out = (g / (1.0f + expf(-g))) * u;  // silu_multiply.cu:9-10
+                    const float g = acc[0][m], up = acc[NR - 1][m];
+                    const float a = (g / (1.0f + expf(-g))) * up;  // silu_multiply.cu:9-10
+                    *out = a;
+                    if (PAIR && p.out_image.base)
+                        reinterpret_cast<float*>(smem + p.off_ostage)[row - s_begin * p.rows_per_stage] = a;
                 } else {
                     if (out) *out = acc[0][m];
                     if (candidate_better(acc[0][m], (uint32_t)row, best_score, best_index)) {
@@ -296,6 +391,12 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     }
 
     if (tid == 0) trace_at(p.trace, p.trace_tag, 4);
+    if (PAIR && p.out_image.base) {
+        named_barrier(kAllConsumersBarrier, nthreads);  // every output row of this CTA is written
+        quantise_output_groups(p, s_begin * p.rows_per_stage, min(s_end * p.rows_per_stage, p.seg[0].rows), smem,
+                               lane, warp, nthreads);
+        if (tid == 0) trace_at(p.trace, p.trace_tag, 6);
+    }
     if (p.epilogue == EPI_ARGMAX) {
         // CTA best, then the last CTA to finish reduces all CTAs in index
         // order (argmax.cu:25-61, :89-97).
@@ -432,6 +533,11 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     p.trace = rq.trace;
     p.trace_tag = rq.trace_tag;
     for (int e = 0; e < kMaxPrefetch; ++e) p.prefetch[e] = rq.prefetch[e];
+    p.in_image = rq.in_image;
+    p.out_image = rq.out_image;
+    if (p.in_image.base && (rq.M != 1 || rq.gamma || p.in_image.K != rq.K)) return cudaErrorInvalidValue;
+    if (p.out_image.base && (!pair || rq.M != 1 || p.out_image.K != rq.seg[0].rows || p.out_image.K % 256 != 0))
+        return cudaErrorInvalidValue;
     bool need_q4 = false, need_q6 = false;
     int max_row = 0;
     for (int s = 0; s < rq.nseg; ++s) {
@@ -502,6 +608,34 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     const int R = kTeamWarps * 32 / lpr;
     const int rows_in_stage = pair ? 2 * R : R;
     const int stage_bytes = align_up(rows_in_stage * max_row, 128);
+
+    // stages of R output rows, never crossing a segment
+    int stages = 0;
+    const int stage_segs = pair ? 1 : rq.nseg;
+    for (int s = 0; s < stage_segs; ++s) {
+        p.stage_start[s] = stages;
+        stages += (rq.seg[s].rows + R - 1) / R;
+    }
+    for (int s = stage_segs; s <= kMaxSegments; ++s) p.stage_start[s] = stages;
+    p.nseg = stage_segs;
+    p.total_stages = stages;
+
+    int ctas = rq.ctas > 0 ? rq.ctas : env_int("Q4K_GEMV_CTAS_PER_SM", 1) * sm_count();
+    ctas = std::min(ctas, stages);
+    if (rq.epilogue == EPI_ARGMAX) ctas = std::min(ctas, 1024);
+    // SwiGLU with an output image: CTA shares start on 32-row groups, so
+    // that each CTA quantises whole groups of its own rows
+    p.group_stages = 1;
+    p.off_ostage = -1;
+    if (p.out_image.base) {
+        if (32 % R != 0) return cudaErrorInvalidValue;
+        p.group_stages = 32 / R;
+        const int units = (stages + p.group_stages - 1) / p.group_stages;
+        ctas = std::min(ctas, units);
+        const int max_rows = p.group_stages * ((units + ctas - 1) / ctas) * R;
+        p.off_ostage = off;
+        off += align_up(max_rows * 4, 128);
+    }
     const int budget = std::max(env_int("Q4K_GEMV_SMEM_KB", 200) * 1024 - off, stage_bytes);
     int S = std::min(budget / stage_bytes, 8);
     if (S < 2) S = 2;
@@ -520,21 +654,6 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     p.off_bars = off;
     off += 2 * S * 8;
     const size_t smem = (size_t)off;
-
-    // stages of R output rows, never crossing a segment
-    int stages = 0;
-    const int stage_segs = pair ? 1 : rq.nseg;
-    for (int s = 0; s < stage_segs; ++s) {
-        p.stage_start[s] = stages;
-        stages += (rq.seg[s].rows + R - 1) / R;
-    }
-    for (int s = stage_segs; s <= kMaxSegments; ++s) p.stage_start[s] = stages;
-    p.nseg = stage_segs;
-    p.total_stages = stages;
-
-    int ctas = rq.ctas > 0 ? rq.ctas : env_int("Q4K_GEMV_CTAS_PER_SM", 1) * sm_count();
-    ctas = std::min(ctas, stages);
-    if (rq.epilogue == EPI_ARGMAX) ctas = std::min(ctas, 1024);
     const dim3 grid(ctas, (rq.M + MT - 1) / MT), block((W + 1) * 32);
 
     const int NR = pair ? 2 : 1;

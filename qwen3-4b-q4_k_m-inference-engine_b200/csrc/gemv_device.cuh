@@ -260,7 +260,7 @@ __device__ __forceinline__ bool q8_fast_ok(float amax) { return amax >= 1.2e-38f
 // one 32-group (matmul.cu:8-22). Stores the codes (Q4_K and/or Q6_K
 // permuted order), the group scale, and the 16- and 32-value code sums.
 __device__ __forceinline__ void quantise_vec4(float4 v, int e, int K, int m, uint8_t* xq4, uint8_t* xq6, float* xs,
-                                              int* xsum16, float* xsum32, int lane) {
+                                              int* xsum16, float* xsum32, int lane, bool store = true) {
     float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
@@ -275,6 +275,7 @@ __device__ __forceinline__ void quantise_vec4(float4 v, int e, int K, int m, uin
     run += __shfl_xor_sync(0xffffffffu, run, 1);
     run += __shfl_xor_sync(0xffffffffu, run, 2);
     const int group = run + __shfl_xor_sync(0xffffffffu, run, 4);
+    if (!store) return;  // a lane that only took part in its warp's shuffles
     const int b = e >> 8, r16 = (e & 255) >> 4, o = e & 15;
     if (xq4) *reinterpret_cast<uint32_t*>(xq4 + m * K + b * 256 + 16 * perm_q4(r16, b) + o) = word;
     if (xq6) *reinterpret_cast<uint32_t*>(xq6 + m * K + b * 256 + 16 * perm_q6(r16, b) + o) = word;
@@ -285,6 +286,53 @@ __device__ __forceinline__ void quantise_vec4(float4 v, int e, int K, int m, uin
         xsum32[m * (K / 32) + (e >> 5)] = (float)group;
         xs[m * (K / 32) + (e >> 5)] = amax / 127.0f;  // matmul.cu:18
     }
+}
+
+// Q8-quantise elements e and e + 1 (e even) of a row whose 32-value group
+// is held two values per lane by the 16 lanes (lane & 15) = (e & 31) / 2 of
+// a half-warp (all 32 lanes of the warp take part). Bit for bit what
+// quantise_vec4 computes for the same group.
+__device__ __forceinline__ void quantise_pair(float v0, float v1, int e, int K, uint8_t* xq4, uint8_t* xq6, float* xs,
+                                              int* xsum16, float* xsum32, int lane) {
+    float amax = fmaxf(fabsf(v0), fabsf(v1));
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const bool fast_ok = q8_fast_ok(amax);
+    const float c127 = __fdividef(127.0f, amax);
+    const int8_t c0 = q8_code_fast(v0, amax, c127, fast_ok), c1 = q8_code_fast(v1, amax, c127, fast_ok);
+    int run = (int)c0 + (int)c1;
+    run += __shfl_xor_sync(0xffffffffu, run, 1);
+    run += __shfl_xor_sync(0xffffffffu, run, 2);
+    run += __shfl_xor_sync(0xffffffffu, run, 4);
+    const int group = run + __shfl_xor_sync(0xffffffffu, run, 8);
+    const uint16_t word = (uint16_t)((uint32_t)(uint8_t)c0 | ((uint32_t)(uint8_t)c1 << 8));
+    const int b = e >> 8, r16 = (e & 255) >> 4, o = e & 15;
+    if (xq4) *reinterpret_cast<uint16_t*>(xq4 + b * 256 + 16 * perm_q4(r16, b) + o) = word;
+    if (xq6) *reinterpret_cast<uint16_t*>(xq6 + b * 256 + 16 * perm_q6(r16, b) + o) = word;
+    if ((lane & 7) == 0)
+        xsum16[b * 16 + 4 * (2 * (r16 >> 3) + (r16 & 1)) + ((r16 >> 1) & 3)] = 32 * run;
+    if ((lane & 15) == 0) {
+        xsum32[e >> 5] = (float)group;
+        xs[e >> 5] = amax / 127.0f;  // matmul.cu:18
+    }
+}
+
+// The parts of an ActImage (q4k_internal.h) for K inputs.
+struct ImageParts {
+    uint8_t* q4;
+    uint8_t* q6;
+    float* xs;
+    int* xsum16;
+    float* xsum32;
+};
+__device__ __forceinline__ ImageParts image_parts(uint8_t* base, int K) {
+    ImageParts v;
+    v.q4 = base;
+    v.q6 = base + K;
+    v.xs = reinterpret_cast<float*>(base + 2 * K);
+    v.xsum16 = reinterpret_cast<int*>(base + 2 * K + K / 8);
+    v.xsum32 = reinterpret_cast<float*>(base + 2 * K + K / 8 + K / 4);
+    return v;
 }
 
 template <int kHeld>

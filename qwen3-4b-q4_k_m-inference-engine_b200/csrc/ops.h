@@ -54,6 +54,7 @@ struct DecodeAttnArgs {
     unsigned long long* trace = nullptr;  // optional timeline records
     int trace_tag = 0;
     L2Prefetch prefetch[kMaxPrefetch];    // the next kernel's operands (optional)
+    ActImage out_image;                   // optional: the attended output, quantised for the O product
 };
 constexpr int kDecodeHeadDim = 128;
 // Opaque storage of a TMA tensor map (CUtensorMap) over an fp16 KV cache

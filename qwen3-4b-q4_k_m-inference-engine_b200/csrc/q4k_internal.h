@@ -40,6 +40,18 @@ struct L2Prefetch {
 };
 constexpr int kMaxPrefetch = 3;
 
+// A batch-of-one activation already quantised the way the product kernel
+// holds it in shared memory (gemv_device.cuh), written by the kernel that
+// produces the activation, so that the product kernel only copies it. For
+// K inputs, from `base`: codes in the Q4_K order [K], codes in the Q6_K
+// order [K], scales [K/32] f32, 16-value code sums [K/16] i32, 32-value
+// code sums [K/32] f32 (act_image_bytes(K) bytes; K a multiple of 256).
+struct ActImage {
+    uint8_t* base = nullptr;
+    int K = 0;
+};
+inline size_t act_image_bytes(int K) { return (size_t)K * 2 + (size_t)K / 8 + (size_t)K / 4 + (size_t)K / 8; }
+
 struct ArgmaxTarget {
     float* cand_score = nullptr;     // [grid] per-CTA best logit
     uint32_t* cand_index = nullptr;  // [grid] per-CTA best row
@@ -67,6 +79,8 @@ struct GemvRequest {
     int ctas = 0;        // 0: one CTA per SM
     bool pdl = false;    // launch with programmatic stream serialisation
     L2Prefetch prefetch[kMaxPrefetch];  // the next kernel's operands (optional)
+    ActImage in_image;   // M == 1, no gamma: copy this quantised activation instead of quantising x
+    ActImage out_image;  // EPI_SWIGLU, M == 1: also quantise the output rows into this image
 };
 
 // Plans and launches one product. Returns cudaErrorInvalidValue for shapes it

@@ -322,13 +322,16 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
     float M = -CUDART_INF_F;
     for (int w = 0; w < kComputeWarps; ++w) M = fmaxf(M, wm[w * G + hq]);
     float L = 0.0f, acc0 = 0.0f, acc1 = 0.0f;
+    // branch-free (a select keeps each sum unchanged for an empty warp), so
+    // that the exponentials of all warps are in flight at once
+#pragma unroll
     for (int w = 0; w < kComputeWarps; ++w) {
         const float l = wl[w * G + hq];
-        if (!(l > 0.0f)) continue;
+        const bool live = l > 0.0f;
         const float f = expf(wm[w * G + hq] - M);
-        L += l * f;
-        acc0 += wo[(w * G + hq) * D + d0] * f;
-        acc1 += wo[(w * G + hq) * D + d0 + 1] * f;
+        L = live ? L + l * f : L;
+        acc0 = live ? acc0 + wo[(w * G + hq) * D + d0] * f : acc0;
+        acc1 = live ? acc1 + wo[(w * G + hq) * D + d0 + 1] * f : acc1;
     }
     if (aborted) {
         M = -CUDART_INF_F;
@@ -370,7 +373,7 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
     if (tid == 0) trace_at(a.trace, a.trace_tag, 5);
     float MM = -CUDART_INF_F;
     for (int sp = 0; sp < splits; ++sp)
-        if (mls[(sp * G + hq) * 2 + 1] > 0.0f) MM = fmaxf(MM, mls[(sp * G + hq) * 2]);
+        MM = fmaxf(MM, mls[(sp * G + hq) * 2 + 1] > 0.0f ? mls[(sp * G + hq) * 2] : -CUDART_INF_F);
     float LL = 0.0f, o0 = 0.0f, o1 = 0.0f;
     for (int sp0 = 0; sp0 < splits; sp0 += kBatch) {
         if (sp0 > 0) {
@@ -378,17 +381,15 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
             for (int u = 0; u < kBatch; ++u)
                 v[u] = sp0 + u < splits ? __ldcg(po + (size_t)(sp0 + u) * (G * D / 2)) : make_float2(0.0f, 0.0f);
         }
+        // branch-free, as above: all exponentials of the batch in flight
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
-            if (sp0 + u < splits) {
-                const float l = mls[((sp0 + u) * G + hq) * 2 + 1];
-                if (l > 0.0f) {
-                    const float f = expf(mls[((sp0 + u) * G + hq) * 2] - MM);
-                    LL += l * f;
-                    o0 += v[u].x * f;
-                    o1 += v[u].y * f;
-                }
-            }
+            const float l = mls[((sp0 + u) * G + hq) * 2 + 1];
+            const bool live = sp0 + u < splits && l > 0.0f;
+            const float f = expf(mls[((sp0 + u) * G + hq) * 2] - MM);
+            LL = live ? LL + l * f : LL;
+            o0 = live ? o0 + v[u].x * f : o0;
+            o1 = live ? o1 + v[u].y * f : o1;
         }
     }
     float* out = a.out + ((size_t)kvh * G + hq) * D;

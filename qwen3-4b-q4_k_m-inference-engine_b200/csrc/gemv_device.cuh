@@ -249,6 +249,18 @@ __device__ __forceinline__ int8_t q8_code_fast(float v, float amax, float c127, 
     if (fast_ok && fabsf(f - 0.5f) > 2e-4f) return static_cast<int8_t>(__float2int_rn(q));
     return q8_code(v, amax);
 }
+// The fast path of q8_code_fast without its branch, for code computed for
+// many values side by side: `near` is set where the exact form must decide
+// (within the margin of a rounding boundary, or NaN).
+__device__ __forceinline__ int8_t q8_code_rn(float v, float c127, bool& near) {
+    const float q = v * c127;
+    const float r = rintf(q);
+    near = !(fabsf(fabsf(q - r) - 0.5f) > 2e-4f);
+    return static_cast<int8_t>(static_cast<int>(r));
+}
+// Out of line: rarely taken.
+static __device__ __noinline__ int8_t q8_code_exact(float v, float amax) { return q8_code(v, amax); }
+
 // Whether the fast path's error bound holds for this group maximum.
 __device__ __forceinline__ bool q8_fast_ok(float amax) { return amax >= 1.2e-38f && amax <= 8.0e37f; }
 
@@ -297,9 +309,13 @@ __device__ __forceinline__ void quantise_pair(float v0, float v1, int e, int K, 
     float amax = fmaxf(fabsf(v0), fabsf(v1));
 #pragma unroll
     for (int o = 1; o < 16; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const bool fast_ok = q8_fast_ok(amax);
     const float c127 = __fdividef(127.0f, amax);
-    const int8_t c0 = q8_code_fast(v0, amax, c127, fast_ok), c1 = q8_code_fast(v1, amax, c127, fast_ok);
+    bool n0, n1;
+    int8_t c0 = q8_code_rn(v0, c127, n0), c1 = q8_code_rn(v1, c127, n1);
+    if (!q8_fast_ok(amax) || n0 || n1) {  // rare
+        c0 = q8_code_exact(v0, amax);
+        c1 = q8_code_exact(v1, amax);
+    }
     int run = (int)c0 + (int)c1;
     run += __shfl_xor_sync(0xffffffffu, run, 1);
     run += __shfl_xor_sync(0xffffffffu, run, 2);

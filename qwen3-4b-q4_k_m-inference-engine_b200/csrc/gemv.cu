@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     const int sub = lane % LPR;                                        // lane within the row's lanes
     const int slot_row = (warp % kTeamWarps) * (32 / LPR) + lane / LPR;  // row of the stage
     const int chunks = p.nb * 4;  // 64-value pair-chunks (Q4_K) or quarters (Q6_K) per row
-    const int iters = (chunks + LPR - 1) / LPR;
+    const int full_iters = chunks / LPR;  // chunks every lane of a row takes
     const int lane_part = sub & 3;  // the lane's chunk within a block (LPR is a multiple of 4)
     float best_score = -__int_as_float(0x7f800000);
     uint32_t best_index = 0xffffffffu;
@@ -319,17 +319,19 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
                 mred[wt * 16 + gq + 8] = ah;
             }
         } else if (p.seg[seg].type == Q4K_TYPE_Q4_K) {
+            // unconditional chunks, then at most one guarded remainder (no
+            // branch inside the unrolled loop)
 #pragma unroll 2
-            for (int k = 0; k < iters; ++k) {
-                const int f = sub + LPR * k;
-                if (f < chunks) q4_pair<MT, NR>(rows, f, lane_part, xq4, xs, xsum32, K, mcount, acc);
-            }
+            for (int k = 0; k < full_iters; ++k)
+                q4_pair<MT, NR>(rows, sub + LPR * k, lane_part, xq4, xs, xsum32, K, mcount, acc);
+            if (sub + LPR * full_iters < chunks)
+                q4_pair<MT, NR>(rows, sub + LPR * full_iters, lane_part, xq4, xs, xsum32, K, mcount, acc);
         } else {
 #pragma unroll 2
-            for (int k = 0; k < iters; ++k) {
-                const int f = sub + LPR * k;
-                if (f < chunks) q6_quarter<MT, NR>(rows, p.nb, f, lane_part, xq6, xs, xsum16, K, mcount, acc);
-            }
+            for (int k = 0; k < full_iters; ++k)
+                q6_quarter<MT, NR>(rows, p.nb, sub + LPR * k, lane_part, xq6, xs, xsum16, K, mcount, acc);
+            if (sub + LPR * full_iters < chunks)
+                q6_quarter<MT, NR>(rows, p.nb, sub + LPR * full_iters, lane_part, xq6, xs, xsum16, K, mcount, acc);
         }
         // all of this team's reads of the stage are done: release it
         named_barrier(1 + team, team_threads);

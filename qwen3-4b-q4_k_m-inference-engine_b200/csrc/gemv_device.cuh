@@ -70,7 +70,7 @@ __device__ __forceinline__ void q4_pair(const uint8_t* const (&rows)[NR], int p,
     }
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
-        if (m < mcount) {
+        if (MT == 1 || m < mcount) {  // a batch of one: always (mcount is 1)
             const uint8_t* xb = xq + m * K + b * 256;
             uint4 xv[4];
 #pragma unroll
@@ -205,7 +205,7 @@ __device__ __forceinline__ void q6_quarter(const uint8_t* const (&rows)[NR], int
     }
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
-        if (m < mcount) {
+        if (MT == 1 || m < mcount) {  // a batch of one: always (mcount is 1)
             const uint8_t* xb = xq + m * K + b * 256;
             const float4 s4 = *reinterpret_cast<const float4*>(xs + m * (K / 32) + b * 8 + 4 * h);
             const int4 c4 = *reinterpret_cast<const int4*>(xs16 + m * (K / 16) + b * 16 + 4 * i);

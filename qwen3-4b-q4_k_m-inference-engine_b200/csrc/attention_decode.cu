@@ -255,12 +255,11 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
         tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
         tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
         const float m_new = fmaxf(m_run, tmax);
-        float p0v = 0.0f, p1v = 0.0f, rescale = 1.0f;
-        if (m_new != -CUDART_INF_F) {
-            p0v = expf(s0 - m_new);
-            p1v = expf(s1 - m_new);
-            rescale = expf(m_run - m_new);
-        }
+        // branch-free: selects give the values of the empty case (every
+        // score so far masked) without a branch around the exponentials
+        const bool any = m_new != -CUDART_INF_F;
+        const float e0 = expf(s0 - m_new), e1 = expf(s1 - m_new), er = expf(m_run - m_new);
+        const float p0v = any ? e0 : 0.0f, p1v = any ? e1 : 0.0f, rescale = any ? er : 1.0f;
         float psum = p0v + p1v;
         psum += __shfl_xor_sync(0xffffffffu, psum, 1);
         psum += __shfl_xor_sync(0xffffffffu, psum, 2);

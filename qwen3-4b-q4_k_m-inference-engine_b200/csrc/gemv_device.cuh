@@ -234,24 +234,16 @@ __device__ __forceinline__ int8_t q8_code(float v, float amax) {
     return amax == 0.0f ? 0 : static_cast<int8_t>(roundf(__fmul_rn(__fdiv_rn(v, amax), 127.0f)));
 }
 
-// The same code, bit for bit, without a division per value. c127 is
-// 127 / amax from __fdividef (at most 2 ulp, i.e. 4 * 2^-24 relative, off
-// for amax in [2^-126, 2^126]), so q = v * c127 is within 5 * 2^-24
-// (relative) of the true 127 v / amax, and the reference's
-// fl(fl(v / amax) * 127) within 2 * 2^-24: as |q| <= 127 the two differ by
-// less than 7 * 2^-24 * 127 < 6e-5. When q is more than 2e-4 from
-// a rounding boundary k + 0.5, both therefore round to the same integer, and
-// there round-to-nearest-even (__float2int_rn) equals roundf; closer to a
-// boundary the exact form above is evaluated.
-__device__ __forceinline__ int8_t q8_code_fast(float v, float amax, float c127, bool fast_ok) {
-    const float q = v * c127;
-    const float f = fabsf(q - truncf(q));  // distance above the integer towards zero
-    if (fast_ok && fabsf(f - 0.5f) > 2e-4f) return static_cast<int8_t>(__float2int_rn(q));
-    return q8_code(v, amax);
-}
-// The fast path of q8_code_fast without its branch, for code computed for
-// many values side by side: `near` is set where the exact form must decide
-// (within the margin of a rounding boundary, or NaN).
+// The same code, bit for bit, without a division per value and without a
+// branch (so that the codes of many values are computed side by side).
+// c127 is 127 / amax from __fdividef (at most 2 ulp, i.e. 4 * 2^-24
+// relative, off for amax in [2^-126, 2^126]: see q8_fast_ok), so
+// q = v * c127 is within 5 * 2^-24 (relative) of the true 127 v / amax, and
+// the reference's fl(fl(v / amax) * 127) within 2 * 2^-24: as |q| <= 127 the
+// two differ by less than 7 * 2^-24 * 127 < 6e-5. When q is more than 2e-4
+// from a rounding boundary k + 0.5, both round to the same integer, and
+// there round-to-nearest-even (rintf) equals roundf. Closer to a boundary
+// (or for NaN) `near` is set and the caller takes q8_code_exact instead.
 __device__ __forceinline__ int8_t q8_code_rn(float v, float c127, bool& near) {
     const float q = v * c127;
     const float r = rintf(q);
@@ -277,10 +269,16 @@ __device__ __forceinline__ void quantise_vec4(float4 v, int e, int K, int m, uin
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-    const bool fast_ok = q8_fast_ok(amax);
     const float c127 = __fdividef(127.0f, amax);
-    const int8_t c0 = q8_code_fast(v.x, amax, c127, fast_ok), c1 = q8_code_fast(v.y, amax, c127, fast_ok);
-    const int8_t c2 = q8_code_fast(v.z, amax, c127, fast_ok), c3 = q8_code_fast(v.w, amax, c127, fast_ok);
+    bool n0, n1, n2, n3;
+    int8_t c0 = q8_code_rn(v.x, c127, n0), c1 = q8_code_rn(v.y, c127, n1);
+    int8_t c2 = q8_code_rn(v.z, c127, n2), c3 = q8_code_rn(v.w, c127, n3);
+    if (!q8_fast_ok(amax) || n0 || n1 || n2 || n3) {  // rare: the exact form decides all four
+        c0 = q8_code_exact(v.x, amax);
+        c1 = q8_code_exact(v.y, amax);
+        c2 = q8_code_exact(v.z, amax);
+        c3 = q8_code_exact(v.w, amax);
+    }
     const uint32_t word = (uint32_t)(uint8_t)c0 | ((uint32_t)(uint8_t)c1 << 8) |
                           ((uint32_t)(uint8_t)c2 << 16) | ((uint32_t)(uint8_t)c3 << 24);
     int run = (int)c0 + (int)c1 + (int)c2 + (int)c3;

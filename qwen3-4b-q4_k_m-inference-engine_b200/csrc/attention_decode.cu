@@ -235,18 +235,24 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
             __syncwarp();
         }
         // scores for 8 positions x 4 heads
-        float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        // four independent accumulator chains (hi / lo parts of the even /
+        // odd k-steps), summed at the end, instead of one chain of 16 MMAs
+        float ca[4] = {0.0f, 0.0f, 0.0f, 0.0f}, cb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        float cc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, cd[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         const uint32_t kbase = smem_addr(kt);
 #pragma unroll
         for (int s2 = 0; s2 < 8; s2 += 2) {
             uint32_t b0, b1, b2, b3;
             ldsm_x4(kbase + tile_off(r_lane, 2 * s2 + (lane >> 3)), b0, b1, b2, b3);
             const uint4 fa = sm.qf[s2][lane], fb = sm.qf[s2 + 1][lane];
-            mma16816(sc, fa.x, fa.z, b0, b1);  // hi parts
-            mma16816(sc, fa.y, fa.w, b0, b1);  // lo parts
-            mma16816(sc, fb.x, fb.z, b2, b3);
-            mma16816(sc, fb.y, fb.w, b2, b3);
+            mma16816(ca, fa.x, fa.z, b0, b1);  // hi parts
+            mma16816(cb, fa.y, fa.w, b0, b1);  // lo parts
+            mma16816(cc, fb.x, fb.z, b2, b3);
+            mma16816(cd, fb.y, fb.w, b2, b3);
         }
+        float sc[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sc[i] = (ca[i] + cc[i]) + (cb[i] + cd[i]);
         // online softmax over this warp's 8 positions (lane (g, tq): positions 2tq, 2tq+1)
         const int c0 = 8 * warp + 2 * tq;
         const float s0 = c0 < n ? sc[0] * scale : -CUDART_INF_F;

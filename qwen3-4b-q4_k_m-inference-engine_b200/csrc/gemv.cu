@@ -210,7 +210,10 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     if (tid == 0) {
         for (int i = 0; i < S; ++i) {
             mbar_init(full + i, 1);
-            mbar_init(empty + i, 1);
+            // a slot is free once every warp of its team has read it (one
+            // arrival per warp); tensor-core stages release it once, after
+            // their team barrier
+            mbar_init(empty + i, MMA ? 1 : kTeamWarps);
         }
         for (int k = 0; k < 4; ++k) team_abort[k] = 0;
         mbar_fence_init();
@@ -283,7 +286,8 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     // a parity wait can never see a phase two uses old.
     for (int i = team, st = s_begin + team; team < T && st < s_end; i += T, st += T) {
         const int slot = i % S, use = i / S;
-        if (!mbar_wait_bounded(full + slot, use & 1, p.err, ERR_WAIT_TIMEOUT_FULL)) team_abort[team] = 1;
+        const bool landed = __all_sync(0xffffffffu, mbar_wait_bounded(full + slot, use & 1, p.err, ERR_WAIT_TIMEOUT_FULL));
+        if (!landed) team_abort[team] = 1;
         if (tid == 0 && i == 0) trace_at(p.trace, p.trace_tag, 3);
         int seg, r0, nr;
         stage_rows(p, st, seg, r0, nr);
@@ -333,10 +337,17 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
             if (sub + LPR * full_iters < chunks)
                 q6_quarter<MT, NR>(rows, p.nb, sub + LPR * full_iters, lane_part, xq6, xs, xsum16, K, mcount, acc);
         }
-        // all of this team's reads of the stage are done: release it
-        named_barrier(1 + team, team_threads);
-        if (warp % kTeamWarps == 0 && lane == 0) mbar_arrive(empty + slot);
-        const bool abort_now = team_abort[team] != 0;
+        // this warp's reads of the stage are done (its results are computed):
+        // release its share of the slot; no team barrier on the dp4a path,
+        // where a row's lanes are all in one warp
+        if (MMA) {
+            named_barrier(1 + team, team_threads);
+            if (warp % kTeamWarps == 0 && lane == 0) mbar_arrive(empty + slot);
+        } else {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty + slot);
+        }
+        const bool abort_now = MMA ? team_abort[team] != 0 : !landed;
         bool owner;
         int out_row;
         if (mma) {

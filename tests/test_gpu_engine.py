@@ -336,3 +336,28 @@ def test_full_model_step_kernel_matches_launch_sequence(cuda, full_model, monkey
         seq.append(tok)
     assert list(gen) == seq
     step.close()
+
+
+@pytest.mark.parametrize("switch", ["Q4K_ACT_IMAGE", "Q4K_L2_PREFETCH"])
+def test_full_model_engine_options_bit_identical(cuda, full_model, monkeypatch, switch):
+    """The quantised activation images (the SwiGLU and attention launches
+    quantise their outputs for the next product, which only copies them) and
+    the L2 prefetch chain change where work happens, not what is computed:
+    an engine with the option turned off gives the same greedy tokens and the
+    same logits, bit for bit, on a teacher-forced run."""
+    cfg, c, eng, tensors, handles = full_model
+    monkeypatch.setenv(switch, "0")
+    off = q.Engine(cfg)
+    monkeypatch.delenv(switch)
+    off.load_synthetic(SEED)
+    start = 4096 - 8
+    eng.fill_kv_synthetic(SEED, start)
+    off.fill_kv_synthetic(SEED, start)
+    tok = 4242
+    for s in range(6):
+        a_next, a_logits, _ = eng.decode(tok, start + s, want_logits=True)
+        b_next, b_logits, _ = off.decode(tok, start + s, want_logits=True)
+        assert a_next == b_next, (switch, s)
+        assert np.array_equal(a_logits.view(np.uint32), b_logits.view(np.uint32)), (switch, s)
+        tok = a_next
+    off.close()

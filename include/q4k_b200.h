@@ -252,9 +252,14 @@ void* q4k_engine_stream(q4k_engine* engine);
  * q4k_engine_decode) whose kernels store %globaltimer nanoseconds into a
  * [256 launches][1024 CTAs][8 slots] array of words: launch 5*layer + k
  * (k: 0 QKV, 1 attention, 2 O, 3 gate/up, 4 down), 5*layers the output
- * head; slot 0 a CTA's start, 7 its end, 1..6 kernel checkpoints (6 marks the
- * attention CTA that merged a head); 0 where nothing was recorded. Up to
- * max_records words go to records_host; *count receives how many. */
+ * head; slot 0 a CTA's start, 7 its end, 1..6 kernel checkpoints; 0 where
+ * nothing was recorded. Products: 1 dependency wait returned, 5 first
+ * activation load landed, 2 activation quantised (or its image copied),
+ * 3 first stage landed, 4 stages done, 6 output image written (SwiGLU).
+ * Attention: 1 query ready, 2 / 3 first / last tile landed, 4 partials
+ * written; the CTA that merged a head also records 3 (last split seen),
+ * 5 (merge inputs loaded) and 6. Up to max_records words go to
+ * records_host; *count receives how many. */
 int q4k_engine_trace(q4k_engine* engine, uint32_t token, int position, unsigned long long* records_host,
                      size_t max_records, size_t* count);
 

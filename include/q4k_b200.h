@@ -248,6 +248,43 @@ int q4k_engine_layer(q4k_engine* engine, int layer, const float* x_host, int pos
 /* Stream the engine launches on (cudaStream_t), e.g. to time with events. */
 void* q4k_engine_stream(q4k_engine* engine);
 
+/* ------------------------------------------------------ GGUF model files */
+
+/* A GGUF model file (format versions 2 and 3), mapped read-only: replaces
+ * the reference's loader (src/GGUF.cpp:81-145) and its metadata reads
+ * (src/Engine.cpp:49-55). Host-only: none of these touch a GPU except
+ * q4k_engine_load_gguf. Opening fails with Q4K_EINVAL on a file that is not
+ * well-formed GGUF (bad magic, truncation, tensors off their alignment or
+ * past the end). */
+typedef struct q4k_gguf q4k_gguf;
+int q4k_gguf_open(const char* path, q4k_gguf** out);
+int q4k_gguf_close(q4k_gguf* file);
+int q4k_gguf_tensor_count(const q4k_gguf* file, int64_t* count);
+/* Tensor i: name, ggml type, ne0 and ne1 (the product of the other
+ * extents), and a pointer to its bytes inside the mapping (valid until
+ * q4k_gguf_close). Q4K_ERANGE past the end. */
+int q4k_gguf_tensor_info(const q4k_gguf* file, int64_t i, char* name, size_t name_len, int* type, int64_t* ne0,
+                         int64_t* ne1, const void** data);
+/* Metadata by key; Q4K_ERANGE when the key is absent or of another kind
+ * (any integer type reads as int, any number as float). */
+int q4k_gguf_meta_int(const q4k_gguf* file, const char* key, int64_t* value);
+int q4k_gguf_meta_float(const q4k_gguf* file, const char* key, double* value);
+int q4k_gguf_meta_string(const q4k_gguf* file, const char* key, char* value, size_t len);
+/* Engine configuration from the metadata the reference reads
+ * (Engine.cpp:49-55) under arch = general.architecture: {arch}.block_count,
+ * .embedding_length, .attention.head_count, .attention.head_count_kv,
+ * .attention.key_length (else hidden / heads), .feed_forward_length,
+ * .attention.layer_norm_rms_epsilon, .rope.freq_base; vocab = rows of
+ * token_embd.weight; the given KV capacity; one GPU (tp fields as for a
+ * single device, device 0). */
+int q4k_gguf_engine_config(const q4k_gguf* file, int capacity, q4k_engine_config* cfg);
+/* Loads every tensor the engine needs from the file (this rank's shard when
+ * tp_world > 1), checking name, shape and type: F32 norms, Q4_K or Q6_K
+ * matrices (ffn_gate and ffn_up of a layer of one type). output.weight, if
+ * present, is not used: the output head is token_embd.weight, as in the
+ * reference. */
+int q4k_engine_load_gguf(q4k_engine* engine, const q4k_gguf* file);
+
 /* Diagnostics, no counterpart in the reference: one decode step (like
  * q4k_engine_decode) whose kernels store %globaltimer nanoseconds into a
  * [256 launches][1024 CTAs][8 slots] array of words: launch 5*layer + k

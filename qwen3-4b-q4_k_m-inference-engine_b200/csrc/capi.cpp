@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "engine.h"
+#include "gguf.h"
 #include "nccl_api.h"
 #include "ops.h"
 #include "q4k_format.h"
@@ -439,6 +440,148 @@ Q4K_API int q4k_model_tensor(const q4k_engine_config* cfg, int i, char* name, si
         if (type) *type = t.type;
         if (ne0) *ne0 = t.ne0;
         if (ne1) *ne1 = t.ne1;
+    });
+}
+
+// ------------------------------------------------------ GGUF model files
+
+struct q4k_gguf {
+    q4k::GgufFile file;
+    explicit q4k_gguf(const char* path) : file(path) {}
+};
+
+Q4K_API int q4k_gguf_open(const char* path, q4k_gguf** out) {
+    return guarded([&] {
+        if (!path || !out) invalid("path and output required");
+        *out = nullptr;
+        *out = new q4k_gguf(path);
+    });
+}
+
+Q4K_API int q4k_gguf_close(q4k_gguf* f) {
+    return guarded([&] { delete f; });
+}
+
+Q4K_API int q4k_gguf_tensor_count(const q4k_gguf* f, int64_t* count) {
+    return guarded([&] {
+        if (!f || !count) invalid("file and output required");
+        *count = (int64_t)f->file.tensors().size();
+    });
+}
+
+Q4K_API int q4k_gguf_tensor_info(const q4k_gguf* f, int64_t i, char* name, size_t name_len, int* type, int64_t* ne0,
+                                 int64_t* ne1, const void** data) {
+    return guarded([&] {
+        if (!f) invalid("file required");
+        const auto& ts = f->file.tensors();
+        if (i < 0 || (size_t)i >= ts.size()) throw q4k::Error(Q4K_ERANGE, "tensor index out of range");
+        const q4k::GgufTensor& t = ts[(size_t)i];
+        if (name && name_len) {
+            std::strncpy(name, t.name.c_str(), name_len - 1);
+            name[name_len - 1] = 0;
+        }
+        int64_t rows = 1;
+        for (size_t d = 1; d < t.ne.size(); ++d) rows *= t.ne[d];
+        if (type) *type = (int)t.type;
+        if (ne0) *ne0 = t.ne[0];
+        if (ne1) *ne1 = rows;
+        if (data) *data = f->file.data(t);
+    });
+}
+
+namespace {
+const q4k::GgufValue& gguf_meta(const q4k_gguf* f, const char* key) {
+    if (!f || !key) invalid("file and key required");
+    const q4k::GgufValue* v = f->file.find(key);
+    if (!v) throw q4k::Error(Q4K_ERANGE, std::string("no metadata key ") + key);
+    return *v;
+}
+}  // namespace
+
+Q4K_API int q4k_gguf_meta_int(const q4k_gguf* f, const char* key, int64_t* value) {
+    return guarded([&] {
+        if (!value) invalid("output required");
+        if (!gguf_meta(f, key).as_int(*value)) throw q4k::Error(Q4K_ERANGE, std::string(key) + " is not an integer");
+    });
+}
+
+Q4K_API int q4k_gguf_meta_float(const q4k_gguf* f, const char* key, double* value) {
+    return guarded([&] {
+        if (!value) invalid("output required");
+        if (!gguf_meta(f, key).as_float(*value)) throw q4k::Error(Q4K_ERANGE, std::string(key) + " is not a number");
+    });
+}
+
+Q4K_API int q4k_gguf_meta_string(const q4k_gguf* f, const char* key, char* value, size_t len) {
+    return guarded([&] {
+        if (!value || !len) invalid("output required");
+        const q4k::GgufValue& v = gguf_meta(f, key);
+        if (v.kind != q4k::GgufValue::kString) throw q4k::Error(Q4K_ERANGE, std::string(key) + " is not a string");
+        std::strncpy(value, v.s.c_str(), len - 1);
+        value[len - 1] = 0;
+    });
+}
+
+Q4K_API int q4k_gguf_engine_config(const q4k_gguf* f, int capacity, q4k_engine_config* c) {
+    return guarded([&] {
+        if (!f || !c) invalid("file and config required");
+        if (capacity <= 0) invalid("capacity must be positive");
+        const q4k::GgufValue* arch_v = f->file.find("general.architecture");
+        const std::string arch = arch_v && arch_v->kind == q4k::GgufValue::kString ? arch_v->s : "qwen3";
+        auto need_int = [&](const std::string& key) {
+            const q4k::GgufValue* v = f->file.find(key);
+            int64_t n = 0;
+            if (!v || !v->as_int(n) || n <= 0 || n > (1 << 24))
+                throw q4k::Error(Q4K_EINVAL, "GGUF: missing or invalid " + key);
+            return (int)n;
+        };
+        auto opt_float = [&](const std::string& key, double fallback) {
+            const q4k::GgufValue* v = f->file.find(key);
+            double x = fallback;
+            if (v && !v->as_float(x)) throw q4k::Error(Q4K_EINVAL, "GGUF: invalid " + key);
+            return x;
+        };
+        q4k_engine_config cfg{};
+        cfg.layers = need_int(arch + ".block_count");
+        cfg.hidden = need_int(arch + ".embedding_length");
+        cfg.heads = need_int(arch + ".attention.head_count");
+        cfg.kv_heads = need_int(arch + ".attention.head_count_kv");
+        cfg.head_dim = f->file.find(arch + ".attention.key_length") ? need_int(arch + ".attention.key_length")
+                                                                   : cfg.hidden / cfg.heads;
+        cfg.ffn = need_int(arch + ".feed_forward_length");
+        cfg.eps = (float)opt_float(arch + ".attention.layer_norm_rms_epsilon", 1e-6);
+        cfg.rope_base = (float)opt_float(arch + ".rope.freq_base", 1e6);
+        const q4k::GgufTensor* embd = f->file.tensor("token_embd.weight");
+        if (!embd || embd->ne.size() < 2) throw q4k::Error(Q4K_EINVAL, "GGUF: no token_embd.weight matrix");
+        cfg.vocab = (int)embd->ne[1];
+        cfg.capacity = capacity;
+        cfg.tp_rank = 0;
+        cfg.tp_world = 1;
+        cfg.device = 0;
+        *c = cfg;
+    });
+}
+
+Q4K_API int q4k_engine_load_gguf(q4k_engine* e, const q4k_gguf* f) {
+    return guarded_cuda([&] {
+        if (!e || !f) invalid("engine and file required");
+        const auto specs = q4k::model_tensors(e->impl.config());
+        // a layer's gate and up rows are worked together, so they must share a type
+        for (int L = 0; L < e->impl.config().layers; ++L) {
+            const std::string p = "blk." + std::to_string(L) + ".";
+            const q4k::GgufTensor* g = f->file.tensor(p + "ffn_gate.weight");
+            const q4k::GgufTensor* u = f->file.tensor(p + "ffn_up.weight");
+            if (g && u && g->type != u->type)
+                throw q4k::Error(Q4K_EINVAL, "GGUF: " + p + "ffn_gate and ffn_up must share a type");
+        }
+        for (const auto& t : specs) {
+            const q4k::GgufTensor* g = f->file.tensor(t.name);
+            if (!g) throw q4k::Error(Q4K_EINVAL, "GGUF: missing tensor " + t.name);
+            int64_t rows = 1;
+            for (size_t d = 1; d < g->ne.size(); ++d) rows *= g->ne[d];
+            if (g->bytes == 0) throw q4k::Error(Q4K_EINVAL, "GGUF: tensor " + t.name + " has an unsupported type");
+            e->impl.set_tensor(t.name, (int)g->type, g->ne[0], rows, f->file.data(*g));
+        }
     });
 }
 

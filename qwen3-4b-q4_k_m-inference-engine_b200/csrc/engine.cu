@@ -356,7 +356,10 @@ void Engine::set_tensor(const std::string& name, int type, int64_t ne0, int64_t 
     if (idx == specs.size()) throw Error(Q4K_EINVAL, "unknown tensor " + name);
     const auto& t = specs[idx];
     if (t.ne0 != ne0 || t.ne1 != ne1) throw Error(Q4K_EINVAL, "tensor " + name + " has the wrong shape");
-    if (type != t.type && !(t.slot == 10 && t.layer >= 0 && (type == Q4K_TYPE_Q4_K || type == Q4K_TYPE_Q6_K)))
+    // norms are F32; every matrix may be Q4_K or Q6_K (a real Q4_K_M file
+    // mixes them per layer)
+    const bool matrix = t.type != Q4K_TYPE_F32;
+    if (matrix ? (type != Q4K_TYPE_Q4_K && type != Q4K_TYPE_Q6_K) : type != Q4K_TYPE_F32)
         throw Error(Q4K_EINVAL, "tensor " + name + " has an unsupported type");
     TensorSpec ts = t;
     ts.type = type;

@@ -59,6 +59,7 @@ public:
     // One step with every kernel CTA's %globaltimer start/end recorded.
     size_t trace_step(uint32_t token, int position, unsigned long long* records_host, size_t max_records);
     cudaStream_t stream() const { return stream_; }
+    const q4k_engine_config& config() const { return c_; }
 
 private:
     struct Layer {

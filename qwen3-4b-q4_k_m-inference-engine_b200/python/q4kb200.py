@@ -30,7 +30,9 @@ EXPORTS = (
     "q4k_engine_create", "q4k_engine_destroy", "q4k_engine_load_synthetic", "q4k_engine_set_tensor",
     "q4k_engine_fill_kv_synthetic", "q4k_engine_read_kv", "q4k_engine_decode", "q4k_engine_generate",
     "q4k_engine_stream", "q4k_tp_shard", "q4k_engine_layer", "q4k_engine_write_kv",
-    "q4k_engine_trace", "q4k_attention_decode_f16_static",
+    "q4k_engine_trace", "q4k_attention_decode_f16_static", "q4k_gguf_open", "q4k_gguf_close",
+    "q4k_gguf_tensor_count", "q4k_gguf_tensor_info", "q4k_gguf_meta_int", "q4k_gguf_meta_float",
+    "q4k_gguf_meta_string", "q4k_gguf_engine_config", "q4k_engine_load_gguf",
 )
 
 
@@ -109,6 +111,16 @@ def lib():
             "q4k_engine_trace": ([P, C.c_uint32, I, P, C.c_size_t, C.POINTER(C.c_size_t)], I),
             "q4k_tp_shard": ([C.POINTER(EngineConfig), I, I, I, C.POINTER(I64), C.POINTER(I64), C.POINTER(I64),
                               C.POINTER(I64)], I),
+            "q4k_gguf_open": ([C.c_char_p, C.POINTER(P)], I),
+            "q4k_gguf_close": ([P], I),
+            "q4k_gguf_tensor_count": ([P, C.POINTER(I64)], I),
+            "q4k_gguf_tensor_info": ([P, I64, C.c_char_p, S, C.POINTER(I), C.POINTER(I64), C.POINTER(I64),
+                                      C.POINTER(P)], I),
+            "q4k_gguf_meta_int": ([P, C.c_char_p, C.POINTER(I64)], I),
+            "q4k_gguf_meta_float": ([P, C.c_char_p, C.POINTER(C.c_double)], I),
+            "q4k_gguf_meta_string": ([P, C.c_char_p, C.c_char_p, S], I),
+            "q4k_gguf_engine_config": ([P, I, C.POINTER(EngineConfig)], I),
+            "q4k_engine_load_gguf": ([P, P], I),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -214,6 +226,58 @@ def tp_shard(cfg: EngineConfig, i: int, rank: int, world: int):
     return tuple(x.value for x in v)
 
 
+class Gguf:
+    """A GGUF model file mapped read-only (q4k_gguf_* in include/q4k_b200.h)."""
+
+    def __init__(self, path: str):
+        h = C.c_void_p()
+        check(lib().q4k_gguf_open(path.encode(), C.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            check(lib().q4k_gguf_close(self.h))
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def tensors(self) -> dict:
+        """name -> (ggml type, ne0, ne1, address of the bytes in the mapping)."""
+        n = C.c_int64()
+        check(lib().q4k_gguf_tensor_count(self.h, C.byref(n)))
+        out = {}
+        for i in range(n.value):
+            buf = C.create_string_buffer(256)
+            t, a, b, d = C.c_int(), C.c_int64(), C.c_int64(), C.c_void_p()
+            check(lib().q4k_gguf_tensor_info(self.h, i, buf, 256, C.byref(t), C.byref(a), C.byref(b), C.byref(d)))
+            out[buf.value.decode()] = (t.value, a.value, b.value, d.value)
+        return out
+
+    def meta_int(self, key: str) -> int:
+        v = C.c_int64()
+        check(lib().q4k_gguf_meta_int(self.h, key.encode(), C.byref(v)))
+        return v.value
+
+    def meta_float(self, key: str) -> float:
+        v = C.c_double()
+        check(lib().q4k_gguf_meta_float(self.h, key.encode(), C.byref(v)))
+        return v.value
+
+    def meta_string(self, key: str) -> str:
+        buf = C.create_string_buffer(4096)
+        check(lib().q4k_gguf_meta_string(self.h, key.encode(), buf, 4096))
+        return buf.value.decode()
+
+    def engine_config(self, capacity: int) -> EngineConfig:
+        cfg = EngineConfig()
+        check(lib().q4k_gguf_engine_config(self.h, capacity, C.byref(cfg)))
+        return cfg
+
+
 class Engine:
     """Decode engine (q4k_engine_*)."""
 
@@ -228,6 +292,9 @@ class Engine:
         if getattr(self, "h", None):
             check(lib().q4k_engine_destroy(self.h))
             self.h = None
+
+    def load_gguf(self, f: "Gguf"):
+        check(lib().q4k_engine_load_gguf(self.h, f.h))
 
     def __del__(self):
         try:

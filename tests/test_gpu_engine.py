@@ -361,3 +361,30 @@ def test_full_model_engine_options_bit_identical(cuda, full_model, monkeypatch, 
         assert np.array_equal(a_logits.view(np.uint32), b_logits.view(np.uint32)), (switch, s)
         tok = a_next
     off.close()
+
+
+def test_engine_from_gguf_matches_set_tensor(cuda, tmp_path):
+    """An engine configured and loaded from a GGUF file (written by the
+    ggml project's `gguf` package) computes what an engine given the same
+    tensors one by one does, bit for bit, for every step of a short run."""
+    gguf = pytest.importorskip("gguf")
+    from test_gguf import write_model
+
+    tensors = tiny_tensors()
+    path = str(tmp_path / "tiny.gguf")
+    write_model(path, tensors)
+    f = q.Gguf(path)
+    a = q.Engine(f.engine_config(16))
+    a.load_gguf(f)
+    f.close()  # the engine keeps its own device copies
+    b = q.Engine(engine_config(TINY, capacity=16))
+    for n, (t, x, y, d) in tensors.items():
+        b.set_tensor(n, t, x, y, d)
+    tok = 3
+    for pos in range(6):
+        ta, la, _ = a.decode(tok, pos, want_logits=True)
+        tb, lb, _ = b.decode(tok, pos, want_logits=True)
+        assert ta == tb and np.array_equal(la.view(np.uint32), lb.view(np.uint32)), pos
+        tok = ta
+    a.close()
+    b.close()

@@ -231,6 +231,17 @@ int q4k_engine_write_kv(q4k_engine* engine, int layer, const uint16_t* k_host, c
 int q4k_engine_decode(q4k_engine* engine, uint32_t token, int position, uint32_t* next_token, float* logits_host,
                       float* hidden_host);
 
+/* A whole prompt (Engine::inference's pass over the session's uncached
+ * tokens, src/Engine.cpp:37-114 with tokens = n): embeds tokens[0..n) at
+ * positions position .. position+n-1, runs every layer over all n rows
+ * (batched products, causal GQA attention over the cache, the n K/V rows
+ * written to the cache) and the output head on the last row only
+ * (Engine.cpp:106-111). Returns the greedy next token; logits_host as for
+ * q4k_engine_decode. Decoding continues at position + n. Token ids >= vocab
+ * and position + n > capacity are Q4K_ERANGE. Synchronous. */
+int q4k_engine_prefill(q4k_engine* engine, const uint32_t* tokens, int n, int position, uint32_t* next_token,
+                       float* logits_host);
+
 /* `steps` greedy decode steps with the token fed back on the device; one
  * graph launch per step and no host synchronisation between steps.
  * advance != 0: position increases by one per step; advance == 0: every

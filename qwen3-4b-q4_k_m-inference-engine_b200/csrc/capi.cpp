@@ -667,6 +667,14 @@ Q4K_API int q4k_engine_decode(q4k_engine* e, uint32_t token, int position, uint3
     });
 }
 
+Q4K_API int q4k_engine_prefill(q4k_engine* e, const uint32_t* tokens, int n, int position, uint32_t* next_token,
+                               float* logits_host) {
+    return guarded_cuda([&] {
+        if (!e || !next_token || !tokens) invalid("engine, tokens and output required");
+        *next_token = e->impl.prefill(tokens, n, position, logits_host);
+    });
+}
+
 Q4K_API int q4k_engine_generate(q4k_engine* e, uint32_t token, int position, int steps, int advance,
                                 uint32_t* tokens_host) {
     return guarded_cuda([&] {

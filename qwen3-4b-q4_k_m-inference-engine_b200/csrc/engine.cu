@@ -564,7 +564,6 @@ void Engine::enqueue_layer(int i) {
 void Engine::enqueue_step(bool record_hidden) {
     const auto& c = c_;
     const int H = c.hidden;
-    auto gemv = [&](GemvRequest& r) { cuda_check(launch_gemv(r, stream_), "gemv launch"); };
     auto snapshot = [&](int i) {
         if (record_hidden)
             cuda_check(cudaMemcpyAsync(hidden_ + (size_t)i * H, x_, sizeof(float) * H, cudaMemcpyDeviceToDevice,
@@ -578,6 +577,16 @@ void Engine::enqueue_step(bool record_hidden) {
         enqueue_layer(i);
         snapshot(i + 1);
     }
+    enqueue_head();
+}
+
+// Output head on x_ (Engine.cpp:106-111): final RMSNorm, the token_embd
+// product with the greedy choice fused, the shard merge when tp_world > 1, and
+// the step's bookkeeping (token_, history, *pos_ += *advance_).
+void Engine::enqueue_head() {
+    const auto& c = c_;
+    const int H = c.hidden;
+    auto gemv = [&](GemvRequest& r) { cuda_check(launch_gemv(r, stream_), "gemv launch"); };
     {
         GemvRequest r;
         r.nseg = 1;
@@ -884,6 +893,177 @@ size_t Engine::trace_step(uint32_t token, int position, unsigned long long* reco
     trace_ = nullptr;
     check_device_error();
     return n;
+}
+
+// Rows of one prefill pass: longer prompts run as consecutive passes, each
+// attending to the cache rows the previous passes wrote.
+constexpr int kPrefillRows = 512;
+
+void Engine::ensure_prefill() {
+    if (pf_rows_) return;
+    int rows = kPrefillRows;
+    // Q4K_PREFILL_ROWS=r: r rows per pass (tests split prompts with it)
+    if (const char* r = std::getenv("Q4K_PREFILL_ROWS")) rows = std::max(1, std::atoi(r));
+    rows = std::min(rows, c_.capacity);
+    const size_t H = c_.hidden;
+    pf_tokens_ = static_cast<uint32_t*>(alloc(sizeof(uint32_t) * rows));
+    pf_x_ = static_cast<float*>(alloc(sizeof(float) * rows * H));
+    pf_qkv_ = static_cast<float*>(alloc(sizeof(float) * rows * (size_t)(qd_ + 2 * kvd_)));
+    pf_q_ = static_cast<float*>(alloc(sizeof(float) * rows * (size_t)qd_));
+    pf_att_ = static_cast<float*>(alloc(sizeof(float) * rows * (size_t)qd_));
+    pf_act_ = static_cast<float*>(alloc(sizeof(float) * rows * (size_t)ffn_l_));
+    if (world_ > 1) pf_partial_ = static_cast<float*>(alloc(sizeof(float) * rows * H));
+    pf_rows_ = rows;
+}
+
+// One block (Engine.cpp:71-103) for `rows` prompt tokens at positions
+// pos0 .. pos0+rows-1: each product runs once over all rows (the weights are
+// streamed once per batch tile instead of once per token).
+void Engine::enqueue_prefill_layer(int i, int rows, int pos0) {
+    const auto& c = c_;
+    const int H = c.hidden;
+    const int W = qd_ + 2 * kvd_;
+    auto gemv = [&](GemvRequest& r) { cuda_check(launch_gemv(r, stream_), "gemv launch"); };
+    auto all_reduce_into_x = [&]() {
+        const size_t n = (size_t)rows * H;
+        nccl_check(nccl().AllReduce(pf_partial_, pf_partial_, n, ncclFloat, ncclSum, comm_, stream_),
+                   "ncclAllReduce");
+        cuda_check(residual_add(pf_x_, pf_partial_, n, stream_), "residual_add");
+    };
+    const Layer& L = layers_[i];
+    const size_t kv_layer = (size_t)i * KVHl_ * c.capacity * c.head_dim;
+    {
+        GemvRequest r;
+        r.nseg = 3;
+        r.seg[0] = {L.q, pf_qkv_, L.tq, qd_};
+        r.seg[1] = {L.k, pf_qkv_ + qd_, L.tk, kvd_};
+        r.seg[2] = {L.v, pf_qkv_ + qd_ + kvd_, L.tv, kvd_};
+        r.K = H;
+        r.M = rows;
+        r.ldx = H;
+        r.ldy = W;
+        r.x = pf_x_;
+        r.gamma = L.attn_norm;
+        r.eps = c.eps;
+        r.epilogue = EPI_STORE;
+        r.err = err_;
+        r.pdl = true;
+        gemv(r);
+    }
+    {
+        PrefillQkArgs a;
+        a.qkv = pf_qkv_;
+        a.ld_qkv = W;
+        a.q_gamma = L.q_norm;
+        a.k_gamma = L.k_norm;
+        a.q_out = pf_q_;
+        a.k_cache = kcache_ + kv_layer;
+        a.v_cache = vcache_ + kv_layer;
+        a.capacity = c.capacity;
+        a.pos0 = pos0;
+        a.heads = Hl_;
+        a.kv_heads = KVHl_;
+        a.eps = c.eps;
+        a.rope_base = c.rope_base;
+        cuda_check(prefill_qk(a, rows, stream_), "prefill_qk launch");
+    }
+    {
+        PrefillAttnArgs a;
+        a.q = pf_q_;
+        a.k_cache = kcache_ + kv_layer;
+        a.v_cache = vcache_ + kv_layer;
+        a.out = pf_att_;
+        a.capacity = c.capacity;
+        a.pos0 = pos0;
+        a.heads = Hl_;
+        a.kv_heads = KVHl_;
+        cuda_check(prefill_attention(a, rows, stream_), "prefill_attention launch");
+    }
+    {
+        GemvRequest r;
+        r.nseg = 1;
+        r.seg[0] = {L.o, world_ > 1 ? pf_partial_ : pf_x_, L.to, H};
+        r.K = qd_;
+        r.M = rows;
+        r.ldx = qd_;
+        r.ldy = H;
+        r.x = pf_att_;
+        r.epilogue = world_ > 1 ? EPI_STORE : EPI_ADD;
+        r.err = err_;
+        r.pdl = true;
+        gemv(r);
+        if (world_ > 1) all_reduce_into_x();
+    }
+    {
+        GemvRequest r;
+        r.nseg = 2;
+        r.seg[0] = {L.gate, pf_act_, L.tgate, ffn_l_};
+        r.seg[1] = {L.up, pf_act_, L.tup, ffn_l_};
+        r.K = H;
+        r.M = rows;
+        r.ldx = H;
+        r.ldy = ffn_l_;
+        r.x = pf_x_;
+        r.gamma = L.ffn_norm;
+        r.eps = c.eps;
+        r.epilogue = EPI_SWIGLU;
+        r.err = err_;
+        r.pdl = true;
+        gemv(r);
+    }
+    {
+        GemvRequest r;
+        r.nseg = 1;
+        r.seg[0] = {L.down, world_ > 1 ? pf_partial_ : pf_x_, L.tdown, H};
+        r.K = ffn_l_;
+        r.M = rows;
+        r.ldx = ffn_l_;
+        r.ldy = H;
+        r.x = pf_act_;
+        r.epilogue = world_ > 1 ? EPI_STORE : EPI_ADD;
+        r.err = err_;
+        r.pdl = true;
+        gemv(r);
+        if (world_ > 1) all_reduce_into_x();
+    }
+}
+
+uint32_t Engine::prefill(const uint32_t* tokens_host, int n, int position, float* logits_host) {
+    if (!loaded_) throw Error(Q4K_EINVAL, "weights are not loaded");
+    if (n <= 0 || !tokens_host) throw Error(Q4K_EINVAL, "prefill needs at least one token");
+    // Engine.cpp:126-128 (capacity) and EmbedLookup's token check
+    if (position < 0 || (long long)position + n > c_.capacity) throw Error(Q4K_ERANGE, "KV cache capacity exceeded");
+    for (int t = 0; t < n; ++t)
+        if (tokens_host[t] >= (uint32_t)c_.vocab) throw Error(Q4K_ERANGE, "Token ID out of range");
+    ensure_prefill();
+    const int H = c_.hidden;
+    host_io_[1] = (uint32_t)(position + n - 1);
+    host_io_[2] = 0;
+    cuda_check(cudaMemcpyAsync(pos_, &host_io_[1], 4, cudaMemcpyHostToDevice, stream_), "h2d");
+    cuda_check(cudaMemcpyAsync(advance_, &host_io_[2], 4, cudaMemcpyHostToDevice, stream_), "h2d");
+    cuda_check(cudaMemsetAsync(history_n_, 0, 4, stream_), "memset");
+    int rows = 0;
+    for (int t0 = 0; t0 < n; t0 += pf_rows_) {
+        rows = std::min(pf_rows_, n - t0);
+        cuda_check(cudaMemcpyAsync(pf_tokens_, tokens_host + t0, sizeof(uint32_t) * rows, cudaMemcpyHostToDevice,
+                                   stream_),
+                   "h2d tokens");
+        cuda_check(embed_rows(token_embd_, t_embd_, H, c_.vocab, pf_tokens_, rows, pf_x_, err_, stream_, false),
+                   "embed");
+        for (int i = 0; i < c_.layers; ++i) enqueue_prefill_layer(i, rows, position + t0);
+    }
+    // Engine.cpp:106-111: only the last prompt token's state feeds the head
+    cuda_check(cudaMemcpyAsync(x_, pf_x_ + (size_t)(rows - 1) * H, sizeof(float) * H, cudaMemcpyDeviceToDevice,
+                               stream_),
+               "last row");
+    enqueue_head();
+    cuda_check(cudaMemcpyAsync(&host_io_[4], token_, 4, cudaMemcpyDeviceToHost, stream_), "d2h");
+    if (logits_host)
+        cuda_check(cudaMemcpyAsync(logits_host, logits_, sizeof(float) * (vocab1_ - vocab0_), cudaMemcpyDeviceToHost,
+                                   stream_),
+                   "d2h logits");
+    check_device_error();
+    return host_io_[4];
 }
 
 void Engine::layer_step(int layer, const float* x_host, int position, float* x_out_host) {

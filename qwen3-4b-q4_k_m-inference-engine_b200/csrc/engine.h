@@ -54,6 +54,11 @@ public:
     void write_kv(int layer, const uint16_t* k_host, const uint16_t* v_host);
     uint32_t decode(uint32_t token, int position, float* logits_host, float* hidden_host);
     void generate(uint32_t token, int position, int steps, int advance, uint32_t* tokens_host);
+    // A whole prompt at positions position .. position+n-1 (Engine.cpp:37-114
+    // with tokens = n): every layer as batched products over the prompt rows,
+    // the K/V rows written to the cache, the output head on the last row.
+    // Returns the greedy next token.
+    uint32_t prefill(const uint32_t* tokens_host, int n, int position, float* logits_host);
     // One block on a given residual-stream input (tp_world == 1 or all ranks).
     void layer_step(int layer, const float* x_host, int position, float* x_out_host);
     // One step with every kernel CTA's %globaltimer start/end recorded.
@@ -75,6 +80,10 @@ private:
     void place(const TensorSpec& t, const void* raw_device);
     void enqueue_step(bool record_hidden);
     void enqueue_layer(int i);
+    void enqueue_head();
+    // Prompt rows per prefill pass and their buffers (allocated on first use).
+    void ensure_prefill();
+    void enqueue_prefill_layer(int i, int rows, int pos0);
     // L2 prefetch descriptors of layer i's weights (q, k, v; o; gate, up; down).
     L2Prefetch weight_prefetch(const uint8_t* w, int type, int K, int rows) const;
     void check_device_error();
@@ -119,6 +128,11 @@ private:
     float* tp_cand_local_ = nullptr;  // [2] score, index (as float bits)
     float* tp_cand_all_ = nullptr;    // [2 * world]
     uint32_t* host_io_ = nullptr;     // pinned: token, position, result
+
+    int pf_rows_ = 0;  // prompt rows one prefill pass holds
+    uint32_t* pf_tokens_ = nullptr;
+    float *pf_x_ = nullptr, *pf_qkv_ = nullptr, *pf_q_ = nullptr, *pf_att_ = nullptr, *pf_act_ = nullptr,
+          *pf_partial_ = nullptr;
 
     cudaGraphExec_t exec_ = nullptr;
     bool l2_prefetch_ = true;        // each launch prefetches the next one's operands into L2

@@ -57,6 +57,31 @@ struct DecodeAttnArgs {
     ActImage out_image;                   // optional: the attended output, quantised for the O product
 };
 constexpr int kDecodeHeadDim = 128;
+
+// Prompt prefill (prefill.cu): M tokens at positions pos0 .. pos0+M-1.
+struct PrefillQkArgs {
+    const float* qkv = nullptr;  // [M][ld_qkv]: q (heads x 128) | k (kv_heads x 128) | v (kv_heads x 128)
+    int ld_qkv = 0;
+    const float* q_gamma = nullptr;  // [128]
+    const float* k_gamma = nullptr;  // [128]
+    float* q_out = nullptr;          // [M][heads x 128]: normed, rotated queries
+    uint16_t* k_cache = nullptr;     // [kv_heads][capacity][128] fp16 (this layer)
+    uint16_t* v_cache = nullptr;
+    int capacity = 0, pos0 = 0, heads = 0, kv_heads = 0;
+    float eps = 1e-6f, rope_base = 1e6f;
+};
+// Per token and head: QK RMSNorm and RoPE; for KV heads, K and V appended to the cache.
+cudaError_t prefill_qk(const PrefillQkArgs& a, int tokens, cudaStream_t s);
+
+struct PrefillAttnArgs {
+    const float* q = nullptr;             // [M][heads x 128]
+    const uint16_t* k_cache = nullptr;    // [kv_heads][capacity][128] fp16, rows 0 .. pos0+M-1 written
+    const uint16_t* v_cache = nullptr;
+    float* out = nullptr;                 // [M][heads x 128]
+    int capacity = 0, pos0 = 0, heads = 0, kv_heads = 0;
+};
+// Causal GQA attention of every prompt token over cache positions 0 .. its own.
+cudaError_t prefill_attention(const PrefillAttnArgs& a, int tokens, cudaStream_t s);
 // Opaque storage of a TMA tensor map (CUtensorMap) over an fp16 KV cache
 // viewed as [rows][128]: 64-row x 64-dim boxes, 128-byte swizzle.
 struct alignas(64) KvTensorMap {

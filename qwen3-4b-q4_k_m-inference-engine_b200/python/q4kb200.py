@@ -28,7 +28,7 @@ EXPORTS = (
     "q4k_argmax", "q4k_matmul_ex", "q4k_matmul_argmax_scratch_bytes", "q4k_attention_decode_f16",
     "q4k_attention_decode_scratch_bytes", "q4k_engine_config_qwen3_4b", "q4k_model_tensor", "q4k_nccl_unique_id",
     "q4k_engine_create", "q4k_engine_destroy", "q4k_engine_load_synthetic", "q4k_engine_set_tensor",
-    "q4k_engine_fill_kv_synthetic", "q4k_engine_read_kv", "q4k_engine_decode", "q4k_engine_generate",
+    "q4k_engine_fill_kv_synthetic", "q4k_engine_read_kv", "q4k_engine_decode", "q4k_engine_prefill", "q4k_engine_generate",
     "q4k_engine_stream", "q4k_tp_shard", "q4k_engine_layer", "q4k_engine_write_kv",
     "q4k_engine_trace", "q4k_attention_decode_f16_static", "q4k_gguf_open", "q4k_gguf_close",
     "q4k_gguf_tensor_count", "q4k_gguf_tensor_info", "q4k_gguf_meta_int", "q4k_gguf_meta_float",
@@ -104,6 +104,7 @@ def lib():
             "q4k_engine_fill_kv_synthetic": ([P, U64, I], I),
             "q4k_engine_read_kv": ([P, I, P, P], I),
             "q4k_engine_decode": ([P, C.c_uint32, I, C.POINTER(C.c_uint32), P, P], I),
+            "q4k_engine_prefill": ([P, P, I, I, C.POINTER(C.c_uint32), P], I),
             "q4k_engine_generate": ([P, C.c_uint32, I, I, I, P], I),
             "q4k_engine_stream": ([P], P),
             "q4k_engine_layer": ([P, I, P, I, P], I),
@@ -335,6 +336,19 @@ class Engine:
         nxt = C.c_uint32()
         check(lib().q4k_engine_decode(self.h, token, position, C.byref(nxt), hptr(logits), hptr(hidden)))
         return nxt.value, logits, hidden
+
+    def prefill(self, tokens, position: int = 0, want_logits=False):
+        """A whole prompt at positions position .. position+len(tokens)-1
+        (q4k_engine_prefill): returns (next token, logits of the last row)."""
+        c = self.cfg
+        world = max(c.tp_world, 1)
+        v0 = c.vocab * c.tp_rank // world
+        v1 = c.vocab * (c.tp_rank + 1) // world
+        toks = np.ascontiguousarray(tokens, np.uint32)
+        logits = np.empty(v1 - v0, np.float32) if want_logits else None
+        nxt = C.c_uint32()
+        check(lib().q4k_engine_prefill(self.h, hptr(toks), int(toks.size), position, C.byref(nxt), hptr(logits)))
+        return nxt.value, logits
 
     def generate(self, token: int, position: int, steps: int, advance: bool = True, want_tokens=True):
         out = np.empty(max(steps, 1), np.uint32) if want_tokens else None

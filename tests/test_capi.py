@@ -149,6 +149,8 @@ def test_argument_validation_needs_no_gpu():
     # fused entry points
     assert L.q4k_attention_decode_f16(P(16), P(16), P(16), P(16), P(16), 8, P(16), 8, 4, 128, 1e-6, 1e6, P(16),
                                       P(16), None) == q.EINVAL
+    # prefill without an engine, tokens or result
+    assert L.q4k_engine_prefill(None, P(16), 1, 0, C.byref(r), None) == q.EINVAL
     # engine configuration checks happen before any device work
     cfg = q.qwen3_4b_config(4096)
     cfg.head_dim = 64

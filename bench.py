@@ -48,8 +48,8 @@ def load_peaks() -> dict:
     if os.path.exists(path):
         with open(path) as f:
             p = json.load(f)
-        return {"hbm_gbs": float(p["hbm_gbs"]), "src": "measured"}
-    return {"hbm_gbs": 6650.0, "src": "fallback"}
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p.get("bf16_tflops", 1590.0)), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
 
 
 class ClockSampler:
@@ -483,6 +483,94 @@ def run_attention(args, world, rank, local):
             "gpu_launches": args.steps}
 
 
+def run_prefill(args, world, rank, local):
+    """Prompt prefill (q4k_engine_prefill, the reference's Engine::inference
+    over a whole prompt): a 512-token prompt on the synthetic Qwen3-4B, plus
+    the reference benchmark's first-token latency shape (a 23-token prompt,
+    then one decode step; benchmark.cpp:86-91). The roofline object is the
+    tensor-core product behind it (ffn_gate/ffn_up SwiGLU at 512 rows)."""
+    import ctypes as C
+
+    import numpy as np
+    import torch
+
+    import q4kb200 as q
+
+    torch.cuda.set_device(local)
+    peaks = load_peaks()
+    n = 512
+    cfg = q.qwen3_4b_config(CTX)
+    eng = q.Engine(cfg)
+    eng.load_synthetic(SEED)
+    rng = np.random.default_rng(SEED)
+    toks = rng.integers(0, cfg.vocab, n).astype(np.uint32)
+    for _ in range(max(3, args.warmup)):
+        eng.prefill(toks, 0)
+    steps = max(1, min(args.steps, 20))
+    stream = torch.cuda.ExternalStream(eng.stream)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    ev0.record(stream)
+    for _ in range(steps):
+        eng.prefill(toks, 0)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    wall = (time.perf_counter() - t0) / steps
+    dev = ev0.elapsed_time(ev1) / 1e3 / steps
+    # first-token latency: 23-token prompt + one decode step, host wall clock
+    short = rng.integers(0, cfg.vocab, 23).astype(np.uint32)
+    firsts = []
+    for _ in range(5):
+        a = time.perf_counter()
+        nxt, _ = eng.prefill(short, 0)
+        eng.decode(nxt, 23)
+        firsts.append(time.perf_counter() - a)
+    eng.close()
+    # the dominant product alone, events around each launch pair (quantise + GEMM)
+    K, N = 2560, 9728
+    ws = []
+    for nm in ("gate", "up"):
+        raw = q.synth_tensor_host(SEED, f"bench.pf.{nm}", q.Q4_K, K, N)
+        buf = torch.empty(q.device_bytes(q.Q4_K, K, N), dtype=torch.uint8, device="cuda")
+        q.check(q.lib().q4k_weight_upload(q.Q4_K, K, N, q.hptr(raw), buf.data_ptr(), None))
+        ws.append(buf)
+    x = torch.from_numpy(q.synth_f32_host(SEED, "bench.pf.x", n * K)).cuda()
+    y = torch.empty(n * N, device="cuda")
+    call = lambda: q.check(q.lib().q4k_matmul_batch(
+        x.data_ptr(), None, 0.0, 2, (C.c_void_p * 2)(ws[0].data_ptr(), ws[1].data_ptr()), (C.c_int * 2)(q.Q4_K, q.Q4_K),
+        (C.c_int64 * 2)(N, N), (C.c_void_p * 2)(y.data_ptr(), y.data_ptr()), N, K, n, q.EPI_SWIGLU, None))
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(20):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    launch = e0.elapsed_time(e1) / 1e3 / 20
+    flops = 2.0 * n * 2 * N * K
+    tf = flops / launch / 1e12
+    return {"metric": "Qwen3-4B prompt prefill tok/s (512-token prompt)", "value": round(n / dev, 1),
+            "unit": "tok/s", "n_gpus": 1, "steps": steps, "warmup": max(3, args.warmup),
+            "ms_per_step": round(dev * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp16 tensor-core products of Q8-dequantised activations and dequantised weights, fp32 accumulate",
+            "data": "synthetic (seeded random-init Q4_K_M weights, random token ids)",
+            "config": {"workload": "prefill of a 512-token prompt from an empty cache", "model": MODEL,
+                       "global_batch": 1, "seq_len": n, "parallelism": "tp1",
+                       "l2": "2.5 GB of weights streamed per prompt (larger than L2)"},
+            "first_token_ms": round(min(firsts) * 1e3, 3),
+            "first_token_note": "23-token prompt prefill + 1 decode step, host wall clock (reference benchmark.cpp "
+                                "'first token' shape; BASELINE.md quotes 186.5 ms on an RTX 4060 Laptop GPU)",
+            "roofline": {"kernel": "prefill_quantise + prefill_gemm_kernel (ffn_gate/ffn_up SwiGLU, 512 x 2560 x "
+                                   "2x9728, Q4_K)", "bound": "tensor", "achieved": round(tf, 2),
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(tf / peaks["bf16_tflops"], 4),
+                         "traffic": None, "algorithmic_flops": flops, "launch_us": round(launch * 1e6, 2)},
+            "e2e": {"value": round(n / wall, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * n, "d2h_bytes_per_step": 8,
+                    "how": "q4k_engine_prefill per prompt from host token ids, host wall clock"},
+            "gpu_launches": steps * (36 * 10 + 4)}
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return None
@@ -512,7 +600,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("decode", "gemv", "swiglu", "attention"), default="decode")
+    ap.add_argument("--workload", choices=("decode", "gemv", "swiglu", "attention", "prefill"), default="decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     world, rank, local = dist_init()
@@ -529,6 +617,8 @@ def main() -> None:
         out = run_attention(args, world, rank, local)
     elif args.workload == "swiglu":
         out = run_swiglu(args, world, rank, local)
+    elif args.workload == "prefill":
+        out = run_prefill(args, world, rank, local)
     else:
         out = run_gemv(args, world, rank, local)
     if rank == 0 and out is not None:

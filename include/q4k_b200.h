@@ -135,6 +135,19 @@ int q4k_matmul_ex(const float* input, const float* norm_gamma, float epsilon, in
                   int epilogue, uint32_t* token_device, void* scratch, void* stream);
 size_t q4k_matmul_argmax_scratch_bytes(void);
 
+/* The same products for many activation rows (the reference's
+ * kernels::matmul with rows = n prompt tokens, src/Engine.cpp:83-101) on the
+ * tensor cores (tcgen05, fp32 accumulation in tensor memory). Each row is
+ * Q8-quantised as the reference does (after RMSNorm with norm_gamma, if
+ * given); the codes times their scales and the dequantised weights meet as
+ * fp16 (2^-11 relative rounding of each) instead of in an integer dot.
+ * count: 1..3 weights; outputs[i][m * ld_out + n] (SWIGLU: two weights of one
+ * type and shape, output in outputs[0]). epilogue: Q4K_EPI_STORE, _ADD or
+ * _SWIGLU. ne0 <= 10240. Allocates its workspace on the stream. */
+int q4k_matmul_batch(const float* input, const float* norm_gamma, float epsilon, int count, const void* const* weights,
+                     const int* types, const int64_t* out_rows, float* const* outputs, int64_t ld_out, int64_t ne0,
+                     size_t rows, int epilogue, void* stream);
+
 /* Decode attention for one token over an fp16 KV cache (new): fuses the
  * per-head q/k RMSNorm (src/Engine.cpp:87-88), RoPE (:89-90), the K/V cache
  * write and split-K attention (:92). qkv = [q | k | v] raw projections of

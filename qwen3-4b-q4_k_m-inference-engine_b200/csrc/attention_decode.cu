@@ -419,22 +419,24 @@ using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, 
                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-EncodeTiled encoder() {
-    static EncodeTiled fn = nullptr;
+EncodeTiled encoder() { return reinterpret_cast<EncodeTiled>(tensor_map_encoder()); }
+
+size_t smem_bytes(int stages) { return (size_t)stages * kStageBytes + sizeof(SmemTail) + 1024; }
+
+}  // namespace
+
+void* tensor_map_encoder() {
+    static void* fn = nullptr;
     static std::once_flag once;
     std::call_once(once, [] {
         void* p = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiled>(p);
+            fn = p;
     });
     return fn;
 }
-
-size_t smem_bytes(int stages) { return (size_t)stages * kStageBytes + sizeof(SmemTail) + 1024; }
-
-}  // namespace
 
 cudaError_t make_kv_tensor_map(const uint16_t* base, long long rows, KvTensorMap* out) {
     static_assert(sizeof(KvTensorMap) == sizeof(CUtensorMap), "tensor map storage size");

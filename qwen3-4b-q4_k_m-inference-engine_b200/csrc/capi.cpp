@@ -331,6 +331,60 @@ Q4K_API int q4k_matmul_ex(const float* input, const float* norm_gamma, float eps
     });
 }
 
+Q4K_API int q4k_matmul_batch(const float* input, const float* norm_gamma, float epsilon, int count,
+                             const void* const* weights, const int* types, const int64_t* out_rows,
+                             float* const* outputs, int64_t ld_out, int64_t ne0, size_t rows, int epilogue,
+                             void* stream) {
+    return guarded_cuda([&] {
+        if (count < 1 || count > 3 || !weights || !types || !out_rows || !outputs)
+            invalid("matmul_batch needs 1..3 weights");
+        if (epilogue != Q4K_EPI_STORE && epilogue != Q4K_EPI_ADD && epilogue != Q4K_EPI_SWIGLU)
+            invalid("matmul_batch epilogues: STORE, ADD, SWIGLU");
+        if (rows == 0) return;
+        if (rows > (1u << 20)) invalid("too many rows");
+        if (!input || reinterpret_cast<uintptr_t>(input) % 16) invalid("input must be a 16-byte aligned buffer");
+        if (norm_gamma && !(epsilon > 0.0f)) invalid("RMSNorm requires a positive epsilon");
+        q4k::PrefillGemmArgs g;
+        g.nseg = count;
+        for (int i = 0; i < count; ++i) {
+            check_matrix(types[i], ne0, out_rows[i]);
+            if (!weights[i] || reinterpret_cast<uintptr_t>(weights[i]) % 16) invalid("weights must be 16-byte aligned");
+            float* y = epilogue == Q4K_EPI_SWIGLU ? outputs[0] : outputs[i];
+            if (!y) invalid("missing output buffer");
+            g.seg[i] = {static_cast<const uint8_t*>(weights[i]), types[i], (int)out_rows[i], y};
+        }
+        if (epilogue == Q4K_EPI_SWIGLU && (count != 2 || out_rows[0] != out_rows[1] || types[0] != types[1]))
+            invalid("SWIGLU needs two weights of the same type and shape");
+        if (ld_out < out_rows[0] || ld_out > (int64_t)1 << 30) invalid("ld_out must cover the output rows");
+        if (ne0 > 10240) invalid("at most 10240 inputs per row");
+        const cudaStream_t s = as_stream(stream);
+        // per-call workspace, as the reference's matmul allocates one (matmul.cu:142-145)
+        void* ws = nullptr;
+        const size_t a_bytes = ((rows * (size_t)ne0 * 2 + 255) / 256) * 256;
+        const size_t s_bytes = ((rows * sizeof(float) + 255) / 256) * 256;
+        size_t ntot = 0;
+        for (int i = 0; i < count; ++i) ntot += (size_t)out_rows[i];
+        const size_t part_floats = epilogue == Q4K_EPI_SWIGLU ? 0 : rows * ntot * 4;  // up to 4 K splits
+        launched(cudaMallocAsync(&ws, a_bytes + s_bytes + part_floats * sizeof(float), s));
+        uint16_t* a = static_cast<uint16_t*>(ws);
+        float* scale = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + a_bytes);
+        g.partial = part_floats ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + a_bytes + s_bytes) : nullptr;
+        g.partial_floats = part_floats;
+        cudaError_t e = q4k::prefill_quantise(input, (int)ne0, norm_gamma, epsilon, (int)rows, (int)ne0, a, scale, s);
+        if (e == cudaSuccess) {
+            g.K = (int)ne0;
+            g.M = (int)rows;
+            g.ldy = (int)ld_out;
+            g.epilogue = epilogue;
+            g.a = a;
+            g.row_scale = scale;
+            e = q4k::prefill_gemm(g, s);
+        }
+        cudaFreeAsync(ws, s);
+        launched(e);
+    });
+}
+
 Q4K_API size_t q4k_attention_decode_scratch_bytes(int query_heads, int kv_heads) {
     if (kv_heads <= 0 || query_heads <= 0) return 0;
     const int splits = q4k::decode_attention_splits(kv_heads);

@@ -346,6 +346,7 @@ void Engine::load_synthetic(uint64_t seed) {
     cudaFree(tmp);
     loaded_ = true;
     step_ready_ = false;
+    pf_maps_ready_ = false;
 }
 
 void Engine::set_tensor(const std::string& name, int type, int64_t ne0, int64_t ne1, const void* host_gguf) {
@@ -382,6 +383,7 @@ void Engine::set_tensor(const std::string& name, int type, int64_t ne0, int64_t 
     have_[idx] = true;
     loaded_ = std::all_of(have_.begin(), have_.end(), [](bool b) { return b; });
     step_ready_ = false;
+    pf_maps_ready_ = false;
     if (exec_) {
         cudaGraphExecDestroy(exec_);
         exec_ = nullptr;
@@ -913,7 +915,45 @@ void Engine::ensure_prefill() {
     pf_att_ = static_cast<float*>(alloc(sizeof(float) * rows * (size_t)qd_));
     pf_act_ = static_cast<float*>(alloc(sizeof(float) * rows * (size_t)ffn_l_));
     if (world_ > 1) pf_partial_ = static_cast<float*>(alloc(sizeof(float) * rows * H));
+    // Prompt products: the tensor-core GEMM for passes of 9 rows or more, the
+    // batched dp4a GEMV (which streams each weight once per 8 rows) below
+    // that, where it measured faster. Q4K_PREFILL_GEMM=0 / =1 forces one.
+    if (const char* g = std::getenv("Q4K_PREFILL_GEMM")) {
+        pf_gemm_ = g[0] != '0';
+        pf_gemm_min_rows_ = pf_gemm_ ? 1 : INT32_MAX;
+    }
+    if (pf_gemm_) {
+        const size_t max_k = std::max<size_t>({H, (size_t)qd_, (size_t)ffn_l_});
+        pf_a_ = static_cast<uint16_t*>(alloc(sizeof(uint16_t) * rows * max_k));
+        pf_rs_ = static_cast<float*>(alloc(sizeof(float) * rows));
+        pf_part_floats_ = (size_t)rows * std::max<size_t>(H, (size_t)(qd_ + 2 * kvd_)) * 2;
+        pf_part_ = static_cast<float*>(alloc(sizeof(float) * pf_part_floats_));
+        const int ks[3] = {(int)H, qd_, ffn_l_};
+        for (int i = 0; i < 3; ++i) cuda_check(make_act_map(pf_a_, ks[i], rows, &pf_amap_[i]), "activation map");
+    }
     pf_rows_ = rows;
+}
+
+// TMA maps of every layer's weights for the prefill GEMM, built once per
+// placement of the tensors (encoding a map is host work).
+void Engine::ensure_prefill_maps() {
+    if (pf_maps_ready_) return;
+    const int H = c_.hidden;
+    pf_wmaps_.assign((size_t)c_.layers * 7 * kPrefillWeightMaps, KvTensorMap{});
+    for (int i = 0; i < c_.layers; ++i) {
+        const Layer& L = layers_[i];
+        const struct {
+            const uint8_t* w;
+            int type, K, rows;
+        } m[7] = {{L.q, L.tq, H, qd_},     {L.k, L.tk, H, kvd_},       {L.v, L.tv, H, kvd_},
+                  {L.o, L.to, qd_, H},     {L.gate, L.tgate, H, ffn_l_}, {L.up, L.tup, H, ffn_l_},
+                  {L.down, L.tdown, ffn_l_, H}};
+        for (int j = 0; j < 7; ++j)
+            cuda_check(make_weight_map(m[j].w, m[j].type, m[j].K, m[j].rows,
+                                       &pf_wmaps_[((size_t)i * 7 + j) * kPrefillWeightMaps]),
+                       "weight map");
+    }
+    pf_maps_ready_ = true;
 }
 
 // One block (Engine.cpp:71-103) for `rows` prompt tokens at positions
@@ -923,7 +963,32 @@ void Engine::enqueue_prefill_layer(int i, int rows, int pos0) {
     const auto& c = c_;
     const int H = c.hidden;
     const int W = qd_ + 2 * kvd_;
-    auto gemv = [&](GemvRequest& r) { cuda_check(launch_gemv(r, stream_), "gemv launch"); };
+    // One product over all rows: the tensor-core GEMM (activation rows
+    // quantised once into pf_a_), or the batched GEMV.
+    // slot: index of the product's first weight among the layer's seven maps
+    auto gemv = [&](GemvRequest& r, int slot) {
+        if (!pf_gemm_ || rows < pf_gemm_min_rows_) {
+            cuda_check(launch_gemv(r, stream_), "gemv launch");
+            return;
+        }
+        cuda_check(prefill_quantise(r.x, r.ldx, r.gamma, r.eps, r.M, r.K, pf_a_, pf_rs_, stream_),
+                   "prefill_quantise launch");
+        PrefillGemmArgs g;
+        g.nseg = r.nseg;
+        for (int s = 0; s < r.nseg; ++s) g.seg[s] = {r.seg[s].w, r.seg[s].type, r.seg[s].rows, r.seg[s].y};
+        g.K = r.K;
+        g.M = r.M;
+        g.ldy = r.ldy;
+        g.epilogue = r.epilogue;
+        for (int s = 0; s < r.nseg; ++s) g.wmap[s] = &pf_wmaps_[((size_t)i * 7 + slot + s) * kPrefillWeightMaps];
+        g.amap = &pf_amap_[r.K == H ? 0 : r.K == qd_ ? 1 : 2];
+        g.a = pf_a_;
+        g.row_scale = pf_rs_;
+        g.partial = pf_part_;
+        g.partial_floats = pf_part_floats_;
+        g.err = err_;
+        cuda_check(prefill_gemm(g, stream_), "prefill_gemm launch");
+    };
     auto all_reduce_into_x = [&]() {
         const size_t n = (size_t)rows * H;
         nccl_check(nccl().AllReduce(pf_partial_, pf_partial_, n, ncclFloat, ncclSum, comm_, stream_),
@@ -948,7 +1013,7 @@ void Engine::enqueue_prefill_layer(int i, int rows, int pos0) {
         r.epilogue = EPI_STORE;
         r.err = err_;
         r.pdl = true;
-        gemv(r);
+        gemv(r, 0);
     }
     {
         PrefillQkArgs a;
@@ -977,6 +1042,10 @@ void Engine::enqueue_prefill_layer(int i, int rows, int pos0) {
         a.pos0 = pos0;
         a.heads = Hl_;
         a.kv_heads = KVHl_;
+        a.kmap = &kmap_;
+        a.vmap = &vmap_;
+        a.row_base = i * KVHl_ * c.capacity;
+        a.err = err_;
         cuda_check(prefill_attention(a, rows, stream_), "prefill_attention launch");
     }
     {
@@ -991,7 +1060,7 @@ void Engine::enqueue_prefill_layer(int i, int rows, int pos0) {
         r.epilogue = world_ > 1 ? EPI_STORE : EPI_ADD;
         r.err = err_;
         r.pdl = true;
-        gemv(r);
+        gemv(r, 3);
         if (world_ > 1) all_reduce_into_x();
     }
     {
@@ -1009,7 +1078,7 @@ void Engine::enqueue_prefill_layer(int i, int rows, int pos0) {
         r.epilogue = EPI_SWIGLU;
         r.err = err_;
         r.pdl = true;
-        gemv(r);
+        gemv(r, 4);
     }
     {
         GemvRequest r;
@@ -1023,7 +1092,7 @@ void Engine::enqueue_prefill_layer(int i, int rows, int pos0) {
         r.epilogue = world_ > 1 ? EPI_STORE : EPI_ADD;
         r.err = err_;
         r.pdl = true;
-        gemv(r);
+        gemv(r, 6);
         if (world_ > 1) all_reduce_into_x();
     }
 }
@@ -1036,6 +1105,7 @@ uint32_t Engine::prefill(const uint32_t* tokens_host, int n, int position, float
     for (int t = 0; t < n; ++t)
         if (tokens_host[t] >= (uint32_t)c_.vocab) throw Error(Q4K_ERANGE, "Token ID out of range");
     ensure_prefill();
+    if (pf_gemm_) ensure_prefill_maps();
     const int H = c_.hidden;
     host_io_[1] = (uint32_t)(position + n - 1);
     host_io_[2] = 0;

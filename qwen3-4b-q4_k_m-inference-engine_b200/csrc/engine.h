@@ -84,6 +84,7 @@ private:
     // Prompt rows per prefill pass and their buffers (allocated on first use).
     void ensure_prefill();
     void enqueue_prefill_layer(int i, int rows, int pos0);
+    void ensure_prefill_maps();
     // L2 prefetch descriptors of layer i's weights (q, k, v; o; gate, up; down).
     L2Prefetch weight_prefetch(const uint8_t* w, int type, int K, int rows) const;
     void check_device_error();
@@ -133,6 +134,15 @@ private:
     uint32_t* pf_tokens_ = nullptr;
     float *pf_x_ = nullptr, *pf_qkv_ = nullptr, *pf_q_ = nullptr, *pf_att_ = nullptr, *pf_act_ = nullptr,
           *pf_partial_ = nullptr;
+    bool pf_gemm_ = true;        // the tensor-core GEMM is available (prefill_gemm.cu)
+    int pf_gemm_min_rows_ = 9;   // passes of fewer rows use the batched GEMV
+    bool pf_maps_ready_ = false;  // pf_wmaps_ matches the placed tensors
+    std::vector<KvTensorMap> pf_wmaps_;  // per layer: q, k, v, o, gate, up, down
+    KvTensorMap pf_amap_[3];     // pf_a_ with K = hidden, q width, ffn width
+    uint16_t* pf_a_ = nullptr;   // fp16 activation operand [rows][max K]
+    float* pf_rs_ = nullptr;     // its row scales
+    float* pf_part_ = nullptr;   // split-K partial sums of the GEMM
+    size_t pf_part_floats_ = 0;
 
     cudaGraphExec_t exec_ = nullptr;
     bool l2_prefetch_ = true;        // each launch prefetches the next one's operands into L2

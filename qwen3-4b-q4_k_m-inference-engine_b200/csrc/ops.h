@@ -73,20 +73,70 @@ struct PrefillQkArgs {
 // Per token and head: QK RMSNorm and RoPE; for KV heads, K and V appended to the cache.
 cudaError_t prefill_qk(const PrefillQkArgs& a, int tokens, cudaStream_t s);
 
+// Opaque storage of a TMA tensor map (CUtensorMap); make_kv_tensor_map's
+// views an fp16 KV cache as [rows][128]: 64-row x 64-dim boxes, 128-byte
+// swizzle.
+struct alignas(64) KvTensorMap {
+    unsigned char bytes[128];
+};
 struct PrefillAttnArgs {
     const float* q = nullptr;             // [M][heads x 128]
     const uint16_t* k_cache = nullptr;    // [kv_heads][capacity][128] fp16, rows 0 .. pos0+M-1 written
     const uint16_t* v_cache = nullptr;
     float* out = nullptr;                 // [M][heads x 128]
     int capacity = 0, pos0 = 0, heads = 0, kv_heads = 0;
+    // Optional: TMA maps of the whole cache (make_kv_tensor_map) and the map
+    // row of this layer's KV head 0, position 0; with them and 4 query heads
+    // per KV head the tensor-core kernel runs.
+    const KvTensorMap* kmap = nullptr;
+    const KvTensorMap* vmap = nullptr;
+    int row_base = 0;
+    int* err = nullptr;
 };
 // Causal GQA attention of every prompt token over cache positions 0 .. its own.
 cudaError_t prefill_attention(const PrefillAttnArgs& a, int tokens, cudaStream_t s);
-// Opaque storage of a TMA tensor map (CUtensorMap) over an fp16 KV cache
-// viewed as [rows][128]: 64-row x 64-dim boxes, 128-byte swizzle.
-struct alignas(64) KvTensorMap {
-    unsigned char bytes[128];
+// Prompt-prefill products on the tensor cores (prefill_gemm.cu).
+//
+// prefill_quantise: each of M activation rows (optionally RMSNorm-ed with
+// gamma) is Q8-quantised as the reference does (per 32 values, scale
+// amax/127, code roundf(x/amax*127)), and stored as fp16 code * (scale /
+// row_scale[m]), row_scale[m] being the row's largest group scale: the
+// Q8-dequantised activation over a per-row factor, within [-127, 127].
+cudaError_t prefill_quantise(const float* x, int ldx, const float* gamma, float eps, int M, int K, uint16_t* a,
+                             float* row_scale, cudaStream_t s);
+struct PrefillGemmSegment {
+    const uint8_t* w = nullptr;  // device layout rows (q4k_format.h)
+    int type = 0;                // Q4K_TYPE_Q4_K or Q4K_TYPE_Q6_K
+    int rows = 0;
+    float* y = nullptr;          // y[m * ldy + n]
 };
+struct PrefillGemmArgs {
+    PrefillGemmSegment seg[3];
+    // Prebuilt TMA maps (make_weight_map: kPrefillWeightMaps per segment;
+    // make_act_map), or nullptr to encode them for this call. An activation
+    // map may cover more rows than M.
+    const KvTensorMap* wmap[3] = {nullptr, nullptr, nullptr};
+    const KvTensorMap* amap = nullptr;
+    int nseg = 0;
+    int K = 0, M = 0, ldy = 0;
+    int epilogue = 0;                 // EPI_STORE, EPI_ADD or EPI_SWIGLU (segments 0, 1 paired; output in seg[0].y)
+    const uint16_t* a = nullptr;      // prefill_quantise output [M][K]
+    const float* row_scale = nullptr;  // [M]
+    float* partial = nullptr;          // optional split-K workspace (STORE / ADD products)
+    size_t partial_floats = 0;
+    int* err = nullptr;
+};
+// y = (a * row_scale) . W^T over every segment, fp32 accumulation in TMEM.
+cudaError_t prefill_gemm(const PrefillGemmArgs& g, cudaStream_t s);
+// TMA maps of the GEMM's operands: a weight matrix's raw rows as 64-row
+// boxes (kPrefillWeightMaps maps written to out: one per Q4_K block or Q6_K
+// plane width); the fp16 activation operand as 64 x 128-row boxes, 128-byte
+// swizzle.
+constexpr int kPrefillWeightMaps = 3;
+cudaError_t make_weight_map(const uint8_t* w, int type, int K, int rows, KvTensorMap* out);
+cudaError_t make_act_map(const uint16_t* a, int K, int rows, KvTensorMap* out);
+// cuTensorMapEncodeTiled from the driver (nullptr if unavailable).
+void* tensor_map_encoder();
 cudaError_t make_kv_tensor_map(const uint16_t* base, long long rows, KvTensorMap* out);
 int decode_attention_splits(int kv_heads);
 size_t decode_attention_scratch_floats(int heads, int kv_heads, int splits);

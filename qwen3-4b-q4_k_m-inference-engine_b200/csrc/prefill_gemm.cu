@@ -1,0 +1,733 @@
+// Prompt-prefill products on the 5th-generation tensor cores (sm_100a).
+//
+// The reference's prefill pass multiplies all n prompt rows by each weight
+// matrix (matmul.cu:86-125 with rows = n): per 32 inputs, an integer dot of
+// Q8 activation codes with the 4-/6-bit weights, scaled by the activation
+// scale and the block's weight scales. Summed over the groups that is the
+// product of the Q8-dequantised activations (matmul.cu:8-22) with the
+// dequantised weights (embedding.cu:14-58), which is what runs here:
+//
+//   A  = fp16(code * scale / row_scale)   [M][K]  prefill_quantise
+//   B  = fp16((d*sc)*q - dmin*m)           [N][K]  dequantised per tile here
+//   y  = row_scale * (A . B^T)             fp32 accumulation in TMEM
+//
+// The rounding of A and B to fp16 (2^-11 relative) is the only departure from
+// the reference's arithmetic besides the summation order.
+//
+// One CTA computes 128 activation rows x 128 output columns (SwiGLU: 64 gate
+// and the same 64 up columns), K in 64-value stages:
+//   warp 0     TMA producer of the A boxes (128 rows x 64 fp16, 128-byte
+//              swizzle).
+//   warp 1     TMEM allocation; one thread issues 4 tcgen05.mma.kind::f16
+//              (M 128, N 128, K 16) per stage and commits each stage back to
+//              its empty barrier.
+//   warp 2     TMA producer of each super-block's raw weight rows (64-row
+//              boxes; Q6_K planes swizzled), after asking L2 for the CTA's
+//              whole weight slice.
+//   warps 3-18 dequantise each stage's weights into the K-major, 128-byte
+//              swizzled fp16 tile the MMA reads (thread: one row, 16 values),
+//              then the epilogue: tcgen05.ld of the accumulator, row scale,
+//              store / add / SwiGLU.
+// Every wait is bounded (kWaitLimitNs): on a timeout the kernel records an
+// error bit, drains what it issued and releases its TMEM.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+#include "gemv_device.cuh"
+#include "ops.h"
+#include "q4k_device.cuh"
+#include "q4k_format.h"
+#include "q4k_internal.h"
+
+namespace q4k {
+namespace {
+
+constexpr int BM = 128;                  // activation rows per CTA (MMA M)
+constexpr int BN = 128;                  // output columns per CTA (MMA N, TMEM columns)
+constexpr int KS = 64;                   // K per stage: one 128-byte swizzle row of fp16
+constexpr int kStagesA = 7;              // activation stages (L2 latency to cover)
+constexpr int kStagesB = 3;              // dequantised weight stages
+constexpr int kRawStages = 2;            // raw weight super-block stages (the slice is prefetched to L2)
+constexpr int kDeqWarps = 16;
+constexpr int kThreads = (3 + kDeqWarps) * 32;  // A producer, MMA, raw producer, dequant
+constexpr int kStageA = BM * KS * 2;                 // 16 KB
+constexpr int kStageB = BN * KS * 2;                 // 16 KB
+constexpr int kRawChunksQ4 = 9;                      // 144 B
+constexpr int kRawChunksQ6 = 14;                     // ql 128 B, qh 64 B, scales 16 B, d 16 B
+constexpr int kRawStage = kRawChunksQ6 * BN * 16;    // 28 KB
+constexpr int kOffB = kStagesA * kStageA;
+constexpr int kOffRaw = kOffB + kStagesB * kStageB;
+constexpr int kOffBars = kOffRaw + kRawStages * kRawStage;
+constexpr int kSmemBytes = kOffBars + 256 + 1024;    // barriers, TMEM slot, alignment slack
+
+struct Params {
+    int nseg;
+    int tile_start[4];  // first column tile of each segment; tile_start[nseg] = tiles
+    int rows[3], type[3];
+    int col_off[3];     // column of each segment in the split-K partials
+    float* y[3];
+    const uint8_t* w[3];
+    int K, nb, M, ldy, epilogue;
+    int splits;         // K ranges per tile (gridDim.z); > 1: partial sums to `partial`
+    int ntot;           // columns of a partial row (all segments)
+    float* partial;     // [splits][M][ntot]
+    const float* row_scale;
+    int* err;
+};
+
+// Raw weight maps per segment: Q4_K [0] = 144-byte rows; Q6_K [0] = ql
+// (128 B, 128-byte swizzle), [1] = qh (64 B, 64-byte swizzle), [2] = 16-byte
+// scale and d chunks. 64-row boxes.
+constexpr int kWeightMaps = 3;
+struct Maps {
+    CUtensorMap a;
+    CUtensorMap w[3][kWeightMaps];
+};
+
+// Raw stage layout (row r of the CTA's 128 weight rows):
+//   Q4_K  r * 144                      the block (header chunk, 8 nibble chunks)
+//   Q6_K  kQl + r * 128 (swizzled)     ql;  kQh + r * 64 (swizzled) qh;
+//         kSc + r * 16                 scales; kD + r * 16  d chunk
+constexpr int kQl = 0, kQh = 128 * BN, kSc = kQh + 64 * BN, kD = kSc + 16 * BN;
+static_assert(kD + 16 * BN <= kRawStage, "raw stage layout");
+
+// ---------------------------------------------------------------- tcgen05
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)), "r"(cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), version 1 (sm_100).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor of kind::f16: fp16 A and B (K-major), fp32 D,
+// M = BM, N = BN.
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrives on `bar` once every MMA this thread issued so far has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ uint4 ld16(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+__device__ __forceinline__ uint32_t byte_of(const uint4& v, int i) { return (word_of(v, i >> 2) >> (8 * (i & 3))) & 0xFFu; }
+
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Byte i of `q` (a value < 2^8) as an exact float: the bits 0x4B0000qq are
+// 2^23 + q.
+__device__ __forceinline__ float byte_plus_2p23(uint32_t q, int i) {
+    return __uint_as_float(__byte_perm(q, 0x4B000000u, 0x7440u + (uint32_t)i));
+}
+
+// Byte offset of 16-byte chunk c (0..7) of row r in a 128-row x 128-byte
+// tile with the 128-byte swizzle (the layout TMA writes and the MMA reads).
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+    return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+// Issue the raw bytes of super-block b for this CTA's 128 weight rows.
+__device__ __forceinline__ void load_raw(uint8_t* dst, const Params& p, const Maps& maps, int seg, int n0, bool pair,
+                                         int type, int b, uint64_t* bar) {
+    const int nb = p.nb;
+#pragma unroll 1
+    for (int hh = 0; hh < 2; ++hh) {
+        const CUtensorMap* m = maps.w[pair ? hh : seg];
+        const int y = pair ? n0 : n0 + 64 * hh;
+        if (type == Q4K_TYPE_Q4_K) {
+            tma_load_2d(dst + hh * 64 * 144, &m[0], b * 144, y, bar);
+        } else {
+            tma_load_2d(dst + kQl + hh * 64 * 128, &m[0], b * 128, y, bar);
+            tma_load_2d(dst + kQh + hh * 64 * 64, &m[1], nb * 128 + b * 64, y, bar);
+            tma_load_2d(dst + kSc + hh * 64 * 16, &m[2], nb * 192 + b * 16, y, bar);
+            tma_load_2d(dst + kD + hh * 64 * 16, &m[2], nb * 208 + (b >> 3) * 16, y, bar);
+        }
+    }
+}
+
+// Dequantise 16 values (quarter p of K-stage j of the super-block) of weight
+// row r into its row of the stage's B tile, in packed fp16 arithmetic:
+// each code byte q becomes the half 1024 + q by a byte permute with 0x64
+// (0x6400 | q), an exact subtraction gives q, then
+//   Q4_K  (embedding.cu:14-31): (q * sc) exact in fp16 (<= 945), times d,
+//         minus dmin * m (rounded to fp16 once), one rounding: fma
+//   Q6_K  (embedding.cu:42-58): (q - 32) * sc exact unless odd and above
+//         2048, times d.
+// Values k = 16p .. 16p+15 of the stage: 16-byte chunks 2p and 2p+1 of the
+// row's 128 bytes.
+__device__ __forceinline__ __half2 half2_bits(uint32_t v) { return *reinterpret_cast<const __half2*>(&v); }
+__device__ __forceinline__ uint32_t bits_half2(__half2 v) { return *reinterpret_cast<const uint32_t*>(&v); }
+
+__device__ __forceinline__ void dequant_q4(const uint8_t* raw, uint8_t* bt, int r, int p, int j) {
+    const uint8_t* blk = raw + r * 144;
+    const uint4 head = ld16(blk);
+    const int g = 2 * j + (p >> 1);  // 32-value group of the super-block
+    // 6-bit scale and min of group g (matmul.cu:40-47): bytes 4..15
+    uint32_t sc, mn;
+    if (g < 4) {
+        sc = byte_of(head, 4 + g) & 63;
+        mn = byte_of(head, 8 + g) & 63;
+    } else {
+        sc = (byte_of(head, 8 + g) & 15) | ((byte_of(head, g) >> 6) << 4);
+        mn = (byte_of(head, 8 + g) >> 4) | ((byte_of(head, 4 + g) >> 6) << 4);
+    }
+    const __half2 d2 = half2_bits((head.x & 0xFFFFu) * 0x10001u);
+    const __half2 sc2 = __float2half2_rn((float)sc);
+    const __half2 ndm2 = __float2half2_rn(-(half_bits_to_float(head.x >> 16) * (float)mn));
+    const __half2 k1024 = half2_bits(0x64006400u);
+    // nibbles of values 16(p&1) .. +15 of group g: bytes 16 + 32j + 16(p&1) .., low or high nibble
+    const uint4 nb = ld16(blk + 16 * (1 + 2 * j + (p & 1)));
+    const int shift = 4 * (p >> 1);
+    uint32_t o[8];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const uint32_t nib = (word_of(nb, t) >> shift) & 0x0F0F0F0Fu;
+        const __half2 q01 = __hsub2(half2_bits(__byte_perm(nib, 0x64646464u, 0x5140u)), k1024);
+        const __half2 q23 = __hsub2(half2_bits(__byte_perm(nib, 0x64646464u, 0x7362u)), k1024);
+        o[2 * t] = bits_half2(__hfma2(__hmul2(q01, sc2), d2, ndm2));
+        o[2 * t + 1] = bits_half2(__hfma2(__hmul2(q23, sc2), d2, ndm2));
+    }
+    *reinterpret_cast<uint4*>(bt + swz(r, 2 * p)) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(bt + swz(r, 2 * p + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+__device__ __forceinline__ void dequant_q6(const uint8_t* raw, uint8_t* bt, int r, int p, int j, int b) {
+    const uint4 dch = ld16(raw + kD + r * 16);
+    const uint32_t dbits = (word_of(dch, (b & 7) >> 1) >> (16 * (b & 1))) & 0xFFFFu;
+    const __half2 d2 = half2_bits(dbits * 0x10001u);
+    const uint4 scw = ld16(raw + kSc + r * 16);
+    const __half2 sc2 = __float2half2_rn((float)(int8_t)byte_of(scw, 4 * j + p));  // scale of these 16 values
+    // ql: bytes 64(j>>1) + 16p .. ; qh: bytes 32(j>>1) + 16(p&1) ..
+    const int cl = (j >> 1) * 4 + p, ch = (j >> 1) * 2 + (p & 1);  // ql chunk 0..7, qh chunk 0..3
+    const uint4 lq = ld16(raw + kQl + r * 128 + ((cl ^ (r & 7)) << 4));
+    const uint4 hq = ld16(raw + kQh + r * 64 + ((ch ^ ((r >> 1) & 3)) << 4));
+    const int s4 = 4 * (j & 1), s2 = 2 * (2 * (j & 1) + (p >> 1));
+    const __half2 k1056 = half2_bits(0x64206420u);  // 1024 + 32
+    uint32_t o[8];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const uint32_t q = ((word_of(lq, t) >> s4) & 0x0F0F0F0Fu) | (((word_of(hq, t) >> s2) & 0x03030303u) << 4);
+        const __half2 q01 = __hsub2(half2_bits(__byte_perm(q, 0x64646464u, 0x5140u)), k1056);
+        const __half2 q23 = __hsub2(half2_bits(__byte_perm(q, 0x64646464u, 0x7362u)), k1056);
+        o[2 * t] = bits_half2(__hmul2(__hmul2(q01, sc2), d2));
+        o[2 * t + 1] = bits_half2(__hmul2(__hmul2(q23, sc2), d2));
+    }
+    *reinterpret_cast<uint4*>(bt + swz(r, 2 * p)) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(bt + swz(r, 2 * p + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+// Lane 0 polls the barrier (one poller per warp keeps the barrier traffic
+// low); once it has seen the phase complete, every lane observes it with one
+// try_wait that succeeds at once.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+    bool ok = true;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait_bounded(bar, parity, err, code);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (ok) (void)mbar_try_wait(bar, parity);
+    return ok;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ Maps maps) {
+    extern __shared__ uint8_t smem_dyn[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
+    uint64_t* a_full = bars;
+    uint64_t* a_empty = a_full + kStagesA;
+    uint64_t* b_full = a_empty + kStagesA;
+    uint64_t* b_empty = b_full + kStagesB;
+    uint64_t* raw_full = b_empty + kStagesB;
+    uint64_t* raw_empty = raw_full + kRawStages;
+    uint64_t* done = raw_empty + kRawStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool pair = p.epilogue == EPI_SWIGLU;
+    const int tile = blockIdx.y, m0 = blockIdx.x * BM;
+    int seg = 0;
+    while (seg + 1 < p.nseg && tile >= p.tile_start[seg + 1]) ++seg;
+    if (pair) seg = 0;
+    const int n0 = (tile - p.tile_start[seg]) * (pair ? BN / 2 : BN);
+    const int type = p.type[seg];
+    // this CTA's super-blocks [b_begin, b_end) of the K range
+    const int split = blockIdx.z;
+    const int b_begin = split * p.nb / p.splits, b_end = (split + 1) * p.nb / p.splits;
+    const int nblk = b_end - b_begin;
+    const int nsteps = nblk * 4;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kStagesA; ++i) {
+            mbar_init(a_full + i, 1);
+            mbar_init(a_empty + i, 1);
+        }
+        for (int i = 0; i < kStagesB; ++i) {
+            mbar_init(b_full + i, kDeqWarps);
+            mbar_init(b_empty + i, 1);
+        }
+        for (int i = 0; i < kRawStages; ++i) {
+            mbar_init(raw_full + i, 1);
+            mbar_init(raw_empty + i, kDeqWarps);
+        }
+        mbar_init(done, 1);
+        mbar_fence_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, BN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- producer of the activation stages
+            int issued = 0;
+            for (int s = 0; s < nsteps; ++s) {
+                const int st = s % kStagesA;
+                if (!mbar_wait_bounded(a_empty + st, ((s / kStagesA) & 1) ^ 1, p.err, ERR_WAIT_TIMEOUT_EMPTY)) break;
+                mbar_arrive_expect_tx(a_full + st, kStageA);
+                tma_load_2d(smem + st * kStageA, &maps.a, (4 * b_begin + s) * KS, m0, a_full + st);
+                ++issued;
+            }
+            // every copy issued has landed before the CTA can exit (the last
+            // use of each stage is the latest phase of its barrier)
+            for (int s = issued - 1; s >= 0 && s >= issued - kStagesA; --s)
+                mbar_wait_bounded(a_full + s % kStagesA, (s / kStagesA) & 1, p.err, ERR_WAIT_TIMEOUT_FULL);
+        }
+        __syncwarp();
+    } else if (warp == 2) {
+        if (lane == 0) {
+            // ---------------- producer of the raw weight stages (a warp of
+            // its own: two spinning producers in one warp's divergent lanes
+            // starve each other)
+            const uint32_t raw_bytes = (type == Q4K_TYPE_Q4_K ? kRawChunksQ4 : kRawChunksQ6) * BN * 16;
+            int issued = 0;
+            for (int i = 0; i < nblk; ++i) {
+                const int rs = i % kRawStages;
+                if (!mbar_wait_bounded(raw_empty + rs, ((i / kRawStages) & 1) ^ 1, p.err, ERR_WAIT_TIMEOUT_EMPTY))
+                    break;
+                mbar_arrive_expect_tx(raw_full + rs, raw_bytes);
+                load_raw(smem + kOffRaw + rs * kRawStage, p, maps, seg, n0, pair, type, b_begin + i, raw_full + rs);
+                ++issued;
+            }
+            for (int i = issued - 1; i >= 0 && i >= issued - kRawStages; --i)
+                mbar_wait_bounded(raw_full + i % kRawStages, (i / kRawStages) & 1, p.err, ERR_WAIT_TIMEOUT_FULL);
+        } else {
+            // the rest of the warp asks L2 for this CTA's whole weight slice up
+            // front, so the raw stages find it there
+            const int row_bytes = (int)q4k_device_row_bytes(type, p.K);
+            for (int r = lane - 1; r < BN; r += 31) {
+                const int hh = r >> 6;
+                const int wrow = pair ? n0 + (r & 63) : n0 + r;
+                const int rows = p.rows[pair ? hh : seg];
+                if (wrow >= rows) continue;
+                const uint8_t* w = (pair ? p.w[hh] : p.w[seg]) + (size_t)wrow * row_bytes;
+                if (type == Q4K_TYPE_Q4_K) {
+                    l2_prefetch_bulk(w + b_begin * 144, (uint32_t)nblk * 144);
+                } else {
+                    l2_prefetch_bulk(w + b_begin * 128, (uint32_t)nblk * 128);
+                    l2_prefetch_bulk(w + p.nb * 128 + b_begin * 64, (uint32_t)nblk * 64);
+                    l2_prefetch_bulk(w + p.nb * 192 + b_begin * 16, (uint32_t)nblk * 16);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issue
+            for (int s = 0; s < nsteps; ++s) {
+                const int sa = s % kStagesA, sb = s % kStagesB;
+                if (!mbar_wait_bounded(a_full + sa, (s / kStagesA) & 1, p.err, ERR_WAIT_TIMEOUT_FULL)) break;
+                if (!mbar_wait_bounded(b_full + sb, (s / kStagesB) & 1, p.err, ERR_WAIT_TIMEOUT_FULL)) break;
+                tc_fence_after();
+                const uint32_t a_addr = smem_addr(smem + sa * kStageA);
+                const uint32_t b_addr = smem_addr(smem + kOffB + sb * kStageB);
+#pragma unroll
+                for (int kk = 0; kk < KS / 16; ++kk)
+                    mma_f16(tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), (s | kk) != 0);
+                tc_commit(a_empty + sa);
+                tc_commit(b_empty + sb);
+            }
+            tc_commit(done);  // also on an early exit: the epilogue and the TMEM release wait for it
+            mbar_wait_bounded(done, 0, p.err, ERR_WAIT_TIMEOUT_FULL);
+        }
+        __syncwarp();
+    } else {
+        // ---------------- dequantise, then the epilogue
+        const int t = (warp - 3) * 32 + lane, r = t & (BN - 1), part = t >> 7;
+        bool ok = true;
+        for (int i = 0; i < nblk && ok; ++i) {
+            const int rs = i % kRawStages, b = b_begin + i;
+            ok = warp_wait(raw_full + rs, (i / kRawStages) & 1, p.err, ERR_WAIT_TIMEOUT_FULL);
+            if (!ok) break;
+            const uint8_t* raw = smem + kOffRaw + rs * kRawStage;
+            for (int j = 0; j < 4; ++j) {
+                const int s = 4 * i + j, st = s % kStagesB;
+                ok = warp_wait(b_empty + st, ((s / kStagesB) & 1) ^ 1, p.err, ERR_WAIT_TIMEOUT_EMPTY);
+                if (!ok) break;
+                uint8_t* bt = smem + kOffB + st * kStageB;
+                if (type == Q4K_TYPE_Q4_K)
+                    dequant_q4(raw, bt, r, part, j);
+                else
+                    dequant_q6(raw, bt, r, part, j, b);
+                fence_proxy_async();  // generic stores -> the MMA's async-proxy reads
+                __syncwarp();
+                if (lane == 0) mbar_arrive(b_full + st);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(raw_empty + rs);
+        }
+        warp_wait(done, 0, p.err, ERR_WAIT_TIMEOUT_FULL);
+        tc_fence_after();
+        const int quad = warp & 3, cg = (warp - 3) >> 2;  // TMEM lanes 32 quad.., columns 32 cg..
+        const int row = 32 * quad + lane, m = m0 + row;
+        const float rsc = m < p.M ? p.row_scale[m] : 0.0f;
+        const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16);
+        const int rows = p.rows[seg];
+        // the stage buffers are free once `done` has fired: each warp turns
+        // its 32 x 32 block around in shared memory so that the global
+        // stores are whole row segments
+        float* st = reinterpret_cast<float*>(smem) + (warp - 3) * 32 * 33;
+        bool active = true;
+        int c0 = 32 * cg;
+        float v[32];
+        if (!pair || p.splits > 1) {
+            tmem_ld32(taddr + c0, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= rsc;
+        } else if (cg < 2) {
+            // SwiGLU: gate columns 0..63 and up columns 64..127 of the tile
+            float u[32];
+            tmem_ld32(taddr + c0, v);
+            tmem_ld32(taddr + BN / 2 + c0, u);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const float gv = v[i] * rsc, uv = u[i] * rsc;
+                v[i] = (gv / (1.0f + expf(-gv))) * uv;  // silu_multiply.cu:9-10
+            }
+        } else {
+            active = false;
+        }
+        if (active) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) st[lane * 33 + i] = v[i];
+            __syncwarp();
+            const int n = n0 + c0 + lane;
+            const bool col_ok = n < rows;
+            for (int r = 0; r < 32; ++r) {
+                const int mr = m0 + 32 * quad + r;
+                if (mr >= p.M || !col_ok) continue;
+                const float a = st[r * 33 + lane];
+                if (p.splits > 1) {
+                    // this K range's share, reduced in a fixed order by split_reduce_kernel
+                    p.partial[((size_t)split * p.M + mr) * p.ntot + p.col_off[seg] + n] = a;
+                } else {
+                    float* out = p.y[pair ? 0 : seg] + (size_t)mr * p.ldy + n;
+                    if (p.epilogue == EPI_ADD)
+                        *out += a;
+                    else
+                        *out = a;
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, BN);
+    }
+}
+
+// y (=, or += for EPI_ADD) the sum of the split-K partials, in split order.
+struct ReduceArgs {
+    const float* partial;
+    int splits, M, ntot, nseg, ldy, add;
+    int col_off[3];
+    float* y[3];
+};
+
+__global__ void __launch_bounds__(256) split_reduce_kernel(const ReduceArgs r) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)r.M * r.ntot) return;
+    const int m = (int)(i / r.ntot), c = (int)(i % r.ntot);
+    float acc = 0.0f;
+    for (int z = 0; z < r.splits; ++z) acc += r.partial[((size_t)z * r.M + m) * r.ntot + c];
+    const int seg = (r.nseg > 2 && c >= r.col_off[2]) ? 2 : (r.nseg > 1 && c >= r.col_off[1]) ? 1 : 0;
+    float* out = r.y[seg] + (size_t)m * r.ldy + (c - r.col_off[seg]);
+    if (r.add)
+        *out += acc;
+    else
+        *out = acc;
+}
+
+// Q8 codes of each row (matmul.cu:8-22) as fp16 code * (scale / row_scale).
+// One CTA per row; thread t holds elements 256 i + t, so warp w's lanes hold
+// 32-value group 8 i + w at step i and the row is read once.
+constexpr int kQuantMaxSteps = 40;  // K <= 10240
+
+__global__ void __launch_bounds__(256) prefill_quantise_kernel(const float* x, int ldx, const float* gamma, float eps,
+                                                               int K, __half* a, float* row_scale) {
+    const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float* xr = x + (size_t)m * ldx;
+    const int steps = K / 256;
+    __shared__ float red[8];
+    float v[kQuantMaxSteps];
+#pragma unroll
+    for (int i = 0; i < kQuantMaxSteps; ++i) v[i] = i < steps ? xr[256 * i + tid] : 0.0f;
+    if (gamma) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kQuantMaxSteps; ++i) ss += v[i] * v[i];
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        float total = 0.0f;
+        for (int i = 0; i < 8; ++i) total += red[i];
+        const float inv = rsqrtf(total / (float)K + eps);  // rms_norm.cu:17
+#pragma unroll
+        for (int i = 0; i < kQuantMaxSteps; ++i)
+            if (i < steps) v[i] = (v[i] * inv) * gamma[256 * i + tid];  // rms_norm.cu:19
+        __syncthreads();
+    }
+    float am[kQuantMaxSteps];
+    float wmax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kQuantMaxSteps; ++i) {
+        am[i] = warp_max(fabsf(v[i]));
+        wmax = fmaxf(wmax, am[i]);
+    }
+    if (lane == 0) red[warp] = wmax;
+    __syncthreads();
+    float rmax = 0.0f;
+    for (int i = 0; i < 8; ++i) rmax = fmaxf(rmax, red[i]);
+    const float S = rmax / 127.0f;  // the largest group scale (matmul.cu:18)
+#pragma unroll
+    for (int i = 0; i < kQuantMaxSteps; ++i) {
+        if (i >= steps) break;
+        bool near;
+        int8_t code = gemv_dev::q8_code_rn(v[i], __fdividef(127.0f, am[i]), near);
+        if (!gemv_dev::q8_fast_ok(am[i]) || near) code = gemv_dev::q8_code_exact(v[i], am[i]);
+        const float r = S > 0.0f ? __fdiv_rn(am[i] / 127.0f, S) : 0.0f;
+        a[(size_t)m * K + 256 * i + tid] = __float2half_rn((float)code * r);
+    }
+    if (tid == 0) row_scale[m] = S;
+}
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+}  // namespace
+
+cudaError_t prefill_quantise(const float* x, int ldx, const float* gamma, float eps, int M, int K, uint16_t* a,
+                             float* row_scale, cudaStream_t s) {
+    if (M <= 0 || K <= 0 || K % 256 || K / 256 > kQuantMaxSteps || ldx < K || !x || !a || !row_scale)
+        return cudaErrorInvalidValue;
+    prefill_quantise_kernel<<<M, 256, 0, s>>>(x, ldx, gamma, eps, K, reinterpret_cast<__half*>(a), row_scale);
+    return cudaGetLastError();
+}
+
+cudaError_t make_weight_map(const uint8_t* w, int type, int K, int rows, KvTensorMap* out) {
+    static_assert(sizeof(KvTensorMap) == sizeof(CUtensorMap), "tensor map storage size");
+    const EncodeTiled enc = reinterpret_cast<EncodeTiled>(tensor_map_encoder());
+    if (!enc) return cudaErrorNotSupported;
+    if (!w || reinterpret_cast<uintptr_t>(w) % 16 || rows <= 0 || K <= 0 || K % 256 ||
+        (type != Q4K_TYPE_Q4_K && type != Q4K_TYPE_Q6_K))
+        return cudaErrorInvalidValue;
+    const cuuint64_t row_bytes = q4k_device_row_bytes(type, K);
+    const cuuint64_t dims[2] = {row_bytes, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t estr[2] = {1, 1};
+    struct {
+        cuuint32_t width;
+        CUtensorMapSwizzle swizzle;
+    } kinds[kWeightMaps] = {{144, CU_TENSOR_MAP_SWIZZLE_NONE}, {0, CU_TENSOR_MAP_SWIZZLE_NONE},
+                            {0, CU_TENSOR_MAP_SWIZZLE_NONE}};
+    if (type == Q4K_TYPE_Q6_K) {
+        kinds[0] = {128, CU_TENSOR_MAP_SWIZZLE_128B};
+        kinds[1] = {64, CU_TENSOR_MAP_SWIZZLE_64B};
+        kinds[2] = {16, CU_TENSOR_MAP_SWIZZLE_NONE};
+    }
+    for (int i = 0; i < kWeightMaps; ++i) {
+        CUtensorMap map;
+        std::memset(&map, 0, sizeof map);
+        if (kinds[i].width) {
+            const cuuint32_t box[2] = {kinds[i].width, 64};
+            if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, kinds[i].swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+                return cudaErrorInvalidValue;
+        }
+        std::memcpy(&out[i], &map, sizeof map);
+    }
+    return cudaSuccess;
+}
+
+cudaError_t make_act_map(const uint16_t* a, int K, int rows, KvTensorMap* out) {
+    const EncodeTiled enc = reinterpret_cast<EncodeTiled>(tensor_map_encoder());
+    if (!enc) return cudaErrorNotSupported;
+    if (!a || reinterpret_cast<uintptr_t>(a) % 16 || rows <= 0 || K <= 0 || K % 256) return cudaErrorInvalidValue;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {KS, BM};
+    const cuuint32_t estr[2] = {1, 1};
+    CUtensorMap map;
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(a), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    std::memcpy(out, &map, sizeof map);
+    return cudaSuccess;
+}
+
+cudaError_t prefill_gemm(const PrefillGemmArgs& g, cudaStream_t s) {
+    const bool pair = g.epilogue == EPI_SWIGLU;
+    if (g.nseg < 1 || g.nseg > 3 || g.K <= 0 || g.K % 256 || g.M <= 0 || g.ldy <= 0 || !g.a || !g.row_scale ||
+        (g.epilogue != EPI_STORE && g.epilogue != EPI_ADD && !pair))
+        return cudaErrorInvalidValue;
+    if (pair && (g.nseg != 2 || g.seg[0].type != g.seg[1].type || g.seg[0].rows != g.seg[1].rows))
+        return cudaErrorInvalidValue;
+    Params p{};
+    Maps maps;
+    p.nseg = g.nseg;
+    p.K = g.K;
+    p.nb = g.K / 256;
+    p.M = g.M;
+    p.ldy = g.ldy;
+    p.epilogue = g.epilogue;
+    p.row_scale = g.row_scale;
+    p.err = g.err;
+    int tiles = 0, ntot = 0;
+    for (int i = 0; i < g.nseg; ++i) {
+        const PrefillGemmSegment& sg = g.seg[i];
+        p.col_off[i] = ntot;
+        ntot += sg.rows;
+        p.w[i] = sg.w;
+        if (!sg.w || sg.rows <= 0 || (!sg.y && !(pair && i == 1)) || (sg.type != Q4K_TYPE_Q4_K && sg.type != Q4K_TYPE_Q6_K))
+            return cudaErrorInvalidValue;
+        p.rows[i] = sg.rows;
+        p.type[i] = sg.type;
+        p.y[i] = sg.y;
+        p.tile_start[i] = tiles;
+        if (!pair || i == 0) tiles += (sg.rows + (pair ? BN / 2 : BN) - 1) / (pair ? BN / 2 : BN);
+        KvTensorMap m[kWeightMaps];
+        const KvTensorMap* src = g.wmap[i];
+        if (!src) {
+            const cudaError_t e = make_weight_map(sg.w, sg.type, g.K, sg.rows, m);
+            if (e != cudaSuccess) return e;
+            src = m;
+        }
+        std::memcpy(&maps.w[i][0], src, sizeof(CUtensorMap) * kWeightMaps);
+    }
+    for (int i = g.nseg; i < 3; ++i) std::memset(&maps.w[i][0], 0, sizeof(CUtensorMap) * kWeightMaps);
+    for (int i = g.nseg; i < 4; ++i) p.tile_start[i] = tiles;
+    if (g.amap) {
+        std::memcpy(&maps.a, g.amap, sizeof(CUtensorMap));
+    } else {
+        KvTensorMap m;
+        const cudaError_t e = make_act_map(g.a, g.K, g.M, &m);
+        if (e != cudaSuccess) return e;
+        std::memcpy(&maps.a, &m, sizeof m);
+    }
+    static std::once_flag once;
+    static cudaError_t attr = cudaSuccess;
+    std::call_once(once, [] {
+        attr = cudaFuncSetAttribute(prefill_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    });
+    if (attr != cudaSuccess) return attr;
+    // Split K when the tiles alone leave SMs idle (deterministic: partial sums
+    // reduced in split order); each split keeps at least two super-blocks.
+    const int mtiles = (g.M + BM - 1) / BM;
+    const int ctas = mtiles * tiles;
+    int splits = 1;
+    if (!pair && g.partial && ctas < sm_count()) {
+        splits = std::max(1, std::min((sm_count() + ctas / 2) / ctas, std::min(16, p.nb / 2)));
+        while (splits > 1 && (size_t)splits * g.M * ntot > g.partial_floats) --splits;
+    }
+    p.splits = splits;
+    p.ntot = ntot;
+    p.partial = g.partial;
+    const dim3 grid(mtiles, tiles, splits);
+    prefill_gemm_kernel<<<grid, kThreads, kSmemBytes, s>>>(p, maps);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || splits == 1) return e;
+    ReduceArgs r;
+    r.partial = g.partial;
+    r.splits = splits;
+    r.M = g.M;
+    r.ntot = ntot;
+    r.nseg = g.nseg;
+    r.ldy = g.ldy;
+    r.add = g.epilogue == EPI_ADD;
+    for (int i = 0; i < 3; ++i) {
+        r.col_off[i] = i < g.nseg ? p.col_off[i] : ntot;
+        r.y[i] = i < g.nseg ? g.seg[i].y : nullptr;
+    }
+    const size_t n = (size_t)g.M * ntot;
+    split_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(r);
+    return cudaGetLastError();
+}
+
+}  // namespace q4k

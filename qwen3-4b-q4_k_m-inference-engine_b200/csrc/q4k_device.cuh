@@ -66,16 +66,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Waits for the barrier phase with the given parity to complete; returns
 // false (and records `code` in *err) if it has not after kWaitLimitNs.
+// %globaltimer is slow to read (hundreds of ns), so it is read only every
+// 64 polls: a wake-up is never delayed behind a clock read.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err, int code) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t start = global_timer_ns();
-    while (!mbar_try_wait(bar, parity)) {
-        if (global_timer_ns() - start > kWaitLimitNs) {
-            if (err) atomicOr(err, code);
-            return false;
+    uint64_t start = 0;
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63) == 0) {
+            const uint64_t now = global_timer_ns();
+            if (start == 0) {
+                start = now;
+            } else if (now - start > kWaitLimitNs) {
+                if (err) atomicOr(err, code);
+                return false;
+            }
         }
     }
-    return true;
 }
 
 // One bulk copy global -> shared, completing `bytes` of transaction count on

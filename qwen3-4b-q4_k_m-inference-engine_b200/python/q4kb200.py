@@ -25,7 +25,7 @@ EXPORTS = (
     "q4k_last_error", "q4k_abi_version", "q4k_weight_device_bytes", "q4k_weight_upload", "q4k_synth_tensor_host",
     "q4k_synth_tensor_device", "q4k_synth_f16_host", "q4k_synth_f32_host", "q4k_synth_f32_device", "q4k_rms_norm",
     "q4k_matmul", "q4k_rope", "q4k_attention", "q4k_residual_add", "q4k_silu_multiply", "q4k_dequantize_embeddings",
-    "q4k_argmax", "q4k_matmul_ex", "q4k_matmul_argmax_scratch_bytes", "q4k_attention_decode_f16",
+    "q4k_argmax", "q4k_matmul_ex", "q4k_matmul_batch", "q4k_matmul_argmax_scratch_bytes", "q4k_attention_decode_f16",
     "q4k_attention_decode_scratch_bytes", "q4k_engine_config_qwen3_4b", "q4k_model_tensor", "q4k_nccl_unique_id",
     "q4k_engine_create", "q4k_engine_destroy", "q4k_engine_load_synthetic", "q4k_engine_set_tensor",
     "q4k_engine_fill_kv_synthetic", "q4k_engine_read_kv", "q4k_engine_decode", "q4k_engine_prefill", "q4k_engine_generate",
@@ -90,6 +90,7 @@ def lib():
             "q4k_argmax": ([P, S, C.POINTER(C.c_uint32), P], I),
             "q4k_matmul_ex": ([P, P, C.c_float, I, P, P, P, P, I64, S, I, P, P, P], I),
             "q4k_matmul_argmax_scratch_bytes": ([], S),
+            "q4k_matmul_batch": ([P, P, C.c_float, I, P, P, P, P, I64, I64, S, I, P], I),
             "q4k_attention_decode_f16": ([P, P, P, P, P, I, P, I, I, I, C.c_float, C.c_float, P, P, P], I),
             "q4k_attention_decode_f16_static": ([P, P, P, P, P, I, P, I, I, I, C.c_float, C.c_float, P, P], I),
             "q4k_attention_decode_scratch_bytes": ([I, I], S),

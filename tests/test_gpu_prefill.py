@@ -18,9 +18,67 @@ import oracle as o
 import q4kb200 as q
 from conftest import rel_l2
 from test_gpu_engine import full_model, greedy_ok, kv_f32, oracle_model  # noqa: F401 (fixture)
+from test_gpu_kernels import dev
 from tiny_model import SEED, TINY, engine_config, tiny_tensors
 
 pytestmark = pytest.mark.gpu
+
+
+def upload(cuda, qt, K, N, raw):
+    buf = cuda.empty(max(q.device_bytes(qt, K, N), 16), dtype=cuda.uint8, device="cuda")
+    q.check(q.lib().q4k_weight_upload(qt, K, N, q.hptr(np.ascontiguousarray(raw)), buf.data_ptr(), None))
+    return buf
+
+
+# (types, K, output rows per weight, activation rows, epilogue, RMSNorm first)
+BATCH_CASES = {
+    "q4k_two_row_tiles": ([q.Q4_K], 2560, [384], 130, q.EPI_STORE, False),
+    "q6k_ragged_columns": ([q.Q6_K], 2560, [200], 23, q.EPI_STORE, True),
+    "q6k_down_add": ([q.Q6_K], 9728, [256], 20, q.EPI_ADD, False),
+    "q4k_down_add": ([q.Q4_K], 9728, [128], 5, q.EPI_ADD, False),
+    "qkv_segments": ([q.Q4_K, q.Q4_K, q.Q6_K], 2560, [512, 128, 128], 70, q.EPI_STORE, True),
+    "swiglu_pairs": ([q.Q4_K, q.Q4_K], 2560, [192, 192], 129, q.EPI_SWIGLU, True),
+    "one_row": ([q.Q4_K], 4096, [128], 1, q.EPI_STORE, False),
+}
+
+
+@pytest.mark.parametrize("case", list(BATCH_CASES))
+def test_matmul_batch_matches_oracle(cuda, case):
+    """q4k_matmul_batch (tensor cores) against the oracle's integer products
+    (MatmulReference semantics) on the same rows: 1e-3 relative L2 per
+    output, the per-layer bar; columns past each output stay untouched."""
+    types, K, outs, M, epi, norm = BATCH_CASES[case]
+    raws = [q.synth_tensor_host(31 + i, f"mb.{case}.{i}", t, K, n) for i, (t, n) in enumerate(zip(types, outs))]
+    Ws = [upload(cuda, t, K, n, r) for t, n, r in zip(types, outs, raws)]
+    x = q.synth_f32_host(5, f"mb.x.{case}", M * K)
+    gamma = q.synth_tensor_host(5, f"mb.g.{case}", q.F32, K, 1) if norm else None
+    xin = o.rms_norm(x, gamma, K, 1e-6) if norm else x
+    prods = [o.matmul(xin, r, t, K, n).reshape(M, n).astype(np.float32) for t, n, r in zip(types, outs, raws)]
+    if epi == q.EPI_SWIGLU:
+        wants = [o.silu_multiply(prods[0], prods[1]).reshape(M, outs[0])]
+        widths = [outs[0]]
+    else:
+        wants, widths = prods, outs
+    ld = sum(widths) + 8
+    base = q.synth_f32_host(6, f"mb.y.{case}", M * ld).reshape(M, ld)
+    y = dev(cuda, base)
+    offs = np.concatenate([[0], np.cumsum(widths)])[:-1]
+    outs_p = [y.data_ptr() + 4 * int(off) for off in offs]
+    if epi == q.EPI_SWIGLU:
+        outs_p = [outs_p[0], outs_p[0]]
+    n = len(types)
+    q.check(q.lib().q4k_matmul_batch(dev(cuda, x).data_ptr(), dev(cuda, gamma).data_ptr() if norm else None, 1e-6, n,
+                                     (C.c_void_p * n)(*[w.data_ptr() for w in Ws]), (C.c_int * n)(*types),
+                                     (C.c_int64 * n)(*outs), (C.c_void_p * n)(*outs_p), ld, K, M, epi, None))
+    got = y.cpu().numpy()
+    for want, off, w in zip(wants, offs, widths):
+        part = got[:, off : off + w]
+        if epi == q.EPI_ADD:
+            part = part - base[:, off : off + w]  # the product added to what was there
+        e = rel_l2(part, want)
+        print(f"{case}: rel-L2 {e:.2e}")
+        assert e < 1e-3, (case, off, e)
+    assert np.array_equal(got[:, sum(widths) :], base[:, sum(widths) :])  # columns past the outputs
 
 
 def tiny_engine(cap):
@@ -38,7 +96,15 @@ def kv_rows(eng, layer, kv_heads, cap, n0, n1):
     return k, v
 
 
-def test_tiny_prefill_matches_oracle(cuda):
+@pytest.fixture(params=["gemm", "gemv"])
+def products(request, monkeypatch):
+    """Both forms of the prompt products: the tensor-core GEMM (default) and
+    the batched dp4a GEMV (Q4K_PREFILL_GEMM=0)."""
+    monkeypatch.setenv("Q4K_PREFILL_GEMM", "1" if request.param == "gemm" else "0")
+    return request.param
+
+
+def test_tiny_prefill_matches_oracle(cuda, products):
     """A 7-token prompt into an empty cache, a 3-token prompt continuing it
     (its rows attend to the first prompt's cache rows), then a decode step on
     the cache prefill wrote: logits, greedy token and every K/V row."""
@@ -57,11 +123,18 @@ def test_tiny_prefill_matches_oracle(cuda):
         assert rel_l2(got_logits, want_logits) < 1e-2, pos
         assert greedy_ok(got_next, want_next, want_logits, got_logits), pos
         pos += len(prompt)
+    # Layer 0's K/V rows come from the embedding through one product each: the
+    # integer-exact GEMV matches to 1e-4, the GEMM's fp16 operands (3e-4 per
+    # product, test_matmul_batch_matches_oracle) to 1e-3. Later layers see
+    # both amplified ~40x by the Q8 code flips of the synthetic model's large
+    # residual stream (the same factor on both paths): the whole-step bar.
     for layer in range(L):
         k, v = kv_rows(eng, layer, KVH, cap, 0, pos)
         ko = kc.reshape(L, cap, KVH, 128)[layer, :pos].transpose(1, 0, 2)
         vo = vc.reshape(L, cap, KVH, 128)[layer, :pos].transpose(1, 0, 2)
-        assert rel_l2(k, ko) < 1e-2 and rel_l2(v, vo) < 1e-2, layer
+        bar = (1e-3 if products == "gemm" else 1e-4) if layer == 0 else 5e-2
+        print(f"[{products}] layer {layer} K/V rows rel-L2 {rel_l2(k, ko):.2e} {rel_l2(v, vo):.2e}")
+        assert rel_l2(k, ko) < bar and rel_l2(v, vo) < bar, layer
     # decoding continues on the rows prefill wrote
     tok = want_next
     want_next, want_logits, _ = model.forward(kc, vc, cap, [tok], pos, kv_round_f16=True, want_hidden=False)
@@ -71,7 +144,7 @@ def test_tiny_prefill_matches_oracle(cuda):
     eng.close()
 
 
-def test_tiny_prefill_passes_bit_identical(cuda, monkeypatch):
+def test_tiny_prefill_passes_bit_identical(cuda, monkeypatch, products):
     """A prompt split over several prefill passes (Q4K_PREFILL_ROWS rows
     each, the last one ragged) computes what one pass does, bit for bit:
     a row's products and attention do not depend on the other rows of its

@@ -568,7 +568,9 @@ def run_prefill(args, world, rank, local):
                          "traffic": None, "algorithmic_flops": flops, "launch_us": round(launch * 1e6, 2)},
             "e2e": {"value": round(n / wall, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * n, "d2h_bytes_per_step": 8,
                     "how": "q4k_engine_prefill per prompt from host token ids, host wall clock"},
-            "gpu_launches": steps * (36 * 10 + 4)}
+            # per 512-row prompt: embed; per layer 4 x (quantise + GEMM), 2 split-K
+            # reduces (O, down), QK-norm/RoPE, attention; head GEMV; finish
+            "gpu_launches": steps * (1 + 36 * 12 + 2)}
 
 
 def run_reference(args, world, rank):

@@ -191,6 +191,11 @@ typedef struct {
     int capacity; /* KV-cache positions */
     int tp_rank, tp_world;
     int device;
+    /* Independent KV caches (sequences; ChatSession.hpp:10-52 each) the
+     * engine holds; 0 or 1: one. The single-sequence calls work on
+     * sequence 0; q4k_engine_prefill_seq and q4k_engine_decode_batch
+     * address any of them. */
+    int sequences;
 } q4k_engine_config;
 
 /* Qwen3-4B: 36 layers, 2560 hidden, 32/8 heads of 128, ffn 9728, vocab
@@ -254,6 +259,21 @@ int q4k_engine_decode(q4k_engine* engine, uint32_t token, int position, uint32_t
  * and position + n > capacity are Q4K_ERANGE. Synchronous. */
 int q4k_engine_prefill(q4k_engine* engine, const uint32_t* tokens, int n, int position, uint32_t* next_token,
                        float* logits_host);
+
+/* q4k_engine_prefill into sequence `seq` (0 <= seq < sequences). */
+int q4k_engine_prefill_seq(q4k_engine* engine, int seq, const uint32_t* tokens, int n, int position,
+                           uint32_t* next_token, float* logits_host);
+
+/* One decode step for n tokens of n distinct sequences at once (the
+ * reference serves one session per Engine::inference call; batching many
+ * sequences into one step reads every weight once for all of them):
+ * tokens[i] is embedded at positions[i] of sequence seqs[i]; next_tokens[i]
+ * receives its greedy successor. The products run over all n rows (the
+ * batched GEMV up to 8 rows, the tensor-core GEMM above), attention over
+ * each sequence's own cache. logits_host (n x vocab floats) may be NULL.
+ * tp_world == 1; 1 <= n <= sequences. Synchronous. */
+int q4k_engine_decode_batch(q4k_engine* engine, int n, const int* seqs, const uint32_t* tokens, const int* positions,
+                            uint32_t* next_tokens, float* logits_host);
 
 /* `steps` greedy decode steps with the token fed back on the device; one
  * graph launch per step and no host synchronisation between steps.

@@ -65,6 +65,9 @@ struct Args {
     int trace_tag;
     L2Prefetch prefetch[kMaxPrefetch];  // the next kernel's operands, after this CTA's first tiles
     ActImage out_image;                 // optional: the output quantised for the O product
+    const int* seq_of;                  // batched decode: sequence of each token (nullptr: z)
+    int ld_qkv;                         // floats between the tokens' projections
+    long long seq_cache_elems;          // fp16 elements between sequences' caches
 };
 
 struct SmemTail {
@@ -89,9 +92,21 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
     SmemTail& sm = *reinterpret_cast<SmemTail*>(smem + S * kStageBytes);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x, kvh = blockIdx.y, splits = gridDim.x;
-    if (threadIdx.x == 0) trace_at(a.trace, a.trace_tag, 0);
+    // Batched decode: block z serves the z-th token of the step, in sequence
+    // seq_of[z] (z without a map): its projections, output, position and
+    // split partials are row z of theirs, its cache that sequence's.
+    const int z = blockIdx.z;
+    const int sq = a.seq_of ? a.seq_of[z] : z;
+    const float* qkv = a.qkv + (size_t)z * a.ld_qkv;
+    uint16_t* k_cache = a.k_cache + (size_t)sq * a.seq_cache_elems;
+    uint16_t* v_cache = a.v_cache + (size_t)sq * a.seq_cache_elems;
+    float* partial_o = a.partial_o + (size_t)z * a.heads * splits * D;
+    float* partial_ml = a.partial_ml + (size_t)z * a.heads * splits * 2;
+    unsigned* counters = a.counters + (size_t)z * a.kv_heads;
+    unsigned long long* trace = z == 0 ? a.trace : nullptr;
+    if (threadIdx.x == 0) trace_at(trace, a.trace_tag, 0);
 
-    const int pos = *a.position;
+    const int pos = a.position[z];
     if (pos < 0 || pos >= a.capacity) {
         if (tid == 0 && split == 0 && kvh == 0 && a.err) atomicOr(a.err, ERR_BAD_POSITION);
         return;
@@ -100,7 +115,8 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
     const int chunk = (n_keys + splits - 1) / splits;
     const int p0 = min(split * chunk, n_keys), p1 = min(p0 + chunk, n_keys);
     const int tiles = (p1 - p0 + T - 1) / T;
-    const int row0 = a.row_base + kvh * a.capacity;  // tensor-map row of (kvh, position 0)
+    // tensor-map row of (kvh, position 0) in this sequence's cache
+    const int row0 = a.row_base + sq * (int)(a.seq_cache_elems / D) + kvh * a.capacity;
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
@@ -127,18 +143,18 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
                 tma_load_2d(st + kTileBytes, &vmap, 0, y, &sm.full[s]);
                 tma_load_2d(st + kTileBytes + kBox, &vmap, 64, y, &sm.full[s]);
                 if (t == min(S, tiles) - 1)
-                    issue_l2_prefetch(a.prefetch, split + splits * kvh, splits * gridDim.y);
+                    if (z == 0) issue_l2_prefetch(a.prefetch, split + splits * kvh, splits * gridDim.y);
             }
-            if (tiles == 0) issue_l2_prefetch(a.prefetch, split + splits * kvh, splits * gridDim.y);
+            if (tiles == 0) if (z == 0) issue_l2_prefetch(a.prefetch, split + splits * kvh, splits * gridDim.y);
         }
         return;
     }
 
     // ---------------- compute warps: q (and the new k/v) of this token ----------------
     const size_t head_base = (size_t)kvh * a.capacity * D;
-    const float* q_raw = a.qkv + (size_t)kvh * G * D;
-    const float* k_raw = a.qkv + (size_t)a.heads * D + (size_t)kvh * D;
-    const float* v_raw = a.qkv + (size_t)a.heads * D + (size_t)a.kv_heads * D + (size_t)kvh * D;
+    const float* q_raw = qkv + (size_t)kvh * G * D;
+    const float* k_raw = qkv + (size_t)a.heads * D + (size_t)kvh * D;
+    const float* v_raw = qkv + (size_t)a.heads * D + (size_t)a.kv_heads * D + (size_t)kvh * D;
     const bool owner = pos >= p0 && pos < p1;
     {
         // Thread t handles pair (j, j + 64) of head h = t / 64 (4 heads x 64 pairs).
@@ -182,10 +198,10 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
             sm.v_new[j] = v0;
             sm.v_new[j + 64] = v1;
             const size_t at = head_base + (size_t)pos * D;
-            a.k_cache[at + j] = k0;
-            a.k_cache[at + j + 64] = k1;
-            a.v_cache[at + j] = v0;
-            a.v_cache[at + j + 64] = v1;
+            k_cache[at + j] = k0;
+            k_cache[at + j + 64] = k1;
+            v_cache[at + j] = v0;
+            v_cache[at + j + 64] = v1;
         }
         named_barrier(1, kComputeThreads);
     }
@@ -204,7 +220,7 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
         sm.qf[s][l] = f;
     }
     named_barrier(1, kComputeThreads);
-    if (tid == 0) trace_at(a.trace, a.trace_tag, 1);
+    if (tid == 0) trace_at(trace, a.trace_tag, 1);
 
     // ---------------- tiles: this warp owns tile rows [8w, 8w + 8) ----------------
     const float scale = rsqrtf((float)D);  // attention.cu:40
@@ -219,7 +235,7 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
         // A warp whose wait gave up flags the CTA; every warp still reaches the
         // end-of-tile barrier, after which all leave together.
         const bool landed = mbar_wait_bounded(&sm.full[s], use & 1, a.err, ERR_WAIT_TIMEOUT_FULL);
-        if (tid == 0 && (t == 0 || t == tiles - 1)) trace_at(a.trace, a.trace_tag, t == 0 ? 2 : 3);
+        if (tid == 0 && (t == 0 || t == tiles - 1)) trace_at(trace, a.trace_tag, t == 0 ? 2 : 3);
         if (!__all_sync(0xffffffffu, landed) && lane == 0) sm.abort[t & 1] = 1;
         const int lo = p0 + t * T;
         const int n = min(T, p1 - lo);
@@ -345,37 +361,37 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
 
     // ---------------- partials and the cross-split merge ----------------
     const size_t pidx = ((size_t)kvh * splits + split) * G + hq;
-    a.partial_o[pidx * D + d0] = acc0;
-    a.partial_o[pidx * D + d0 + 1] = acc1;
+    partial_o[pidx * D + d0] = acc0;
+    partial_o[pidx * D + d0 + 1] = acc1;
     if ((tid & 63) == 0) {
-        a.partial_ml[pidx * 2 + 0] = M;
-        a.partial_ml[pidx * 2 + 1] = L;
+        partial_ml[pidx * 2 + 0] = M;
+        partial_ml[pidx * 2 + 1] = L;
     }
     __threadfence();
     named_barrier(1, kComputeThreads);
-    if (tid == 0) trace_at(a.trace, a.trace_tag, 4);
-    if (tid == 0) sm.last = atomicAdd(a.counters + kvh, 1u) == (unsigned)(splits - 1);
+    if (tid == 0) trace_at(trace, a.trace_tag, 4);
+    if (tid == 0) sm.last = atomicAdd(counters + kvh, 1u) == (unsigned)(splits - 1);
     named_barrier(1, kComputeThreads);
     if (!sm.last) {
-        if (tid == 0) trace_at(a.trace, a.trace_tag, 7);
+        if (tid == 0) trace_at(trace, a.trace_tag, 7);
         return;
     }
     __threadfence();
-    if (tid == 0) trace_at(a.trace, a.trace_tag, 3);  // the merging CTA: last arrival seen
+    if (tid == 0) trace_at(trace, a.trace_tag, 3);  // the merging CTA: last arrival seen
     // The merge is on the critical path of the step: the o partials of the
     // first kBatch splits are loaded in the same round trip as every
     // split's (m, l) (into shared memory; the stage buffers are free).
     constexpr int kBatch = 24;
-    const float2* po = reinterpret_cast<const float2*>(a.partial_o + ((size_t)kvh * splits * G + hq) * D + d0);
+    const float2* po = reinterpret_cast<const float2*>(partial_o + ((size_t)kvh * splits * G + hq) * D + d0);
     float2 v[kBatch];
 #pragma unroll
     for (int u = 0; u < kBatch; ++u)
         v[u] = u < splits ? __ldcg(po + (size_t)u * (G * D / 2)) : make_float2(0.0f, 0.0f);
     float* mls = reinterpret_cast<float*>(smem);  // [splits][G][2]
-    const float* ml_head = a.partial_ml + (size_t)kvh * splits * G * 2;
+    const float* ml_head = partial_ml + (size_t)kvh * splits * G * 2;
     for (int i = tid; i < splits * G * 2; i += kComputeThreads) mls[i] = __ldcg(ml_head + i);
     named_barrier(1, kComputeThreads);
-    if (tid == 0) trace_at(a.trace, a.trace_tag, 5);
+    if (tid == 0) trace_at(trace, a.trace_tag, 5);
     float MM = -CUDART_INF_F;
     for (int sp = 0; sp < splits; ++sp)
         MM = fmaxf(MM, mls[(sp * G + hq) * 2 + 1] > 0.0f ? mls[(sp * G + hq) * 2] : -CUDART_INF_F);
@@ -397,7 +413,7 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
             o1 = live ? o1 + v[u].y * f : o1;
         }
     }
-    float* out = a.out + ((size_t)kvh * G + hq) * D;
+    float* out = a.out + (size_t)z * a.heads * D + ((size_t)kvh * G + hq) * D;
     out[d0] = o0 / LL;
     out[d0 + 1] = o1 / LL;
     if (a.out_image.base) {
@@ -409,9 +425,9 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
                                 img.xsum16, img.xsum32, lane);
     }
     if (tid == 0) {
-        a.counters[kvh] = 0u;
-        trace_at(a.trace, a.trace_tag, 6);  // slot 6 marks the merging CTA
-        trace_at(a.trace, a.trace_tag, 7);
+        counters[kvh] = 0u;
+        trace_at(trace, a.trace_tag, 6);  // slot 6 marks the merging CTA
+        trace_at(trace, a.trace_tag, 7);
     }
 }
 
@@ -499,6 +515,10 @@ cudaError_t decode_attention(const DecodeAttnArgs& in, const KvTensorMap& kmap, 
     for (int e = 0; e < kMaxPrefetch; ++e) a.prefetch[e] = in.prefetch[e];
     a.out_image = in.out_image;
     if (a.out_image.base && (a.out_image.K != in.heads * D || a.out_image.K % 256 != 0)) return cudaErrorInvalidValue;
+    a.seq_of = in.seq_of;
+    a.ld_qkv = in.ld_qkv;
+    a.seq_cache_elems = in.seq_cache_elems;
+    if (in.batch < 1 || (in.batch > 1 && (a.out_image.base || in.ld_qkv <= 0))) return cudaErrorInvalidValue;
     a.stages = 3;
     const size_t smem = smem_bytes(a.stages);
     static std::once_flag once;
@@ -512,7 +532,7 @@ cudaError_t decode_attention(const DecodeAttnArgs& in, const KvTensorMap& kmap, 
     std::memcpy(&km, &kmap, sizeof km);
     std::memcpy(&vm, &vmap, sizeof vm);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(in.splits, in.kv_heads);
+    cfg.gridDim = dim3(in.splits, in.kv_heads, in.batch);
     cfg.blockDim = dim3(kComputeThreads + 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;

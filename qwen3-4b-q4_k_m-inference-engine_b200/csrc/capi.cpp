@@ -70,7 +70,7 @@ void check_matrix(int type, int64_t ne0, int64_t ne1) {
 
 Q4K_API const char* q4k_last_error(void) { return g_last_error.c_str(); }
 
-Q4K_API int q4k_abi_version(void) { return 1; }
+Q4K_API int q4k_abi_version(void) { return 2; }
 
 Q4K_API size_t q4k_weight_device_bytes(int type, int64_t ne0, int64_t ne1) {
     if (ne0 <= 0 || ne1 <= 0) return 0;
@@ -726,6 +726,22 @@ Q4K_API int q4k_engine_prefill(q4k_engine* e, const uint32_t* tokens, int n, int
     return guarded_cuda([&] {
         if (!e || !next_token || !tokens) invalid("engine, tokens and output required");
         *next_token = e->impl.prefill(tokens, n, position, logits_host);
+    });
+}
+
+Q4K_API int q4k_engine_prefill_seq(q4k_engine* e, int seq, const uint32_t* tokens, int n, int position,
+                                   uint32_t* next_token, float* logits_host) {
+    return guarded_cuda([&] {
+        if (!e || !next_token || !tokens) invalid("engine, tokens and output required");
+        *next_token = e->impl.prefill(tokens, n, position, logits_host, seq);
+    });
+}
+
+Q4K_API int q4k_engine_decode_batch(q4k_engine* e, int n, const int* seqs, const uint32_t* tokens,
+                                    const int* positions, uint32_t* next_tokens, float* logits_host) {
+    return guarded_cuda([&] {
+        if (!e || !seqs || !tokens || !positions || !next_tokens) invalid("engine, inputs and outputs required");
+        e->impl.decode_batch(n, seqs, tokens, positions, next_tokens, logits_host);
     });
 }
 

@@ -19,6 +19,7 @@
 #include "engine.h"
 
 #include <cuda_runtime.h>
+#include <math_constants.h>
 
 #include <dlfcn.h>
 
@@ -99,6 +100,43 @@ __global__ void finish_step_kernel(uint32_t* token, int* pos, const int* advance
     if (n < history_cap) history[n] = *token;
     *history_n = n + 1;
     *pos += *advance;
+}
+
+// Greedy token of each of n logit rows (argmax.cu:25-98 semantics: the
+// largest value, the lowest index among equals).
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* logits, int vocab, uint32_t* out) {
+    const float* row = logits + (size_t)blockIdx.x * vocab;
+    float bs = -CUDART_INF_F;
+    uint32_t bi = 0xFFFFFFFFu;
+    for (int i = threadIdx.x; i < vocab; i += blockDim.x)
+        if (candidate_better(row[i], (uint32_t)i, bs, bi)) {
+            bs = row[i];
+            bi = (uint32_t)i;
+        }
+    __shared__ float ss[32];
+    __shared__ uint32_t si[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float s2 = __shfl_xor_sync(0xffffffffu, bs, o);
+        const uint32_t i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (candidate_better(s2, i2, bs, bi)) {
+            bs = s2;
+            bi = i2;
+        }
+    }
+    if ((threadIdx.x & 31) == 0) {
+        ss[threadIdx.x >> 5] = bs;
+        si[threadIdx.x >> 5] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+            if (candidate_better(ss[w], si[w], bs, bi)) {
+                bs = ss[w];
+                bi = si[w];
+            }
+        out[blockIdx.x] = bi;
+    }
 }
 
 }  // namespace
@@ -185,6 +223,8 @@ Engine::Engine(const q4k_engine_config& cfg, const void* nccl_id) : c_(cfg) {
     vocab0_ = (int64_t)c.vocab * rank_ / world_;
     vocab1_ = (int64_t)c.vocab * (rank_ + 1) / world_;
     if (ffn_l_ <= 0 || qd_ % 256) throw Error(Q4K_EINVAL, "tensor-parallel shards must hold whole super-blocks");
+    if (c.sequences < 0 || c.sequences > 4096) throw Error(Q4K_EINVAL, "sequences must be in 0..4096");
+    seqs_ = c.sequences > 1 ? c.sequences : 1;
 
     cuda_check(cudaSetDevice(c.device), "cudaSetDevice");
     cuda_check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
@@ -219,12 +259,15 @@ Engine::Engine(const q4k_engine_config& cfg, const void* nccl_id) : c_(cfg) {
     err_ = static_cast<int*>(alloc(64));
     history_ = static_cast<uint32_t*>(alloc(sizeof(uint32_t) * (size_t)c.capacity));
     history_n_ = static_cast<unsigned*>(alloc(64));
-    const size_t kv_elems = (size_t)c.layers * KVHl_ * c.capacity * c.head_dim;
+    // [sequence][layer][kv head][position][128]: sequence 0 first
+    seq_elems_ = (size_t)c.layers * KVHl_ * c.capacity * c.head_dim;
+    const size_t kv_elems = seq_elems_ * seqs_;
+    if ((long long)(kv_elems / c.head_dim) >= (1ll << 31)) throw Error(Q4K_EINVAL, "KV cache too large");
     kcache_ = static_cast<uint16_t*>(alloc(kv_elems * 2));
     vcache_ = static_cast<uint16_t*>(alloc(kv_elems * 2));
-    // TMA views of the whole cache: rows = layers * kv_heads * capacity
-    cuda_check(make_kv_tensor_map(kcache_, (long long)c.layers * KVHl_ * c.capacity, &kmap_), "K tensor map");
-    cuda_check(make_kv_tensor_map(vcache_, (long long)c.layers * KVHl_ * c.capacity, &vmap_), "V tensor map");
+    // TMA views of the whole cache: rows = sequences * layers * kv_heads * capacity
+    cuda_check(make_kv_tensor_map(kcache_, (long long)(kv_elems / c.head_dim), &kmap_), "K tensor map");
+    cuda_check(make_kv_tensor_map(vcache_, (long long)(kv_elems / c.head_dim), &vmap_), "V tensor map");
     attn_part_o_ = static_cast<float*>(alloc(sizeof(float) * (size_t)Hl_ * splits_ * c.head_dim));
     attn_part_ml_ = static_cast<float*>(alloc(sizeof(float) * (size_t)Hl_ * splits_ * 2));
     attn_counters_ = static_cast<unsigned*>(alloc(sizeof(unsigned) * KVHl_));
@@ -406,6 +449,13 @@ void Engine::fill_kv_synthetic(uint64_t seed, int n) {
             }
         }
     }
+    // every other sequence gets the same rows 0 .. n-1
+    const size_t row_bytes = (size_t)n * c_.head_dim * 2, pitch = (size_t)c_.capacity * c_.head_dim * 2;
+    for (int sq = 1; sq < seqs_ && n > 0; ++sq)
+        for (uint16_t* cache : {kcache_, vcache_})
+            cuda_check(cudaMemcpy2DAsync(cache + sq * seq_elems_, pitch, cache, pitch, row_bytes,
+                                         (size_t)c_.layers * KVHl_, cudaMemcpyDeviceToDevice, stream_),
+                       "copy kv");
     cuda_check(cudaStreamSynchronize(stream_), "fill_kv");
 }
 
@@ -953,42 +1003,54 @@ void Engine::ensure_prefill_maps() {
                                        &pf_wmaps_[((size_t)i * 7 + j) * kPrefillWeightMaps]),
                        "weight map");
     }
+    const size_t row_bytes = q4k_device_row_bytes(t_embd_, H);
+    cuda_check(make_weight_map(token_embd_ + (size_t)vocab0_ * row_bytes, t_embd_, H, (int)(vocab1_ - vocab0_),
+                               pf_head_map_),
+               "head map");
     pf_maps_ready_ = true;
+}
+
+const KvTensorMap* Engine::layer_maps(int layer, int slot) const {
+    return &pf_wmaps_[((size_t)layer * 7 + slot) * kPrefillWeightMaps];
+}
+
+void Engine::enqueue_product(GemvRequest& r, const KvTensorMap* wmaps) {
+    if (!pf_gemm_ || r.M < pf_gemm_min_rows_ || !wmaps) {
+        cuda_check(launch_gemv(r, stream_), "gemv launch");
+        return;
+    }
+    const int H = c_.hidden;
+    cuda_check(prefill_quantise(r.x, r.ldx ? r.ldx : r.K, r.gamma, r.eps, r.M, r.K, pf_a_, pf_rs_, stream_),
+               "prefill_quantise launch");
+    PrefillGemmArgs g;
+    g.nseg = r.nseg;
+    for (int s = 0; s < r.nseg; ++s) {
+        g.seg[s] = {r.seg[s].w, r.seg[s].type, r.seg[s].rows, r.seg[s].y};
+        g.wmap[s] = wmaps + (size_t)s * kPrefillWeightMaps;
+    }
+    g.K = r.K;
+    g.M = r.M;
+    g.ldy = r.ldy;
+    g.epilogue = r.epilogue;
+    g.amap = &pf_amap_[r.K == H ? 0 : r.K == qd_ ? 1 : 2];
+    g.a = pf_a_;
+    g.row_scale = pf_rs_;
+    g.partial = pf_part_;
+    g.partial_floats = pf_part_floats_;
+    g.err = err_;
+    cuda_check(prefill_gemm(g, stream_), "prefill_gemm launch");
 }
 
 // One block (Engine.cpp:71-103) for `rows` prompt tokens at positions
 // pos0 .. pos0+rows-1: each product runs once over all rows (the weights are
 // streamed once per batch tile instead of once per token).
-void Engine::enqueue_prefill_layer(int i, int rows, int pos0) {
+void Engine::enqueue_prefill_layer(int i, int rows, int pos0, int seq) {
     const auto& c = c_;
     const int H = c.hidden;
     const int W = qd_ + 2 * kvd_;
-    // One product over all rows: the tensor-core GEMM (activation rows
-    // quantised once into pf_a_), or the batched GEMV.
-    // slot: index of the product's first weight among the layer's seven maps
-    auto gemv = [&](GemvRequest& r, int slot) {
-        if (!pf_gemm_ || rows < pf_gemm_min_rows_) {
-            cuda_check(launch_gemv(r, stream_), "gemv launch");
-            return;
-        }
-        cuda_check(prefill_quantise(r.x, r.ldx, r.gamma, r.eps, r.M, r.K, pf_a_, pf_rs_, stream_),
-                   "prefill_quantise launch");
-        PrefillGemmArgs g;
-        g.nseg = r.nseg;
-        for (int s = 0; s < r.nseg; ++s) g.seg[s] = {r.seg[s].w, r.seg[s].type, r.seg[s].rows, r.seg[s].y};
-        g.K = r.K;
-        g.M = r.M;
-        g.ldy = r.ldy;
-        g.epilogue = r.epilogue;
-        for (int s = 0; s < r.nseg; ++s) g.wmap[s] = &pf_wmaps_[((size_t)i * 7 + slot + s) * kPrefillWeightMaps];
-        g.amap = &pf_amap_[r.K == H ? 0 : r.K == qd_ ? 1 : 2];
-        g.a = pf_a_;
-        g.row_scale = pf_rs_;
-        g.partial = pf_part_;
-        g.partial_floats = pf_part_floats_;
-        g.err = err_;
-        cuda_check(prefill_gemm(g, stream_), "prefill_gemm launch");
-    };
+    // one product over all rows; slot: the product's first weight among the
+    // layer's seven maps
+    auto gemv = [&](GemvRequest& r, int slot) { enqueue_product(r, pf_gemm_ ? layer_maps(i, slot) : nullptr); };
     auto all_reduce_into_x = [&]() {
         const size_t n = (size_t)rows * H;
         nccl_check(nccl().AllReduce(pf_partial_, pf_partial_, n, ncclFloat, ncclSum, comm_, stream_),
@@ -996,7 +1058,7 @@ void Engine::enqueue_prefill_layer(int i, int rows, int pos0) {
         cuda_check(residual_add(pf_x_, pf_partial_, n, stream_), "residual_add");
     };
     const Layer& L = layers_[i];
-    const size_t kv_layer = (size_t)i * KVHl_ * c.capacity * c.head_dim;
+    const size_t kv_layer = (size_t)seq * seq_elems_ + (size_t)i * KVHl_ * c.capacity * c.head_dim;
     {
         GemvRequest r;
         r.nseg = 3;
@@ -1044,7 +1106,7 @@ void Engine::enqueue_prefill_layer(int i, int rows, int pos0) {
         a.kv_heads = KVHl_;
         a.kmap = &kmap_;
         a.vmap = &vmap_;
-        a.row_base = i * KVHl_ * c.capacity;
+        a.row_base = (int)(kv_layer / c.head_dim);
         a.err = err_;
         cuda_check(prefill_attention(a, rows, stream_), "prefill_attention launch");
     }
@@ -1097,8 +1159,9 @@ void Engine::enqueue_prefill_layer(int i, int rows, int pos0) {
     }
 }
 
-uint32_t Engine::prefill(const uint32_t* tokens_host, int n, int position, float* logits_host) {
+uint32_t Engine::prefill(const uint32_t* tokens_host, int n, int position, float* logits_host, int seq) {
     if (!loaded_) throw Error(Q4K_EINVAL, "weights are not loaded");
+    if (seq < 0 || seq >= seqs_) throw Error(Q4K_ERANGE, "sequence out of range");
     if (n <= 0 || !tokens_host) throw Error(Q4K_EINVAL, "prefill needs at least one token");
     // Engine.cpp:126-128 (capacity) and EmbedLookup's token check
     if (position < 0 || (long long)position + n > c_.capacity) throw Error(Q4K_ERANGE, "KV cache capacity exceeded");
@@ -1120,7 +1183,7 @@ uint32_t Engine::prefill(const uint32_t* tokens_host, int n, int position, float
                    "h2d tokens");
         cuda_check(embed_rows(token_embd_, t_embd_, H, c_.vocab, pf_tokens_, rows, pf_x_, err_, stream_, false),
                    "embed");
-        for (int i = 0; i < c_.layers; ++i) enqueue_prefill_layer(i, rows, position + t0);
+        for (int i = 0; i < c_.layers; ++i) enqueue_prefill_layer(i, rows, position + t0, seq);
     }
     // Engine.cpp:106-111: only the last prompt token's state feeds the head
     cuda_check(cudaMemcpyAsync(x_, pf_x_ + (size_t)(rows - 1) * H, sizeof(float) * H, cudaMemcpyDeviceToDevice,
@@ -1134,6 +1197,181 @@ uint32_t Engine::prefill(const uint32_t* tokens_host, int n, int position, float
                    "d2h logits");
     check_device_error();
     return host_io_[4];
+}
+
+void Engine::ensure_batch() {
+    if (b_cap_) return;
+    const int B = std::min(seqs_, pf_rows_);
+    const size_t H = c_.hidden, W = (size_t)qd_ + 2 * kvd_;
+    b_x_ = static_cast<float*>(alloc(sizeof(float) * B * H));
+    b_qkv_ = static_cast<float*>(alloc(sizeof(float) * B * W));
+    b_att_ = static_cast<float*>(alloc(sizeof(float) * B * (size_t)qd_));
+    b_act_ = static_cast<float*>(alloc(sizeof(float) * B * (size_t)ffn_l_));
+    b_logits_ = static_cast<float*>(alloc(sizeof(float) * B * (size_t)(vocab1_ - vocab0_)));
+    // split partials for up to splits_ CTAs per KV head (a batch of one)
+    b_part_o_ = static_cast<float*>(alloc(sizeof(float) * B * (size_t)Hl_ * splits_ * c_.head_dim));
+    b_part_ml_ = static_cast<float*>(alloc(sizeof(float) * B * (size_t)Hl_ * splits_ * 2));
+    b_counters_ = static_cast<unsigned*>(alloc(sizeof(unsigned) * B * (size_t)KVHl_));
+    cuda_check(cudaMemsetAsync(b_counters_, 0, sizeof(unsigned) * B * (size_t)KVHl_, stream_), "memset");
+    b_pos_ = static_cast<int*>(alloc(sizeof(int) * B));
+    b_seq_ = static_cast<int*>(alloc(sizeof(int) * B));
+    b_tok_ = static_cast<uint32_t*>(alloc(sizeof(uint32_t) * B));
+    b_next_ = static_cast<uint32_t*>(alloc(sizeof(uint32_t) * B));
+    b_cap_ = B;
+}
+
+// One block (Engine.cpp:71-103) for n tokens of n sequences: the products
+// over all rows, attention per token over its own sequence's cache.
+void Engine::enqueue_batch_layer(int i, int n, int splits) {
+    const auto& c = c_;
+    const int H = c.hidden;
+    const int W = qd_ + 2 * kvd_;
+    auto product = [&](GemvRequest& r, int slot) { enqueue_product(r, pf_gemm_ ? layer_maps(i, slot) : nullptr); };
+    const Layer& L = layers_[i];
+    const size_t kv_layer = (size_t)i * KVHl_ * c.capacity * c.head_dim;
+    {
+        GemvRequest r;
+        r.nseg = 3;
+        r.seg[0] = {L.q, b_qkv_, L.tq, qd_};
+        r.seg[1] = {L.k, b_qkv_ + qd_, L.tk, kvd_};
+        r.seg[2] = {L.v, b_qkv_ + qd_ + kvd_, L.tv, kvd_};
+        r.K = H;
+        r.M = n;
+        r.ldx = H;
+        r.ldy = W;
+        r.x = b_x_;
+        r.gamma = L.attn_norm;
+        r.eps = c.eps;
+        r.epilogue = EPI_STORE;
+        r.err = err_;
+        r.pdl = true;
+        product(r, 0);
+    }
+    {
+        DecodeAttnArgs a;
+        a.qkv = b_qkv_;
+        a.q_gamma = L.q_norm;
+        a.k_gamma = L.k_norm;
+        a.k_cache = kcache_ + kv_layer;
+        a.v_cache = vcache_ + kv_layer;
+        a.capacity = c.capacity;
+        a.position = b_pos_;
+        a.heads = Hl_;
+        a.kv_heads = KVHl_;
+        a.eps = c.eps;
+        a.rope_base = c.rope_base;
+        a.partial_o = b_part_o_;
+        a.partial_ml = b_part_ml_;
+        a.counters = b_counters_;
+        a.out = b_att_;
+        a.err = err_;
+        a.splits = splits;
+        a.row_base = i * KVHl_ * c.capacity;
+        a.batch = n;
+        a.seq_of = b_seq_;
+        a.ld_qkv = W;
+        a.seq_cache_elems = (long long)seq_elems_;
+        cuda_check(decode_attention(a, kmap_, vmap_, stream_, true), "attention launch");
+    }
+    {
+        GemvRequest r;
+        r.nseg = 1;
+        r.seg[0] = {L.o, b_x_, L.to, H};
+        r.K = qd_;
+        r.M = n;
+        r.ldx = qd_;
+        r.ldy = H;
+        r.x = b_att_;
+        r.epilogue = EPI_ADD;
+        r.err = err_;
+        r.pdl = true;
+        product(r, 3);
+    }
+    {
+        GemvRequest r;
+        r.nseg = 2;
+        r.seg[0] = {L.gate, b_act_, L.tgate, ffn_l_};
+        r.seg[1] = {L.up, b_act_, L.tup, ffn_l_};
+        r.K = H;
+        r.M = n;
+        r.ldx = H;
+        r.ldy = ffn_l_;
+        r.x = b_x_;
+        r.gamma = L.ffn_norm;
+        r.eps = c.eps;
+        r.epilogue = EPI_SWIGLU;
+        r.err = err_;
+        r.pdl = true;
+        product(r, 4);
+    }
+    {
+        GemvRequest r;
+        r.nseg = 1;
+        r.seg[0] = {L.down, b_x_, L.tdown, H};
+        r.K = ffn_l_;
+        r.M = n;
+        r.ldx = ffn_l_;
+        r.ldy = H;
+        r.x = b_act_;
+        r.epilogue = EPI_ADD;
+        r.err = err_;
+        r.pdl = true;
+        product(r, 6);
+    }
+}
+
+void Engine::decode_batch(int n, const int* seqs, const uint32_t* tokens, const int* positions, uint32_t* next_host,
+                          float* logits_host) {
+    if (!loaded_) throw Error(Q4K_EINVAL, "weights are not loaded");
+    if (world_ > 1) throw Error(Q4K_EINVAL, "batched decode needs tp_world == 1");
+    ensure_prefill();
+    if (n < 1 || n > std::min(seqs_, pf_rows_)) throw Error(Q4K_ERANGE, "batch size out of range");
+    std::vector<char> used(seqs_, 0);
+    for (int b = 0; b < n; ++b) {
+        if (seqs[b] < 0 || seqs[b] >= seqs_) throw Error(Q4K_ERANGE, "sequence out of range");
+        if (used[seqs[b]]++) throw Error(Q4K_EINVAL, "a sequence appears twice in one step");
+        if (tokens[b] >= (uint32_t)c_.vocab) throw Error(Q4K_ERANGE, "Token ID out of range");
+        if (positions[b] < 0 || positions[b] >= c_.capacity) throw Error(Q4K_ERANGE, "KV cache capacity exceeded");
+    }
+    if (pf_gemm_) ensure_prefill_maps();
+    ensure_batch();
+    // split the attention of each token over fewer CTAs as the batch grows
+    // (a batch of one uses the single-token split count)
+    int splits = std::max(1, splits_ / n);
+    if (const char* e = std::getenv("Q4K_BATCH_SPLITS")) splits = std::min(std::max(1, std::atoi(e)), splits_);
+    const int H = c_.hidden;
+    const int vocab_l = (int)(vocab1_ - vocab0_);
+    cuda_check(cudaMemcpyAsync(b_seq_, seqs, sizeof(int) * n, cudaMemcpyHostToDevice, stream_), "h2d");
+    cuda_check(cudaMemcpyAsync(b_tok_, tokens, sizeof(uint32_t) * n, cudaMemcpyHostToDevice, stream_), "h2d");
+    cuda_check(cudaMemcpyAsync(b_pos_, positions, sizeof(int) * n, cudaMemcpyHostToDevice, stream_), "h2d");
+    cuda_check(embed_rows(token_embd_, t_embd_, H, c_.vocab, b_tok_, n, b_x_, err_, stream_, false), "embed");
+    for (int i = 0; i < c_.layers; ++i) enqueue_batch_layer(i, n, splits);
+    {
+        // output head on every row (Engine.cpp:106-111), then each row's argmax
+        GemvRequest r;
+        r.nseg = 1;
+        const size_t row_bytes = q4k_device_row_bytes(t_embd_, H);
+        r.seg[0] = {token_embd_ + (size_t)vocab0_ * row_bytes, b_logits_, t_embd_, vocab_l};
+        r.K = H;
+        r.M = n;
+        r.ldx = H;
+        r.ldy = vocab_l;
+        r.x = b_x_;
+        r.gamma = output_norm_;
+        r.eps = c_.eps;
+        r.epilogue = EPI_STORE;
+        r.err = err_;
+        r.pdl = true;
+        enqueue_product(r, pf_gemm_ ? pf_head_map_ : nullptr);
+    }
+    argmax_rows_kernel<<<n, 1024, 0, stream_>>>(b_logits_, vocab_l, b_next_);
+    cuda_check(cudaGetLastError(), "argmax launch");
+    cuda_check(cudaMemcpyAsync(next_host, b_next_, sizeof(uint32_t) * n, cudaMemcpyDeviceToHost, stream_), "d2h");
+    if (logits_host)
+        cuda_check(cudaMemcpyAsync(logits_host, b_logits_, sizeof(float) * n * (size_t)vocab_l, cudaMemcpyDeviceToHost,
+                                   stream_),
+                   "d2h logits");
+    check_device_error();
 }
 
 void Engine::layer_step(int layer, const float* x_host, int position, float* x_out_host) {

@@ -58,7 +58,11 @@ public:
     // with tokens = n): every layer as batched products over the prompt rows,
     // the K/V rows written to the cache, the output head on the last row.
     // Returns the greedy next token.
-    uint32_t prefill(const uint32_t* tokens_host, int n, int position, float* logits_host);
+    uint32_t prefill(const uint32_t* tokens_host, int n, int position, float* logits_host, int seq = 0);
+    // One decode step for n tokens of n distinct sequences (tp_world == 1):
+    // the products over all n rows, attention over each sequence's cache.
+    void decode_batch(int n, const int* seqs, const uint32_t* tokens, const int* positions, uint32_t* next_host,
+                      float* logits_host);
     // One block on a given residual-stream input (tp_world == 1 or all ranks).
     void layer_step(int layer, const float* x_host, int position, float* x_out_host);
     // One step with every kernel CTA's %globaltimer start/end recorded.
@@ -83,8 +87,14 @@ private:
     void enqueue_head();
     // Prompt rows per prefill pass and their buffers (allocated on first use).
     void ensure_prefill();
-    void enqueue_prefill_layer(int i, int rows, int pos0);
+    void enqueue_prefill_layer(int i, int rows, int pos0, int seq);
     void ensure_prefill_maps();
+    // One product over r.M rows: the tensor-core GEMM (with the given weight
+    // maps) from pf_gemm_min_rows_ rows, else the batched GEMV.
+    void enqueue_product(GemvRequest& r, const KvTensorMap* wmaps);
+    const KvTensorMap* layer_maps(int layer, int slot) const;
+    void ensure_batch();
+    void enqueue_batch_layer(int i, int n, int splits);
     // L2 prefetch descriptors of layer i's weights (q, k, v; o; gate, up; down).
     L2Prefetch weight_prefetch(const uint8_t* w, int type, int K, int rows) const;
     void check_device_error();
@@ -129,6 +139,17 @@ private:
     float* tp_cand_local_ = nullptr;  // [2] score, index (as float bits)
     float* tp_cand_all_ = nullptr;    // [2 * world]
     uint32_t* host_io_ = nullptr;     // pinned: token, position, result
+
+    int seqs_ = 1;             // KV caches held (sequences)
+    size_t seq_elems_ = 0;     // fp16 elements of one sequence's K (or V) cache
+    // decode_batch buffers (up to b_cap_ tokens per step)
+    int b_cap_ = 0;
+    float *b_x_ = nullptr, *b_qkv_ = nullptr, *b_att_ = nullptr, *b_act_ = nullptr, *b_logits_ = nullptr;
+    float *b_part_o_ = nullptr, *b_part_ml_ = nullptr;
+    unsigned* b_counters_ = nullptr;
+    int *b_pos_ = nullptr, *b_seq_ = nullptr;
+    uint32_t *b_tok_ = nullptr, *b_next_ = nullptr;
+    KvTensorMap pf_head_map_[kPrefillWeightMaps];  // token_embd as the output head
 
     int pf_rows_ = 0;  // prompt rows one prefill pass holds
     uint32_t* pf_tokens_ = nullptr;

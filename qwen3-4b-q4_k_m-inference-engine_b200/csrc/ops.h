@@ -55,6 +55,15 @@ struct DecodeAttnArgs {
     int trace_tag = 0;
     L2Prefetch prefetch[kMaxPrefetch];    // the next kernel's operands (optional)
     ActImage out_image;                   // optional: the attended output, quantised for the O product
+    // Batched decode (one new token in each of `batch` sequences): qkv, out,
+    // position, partial_o / partial_ml and counters hold one row / block per
+    // token (qkv rows ld_qkv floats apart); token z's cache is that of
+    // sequence seq_of[z] (z if null), seq_cache_elems fp16 elements per
+    // sequence from k_cache / v_cache and from row_base in the tensor maps.
+    int batch = 1;
+    const int* seq_of = nullptr;
+    int ld_qkv = 0;
+    long long seq_cache_elems = 0;
 };
 constexpr int kDecodeHeadDim = 128;
 

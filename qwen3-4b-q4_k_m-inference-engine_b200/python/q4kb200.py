@@ -28,7 +28,7 @@ EXPORTS = (
     "q4k_argmax", "q4k_matmul_ex", "q4k_matmul_batch", "q4k_matmul_argmax_scratch_bytes", "q4k_attention_decode_f16",
     "q4k_attention_decode_scratch_bytes", "q4k_engine_config_qwen3_4b", "q4k_model_tensor", "q4k_nccl_unique_id",
     "q4k_engine_create", "q4k_engine_destroy", "q4k_engine_load_synthetic", "q4k_engine_set_tensor",
-    "q4k_engine_fill_kv_synthetic", "q4k_engine_read_kv", "q4k_engine_decode", "q4k_engine_prefill", "q4k_engine_generate",
+    "q4k_engine_fill_kv_synthetic", "q4k_engine_read_kv", "q4k_engine_decode", "q4k_engine_prefill", "q4k_engine_prefill_seq", "q4k_engine_decode_batch", "q4k_engine_generate",
     "q4k_engine_stream", "q4k_tp_shard", "q4k_engine_layer", "q4k_engine_write_kv",
     "q4k_engine_trace", "q4k_attention_decode_f16_static", "q4k_gguf_open", "q4k_gguf_close",
     "q4k_gguf_tensor_count", "q4k_gguf_tensor_info", "q4k_gguf_meta_int", "q4k_gguf_meta_float",
@@ -54,7 +54,7 @@ class EngineConfig(C.Structure):
     _fields_ = [("layers", C.c_int), ("hidden", C.c_int), ("heads", C.c_int), ("kv_heads", C.c_int),
                 ("head_dim", C.c_int), ("ffn", C.c_int), ("vocab", C.c_int), ("eps", C.c_float),
                 ("rope_base", C.c_float), ("capacity", C.c_int), ("tp_rank", C.c_int), ("tp_world", C.c_int),
-                ("device", C.c_int)]
+                ("device", C.c_int), ("sequences", C.c_int)]
 
     def as_dict(self) -> dict:
         return {f: getattr(self, f) for f, _ in self._fields_}
@@ -106,6 +106,8 @@ def lib():
             "q4k_engine_read_kv": ([P, I, P, P], I),
             "q4k_engine_decode": ([P, C.c_uint32, I, C.POINTER(C.c_uint32), P, P], I),
             "q4k_engine_prefill": ([P, P, I, I, C.POINTER(C.c_uint32), P], I),
+            "q4k_engine_prefill_seq": ([P, I, P, I, I, C.POINTER(C.c_uint32), P], I),
+            "q4k_engine_decode_batch": ([P, I, P, P, P, P, P], I),
             "q4k_engine_generate": ([P, C.c_uint32, I, I, I, P], I),
             "q4k_engine_stream": ([P], P),
             "q4k_engine_layer": ([P, I, P, I, P], I),
@@ -350,6 +352,28 @@ class Engine:
         nxt = C.c_uint32()
         check(lib().q4k_engine_prefill(self.h, hptr(toks), int(toks.size), position, C.byref(nxt), hptr(logits)))
         return nxt.value, logits
+
+    def prefill_seq(self, seq: int, tokens, position: int = 0, want_logits=False):
+        """q4k_engine_prefill into sequence `seq`."""
+        toks = np.ascontiguousarray(tokens, np.uint32)
+        logits = np.empty(self.cfg.vocab, np.float32) if want_logits else None
+        nxt = C.c_uint32()
+        check(lib().q4k_engine_prefill_seq(self.h, seq, hptr(toks), int(toks.size), position, C.byref(nxt),
+                                           hptr(logits)))
+        return nxt.value, logits
+
+    def decode_batch(self, seqs, tokens, positions, want_logits=False):
+        """One step for len(seqs) sequences (q4k_engine_decode_batch):
+        returns (next tokens, logits [n][vocab] or None)."""
+        sq = np.ascontiguousarray(seqs, np.int32)
+        tk = np.ascontiguousarray(tokens, np.uint32)
+        ps = np.ascontiguousarray(positions, np.int32)
+        n = int(sq.size)
+        assert tk.size == n and ps.size == n
+        out = np.empty(n, np.uint32)
+        logits = np.empty((n, self.cfg.vocab), np.float32) if want_logits else None
+        check(lib().q4k_engine_decode_batch(self.h, n, hptr(sq), hptr(tk), hptr(ps), hptr(out), hptr(logits)))
+        return out, logits
 
     def generate(self, token: int, position: int, steps: int, advance: bool = True, want_tokens=True):
         out = np.empty(max(steps, 1), np.uint32) if want_tokens else None

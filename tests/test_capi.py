@@ -45,7 +45,8 @@ def test_cpp_dropin_symbols_exported():
 
 def test_abi_version_and_sizes():
     L = q.lib()
-    assert L.q4k_abi_version() == 1
+    assert L.q4k_abi_version() == 2
+    assert C.sizeof(q.EngineConfig) == 14 * 4
     assert q.device_bytes(q.Q4_K, 2560, 9728) == 9728 * 1440
     assert q.device_bytes(q.Q6_K, 2560, 1024) == 1024 * (10 * 208 + 32)
     assert q.device_bytes(q.Q6_K, 9728, 2560) == 2560 * (38 * 208 + 80)

@@ -171,17 +171,6 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
 
 __device__ __forceinline__ uint32_t byte_of(const uint4& v, int i) { return (word_of(v, i >> 2) >> (8 * (i & 3))) & 0xFFu; }
 
-__device__ __forceinline__ uint32_t pack2(float a, float b) {
-    const __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<const uint32_t*>(&h);
-}
-
-// Byte i of `q` (a value < 2^8) as an exact float: the bits 0x4B0000qq are
-// 2^23 + q.
-__device__ __forceinline__ float byte_plus_2p23(uint32_t q, int i) {
-    return __uint_as_float(__byte_perm(q, 0x4B000000u, 0x7440u + (uint32_t)i));
-}
-
 // Byte offset of 16-byte chunk c (0..7) of row r in a 128-row x 128-byte
 // tile with the 128-byte swizzle (the layout TMA writes and the MMA reads).
 __device__ __forceinline__ uint32_t swz(int r, int c) {

@@ -490,25 +490,42 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // y (=, or += for EPI_ADD) the sum of the split-K partials, in split order.
+// Each thread sums V consecutive columns of one segment (V = 4 when every
+// column offset, width and row stride is a multiple of 4); the segments are
+// picked by selects, so the arguments stay out of local memory.
 struct ReduceArgs {
     const float* partial;
     int splits, M, ntot, nseg, ldy, add;
-    int col_off[3];
-    float* y[3];
+    int off1, off2;  // first column of segments 1 and 2 (ntot when absent)
+    float *y0, *y1, *y2;
 };
 
+template <int V>
 __global__ void __launch_bounds__(256) split_reduce_kernel(const ReduceArgs r) {
-    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t i = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * V;
     if (i >= (size_t)r.M * r.ntot) return;
     const int m = (int)(i / r.ntot), c = (int)(i % r.ntot);
-    float acc = 0.0f;
-    for (int z = 0; z < r.splits; ++z) acc += r.partial[((size_t)z * r.M + m) * r.ntot + c];
-    const int seg = (r.nseg > 2 && c >= r.col_off[2]) ? 2 : (r.nseg > 1 && c >= r.col_off[1]) ? 1 : 0;
-    float* out = r.y[seg] + (size_t)m * r.ldy + (c - r.col_off[seg]);
-    if (r.add)
-        *out += acc;
-    else
-        *out = acc;
+    float acc[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) acc[v] = 0.0f;
+    for (int z = 0; z < r.splits; ++z) {
+        const float* src = r.partial + ((size_t)z * r.M + m) * r.ntot + c;
+        if constexpr (V == 4) {
+            const float4 t = *reinterpret_cast<const float4*>(src);
+            acc[0] += t.x;
+            acc[1] += t.y;
+            acc[2] += t.z;
+            acc[3] += t.w;
+        } else {
+            acc[0] += *src;
+        }
+    }
+    const bool s2 = c >= r.off2, s1 = c >= r.off1;
+    float* yb = s2 ? r.y2 : s1 ? r.y1 : r.y0;
+    const int col = c - (s2 ? r.off2 : s1 ? r.off1 : 0);
+    float* out = yb + (size_t)m * r.ldy + col;
+#pragma unroll
+    for (int v = 0; v < V; ++v) out[v] = r.add ? out[v] + acc[v] : acc[v];
 }
 
 // Q8 codes of each row (matmul.cu:8-22) as fp16 code * (scale / row_scale).
@@ -516,19 +533,22 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const ReduceArgs r) {
 // 32-value group 8 i + w at step i and the row is read once.
 constexpr int kQuantMaxSteps = 40;  // K <= 10240
 
+// kSteps: register slots per thread, the smallest instantiation >= K / 256
+// (fewer registers, more rows resident per SM for the common widths).
+template <int kSteps>
 __global__ void __launch_bounds__(256) prefill_quantise_kernel(const float* x, int ldx, const float* gamma, float eps,
                                                                int K, __half* a, float* row_scale) {
     const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float* xr = x + (size_t)m * ldx;
     const int steps = K / 256;
     __shared__ float red[8];
-    float v[kQuantMaxSteps];
+    float v[kSteps];
 #pragma unroll
-    for (int i = 0; i < kQuantMaxSteps; ++i) v[i] = i < steps ? xr[256 * i + tid] : 0.0f;
+    for (int i = 0; i < kSteps; ++i) v[i] = i < steps ? xr[256 * i + tid] : 0.0f;
     if (gamma) {
         float ss = 0.0f;
 #pragma unroll
-        for (int i = 0; i < kQuantMaxSteps; ++i) ss += v[i] * v[i];
+        for (int i = 0; i < kSteps; ++i) ss += v[i] * v[i];
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
         __syncthreads();
@@ -536,14 +556,14 @@ __global__ void __launch_bounds__(256) prefill_quantise_kernel(const float* x, i
         for (int i = 0; i < 8; ++i) total += red[i];
         const float inv = rsqrtf(total / (float)K + eps);  // rms_norm.cu:17
 #pragma unroll
-        for (int i = 0; i < kQuantMaxSteps; ++i)
+        for (int i = 0; i < kSteps; ++i)
             if (i < steps) v[i] = (v[i] * inv) * gamma[256 * i + tid];  // rms_norm.cu:19
         __syncthreads();
     }
-    float am[kQuantMaxSteps];
+    float am[kSteps];
     float wmax = 0.0f;
 #pragma unroll
-    for (int i = 0; i < kQuantMaxSteps; ++i) {
+    for (int i = 0; i < kSteps; ++i) {
         am[i] = warp_max(fabsf(v[i]));
         wmax = fmaxf(wmax, am[i]);
     }
@@ -553,7 +573,7 @@ __global__ void __launch_bounds__(256) prefill_quantise_kernel(const float* x, i
     for (int i = 0; i < 8; ++i) rmax = fmaxf(rmax, red[i]);
     const float S = rmax / 127.0f;  // the largest group scale (matmul.cu:18)
 #pragma unroll
-    for (int i = 0; i < kQuantMaxSteps; ++i) {
+    for (int i = 0; i < kSteps; ++i) {
         if (i >= steps) break;
         bool near;
         int8_t code = gemv_dev::q8_code_rn(v[i], __fdividef(127.0f, am[i]), near);
@@ -574,7 +594,14 @@ cudaError_t prefill_quantise(const float* x, int ldx, const float* gamma, float 
                              float* row_scale, cudaStream_t s) {
     if (M <= 0 || K <= 0 || K % 256 || K / 256 > kQuantMaxSteps || ldx < K || !x || !a || !row_scale)
         return cudaErrorInvalidValue;
-    prefill_quantise_kernel<<<M, 256, 0, s>>>(x, ldx, gamma, eps, K, reinterpret_cast<__half*>(a), row_scale);
+    __half* ah = reinterpret_cast<__half*>(a);
+    const int steps = K / 256;
+    if (steps <= 10)
+        prefill_quantise_kernel<10><<<M, 256, 0, s>>>(x, ldx, gamma, eps, K, ah, row_scale);
+    else if (steps <= 16)
+        prefill_quantise_kernel<16><<<M, 256, 0, s>>>(x, ldx, gamma, eps, K, ah, row_scale);
+    else
+        prefill_quantise_kernel<kQuantMaxSteps><<<M, 256, 0, s>>>(x, ldx, gamma, eps, K, ah, row_scale);
     return cudaGetLastError();
 }
 
@@ -710,12 +737,19 @@ cudaError_t prefill_gemm(const PrefillGemmArgs& g, cudaStream_t s) {
     r.nseg = g.nseg;
     r.ldy = g.ldy;
     r.add = g.epilogue == EPI_ADD;
-    for (int i = 0; i < 3; ++i) {
-        r.col_off[i] = i < g.nseg ? p.col_off[i] : ntot;
-        r.y[i] = i < g.nseg ? g.seg[i].y : nullptr;
-    }
+    r.off1 = g.nseg > 1 ? p.col_off[1] : ntot;
+    r.off2 = g.nseg > 2 ? p.col_off[2] : ntot;
+    r.y0 = g.seg[0].y;
+    r.y1 = g.nseg > 1 ? g.seg[1].y : g.seg[0].y;
+    r.y2 = g.nseg > 2 ? g.seg[2].y : g.seg[0].y;
+    bool vec = ntot % 4 == 0 && g.ldy % 4 == 0 && r.off1 % 4 == 0 && r.off2 % 4 == 0;
+    for (int i = 0; i < g.nseg; ++i) vec = vec && reinterpret_cast<uintptr_t>(g.seg[i].y) % 16 == 0;
+    vec = vec && reinterpret_cast<uintptr_t>(g.partial) % 16 == 0;
     const size_t n = (size_t)g.M * ntot;
-    split_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(r);
+    if (vec)
+        split_reduce_kernel<4><<<(unsigned)((n / 4 + 255) / 256), 256, 0, s>>>(r);
+    else
+        split_reduce_kernel<1><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(r);
     return cudaGetLastError();
 }
 

@@ -1335,9 +1335,25 @@ void Engine::decode_batch(int n, const int* seqs, const uint32_t* tokens, const 
     }
     if (pf_gemm_) ensure_prefill_maps();
     ensure_batch();
-    // split the attention of each token over fewer CTAs as the batch grows
-    // (a batch of one uses the single-token split count)
-    int splits = std::max(1, splits_ / n);
+    // Attention CTAs per token and KV head: with one CTA per SM, a split count
+    // s costs about ceil(n * kv_heads * s / SMs) waves of ceil(tiles / s)
+    // 64-position tiles each, plus about a tile for the cross-split merge;
+    // take the cheapest (the smallest s on ties). One token gets the
+    // single-token count.
+    int max_pos = 0;
+    for (int b = 0; b < n; ++b) max_pos = std::max(max_pos, positions[b]);
+    const long long tiles = max_pos / 64 + 1, sms = sm_count();
+    int splits = 1;
+    long long best = -1;
+    for (int sp = 1; sp <= splits_; ++sp) {
+        const long long waves = ((long long)n * KVHl_ * sp + sms - 1) / sms;
+        const long long cost = waves * ((tiles + sp - 1) / sp) + (sp > 1 ? 1 : 0);
+        if (best < 0 || cost < best) {
+            best = cost;
+            splits = sp;
+        }
+    }
+    if (n == 1) splits = splits_;
     if (const char* e = std::getenv("Q4K_BATCH_SPLITS")) splits = std::min(std::max(1, std::atoi(e)), splits_);
     const int H = c_.hidden;
     const int vocab_l = (int)(vocab1_ - vocab0_);

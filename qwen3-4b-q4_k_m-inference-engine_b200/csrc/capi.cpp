@@ -362,9 +362,10 @@ Q4K_API int q4k_matmul_batch(const float* input, const float* norm_gamma, float 
         void* ws = nullptr;
         const size_t a_bytes = ((rows * (size_t)ne0 * 2 + 255) / 256) * 256;
         const size_t s_bytes = ((rows * sizeof(float) + 255) / 256) * 256;
-        size_t ntot = 0;
-        for (int i = 0; i < count; ++i) ntot += (size_t)out_rows[i];
-        const size_t part_floats = epilogue == Q4K_EPI_SWIGLU ? 0 : rows * ntot * 4;  // up to 4 K splits
+        g.K = (int)ne0;
+        g.M = (int)rows;
+        g.epilogue = epilogue;
+        const size_t part_floats = q4k::prefill_gemm_partial_floats(g);  // exactly the split-K partials it will use
         launched(cudaMallocAsync(&ws, a_bytes + s_bytes + part_floats * sizeof(float), s));
         uint16_t* a = static_cast<uint16_t*>(ws);
         float* scale = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + a_bytes);

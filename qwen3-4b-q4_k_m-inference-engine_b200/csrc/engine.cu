@@ -976,7 +976,7 @@ void Engine::ensure_prefill() {
         const size_t max_k = std::max<size_t>({H, (size_t)qd_, (size_t)ffn_l_});
         pf_a_ = static_cast<uint16_t*>(alloc(sizeof(uint16_t) * rows * max_k));
         pf_rs_ = static_cast<float*>(alloc(sizeof(float) * rows));
-        pf_part_floats_ = (size_t)rows * std::max<size_t>(H, (size_t)(qd_ + 2 * kvd_)) * 2;
+        pf_part_floats_ = (size_t)rows * std::max<size_t>({H, (size_t)(qd_ + 2 * kvd_), 2 * (size_t)ffn_l_}) * 2;
         pf_part_ = static_cast<float*>(alloc(sizeof(float) * pf_part_floats_));
         const int ks[3] = {(int)H, qd_, ffn_l_};
         for (int i = 0; i < 3; ++i) cuda_check(make_act_map(pf_a_, ks[i], rows, &pf_amap_[i]), "activation map");

@@ -137,6 +137,9 @@ struct PrefillGemmArgs {
 };
 // y = (a * row_scale) . W^T over every segment, fp32 accumulation in TMEM.
 cudaError_t prefill_gemm(const PrefillGemmArgs& g, cudaStream_t s);
+// Floats of split-K workspace prefill_gemm would use for g's shapes given
+// unlimited room (0: it would not split).
+size_t prefill_gemm_partial_floats(const PrefillGemmArgs& g);
 // TMA maps of the GEMM's operands: a weight matrix's raw rows as 64-row
 // boxes (kPrefillWeightMaps maps written to out: one per Q4_K block or Q6_K
 // plane width); the fp16 activation operand as 64 x 128-row boxes, 128-byte

@@ -462,7 +462,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) st[lane * 33 + i] = v[i];
             __syncwarp();
-            const int n = n0 + c0 + lane;
+            // a SwiGLU tile's columns 0..63 are gate rows n0.., 64..127 the same up rows
+            const int pseg = pair ? (cg >> 1) : seg;
+            const int n = n0 + (pair ? 32 * (cg & 1) : c0) + lane;
             const bool col_ok = n < rows;
             for (int r = 0; r < 32; ++r) {
                 const int mr = m0 + 32 * quad + r;
@@ -470,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float a = st[r * 33 + lane];
                 if (p.splits > 1) {
                     // this K range's share, reduced in a fixed order by split_reduce_kernel
-                    p.partial[((size_t)split * p.M + mr) * p.ntot + p.col_off[seg] + n] = a;
+                    p.partial[((size_t)split * p.M + mr) * p.ntot + p.col_off[pseg] + n] = a;
                 } else {
                     float* out = p.y[pair ? 0 : seg] + (size_t)mr * p.ldy + n;
                     if (p.epilogue == EPI_ADD)
@@ -526,6 +528,23 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const ReduceArgs r) {
     float* out = yb + (size_t)m * r.ldy + col;
 #pragma unroll
     for (int v = 0; v < V; ++v) out[v] = r.add ? out[v] + acc[v] : acc[v];
+}
+
+// SwiGLU split-K: y = silu(sum of the gate partials) * (sum of the up
+// partials), each sum in split order (gate columns 0..rows-1 of a partial
+// row, up columns rows..2 rows-1).
+__global__ void __launch_bounds__(256) split_reduce_swiglu_kernel(const ReduceArgs r) {
+    const int rows = r.off1;
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)r.M * rows) return;
+    const int m = (int)(i / rows), n = (int)(i % rows);
+    float gs = 0.0f, us = 0.0f;
+    for (int z = 0; z < r.splits; ++z) {
+        const float* src = r.partial + ((size_t)z * r.M + m) * r.ntot;
+        gs += src[n];
+        us += src[rows + n];
+    }
+    r.y0[(size_t)m * r.ldy + n] = (gs / (1.0f + expf(-gs))) * us;  // silu_multiply.cu:9-10
 }
 
 // Q8 codes of each row (matmul.cu:8-22) as fp16 code * (scale / row_scale).
@@ -658,6 +677,40 @@ cudaError_t make_act_map(const uint16_t* a, int K, int rows, KvTensorMap* out) {
     return cudaSuccess;
 }
 
+namespace {
+// K splits for `tiles` column tiles of M rows and nb super-blocks: with one
+// CTA per SM, s splits cost about ceil(ctas * s / SMs) waves of
+// (ceil(nb / s) + 2) super-blocks (2 for a CTA's set-up and epilogue), plus
+// one for the reduce; the cheapest s whose partials fit `partial_floats`
+// wins, each split keeping at least two super-blocks.
+int gemm_splits(int M, int tiles, int nb, int ntot, size_t partial_floats) {
+    const long long ctas = (long long)((M + BM - 1) / BM) * tiles, sms = sm_count();
+    long long best = (ctas + sms - 1) / sms * (nb + 2);
+    int splits = 1;
+    for (int sp = 2; sp <= std::min(16, nb / 2); ++sp) {
+        if ((size_t)sp * M * ntot > partial_floats) break;
+        const long long cost = (ctas * sp + sms - 1) / sms * ((nb + sp - 1) / sp + 2) + 1;
+        if (cost < best) {
+            best = cost;
+            splits = sp;
+        }
+    }
+    return splits;
+}
+}  // namespace
+
+size_t prefill_gemm_partial_floats(const PrefillGemmArgs& g) {
+    const bool pair = g.epilogue == EPI_SWIGLU;
+    if (g.nseg < 1 || g.nseg > 3 || g.K <= 0 || g.K % 256 || g.M <= 0) return 0;
+    int tiles = 0, ntot = 0;
+    for (int i = 0; i < g.nseg; ++i) {
+        ntot += g.seg[i].rows;
+        if (!pair || i == 0) tiles += (g.seg[i].rows + (pair ? BN / 2 : BN) - 1) / (pair ? BN / 2 : BN);
+    }
+    const int sp = gemm_splits(g.M, tiles, g.K / 256, ntot, (size_t)-1);
+    return sp > 1 ? (size_t)sp * g.M * ntot : 0;
+}
+
 cudaError_t prefill_gemm(const PrefillGemmArgs& g, cudaStream_t s) {
     const bool pair = g.epilogue == EPI_SWIGLU;
     if (g.nseg < 1 || g.nseg > 3 || g.K <= 0 || g.K % 256 || g.M <= 0 || g.ldy <= 0 || !g.a || !g.row_scale ||
@@ -713,15 +766,10 @@ cudaError_t prefill_gemm(const PrefillGemmArgs& g, cudaStream_t s) {
         attr = cudaFuncSetAttribute(prefill_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     });
     if (attr != cudaSuccess) return attr;
-    // Split K when the tiles alone leave SMs idle (deterministic: partial sums
-    // reduced in split order); each split keeps at least two super-blocks.
+    // Split K where it shortens the launch (deterministic: the partial sums
+    // are reduced in split order; gemm_splits has the cost model)
+    const int splits = g.partial ? gemm_splits(g.M, tiles, p.nb, ntot, g.partial_floats) : 1;
     const int mtiles = (g.M + BM - 1) / BM;
-    const int ctas = mtiles * tiles;
-    int splits = 1;
-    if (!pair && g.partial && ctas < sm_count()) {
-        splits = std::max(1, std::min((sm_count() + ctas / 2) / ctas, std::min(16, p.nb / 2)));
-        while (splits > 1 && (size_t)splits * g.M * ntot > g.partial_floats) --splits;
-    }
     p.splits = splits;
     p.ntot = ntot;
     p.partial = g.partial;
@@ -745,6 +793,11 @@ cudaError_t prefill_gemm(const PrefillGemmArgs& g, cudaStream_t s) {
     bool vec = ntot % 4 == 0 && g.ldy % 4 == 0 && r.off1 % 4 == 0 && r.off2 % 4 == 0;
     for (int i = 0; i < g.nseg; ++i) vec = vec && reinterpret_cast<uintptr_t>(g.seg[i].y) % 16 == 0;
     vec = vec && reinterpret_cast<uintptr_t>(g.partial) % 16 == 0;
+    if (pair) {
+        const size_t nr = (size_t)g.M * g.seg[0].rows;
+        split_reduce_swiglu_kernel<<<(unsigned)((nr + 255) / 256), 256, 0, s>>>(r);
+        return cudaGetLastError();
+    }
     const size_t n = (size_t)g.M * ntot;
     if (vec)
         split_reduce_kernel<4><<<(unsigned)((n / 4 + 255) / 256), 256, 0, s>>>(r);

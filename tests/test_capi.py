@@ -152,6 +152,16 @@ def test_argument_validation_needs_no_gpu():
                                       P(16), None) == q.EINVAL
     # prefill without an engine, tokens or result
     assert L.q4k_engine_prefill(None, P(16), 1, 0, C.byref(r), None) == q.EINVAL
+    assert L.q4k_engine_prefill_seq(None, 0, P(16), 1, 0, C.byref(r), None) == q.EINVAL
+    assert L.q4k_engine_decode_batch(None, 1, P(16), P(16), P(16), P(16), None) == q.EINVAL
+    # batched products: no argmax epilogue, at most 3 weights, K up to 10240
+    w1, t1 = (C.c_void_p * 1)(16), (C.c_int * 1)(q.Q4_K)
+    r1, o1 = (C.c_int64 * 1)(256), (C.c_void_p * 1)(16)
+    assert L.q4k_matmul_batch(P(16), None, 0.0, 1, w1, t1, r1, o1, 256, 2560, 4, q.EPI_ARGMAX, None) == q.EINVAL
+    assert L.q4k_matmul_batch(P(16), None, 0.0, 4, w1, t1, r1, o1, 256, 2560, 4, q.EPI_STORE, None) == q.EINVAL
+    assert L.q4k_matmul_batch(P(16), None, 0.0, 1, w1, t1, r1, o1, 256, 10496, 4, q.EPI_STORE, None) == q.EINVAL
+    assert L.q4k_matmul_batch(P(16), None, 0.0, 1, w1, t1, r1, o1, 128, 2560, 4, q.EPI_STORE, None) == q.EINVAL
+    assert L.q4k_matmul_batch(P(16), None, 0.0, 1, w1, t1, r1, o1, 256, 2560, 0, q.EPI_STORE, None) == q.OK
     # engine configuration checks happen before any device work
     cfg = q.qwen3_4b_config(4096)
     cfg.head_dim = 64
@@ -159,4 +169,7 @@ def test_argument_validation_needs_no_gpu():
     assert L.q4k_engine_create(C.byref(cfg), None, C.byref(h)) == q.EINVAL
     cfg = q.qwen3_4b_config(4096)
     cfg.tp_world, cfg.tp_rank = 3, 0
+    assert L.q4k_engine_create(C.byref(cfg), None, C.byref(h)) == q.EINVAL
+    cfg = q.qwen3_4b_config(4096)
+    cfg.sequences = -1
     assert L.q4k_engine_create(C.byref(cfg), None, C.byref(h)) == q.EINVAL

@@ -1,6 +1,6 @@
 """Benchmark: Qwen3-4B Q4_K_M batch-1 decode on B200, one JSON line.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload decode|gemv]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload decode|gemv|...]
 
 decode (default): synthetic random-init Q4_K_M weights
 of the Qwen3-4B shapes, fp16 KV cache pre-filled with N(0,1) to 4095
@@ -8,16 +8,21 @@ positions; each step decodes one token at position 4095 (context 4096) with
 the greedy token fed back on the device. N > 1 (torchrun, one process per
 GPU) shards the model tensor-parallel over NCCL; value is tok/s of the
 whole job (strong scaling: the same model and token stream at every N).
+The same line carries two sub-objects measured on the same engine, each
+with its own clock record, roofline and CPU baseline: "prefill" (a
+512-token prompt) and "batch" (64 sequences with
+contexts uniform in [512, 4096], one token each per step, configs[4]).
 
 gemv (BASELINE configs[0]/[1]): the Q4_K 9728x2560 matrix-vector product,
 value in GB/s of algorithmic bytes, 20 distinct weight copies in rotation.
-swiglu / attention: the decode step's fused gate/up product and its decode
-attention alone (profiling targets).
+swiglu / attention / prefill / batch: parts of the default line alone
+(profiling targets).
 
 --impl reference: the reference's hot path on this host's CPU cores (the
-C restatement in oracle/, OpenMP over output rows; the reference has no CPU
-implementation of its own, its test oracle MatmulReference.hpp:42-64 is the
-only host dequant+dot), same metric and config; rank 0 only.
+C restatement in oracle/, OpenMP over output rows with one thread per host
+core; the reference has no CPU implementation of its own, its test oracle
+MatmulReference.hpp:42-64 is the only host dequant+dot), same metric and
+config, its synthetic model built by oracle/ alone; rank 0 only.
 """
 from __future__ import annotations
 
@@ -113,21 +118,42 @@ def dist_init():
 
 
 # --------------------------------------------------------------- CPU leg
-def cpu_decode_model(threads: int = 0):
-    """Host copies of the same synthetic weights and KV cache for the oracle."""
-    from concurrent.futures import ThreadPoolExecutor
-
+# The CPU legs (cpu_baseline and --impl reference) build the synthetic model
+# with oracle/ alone: the process never loads the product library.
+def _oracle():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as o
-    import q4kb200 as q
 
-    cfg = q.qwen3_4b_config(CTX)
-    specs = q.model_tensors(cfg)
-    with ThreadPoolExecutor(max_workers=os.cpu_count() or 4) as ex:
-        datas = list(ex.map(lambda s: q.synth_tensor_host(SEED, s[0], s[1], s[2], s[3]), specs))
-    tensors = {s[0]: (s[1], d) for s, d in zip(specs, datas)}
-    c = cfg.as_dict()
-    model = o.Model(c, tensors)
+    return o
+
+
+def cpu_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_threads() -> int:
+    """Threads the oracle's OpenMP regions get when asked for one per host
+    core (explicitly, so that torchrun's OMP_NUM_THREADS=1 does not apply)."""
+    return _oracle().omp_threads(cpu_cores())
+
+
+def cpu_model(layers: int | None = None, ctx_rows: int = POS):
+    """The seeded synthetic model (oracle/q4k_synth.c) and fp32 KV caches
+    holding the fp16 N(0,1) fill for positions [0, ctx_rows); `layers`
+    limits the model to its first layers (bounded CPU samples)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    o = _oracle()
+    c = o.qwen3_4b_config(CTX)
+    if layers is not None:
+        c = dict(c, layers=layers)
+    specs = [t for t in o.model_tensors(c)]
+    with ThreadPoolExecutor(max_workers=4) as ex:
+        datas = list(ex.map(lambda t: o.synth_tensor(SEED, t[0], t[1], t[2], t[3]), specs))
+    model = o.Model(c, {t[0]: (t[1], d) for t, d in zip(specs, datas)})
     L, KVH, D = c["layers"], c["kv_heads"], c["head_dim"]
     kc = np.zeros((L, CTX, KVH * D), np.float32)
     vc = np.zeros_like(kc)
@@ -136,28 +162,55 @@ def cpu_decode_model(threads: int = 0):
         layer, kv = job
         arr = kc if kv == "k" else vc
         for h in range(KVH):
-            vals = q.synth_f16_host(SEED, f"kv.{layer}.{kv}", h * (1 << 20) * D, POS * D)
-            arr[layer, :POS, h * D:(h + 1) * D] = vals.view(np.float16).astype(np.float32).reshape(POS, D)
+            vals = o.synth_f16(SEED, f"kv.{layer}.{kv}", h * (1 << 20) * D, ctx_rows * D)
+            arr[layer, :ctx_rows, h * D:(h + 1) * D] = vals.view(np.float16).astype(np.float32).reshape(ctx_rows, D)
 
-    with ThreadPoolExecutor(max_workers=os.cpu_count() or 4) as ex:
-        list(ex.map(fill, [(layer, kv) for layer in range(L) for kv in ("k", "v")]))
+    if ctx_rows:
+        with ThreadPoolExecutor(max_workers=os.cpu_count() or 4) as ex:
+            list(ex.map(fill, [(layer, kv) for layer in range(L) for kv in ("k", "v")]))
     return model, kc.ravel(), vc.ravel()
 
 
-def cpu_decode_steps(model, kc, vc, steps: int, threads: int = 0) -> float:
+def cpu_decode_steps(model, kc, vc, steps: int, threads: int, pos: int = POS) -> float:
     t0 = time.perf_counter()
     tok = TOKEN0
     for _ in range(steps):
-        tok, _, _ = model.forward(kc, vc, CTX, [tok], POS, kv_round_f16=True, want_logits=False, want_hidden=False,
+        tok, _, _ = model.forward(kc, vc, CTX, [tok], pos, kv_round_f16=True, want_logits=False, want_hidden=False,
                                   threads=threads)
     return time.perf_counter() - t0
 
 
-def cpu_cores() -> int:
-    try:
-        return len(os.sched_getaffinity(0))
-    except AttributeError:
-        return os.cpu_count() or 1
+def cpu_prefill_sample(threads: int, n: int = 512) -> dict:
+    """A 512-token prompt pass timed through one and through two layers of
+    the model (embedding and head included in both); the whole pass is
+    estimated as t1 + 35 x (t2 - t1)."""
+    rng = np.random.default_rng(SEED)
+    toks = rng.integers(0, 151936, n).astype(np.uint32)
+    times = {}
+    for layers in (1, 2):
+        model, kc, vc = cpu_model(layers=layers, ctx_rows=0)
+        t0 = time.perf_counter()
+        model.forward(kc, vc, CTX, toks, 0, kv_round_f16=True, want_logits=False, want_hidden=False, threads=threads)
+        times[layers] = time.perf_counter() - t0
+        del model, kc, vc
+    per_layer = max(times[2] - times[1], 1e-9)
+    total = times[1] + 35 * per_layer
+    return {"value": round(n / total, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"a {n}-token prompt through 1 and 2 of the 36 layers (+ embedding and head) on {threads} host "
+                      f"threads, whole pass estimated as t1 + 35 x (t2 - t1) = {total:.2f} s; oracle/q4k_oracle.c "
+                      "restating Engine.cpp:37-114 with tokens = 512"}
+
+
+def cpu_batch_sample(threads: int, positions, seqs: int = 2) -> dict:
+    """The reference serves each sequence as its own session: `seqs` of the
+    batch's sequences decoded one after the other at their own contexts."""
+    model, kc, vc = cpu_model()
+    t = 0.0
+    for p in positions[:seqs]:
+        t += cpu_decode_steps(model, kc, vc, 1, threads, pos=int(p))
+    return {"value": round(seqs / t, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{seqs} of the 64 sequences (contexts {', '.join(str(int(p) + 1) for p in positions[:seqs])}), "
+                      f"one decode step each, one after the other as separate sessions, on {threads} host threads"}
 
 
 # ------------------------------------------------------------ GPU legs
@@ -268,15 +321,179 @@ def gemv_bytes(q, qtype, K, N, nmat=1, norm=False):
     return nmat * N * q.gguf_row_bytes(qtype, K) + K * 4 * (2 if norm else 1) + N * 4
 
 
-def read_traffic(name: str):
-    path = os.path.join(ROOT, "profiles", name)
-    if not os.path.exists(path):
-        return None
-    with open(path) as f:
-        for line in f:
-            if line.startswith("traffic_bytes_per_launch:"):
-                return float(line.split(":", 1)[1])
-    return None
+def make_engine(q, torch, world, rank, local, dist, sequences: int = 1):
+    """The synthetic Qwen3-4B on this rank (its tensor-parallel shard when
+    world > 1), KV positions [0, 4095) of every sequence filled."""
+    cfg = q.qwen3_4b_config(CTX)
+    cfg.tp_rank, cfg.tp_world, cfg.device = rank, world, local
+    cfg.sequences = sequences
+    nccl_id = None
+    if world > 1:
+        idt = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            idt.copy_(torch.frombuffer(bytearray(q.nccl_unique_id()), dtype=torch.uint8))
+        dist.broadcast(idt, 0)
+        nccl_id = bytes(idt.cpu().numpy().tobytes())
+    eng = q.Engine(cfg, nccl_id)
+    eng.load_synthetic(SEED)
+    eng.fill_kv_synthetic(SEED, POS)
+    return eng, cfg
+
+
+def max_over_ranks(torch, dist, secs: float) -> float:
+    if dist is None:
+        return secs
+    t = torch.tensor([secs], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+PREFILL_N = 512
+BATCH = 64
+
+
+def batch_rows():
+    """64 sequences with contexts uniform in [512, 4096]
+    (seeded): positions of their new tokens, their sequence slots (not in
+    index order) and their tokens."""
+    rng = np.random.default_rng(SEED + BATCH)
+    ctx = rng.integers(512, CTX + 1, BATCH)
+    return ((ctx - 1).astype(np.int32), rng.permutation(BATCH).astype(np.int32),
+            rng.integers(0, 151936, BATCH).astype(np.uint32))
+
+
+def time_prefill(q, torch, eng, args, dist, local, peaks, world):
+    """A 512-token prompt into sequence 1, from an
+    empty cache, timed on the device; e2e with host token ids per call."""
+    rng = np.random.default_rng(SEED)
+    toks = rng.integers(0, eng.cfg.vocab, PREFILL_N).astype(np.uint32)
+    warm = max(3, args.warmup)
+    for _ in range(warm):
+        eng.prefill_seq(1, toks, 0)
+    stream = torch.cuda.ExternalStream(eng.stream)
+    clocks = ClockSampler(local)
+    clocks.start()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.mark(True)
+    t0 = time.perf_counter()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        eng.prefill_seq(1, toks, 0)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    clocks.mark(False)
+    dev = max_over_ranks(torch, dist, ev0.elapsed_time(ev1) / 1e3) / args.steps
+    wall = max_over_ranks(torch, dist, wall) / args.steps
+    clk = clocks.stop()
+    return {"metric": "Qwen3-4B prompt prefill tok/s (512-token prompt, BASELINE configs[3])",
+            "value": round(PREFILL_N / dev, 1), "unit": "tok/s", "steps": args.steps, "warmup": warm,
+            "ms_per_step": round(dev * 1e3, 3), "higher_is_better": True,
+            "dtype": "fp16 tensor-core products of Q8-dequantised activations and dequantised weights, fp32 "
+                     "accumulate; fp16 KV",
+            "config": {"workload": "prefill of a 512-token prompt into an empty sequence", "seq_len": PREFILL_N,
+                       "parallelism": f"tp{world}", "l2": "2.5 GB of weights streamed per prompt (larger than L2)"},
+            "e2e": {"value": round(PREFILL_N / wall, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * PREFILL_N + 12,
+                    "d2h_bytes_per_step": 8, "how": "q4k_engine_prefill_seq per prompt from host token ids, "
+                                                   "synchronous, host wall clock (max over ranks)"},
+            # embed; per layer 4 x (quantise + GEMM), split-K reduces, QK-norm/RoPE, attention
+            # (+2 all-reduce and residual-add launches with tp); head GEMV; finish
+            "gpu_launches": args.steps * (1 + 36 * (12 + (2 if world > 1 else 0)) + 2),
+            "clocks": clk}
+
+
+def prefill_roofline(q, torch, peaks):
+    """The prefill's dominant product alone: ffn_gate/ffn_up SwiGLU over 512
+    rows (quantise + tcgen05 GEMM, each launch pair timed with CUDA events)."""
+    import ctypes as C
+
+    n, K, N = PREFILL_N, 2560, 9728
+    ws = []
+    for nm in ("gate", "up"):
+        buf = torch.empty(q.device_bytes(q.Q4_K, K, N), dtype=torch.uint8, device="cuda")
+        q.check(q.lib().q4k_synth_tensor_device(SEED, f"bench.pf.{nm}".encode(), q.Q4_K, K, N, buf.data_ptr(), None))
+        ws.append(buf)
+    x = torch.empty(n * K, device="cuda")
+    q.check(q.lib().q4k_synth_f32_device(SEED, b"bench.pf.x", n * K, x.data_ptr(), None))
+    y = torch.empty(n * N, device="cuda")
+    call = lambda: q.check(q.lib().q4k_matmul_batch(
+        x.data_ptr(), None, 0.0, 2, (C.c_void_p * 2)(ws[0].data_ptr(), ws[1].data_ptr()), (C.c_int * 2)(q.Q4_K, q.Q4_K),
+        (C.c_int64 * 2)(N, N), (C.c_void_p * 2)(y.data_ptr(), y.data_ptr()), N, K, n, q.EPI_SWIGLU, None))
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(20):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    launch = e0.elapsed_time(e1) / 1e3 / 20
+    flops = 2.0 * n * 2 * N * K
+    tf = flops / launch / 1e12
+    del ws, x, y
+    return {"kernel": "prefill_quantise + prefill_gemm_kernel (ffn_gate/ffn_up SwiGLU, 512 x 2560 x 2x9728, Q4_K)",
+            "bound": "tensor", "achieved": round(tf, 2), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": round(tf / peaks["bf16_tflops"], 4), "traffic": None, "algorithmic_flops": flops,
+            "launch_us": round(launch * 1e6, 2),
+            "peak_src": peaks["src"] + " (burst dense bf16 GEMM, kernel timed alone)"}
+
+
+def time_batch(q, torch, eng, args, dist, local, peaks, world):
+    """One decode step of 64 sequences at their own contexts (BASELINE
+    configs[4]), the same positions every step (fixed contexts), greedy
+    tokens fed back through the host as the C ABI returns them."""
+    pos, seqs, toks = batch_rows()
+    warm = max(3, args.warmup)
+    for _ in range(warm):
+        toks, _ = eng.decode_batch(seqs, toks, pos)
+    stream = torch.cuda.ExternalStream(eng.stream)
+    clocks = ClockSampler(local)
+    clocks.start()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.mark(True)
+    t0 = time.perf_counter()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        toks, _ = eng.decode_batch(seqs, toks, pos)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    clocks.mark(False)
+    dev = max_over_ranks(torch, dist, ev0.elapsed_time(ev1) / 1e3) / args.steps
+    wall = max_over_ranks(torch, dist, wall) / args.steps
+    clk = clocks.stop()
+    cfg = eng.cfg
+    # bytes a step must stream per GPU: this rank's weights once, its KV heads
+    # of every sequence up to its position
+    kv_bytes = int(np.sum(pos.astype(np.int64) + 1)) * cfg.layers * cfg.kv_heads * cfg.head_dim * 2 * 2 // world
+    w_bytes = sum(q.device_bytes(t, a, b) for _, t, a, b in q.model_tensors(cfg) if t != q.F32) // world
+    step_bytes = w_bytes + kv_bytes
+    gbs = step_bytes / dev / 1e9
+    return {"metric": "Qwen3-4B batched decode tok/s (64 sequences, contexts uniform in [512, 4096], fp16 KV, "
+                      "BASELINE configs[4])",
+            "value": round(BATCH / dev, 1), "unit": "tok/s", "steps": args.steps, "warmup": warm,
+            "ms_per_step": round(dev * 1e3, 3), "higher_is_better": True,
+            "dtype": "fp16 tensor-core products (M=64), fp16 KV, fp32 softmax and accumulation",
+            "config": {"workload": "64 sequences x 1 token per step, contexts uniform in [512, 4096] (seeded)",
+                       "global_batch": BATCH, "contexts": [int(pos.min()) + 1, int(pos.max()) + 1],
+                       "parallelism": f"tp{world}",
+                       "l2": f"{step_bytes / 1e9:.1f} GB streamed per step per GPU (weights + 64 caches)"},
+            "roofline": {"kernel": "whole batched step", "bound": "hbm", "achieved": round(gbs, 1),
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+                         "traffic": None, "algorithmic_bytes": step_bytes,
+                         "peak_src": peaks["src"] + " (copy bandwidth)"},
+            "e2e": {"value": round(BATCH / wall, 1), "unit": "tok/s", "h2d_bytes_per_step": 12 * BATCH,
+                    "d2h_bytes_per_step": 4 * BATCH + 4,
+                    "how": "q4k_engine_decode_batch per step, host rows in, next tokens out, host wall clock"},
+            "gpu_launches": args.steps * (1 + 36 * (11 + (2 if world > 1 else 0)) + 3 + (1 if world > 1 else 0)),
+            "clocks": clk}
 
 
 def run_decode(args, world, rank, local):
@@ -291,18 +508,10 @@ def run_decode(args, world, rank, local):
 
         dist.init_process_group("nccl", device_id=torch.device("cuda", local),
                                 timeout=__import__("datetime").timedelta(seconds=300))
-    cfg = q.qwen3_4b_config(CTX)
-    cfg.tp_rank, cfg.tp_world, cfg.device = rank, world, local
-    nccl_id = None
-    if world > 1:
-        idt = torch.zeros(128, dtype=torch.uint8, device="cuda")
-        if rank == 0:
-            idt.copy_(torch.frombuffer(bytearray(q.nccl_unique_id()), dtype=torch.uint8))
-        dist.broadcast(idt, 0)
-        nccl_id = bytes(idt.cpu().numpy().tobytes())
-    eng = q.Engine(cfg, nccl_id)
-    eng.load_synthetic(SEED)
-    eng.fill_kv_synthetic(SEED, POS)
+    peaks = load_peaks()
+    # one engine for the three workloads: sequence 0 decodes (batch 1),
+    # sequence 1 takes the prompt, all 64 serve the batched step
+    eng, cfg = make_engine(q, torch, world, rank, local, dist, sequences=BATCH)
 
     stream = torch.cuda.ExternalStream(eng.stream)
     clocks = ClockSampler(local)
@@ -320,11 +529,7 @@ def run_decode(args, world, rank, local):
     clocks.mark(False)
     if dist:
         dist.barrier()
-    secs = ev0.elapsed_time(ev1) / 1e3
-    if dist:
-        t = torch.tensor([secs], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        secs = float(t.item())
+    secs = max_over_ranks(torch, dist, ev0.elapsed_time(ev1) / 1e3)
     clk = clocks.stop()
 
     # e2e: the public API call per token, host buffers, H2D token+position,
@@ -337,20 +542,18 @@ def run_decode(args, world, rank, local):
     tok = TOKEN0
     for _ in range(e2e_steps):
         tok, _, _ = eng.decode(tok, POS)
-    e2e_secs = time.perf_counter() - t0
-    if dist:
-        t = torch.tensor([e2e_secs], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_secs = float(t.item())
+    e2e_secs = max_over_ranks(torch, dist, time.perf_counter() - t0)
+
+    prefill = time_prefill(q, torch, eng, args, dist, local, peaks, world)
+    batch = time_batch(q, torch, eng, args, dist, local, peaks, world)
     eng.close()
 
     result = None
     if rank == 0:
-        peaks = load_peaks()
         # dominant kernel: the fused RMSNorm + gate/up + SiLU product (28 MB of
         # Q4_K weights per layer, ~40% of the step's bytes), timed alone
         torch.cuda.empty_cache()
-        K, N = 2560, 9728 // world // 256 * 256 if world > 1 else 9728
+        N = 9728 // 256 // world * 256 if world > 1 else 9728
         t_sw = time_gemv(q, torch, q.Q4_K, 2560, N, copies=8, reps=200, swiglu=True)
         sw_bytes = gemv_bytes(q, q.Q4_K, 2560, N, nmat=2, norm=True)
         achieved = sw_bytes / t_sw / 1e9
@@ -364,8 +567,11 @@ def run_decode(args, world, rank, local):
         t_att, att_bytes = time_attention(q, torch, kv_heads=8 // world)
         gemv["attention_decode_ctx4096"] = {"us": round(t_att * 1e6, 3), "gbs": round(att_bytes / t_att / 1e9, 1),
                                             "frac": round(att_bytes / t_att / 1e9 / peaks["hbm_gbs"], 4)}
+        prefill["roofline"] = prefill_roofline(q, torch, peaks)
         step_bytes = (2503489024 + 36 * 2 * CTX * 8 * 128 * 2) / world
         value = args.steps / secs
+        # embed, 36 x 5, head, finish; with tp the 72 residual adds after the
+        # all-reduces (the NCCL kernels themselves are not counted)
         kernels_per_step = 1 + 36 * 5 + 2 + (72 if world > 1 else 0)
         result = {
             "metric": METRIC_DECODE,
@@ -389,8 +595,7 @@ def run_decode(args, world, rank, local):
                               "peak": peaks["hbm_gbs"], "peak_src": peaks["src"]},
             "roofline": {"kernel": "gemv_kernel<1,2> (RMSNorm + ffn_gate/ffn_up Q4_K 2560x9728 + SiLU)",
                          "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(achieved / peaks["hbm_gbs"], 4),
-                         "traffic": read_traffic("gemv_swiglu_q4k_2560x9728.md"),
+                         "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
                          "algorithmic_bytes": sw_bytes, "launch_us": round(t_sw * 1e6, 3),
                          "peak_src": peaks["src"] + " (burst copy bandwidth, kernel timed alone)"},
             "gemv": gemv,
@@ -400,6 +605,8 @@ def run_decode(args, world, rank, local):
                            "D2H of the token and the error word, stream sync), host wall clock"},
             "gpu_launches": kernels_per_step * args.steps,
             "clocks": clk,
+            "prefill": prefill,
+            "batch": batch,
         }
     if dist:
         dist.barrier()
@@ -430,7 +637,7 @@ def run_gemv(args, world, rank, local):
                        "global_batch": 1, "seq_len": 1, "parallelism": "replica",
                        "l2": "20 distinct weight copies (280 MB) in rotation"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": read_traffic("gemv_q4k_9728x2560.md"),
+                         "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": None,
                          "algorithmic_bytes": b},
             "gpu_launches": args.steps, "clocks": clk}
 
@@ -457,7 +664,7 @@ def run_swiglu(args, world, rank, local):
                        "seq_len": 1, "parallelism": "replica", "l2": "8 distinct weight pairs (224 MB) in rotation"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(gbs / peaks["hbm_gbs"], 4),
-                         "traffic": read_traffic("gemv_swiglu_q4k_2560x9728.md"), "algorithmic_bytes": b},
+                         "traffic": None, "algorithmic_bytes": b},
             "gpu_launches": args.steps}
 
 
@@ -484,40 +691,18 @@ def run_attention(args, world, rank, local):
 
 
 def run_prefill(args, world, rank, local):
-    """Prompt prefill (q4k_engine_prefill, the reference's Engine::inference
-    over a whole prompt): a 512-token prompt on the synthetic Qwen3-4B, plus
-    the reference benchmark's first-token latency shape (a 23-token prompt,
-    then one decode step; benchmark.cpp:86-91). The roofline object is the
-    tensor-core product behind it (ffn_gate/ffn_up SwiGLU at 512 rows)."""
-    import ctypes as C
-
-    import numpy as np
+    """The prefill sub-object alone, plus the reference benchmark's
+    first-token latency shape (a 23-token prompt, then one decode step;
+    benchmark.cpp:86-91)."""
     import torch
 
     import q4kb200 as q
 
     torch.cuda.set_device(local)
     peaks = load_peaks()
-    n = 512
-    cfg = q.qwen3_4b_config(CTX)
-    eng = q.Engine(cfg)
-    eng.load_synthetic(SEED)
-    rng = np.random.default_rng(SEED)
-    toks = rng.integers(0, cfg.vocab, n).astype(np.uint32)
-    for _ in range(max(3, args.warmup)):
-        eng.prefill(toks, 0)
-    steps = max(1, min(args.steps, 20))
-    stream = torch.cuda.ExternalStream(eng.stream)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0 = time.perf_counter()
-    ev0.record(stream)
-    for _ in range(steps):
-        eng.prefill(toks, 0)
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    wall = (time.perf_counter() - t0) / steps
-    dev = ev0.elapsed_time(ev1) / 1e3 / steps
-    # first-token latency: 23-token prompt + one decode step, host wall clock
+    eng, cfg = make_engine(q, torch, 1, 0, local, None, sequences=2)
+    out = time_prefill(q, torch, eng, args, None, local, peaks, 1)
+    rng = np.random.default_rng(SEED + 23)
     short = rng.integers(0, cfg.vocab, 23).astype(np.uint32)
     firsts = []
     for _ in range(5):
@@ -526,132 +711,90 @@ def run_prefill(args, world, rank, local):
         eng.decode(nxt, 23)
         firsts.append(time.perf_counter() - a)
     eng.close()
-    # the dominant product alone, events around each launch pair (quantise + GEMM)
-    K, N = 2560, 9728
-    ws = []
-    for nm in ("gate", "up"):
-        raw = q.synth_tensor_host(SEED, f"bench.pf.{nm}", q.Q4_K, K, N)
-        buf = torch.empty(q.device_bytes(q.Q4_K, K, N), dtype=torch.uint8, device="cuda")
-        q.check(q.lib().q4k_weight_upload(q.Q4_K, K, N, q.hptr(raw), buf.data_ptr(), None))
-        ws.append(buf)
-    x = torch.from_numpy(q.synth_f32_host(SEED, "bench.pf.x", n * K)).cuda()
-    y = torch.empty(n * N, device="cuda")
-    call = lambda: q.check(q.lib().q4k_matmul_batch(
-        x.data_ptr(), None, 0.0, 2, (C.c_void_p * 2)(ws[0].data_ptr(), ws[1].data_ptr()), (C.c_int * 2)(q.Q4_K, q.Q4_K),
-        (C.c_int64 * 2)(N, N), (C.c_void_p * 2)(y.data_ptr(), y.data_ptr()), N, K, n, q.EPI_SWIGLU, None))
-    for _ in range(3):
-        call()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(20):
-        call()
-    e1.record()
-    torch.cuda.synchronize()
-    launch = e0.elapsed_time(e1) / 1e3 / 20
-    flops = 2.0 * n * 2 * N * K
-    tf = flops / launch / 1e12
-    return {"metric": "Qwen3-4B prompt prefill tok/s (512-token prompt)", "value": round(n / dev, 1),
-            "unit": "tok/s", "n_gpus": 1, "steps": steps, "warmup": max(3, args.warmup),
-            "ms_per_step": round(dev * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "fp16 tensor-core products of Q8-dequantised activations and dequantised weights, fp32 accumulate",
-            "data": "synthetic (seeded random-init Q4_K_M weights, random token ids)",
-            "config": {"workload": "prefill of a 512-token prompt from an empty cache", "model": MODEL,
-                       "global_batch": 1, "seq_len": n, "parallelism": "tp1",
-                       "l2": "2.5 GB of weights streamed per prompt (larger than L2)"},
-            "first_token_ms": round(min(firsts) * 1e3, 3),
-            "first_token_note": "23-token prompt prefill + 1 decode step, host wall clock (reference benchmark.cpp "
-                                "'first token' shape; BASELINE.md quotes 186.5 ms on an RTX 4060 Laptop GPU)",
-            "roofline": {"kernel": "prefill_quantise + prefill_gemm_kernel (ffn_gate/ffn_up SwiGLU, 512 x 2560 x "
-                                   "2x9728, Q4_K)", "bound": "tensor", "achieved": round(tf, 2),
-                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(tf / peaks["bf16_tflops"], 4),
-                         "traffic": None, "algorithmic_flops": flops, "launch_us": round(launch * 1e6, 2)},
-            "e2e": {"value": round(n / wall, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * n, "d2h_bytes_per_step": 8,
-                    "how": "q4k_engine_prefill per prompt from host token ids, host wall clock"},
-            # per 512-row prompt: embed; per layer 4 x (quantise + GEMM), 2 split-K
-            # reduces (O, down), QK-norm/RoPE, attention; head GEMV; finish
-            "gpu_launches": steps * (1 + 36 * 12 + 2)}
+    out.update({"n_gpus": 1, "scaling": "weak", "vs_baseline": None, "data": "synthetic (seeded random-init Q4_K_M "
+                "weights, random token ids)", "roofline": prefill_roofline(q, torch, peaks),
+                "first_token_ms": round(min(firsts) * 1e3, 3),
+                "first_token_note": "23-token prompt prefill + 1 decode step, host wall clock (the reference "
+                                    "benchmark's 'first token' shape; the reference publishes 186.5 ms on an RTX "
+                                    "4060 Laptop GPU)"})
+    return out
 
 
 def run_batch(args, world, rank, local):
-    """Batched decode (q4k_engine_decode_batch): 64 sequences, each at context
-    4096 over the same synthetic cache rows, one new token per sequence per
-    step; every step reads each weight once for all 64 (the tensor-core
-    products) and each sequence's own 16.8 MB of fp16 K/V per layer."""
-    import numpy as np
+    """The batch sub-object alone."""
     import torch
 
     import q4kb200 as q
 
     torch.cuda.set_device(local)
     peaks = load_peaks()
-    B = 64
-    cfg = q.qwen3_4b_config(CTX)
-    cfg.sequences = B
-    eng = q.Engine(cfg)
-    eng.load_synthetic(SEED)
-    eng.fill_kv_synthetic(SEED, CTX - 1)
-    rng = np.random.default_rng(SEED)
-    seqs = np.arange(B, dtype=np.int32)
-    pos = np.full(B, CTX - 1, np.int32)  # fixed context: each step re-decodes the last position
-    toks = rng.integers(0, cfg.vocab, B).astype(np.uint32)
-    for _ in range(max(3, args.warmup)):
-        toks, _ = eng.decode_batch(seqs, toks, pos)
-    steps = max(1, min(args.steps, 20))
-    stream = torch.cuda.ExternalStream(eng.stream)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0 = time.perf_counter()
-    ev0.record(stream)
-    for _ in range(steps):
-        toks, _ = eng.decode_batch(seqs, toks, pos)
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    wall = (time.perf_counter() - t0) / steps
-    dev = ev0.elapsed_time(ev1) / 1e3 / steps
+    eng, cfg = make_engine(q, torch, 1, 0, local, None, sequences=BATCH)
+    out = time_batch(q, torch, eng, args, None, local, peaks, 1)
     eng.close()
-    # bytes a step must stream: the weights once, each sequence's K/V
-    kv_bytes = B * cfg.layers * cfg.kv_heads * CTX * cfg.head_dim * 2 * 2
-    w_bytes = sum(q.device_bytes(t, a, b) for _, t, a, b in q.model_tensors(cfg) if t != q.F32)
-    step_bytes = w_bytes + kv_bytes
-    gbs = step_bytes / dev / 1e9
-    return {"metric": "Qwen3-4B batched decode tok/s (64 sequences, context 4096, fp16 KV)",
-            "value": round(B / dev, 1), "unit": "tok/s", "n_gpus": 1, "steps": steps,
-            "warmup": max(3, args.warmup), "ms_per_step": round(dev * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
-            "dtype": "fp16 tensor-core products, fp16 KV, fp32 softmax and accumulation",
-            "data": "synthetic (seeded random-init Q4_K_M weights and N(0,1) fp16 KV)",
-            "config": {"workload": "64 sequences x 1 token per step at context 4096", "model": MODEL,
-                       "global_batch": B, "seq_len": CTX, "parallelism": "tp1",
-                       "l2": f"{step_bytes / 1e9:.1f} GB streamed per step (weights + 64 caches)"},
-            "roofline": {"kernel": "whole step", "bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
-                         "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": None,
-                         "algorithmic_bytes": step_bytes},
-            "e2e": {"value": round(B / wall, 1), "unit": "tok/s", "h2d_bytes_per_step": 12 * B,
-                    "d2h_bytes_per_step": 4 * B + 4, "how": "q4k_engine_decode_batch per step, host wall clock"},
-            "gpu_launches": steps * (1 + 36 * 11 + 3)}
+    out.update({"n_gpus": 1, "scaling": "weak", "vs_baseline": None,
+                "data": "synthetic (seeded random-init Q4_K_M weights and N(0,1) fp16 KV)"})
+    return out
+
+
+def cpu_steps_for(step_s: float, steps: int, budget_s: float = 150.0) -> int:
+    """Steps of the CPU arm: the requested count, unless that would run
+    longer than `budget_s`, then as many as fit (at least one)."""
+    return max(1, min(steps, int(budget_s / max(step_s, 1e-9))))
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return None
-    steps = max(1, min(args.steps, 5))
-    warm = 1
-    model, kc, vc = cpu_decode_model()
-    cpu_decode_steps(model, kc, vc, warm)
-    secs = cpu_decode_steps(model, kc, vc, steps)
+    threads = cpu_threads()
+    model, kc, vc = cpu_model()
+    first = cpu_decode_steps(model, kc, vc, 1, threads)
+    warm = max(0, min(args.warmup, cpu_steps_for(first, args.warmup, 30.0)) - 1)
+    if warm:
+        cpu_decode_steps(model, kc, vc, warm, threads)
+    steps = cpu_steps_for(first, args.steps)
+    secs = cpu_decode_steps(model, kc, vc, steps, threads)
     value = steps / secs
-    cores = cpu_cores()
-    return {"impl": "reference", "metric": METRIC_DECODE, "value": round(value, 4), "unit": "tok/s", "n_gpus": world,
-            "steps": steps, "warmup": warm, "ms_per_step": round(secs / steps * 1e3, 2), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "fp32 activations (Q8-quantised), double accumulate",
-            "data": "synthetic (same seeded weights and KV as the GPU arm)",
-            "config": {"workload": "decode batch 1 at context 4096 (BASELINE configs[2])", "model": MODEL,
-                       "global_batch": 1, "seq_len": CTX, "parallelism": "cpu"},
-            "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": cores, "kind": "port",
-                             "sample": f"{steps} full decode steps (36 layers + head, context 4096) on {cores} "
-                                       "host threads; oracle/q4k_oracle.c restating MatmulReference.hpp:42-64 "
-                                       "and Engine.cpp:37-114"},
-            "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    out = {"impl": "reference", "metric": METRIC_DECODE, "value": round(value, 4), "unit": "tok/s", "n_gpus": world,
+           "steps": steps, "warmup": warm + 1, "ms_per_step": round(secs / steps * 1e3, 2), "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None, "dtype": "fp32 activations (Q8-quantised), double accumulate",
+           "data": "synthetic (the same seeded weights and KV as the GPU arm, generated by oracle/q4k_synth.c)",
+           "config": {"workload": "decode batch 1 at context 4096 (BASELINE configs[2])", "model": MODEL,
+                      "global_batch": 1, "seq_len": CTX, "parallelism": "cpu"},
+           "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+                            "sample": f"{steps} full decode steps (36 layers + head, context 4096) on {threads} "
+                                      "OpenMP threads; oracle/q4k_oracle.c restating MatmulReference.hpp:42-64 "
+                                      "and Engine.cpp:37-114"},
+           "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if steps < args.steps or warm + 1 < args.warmup:
+        out["steps_cap"] = (f"{args.steps} steps / {args.warmup} warm-up requested; {steps} / {warm + 1} run to keep "
+                            "the CPU arm within a few minutes (one step took "
+                            f"{first:.2f} s)")
+    return out
+
+
+def attach_cpu_baselines(out: dict) -> None:
+    """Rank 0 at N = 1: the oracle on this host's cores, bounded samples of
+    the line's three workloads."""
+    threads = cpu_threads()
+    model, kc, vc = cpu_model()
+    cpu_decode_steps(model, kc, vc, 1, threads)
+    secs = cpu_decode_steps(model, kc, vc, 1, threads)
+    out["cpu_baseline"] = {"value": round(1 / secs, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+                           "sample": f"1 full decode step (36 layers + head, context 4096) on {threads} OpenMP "
+                                     "threads, oracle/q4k_oracle.c (MatmulReference.hpp:42-64 restated, OpenMP over "
+                                     "output rows)"}
+    if "batch" in out:
+        pos, _, _ = batch_rows()
+        t = 0.0
+        for p in pos[:2]:
+            t += cpu_decode_steps(model, kc, vc, 1, threads, pos=int(p))
+        out["batch"]["cpu_baseline"] = {
+            "value": round(2 / t, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"2 of the 64 sequences (contexts {int(pos[0]) + 1}, {int(pos[1]) + 1}), one decode step each, "
+                      f"one after the other as separate sessions (the reference's way), on {threads} OpenMP threads"}
+    del model, kc, vc
+    if "prefill" in out:
+        out["prefill"]["cpu_baseline"] = cpu_prefill_sample(threads)
 
 
 def main() -> None:
@@ -685,32 +828,28 @@ def main() -> None:
     else:
         out = run_gemv(args, world, rank, local)
     if rank == 0 and out is not None:
-        if world == 1 and args.workload == "decode" and not args.no_cpu_baseline:
-            model, kc, vc = cpu_decode_model()
-            cpu_decode_steps(model, kc, vc, 1)
-            secs = cpu_decode_steps(model, kc, vc, 1)
-            cores = cpu_cores()
-            out["cpu_baseline"] = {"value": round(1 / secs, 4), "unit": "tok/s", "cores": cores, "kind": "port",
-                                   "sample": f"1 full decode step (36 layers + head, context 4096) on {cores} host "
-                                             "threads, oracle/q4k_oracle.c (MatmulReference.hpp:42-64 restated, "
-                                             "OpenMP over output rows)"}
+        if world == 1 and args.workload in ("decode", "prefill", "batch") and not args.no_cpu_baseline:
+            if args.workload == "decode":
+                attach_cpu_baselines(out)
+            elif args.workload == "prefill":
+                out["cpu_baseline"] = cpu_prefill_sample(cpu_threads())
+            else:
+                attach_cpu_baselines(tmp := {"batch": out})
+                out["cpu_baseline"] = tmp["batch"]["cpu_baseline"]
         elif args.workload == "gemv" and not args.no_cpu_baseline:
-            sys.path.insert(0, os.path.join(ROOT, "oracle"))
-            import oracle as o
-            import q4kb200 as q
-
-            raw = q.synth_tensor_host(SEED, "bench.cpu", q.Q4_K, 2560, 9728)
-            x = q.synth_f32_host(SEED, "bench.x", 2560)
-            o.matmul(x, raw, q.Q4_K, 2560, 9728)
+            o = _oracle()
+            raw = o.synth_tensor(SEED, "bench.cpu", o.Q4_K, 2560, 9728)
+            x = o.synth_f32(SEED, "bench.x", 2560)
+            threads = cpu_threads()
+            o.matmul(x, raw, o.Q4_K, 2560, 9728, threads=threads)
             reps = 20
             t0 = time.perf_counter()
             for _ in range(reps):
-                o.matmul(x, raw, q.Q4_K, 2560, 9728)
+                o.matmul(x, raw, o.Q4_K, 2560, 9728, threads=threads)
             t = (time.perf_counter() - t0) / reps
-            cores = cpu_cores()
-            out["cpu_baseline"] = {"value": round(gemv_bytes(q, q.Q4_K, 2560, 9728) / t / 1e9, 3), "unit": "GB/s",
-                                   "cores": cores, "kind": "port",
-                                   "sample": f"{reps} Q4_K 9728x2560 products on {cores} host threads"}
+            b = 9728 * o.row_bytes(o.Q4_K, 2560) + 2560 * 4 + 9728 * 4
+            out["cpu_baseline"] = {"value": round(b / t / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                                   "sample": f"{reps} Q4_K 9728x2560 products on {threads} OpenMP threads"}
         print(json.dumps(out), flush=True)
 
 

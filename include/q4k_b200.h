@@ -155,7 +155,11 @@ int q4k_matmul_batch(const float* input, const float* norm_gamma, float epsilon,
  * *position_device is the token's position. head_dim must be 128,
  * query_heads == 4 * kv_heads and kv_heads <= 64 (the scratch's 256-byte
  * counter block). scratch: q4k_attention_decode_scratch_bytes
- * bytes, 16-byte aligned, zeroed once before first use. */
+ * bytes, 16-byte aligned; the call clears its counter block on `stream`
+ * before launching. The kernel's waits on its tile copies are bounded
+ * (2 s): if one gives up, `output` is undefined, and this asynchronous
+ * call does not report it (the decode engine reads such timeouts back
+ * through its error word). */
 int q4k_attention_decode_f16(const float* qkv, const float* q_gamma, const float* k_gamma, uint16_t* k_cache,
                              uint16_t* v_cache, int capacity, const int* position_device, int query_heads,
                              int kv_heads, int head_dim, float epsilon, float rope_base, float* output,
@@ -169,7 +173,9 @@ size_t q4k_attention_decode_scratch_bytes(int query_heads, int kv_heads);
  * bytes must fit in 1 MiB (2016 head-splits; with the default one CTA per SM
  * a B200 needs 592), else Q4K_ERANGE; at most 64 KV heads. The first call on
  * a device (with it current) looks up the array's address and should come
- * before any stream capture. Every call clears the per-head counters on
+ * before any stream capture; the address is kept for the life of the
+ * process, so resetting the device (cudaDeviceReset) after that first call
+ * is not supported. Every call clears the per-head counters on
  * `stream` before launching. Calls on one device share the array: calls that
  * can overlap in time race and must be ordered by the caller. */
 int q4k_attention_decode_f16_static(const float* qkv, const float* q_gamma, const float* k_gamma, uint16_t* k_cache,
@@ -270,8 +276,12 @@ int q4k_engine_prefill_seq(q4k_engine* engine, int seq, const uint32_t* tokens, 
  * tokens[i] is embedded at positions[i] of sequence seqs[i]; next_tokens[i]
  * receives its greedy successor. The products run over all n rows (the
  * batched GEMV up to 8 rows, the tensor-core GEMM above), attention over
- * each sequence's own cache. logits_host (n x vocab floats) may be NULL.
- * tp_world == 1; 1 <= n <= sequences. Synchronous. */
+ * each sequence's own cache. logits_host (n x vocab floats; this rank's
+ * vocabulary shard of each row when tp_world > 1) may be NULL. With
+ * tp_world > 1 every rank calls it with the same rows: the row-parallel
+ * sums are all-reduced and each row's greedy token is merged over the
+ * ranks' head shards (lowest index on ties). 1 <= n <= min(sequences, 512).
+ * Synchronous. */
 int q4k_engine_decode_batch(q4k_engine* engine, int n, const int* seqs, const uint32_t* tokens, const int* positions,
                             uint32_t* next_tokens, float* logits_host);
 
@@ -288,6 +298,25 @@ int q4k_engine_generate(q4k_engine* engine, uint32_t token, int position, int st
  * x_out_host; writes that layer's K/V row at `position`. For checking a
  * layer against another implementation on identical inputs. Synchronous. */
 int q4k_engine_layer(q4k_engine* engine, int layer, const float* x_host, int position, float* x_out_host);
+
+/* One transformer block of a prompt pass (src/Engine.cpp:71-103 with
+ * tokens = n, as q4k_engine_prefill runs it: the products over all rows on
+ * the tensor cores from 9 rows up) applied to given residual-stream rows
+ * x_host [n][hidden] at positions position .. position+n-1 of sequence
+ * `seq`; result in x_out_host [n][hidden]; writes the n K/V rows. n is at
+ * most one prefill pass (512 rows). For checking a layer of the GEMM path
+ * against another implementation on identical inputs. With tp_world > 1
+ * every rank calls it (the row-parallel sums are all-reduced). Synchronous. */
+int q4k_engine_layer_rows(q4k_engine* engine, int layer, int seq, int n, int position, const float* x_host,
+                          float* x_out_host);
+
+/* One transformer block of a batched decode step (q4k_engine_decode_batch's
+ * products and per-sequence attention) on given rows: row i of x_host
+ * [n][hidden] is the token at positions[i] of sequence seqs[i]; result in
+ * x_out_host; writes each row's K/V. The reference serves each sequence as
+ * its own session (Engine.cpp:71-103 per ChatSession). Synchronous. */
+int q4k_engine_layer_batch(q4k_engine* engine, int layer, int n, const int* seqs, const int* positions,
+                           const float* x_host, float* x_out_host);
 
 /* Stream the engine launches on (cudaStream_t), e.g. to time with events. */
 void* q4k_engine_stream(q4k_engine* engine);

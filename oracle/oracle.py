@@ -54,6 +54,12 @@ def lib():
         L.orc_float_to_half.argtypes = [C.c_float]
         L.orc_float_to_half.restype = C.c_uint16
         L.orc_forward.argtypes = [P, P, P, C.c_size_t, P, C.c_size_t, C.c_size_t, C.c_int, P, P, P, C.c_int]
+        L.orc_synth_key.argtypes = [C.c_uint64, C.c_char_p]
+        L.orc_synth_key.restype = C.c_uint64
+        L.orc_synth_tensor.argtypes = [C.c_uint64, C.c_char_p, C.c_int, C.c_int64, C.c_int64, P]
+        L.orc_synth_f16.argtypes = [C.c_uint64, C.c_char_p, C.c_uint64, C.c_size_t, P]
+        L.orc_synth_f32.argtypes = [C.c_uint64, C.c_char_p, C.c_size_t, P]
+        L.orc_omp_threads.argtypes = [C.c_int]
         _lib = L
     return _lib
 
@@ -65,6 +71,68 @@ def _p(a: np.ndarray):
 
 def row_bytes(qtype: int, K: int) -> int:
     return (K // 256) * (144 if qtype == Q4_K else 210)
+
+
+# --------------------------------------------------------------------------
+# The benchmark's synthetic model, built here without the product library
+# (q4k_synth.c restates its seeded streams; the CPU tests compare the bytes).
+# --------------------------------------------------------------------------
+def qwen3_4b_config(capacity: int = 4096) -> dict:
+    """Qwen3-4B shapes (Engine.cpp:49-55 metadata of the real model)."""
+    return {"layers": 36, "hidden": 2560, "heads": 32, "kv_heads": 8, "head_dim": 128, "ffn": 9728,
+            "vocab": 151936, "eps": 1e-6, "rope_base": 1e6, "capacity": capacity}
+
+
+def model_tensors(cfg: dict):
+    """(name, type, ne0, ne1) of every tensor of the synthetic Q4_K_M model
+    in the engine's order: per layer the eleven Engine.cpp:82-109 tensors
+    (Q6_K for attn_v and the ffn_down of even layers, Q4_K for the other
+    matrices, F32 norms), then output_norm and token_embd (Q6_K, the head)."""
+    qd, kvd = cfg["heads"] * cfg["head_dim"], cfg["kv_heads"] * cfg["head_dim"]
+    H, F = cfg["hidden"], cfg["ffn"]
+    out = []
+    for i in range(cfg["layers"]):
+        shapes = {"attn_norm": (F32, H, 1), "attn_q": (Q4_K, H, qd), "attn_k": (Q4_K, H, kvd),
+                  "attn_v": (Q6_K, H, kvd), "attn_q_norm": (F32, cfg["head_dim"], 1),
+                  "attn_k_norm": (F32, cfg["head_dim"], 1), "attn_output": (Q4_K, qd, H), "ffn_norm": (F32, H, 1),
+                  "ffn_gate": (Q4_K, H, F), "ffn_up": (Q4_K, H, F),
+                  "ffn_down": (Q6_K if i % 2 == 0 else Q4_K, F, H)}
+        for s in SLOT_NAMES:
+            t, a, b = shapes[s]
+            out.append((f"blk.{i}.{s}.weight", t, a, b))
+    out.append(("output_norm.weight", F32, H, 1))
+    out.append(("token_embd.weight", Q6_K, H, cfg["vocab"]))
+    return out
+
+
+def synth_tensor(seed: int, name: str, qtype: int, ne0: int, ne1: int) -> np.ndarray:
+    """Tensor `name` of the seeded synthetic model in GGUF layout (float32
+    values for F32, raw super-block bytes otherwise)."""
+    if qtype == F32:
+        out = np.empty(ne0 * ne1, np.float32)
+    else:
+        out = np.empty(ne1 * row_bytes(qtype, ne0), np.uint8)
+    if lib().orc_synth_tensor(seed, name.encode(), qtype, ne0, ne1, _p(out)):
+        raise ValueError(f"bad synthetic tensor request {name}")
+    return out
+
+
+def synth_f16(seed: int, name: str, index_base: int, n: int) -> np.ndarray:
+    out = np.empty(n, np.uint16)
+    lib().orc_synth_f16(seed, name.encode(), index_base, n, _p(out))
+    return out
+
+
+def synth_f32(seed: int, name: str, n: int) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    lib().orc_synth_f32(seed, name.encode(), n, _p(out))
+    return out
+
+
+def omp_threads(requested: int = 0) -> int:
+    """Threads an OpenMP region of the oracle gets when asked for
+    `requested` (<= 0: the OpenMP default, e.g. OMP_NUM_THREADS)."""
+    return int(lib().orc_omp_threads(requested))
 
 
 def dequantize_rows(packed: np.ndarray, qtype: int, rows: int, width: int, row_bytes_: int | None = None):
@@ -209,6 +277,8 @@ def ref():
         L.ref_argmax.argtypes = [P, S, C.POINTER(C.c_uint32)]
         L.ref_forward.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
                                   C.c_float, P, S, P, P, S, P, S, S, C.c_int, P, P, C.POINTER(C.c_uint32)]
+        L.ref_layer.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, C.c_float, P, P, P, S, S,
+                                S, C.c_int]
         _ref = L
     return _ref
 
@@ -216,6 +286,18 @@ def ref():
 def ref_check(rc: int) -> None:
     if rc:
         raise RuntimeError(f"reference call failed ({rc}): {ref().ref_last_error().decode()}")
+
+
+def ref_layer(handles: dict, cfg: dict, layer: int, x_dev: int, k_dev: int, v_dev: int, capacity: int,
+              tokens: int, offset: int, kv_round_f16: bool = True) -> None:
+    """One block of Engine::inference with the reference kernels (ref_layer
+    in ref_shim/ref_harness.cu): x_dev [tokens][hidden] updated in place,
+    k_dev / v_dev this layer's fp32 caches [capacity][kv_heads*head_dim];
+    all device addresses. `handles` maps tensor names to RefWeight."""
+    ws = (C.c_void_p * SLOTS)(*[handles[f"blk.{layer}.{s}.weight"].h.value for s in SLOT_NAMES])
+    ref_check(ref().ref_layer(ws, cfg["hidden"], cfg["heads"], cfg["kv_heads"], cfg["head_dim"], cfg["ffn"],
+                              cfg["eps"], cfg["rope_base"], x_dev, k_dev, v_dev, capacity, tokens, offset,
+                              int(kv_round_f16)))
 
 
 class RefWeight:

@@ -303,6 +303,10 @@ int orc_forward(const orc_model* m, float* k_cache, float* v_cache, size_t capac
                 int threads) {
     if (tokens == 0) return -1;
     if (pos + tokens > capacity) return -2; /* ChatSession.hpp:40-41 */
+#ifdef _OPENMP
+    /* the attention's parallel region takes the same thread count */
+    if (threads > 0) omp_set_num_threads(threads);
+#endif
     const size_t W = (size_t)m->hidden, H = (size_t)m->heads, KVH = (size_t)m->kv_heads, D = (size_t)m->head_dim;
     const size_t F = (size_t)m->ffn, V = (size_t)m->vocab;
     const size_t QW = H * D, KW = KVH * D;

@@ -84,6 +84,18 @@ int orc_forward(const orc_model* model, float* k_cache, float* v_cache, size_t c
                 size_t tokens, size_t pos, int kv_round_f16, float* logits, float* hidden, uint32_t* next_token,
                 int threads);
 
+/* Seeded synthetic tensors (q4k_synth.c): the benchmark model's bytes
+ * without the product library. orc_synth_tensor writes a GGUF-layout
+ * Q4_K/Q6_K tensor or an F32 RMSNorm gamma (ne0 * ne1 values); the f16/f32
+ * streams are the KV fill and synthetic activations. Returns 0 or 1 (bad
+ * request). orc_omp_threads reports the threads an OpenMP region asked for
+ * `requested` (<= 0: the default) actually gets. */
+uint64_t orc_synth_key(uint64_t seed, const char* name);
+int orc_synth_tensor(uint64_t seed, const char* name, int type, int64_t ne0, int64_t ne1, void* out);
+void orc_synth_f16(uint64_t seed, const char* name, uint64_t index_base, size_t n, uint16_t* out);
+void orc_synth_f32(uint64_t seed, const char* name, size_t n, float* out);
+int orc_omp_threads(int requested);
+
 #ifdef __cplusplus
 }
 #endif

@@ -226,3 +226,59 @@ REF_API int ref_forward(void* const* weights, int layers, int width, int heads, 
         if (next_token) *next_token = next;
     });
 }
+
+// One block of Engine::inference (src/Engine.cpp:71-103) with the reference
+// kernels on given residual-stream rows: layer_weights are the SLOTS Weight
+// handles of one layer; x (device, [tokens][width]) is updated in place;
+// k_cache / v_cache (device fp32 [capacity][kv_heads*head_dim]) are this
+// layer's caches, rows [0, offset) the prefix, rows offset.. written here
+// (rounded to fp16 when kv_round_f16, as the fp16-KV configuration stores
+// them).
+REF_API int ref_layer(void* const* layer_weights, int width, int heads, int kv_heads, int head_dim, int ffn, float eps,
+                      float rope_base, float* x, float* k_cache, float* v_cache, size_t capacity, size_t tokens,
+                      size_t offset, int kv_round_f16) {
+    return guarded([&] {
+        using namespace kernels;
+        auto W = [&](int slot) -> const Weight& { return *static_cast<const Weight*>(layer_weights[slot]); };
+        if (offset + tokens > capacity) throw std::length_error("Chat session cache capacity exceeded");
+        const size_t kv_width = size_t(kv_heads) * head_dim;
+        DeviceBuffer normalized(tokens * width * sizeof(float));
+        DeviceBuffer q(tokens * heads * head_dim * sizeof(float));
+        DeviceBuffer k(tokens * kv_width * sizeof(float));
+        DeviceBuffer q_normalized(tokens * heads * head_dim * sizeof(float));
+        DeviceBuffer attended(tokens * heads * head_dim * sizeof(float));
+        DeviceBuffer branch(tokens * width * sizeof(float));
+        DeviceBuffer gate(tokens * ffn * sizeof(float));
+        DeviceBuffer up(tokens * ffn * sizeof(float));
+        DeviceBuffer activated(tokens * ffn * sizeof(float));
+        auto fp = [](DeviceBuffer& b) { return static_cast<float*>(b.data); };
+        float* new_k = k_cache + offset * kv_width;
+        float* new_v = v_cache + offset * kv_width;
+
+        rms_norm(x, W(SLOT_ATTN_NORM), fp(normalized), tokens, width, eps);
+        matmul(fp(normalized), W(SLOT_Q), fp(q), tokens);
+        matmul(fp(normalized), W(SLOT_K), fp(k), tokens);
+        matmul(fp(normalized), W(SLOT_V), new_v, tokens);
+        rms_norm(fp(q), W(SLOT_Q_NORM), fp(q_normalized), tokens * heads, head_dim, eps);
+        rms_norm(fp(k), W(SLOT_K_NORM), new_k, tokens * kv_heads, head_dim, eps);
+        rope(fp(q_normalized), tokens, heads, head_dim, offset, rope_base);
+        rope(new_k, tokens, kv_heads, head_dim, offset, rope_base);
+        if (kv_round_f16) {
+            const size_t n = tokens * kv_width;
+            round_rows_f16<<<(n + 255) / 256, 256>>>(new_k, n);
+            round_rows_f16<<<(n + 255) / 256, 256>>>(new_v, n);
+            detail::check_launch();
+        }
+        attention(fp(q_normalized), k_cache, v_cache, fp(attended), tokens, heads, kv_heads, head_dim, offset);
+        matmul(fp(attended), W(SLOT_O), fp(branch), tokens);
+        residual_add(x, fp(branch), tokens * width);
+        rms_norm(x, W(SLOT_FFN_NORM), fp(normalized), tokens, width, eps);
+        matmul(fp(normalized), W(SLOT_GATE), fp(gate), tokens);
+        matmul(fp(normalized), W(SLOT_UP), fp(up), tokens);
+        silu_multiply(fp(gate), fp(up), fp(activated), tokens * ffn);
+        matmul(fp(activated), W(SLOT_DOWN), fp(branch), tokens);
+        residual_add(x, fp(branch), tokens * width);
+        const auto e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) throw std::runtime_error(cudaGetErrorString(e));
+    });
+}

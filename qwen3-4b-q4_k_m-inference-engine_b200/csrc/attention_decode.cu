@@ -43,6 +43,11 @@ constexpr int T = kAttnTile;  // positions per tile
 constexpr int kComputeWarps = 8;
 constexpr int kComputeThreads = kComputeWarps * 32;
 constexpr int kStageBytes = 2 * kTileBytes;  // K + V
+// The merging CTA stages every split's (m, l) pair of its G heads in the
+// stage buffers, reading up to a whole kBatch of splits past the last one:
+// (splits rounded up to kBatch) x G x 2 floats must fit in them.
+constexpr int kMergeBatch = 24;
+constexpr int kMaxSplits = 3 * kStageBytes / (G * 2 * 4) - kMergeBatch;
 
 struct Args {
     const float* qkv;
@@ -381,7 +386,7 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
     // The merge is on the critical path of the step: the o partials of the
     // first kBatch splits are loaded in the same round trip as every
     // split's (m, l) (into shared memory; the stage buffers are free).
-    constexpr int kBatch = 24;
+    constexpr int kBatch = kMergeBatch;
     const float2* po = reinterpret_cast<const float2*>(partial_o + ((size_t)kvh * splits * G + hq) * D + d0);
     float2 v[kBatch];
 #pragma unroll
@@ -478,9 +483,10 @@ cudaError_t make_kv_tensor_map(const uint16_t* base, long long rows, KvTensorMap
 // stream but lengthen the cross-split merge, and one per SM measured faster.
 int decode_attention_splits(int kv_heads) {
     const char* env = std::getenv("Q4K_ATTN_CTAS_PER_SM");
-    const int per_sm = env && *env ? std::atoi(env) : 1;
+    int per_sm = env && *env ? std::atoi(env) : 1;
+    per_sm = per_sm < 1 ? 1 : per_sm > 64 ? 64 : per_sm;
     const int s = per_sm * sm_count() / (kv_heads > 0 ? kv_heads : 1);
-    return s < 1 ? 1 : s;
+    return s < 1 ? 1 : s > kMaxSplits ? kMaxSplits : s;
 }
 
 size_t decode_attention_scratch_floats(int heads, int kv_heads, int splits) {
@@ -490,7 +496,8 @@ size_t decode_attention_scratch_floats(int heads, int kv_heads, int splits) {
 
 cudaError_t decode_attention(const DecodeAttnArgs& in, const KvTensorMap& kmap, const KvTensorMap& vmap,
                              cudaStream_t s, bool pdl) {
-    if (in.kv_heads <= 0 || in.heads != in.kv_heads * G || in.splits <= 0 || in.capacity <= 0)
+    if (in.kv_heads <= 0 || in.heads != in.kv_heads * G || in.splits <= 0 || in.splits > kMaxSplits ||
+        in.capacity <= 0)
         return cudaErrorInvalidValue;
     Args a;
     a.qkv = in.qkv;

@@ -13,7 +13,8 @@
 // gets its own copy with the module). Its address is taken once per device
 // with cudaGetSymbolAddress, with that device current, on the first call
 // made while it is current; that first call should come before any stream
-// capture begins. Layout is the regular scratch layout: 256 bytes of per-KV-
+// capture begins; the address is kept for the life of the process, so a
+// device reset after that first call is not supported. Layout is the regular scratch layout: 256 bytes of per-KV-
 // head counters (they must be zero when a launch starts; static storage
 // starts zeroed, the merging CTA of each head resets its counter, and the
 // entry point clears them before every launch), then the split partials,

@@ -405,8 +405,7 @@ Q4K_API int q4k_attention_decode_f16_static(const float* qkv, const float* q_gam
             invalid("decode attention supports head_dim 128 with 4 query heads per KV head (at most 64 KV heads)");
         const size_t need = 256 + sizeof(float) * (size_t)query_heads *
                                       q4k::decode_attention_splits(kv_heads) * (q4k::kDecodeHeadDim + 2);
-        scratch = q4k::attention_static_scratch(need);
-        q4k::cuda_check(cudaMemsetAsync(scratch, 0, 256, as_stream(stream)), "clear attention counters");
+        scratch = q4k::attention_static_scratch(need);  // the call below clears its counters
     });
     if (rc != Q4K_OK) return rc;
     return q4k_attention_decode_f16(qkv, q_gamma, k_gamma, k_cache, v_cache, capacity, position_device, query_heads,
@@ -452,6 +451,9 @@ Q4K_API int q4k_attention_decode_f16(const float* qkv, const float* q_gamma, con
         q4k::KvTensorMap km, vm;
         q4k::cuda_check(q4k::make_kv_tensor_map(k_cache, (long long)kv_heads * capacity, &km), "K tensor map");
         q4k::cuda_check(q4k::make_kv_tensor_map(v_cache, (long long)kv_heads * capacity, &vm), "V tensor map");
+        // the per-head counters start every call at zero, even after a
+        // launch whose bounded waits gave up before its merge reset them
+        q4k::cuda_check(cudaMemsetAsync(sb, 0, 256, as_stream(stream)), "clear attention counters");
         launched(q4k::decode_attention(a, km, vm, as_stream(stream), false));
     });
 }
@@ -758,6 +760,22 @@ Q4K_API int q4k_engine_layer(q4k_engine* e, int layer, const float* x_host, int 
     return guarded_cuda([&] {
         if (!e || !x_host || !x_out_host) invalid("engine and buffers required");
         e->impl.layer_step(layer, x_host, position, x_out_host);
+    });
+}
+
+Q4K_API int q4k_engine_layer_rows(q4k_engine* e, int layer, int seq, int n, int position, const float* x_host,
+                                  float* x_out_host) {
+    return guarded_cuda([&] {
+        if (!e || !x_host || !x_out_host) invalid("engine and buffers required");
+        e->impl.layer_rows(layer, seq, n, position, x_host, x_out_host);
+    });
+}
+
+Q4K_API int q4k_engine_layer_batch(q4k_engine* e, int layer, int n, const int* seqs, const int* positions,
+                                   const float* x_host, float* x_out_host) {
+    return guarded_cuda([&] {
+        if (!e || !seqs || !positions || !x_host || !x_out_host) invalid("engine, rows and buffers required");
+        e->impl.layer_batch(layer, n, seqs, positions, x_host, x_out_host);
     });
 }
 

@@ -103,8 +103,11 @@ __global__ void finish_step_kernel(uint32_t* token, int* pos, const int* advance
 }
 
 // Greedy token of each of n logit rows (argmax.cu:25-98 semantics: the
-// largest value, the lowest index among equals).
-__global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* logits, int vocab, uint32_t* out) {
+// largest value, the lowest index among equals). With `cand` set (a head
+// sharded over tensor-parallel ranks) row r's best also goes to cand[2r]
+// (score bits) and cand[2r+1] (index + index_base) for the cross-rank merge.
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* logits, int vocab, uint32_t* out,
+                                                           uint32_t* cand, uint32_t index_base) {
     const float* row = logits + (size_t)blockIdx.x * vocab;
     float bs = -CUDART_INF_F;
     uint32_t bi = 0xFFFFFFFFu;
@@ -136,7 +139,29 @@ __global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* logits, 
                 bi = si[w];
             }
         out[blockIdx.x] = bi;
+        if (cand) {
+            cand[2 * blockIdx.x] = __float_as_uint(bs);
+            cand[2 * blockIdx.x + 1] = bi == 0xFFFFFFFFu ? bi : bi + index_base;
+        }
     }
+}
+
+// Greedy token of row r over the ranks' shard winners cand_all[w][r][2]:
+// the larger logit, then the lower global index (argmax.cu ordering).
+__global__ void merge_row_candidates_kernel(const uint32_t* cand_all, int world, int n, uint32_t* out) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= n) return;
+    float bs = __uint_as_float(cand_all[2 * r]);
+    uint32_t bi = cand_all[2 * r + 1];
+    for (int w = 1; w < world; ++w) {
+        const float sc = __uint_as_float(cand_all[((size_t)w * n + r) * 2]);
+        const uint32_t ix = cand_all[((size_t)w * n + r) * 2 + 1];
+        if (candidate_better(sc, ix, bs, bi)) {
+            bs = sc;
+            bi = ix;
+        }
+    }
+    out[r] = bi;
 }
 
 }  // namespace
@@ -976,7 +1001,27 @@ void Engine::ensure_prefill() {
         const size_t max_k = std::max<size_t>({H, (size_t)qd_, (size_t)ffn_l_});
         pf_a_ = static_cast<uint16_t*>(alloc(sizeof(uint16_t) * rows * max_k));
         pf_rs_ = static_cast<float*>(alloc(sizeof(float) * rows));
-        pf_part_floats_ = (size_t)rows * std::max<size_t>({H, (size_t)(qd_ + 2 * kvd_), 2 * (size_t)ffn_l_}) * 2;
+        // split-K workspace: the most any product of a layer (or the batched
+        // head) would use at any row count of a pass, so that the engine's
+        // products take the same K splits as q4k_matmul_batch
+        pf_part_floats_ = 0;
+        for (int m = 1; m <= rows; ++m) {
+            PrefillGemmArgs g;
+            g.M = m;
+            auto need = [&](int nseg, int K, int epi, std::initializer_list<int> outs) {
+                g.nseg = nseg;
+                g.K = K;
+                g.epilogue = epi;
+                int i = 0;
+                for (int n : outs) g.seg[i++].rows = n;
+                pf_part_floats_ = std::max(pf_part_floats_, prefill_gemm_partial_floats(g));
+            };
+            need(3, (int)H, EPI_STORE, {qd_, kvd_, kvd_});
+            need(1, qd_, EPI_ADD, {(int)H});
+            need(2, (int)H, EPI_SWIGLU, {ffn_l_, ffn_l_});
+            need(1, ffn_l_, EPI_ADD, {(int)H});
+            need(1, (int)H, EPI_STORE, {(int)(vocab1_ - vocab0_)});
+        }
         pf_part_ = static_cast<float*>(alloc(sizeof(float) * pf_part_floats_));
         const int ks[3] = {(int)H, qd_, ffn_l_};
         for (int i = 0; i < 3; ++i) cuda_check(make_act_map(pf_a_, ks[i], rows, &pf_amap_[i]), "activation map");
@@ -1217,6 +1262,11 @@ void Engine::ensure_batch() {
     b_seq_ = static_cast<int*>(alloc(sizeof(int) * B));
     b_tok_ = static_cast<uint32_t*>(alloc(sizeof(uint32_t) * B));
     b_next_ = static_cast<uint32_t*>(alloc(sizeof(uint32_t) * B));
+    if (world_ > 1) {
+        b_partial_ = static_cast<float*>(alloc(sizeof(float) * B * H));
+        b_cand_ = static_cast<uint32_t*>(alloc(sizeof(uint32_t) * 2 * B));
+        b_cand_all_ = static_cast<uint32_t*>(alloc(sizeof(uint32_t) * 2 * B * (size_t)world_));
+    }
     b_cap_ = B;
 }
 
@@ -1227,6 +1277,14 @@ void Engine::enqueue_batch_layer(int i, int n, int splits) {
     const int H = c.hidden;
     const int W = qd_ + 2 * kvd_;
     auto product = [&](GemvRequest& r, int slot) { enqueue_product(r, pf_gemm_ ? layer_maps(i, slot) : nullptr); };
+    // tp_world > 1: the row-parallel products write partial sums, summed over
+    // the ranks and added to the residual stream (Engine.cpp:94-95, :101-102)
+    auto all_reduce_into_x = [&]() {
+        const size_t cnt = (size_t)n * H;
+        nccl_check(nccl().AllReduce(b_partial_, b_partial_, cnt, ncclFloat, ncclSum, comm_, stream_),
+                   "ncclAllReduce");
+        cuda_check(residual_add(b_x_, b_partial_, cnt, stream_), "residual_add");
+    };
     const Layer& L = layers_[i];
     const size_t kv_layer = (size_t)i * KVHl_ * c.capacity * c.head_dim;
     {
@@ -1276,16 +1334,17 @@ void Engine::enqueue_batch_layer(int i, int n, int splits) {
     {
         GemvRequest r;
         r.nseg = 1;
-        r.seg[0] = {L.o, b_x_, L.to, H};
+        r.seg[0] = {L.o, world_ > 1 ? b_partial_ : b_x_, L.to, H};
         r.K = qd_;
         r.M = n;
         r.ldx = qd_;
         r.ldy = H;
         r.x = b_att_;
-        r.epilogue = EPI_ADD;
+        r.epilogue = world_ > 1 ? EPI_STORE : EPI_ADD;
         r.err = err_;
         r.pdl = true;
         product(r, 3);
+        if (world_ > 1) all_reduce_into_x();
     }
     {
         GemvRequest r;
@@ -1307,30 +1366,30 @@ void Engine::enqueue_batch_layer(int i, int n, int splits) {
     {
         GemvRequest r;
         r.nseg = 1;
-        r.seg[0] = {L.down, b_x_, L.tdown, H};
+        r.seg[0] = {L.down, world_ > 1 ? b_partial_ : b_x_, L.tdown, H};
         r.K = ffn_l_;
         r.M = n;
         r.ldx = ffn_l_;
         r.ldy = H;
         r.x = b_act_;
-        r.epilogue = EPI_ADD;
+        r.epilogue = world_ > 1 ? EPI_STORE : EPI_ADD;
         r.err = err_;
         r.pdl = true;
         product(r, 6);
+        if (world_ > 1) all_reduce_into_x();
     }
 }
 
-void Engine::decode_batch(int n, const int* seqs, const uint32_t* tokens, const int* positions, uint32_t* next_host,
-                          float* logits_host) {
+int Engine::stage_batch(int n, const int* seqs, const uint32_t* tokens, const int* positions) {
     if (!loaded_) throw Error(Q4K_EINVAL, "weights are not loaded");
-    if (world_ > 1) throw Error(Q4K_EINVAL, "batched decode needs tp_world == 1");
     ensure_prefill();
     if (n < 1 || n > std::min(seqs_, pf_rows_)) throw Error(Q4K_ERANGE, "batch size out of range");
+    if (!seqs || !positions) throw Error(Q4K_EINVAL, "batched step needs sequences and positions");
     std::vector<char> used(seqs_, 0);
     for (int b = 0; b < n; ++b) {
         if (seqs[b] < 0 || seqs[b] >= seqs_) throw Error(Q4K_ERANGE, "sequence out of range");
         if (used[seqs[b]]++) throw Error(Q4K_EINVAL, "a sequence appears twice in one step");
-        if (tokens[b] >= (uint32_t)c_.vocab) throw Error(Q4K_ERANGE, "Token ID out of range");
+        if (tokens && tokens[b] >= (uint32_t)c_.vocab) throw Error(Q4K_ERANGE, "Token ID out of range");
         if (positions[b] < 0 || positions[b] >= c_.capacity) throw Error(Q4K_ERANGE, "KV cache capacity exceeded");
     }
     if (pf_gemm_) ensure_prefill_maps();
@@ -1355,11 +1414,18 @@ void Engine::decode_batch(int n, const int* seqs, const uint32_t* tokens, const 
     }
     if (n == 1) splits = splits_;
     if (const char* e = std::getenv("Q4K_BATCH_SPLITS")) splits = std::min(std::max(1, std::atoi(e)), splits_);
+    cuda_check(cudaMemcpyAsync(b_seq_, seqs, sizeof(int) * n, cudaMemcpyHostToDevice, stream_), "h2d");
+    cuda_check(cudaMemcpyAsync(b_pos_, positions, sizeof(int) * n, cudaMemcpyHostToDevice, stream_), "h2d");
+    if (tokens) cuda_check(cudaMemcpyAsync(b_tok_, tokens, sizeof(uint32_t) * n, cudaMemcpyHostToDevice, stream_), "h2d");
+    return splits;
+}
+
+void Engine::decode_batch(int n, const int* seqs, const uint32_t* tokens, const int* positions, uint32_t* next_host,
+                          float* logits_host) {
+    if (!tokens) throw Error(Q4K_EINVAL, "batched decode needs tokens");
+    const int splits = stage_batch(n, seqs, tokens, positions);
     const int H = c_.hidden;
     const int vocab_l = (int)(vocab1_ - vocab0_);
-    cuda_check(cudaMemcpyAsync(b_seq_, seqs, sizeof(int) * n, cudaMemcpyHostToDevice, stream_), "h2d");
-    cuda_check(cudaMemcpyAsync(b_tok_, tokens, sizeof(uint32_t) * n, cudaMemcpyHostToDevice, stream_), "h2d");
-    cuda_check(cudaMemcpyAsync(b_pos_, positions, sizeof(int) * n, cudaMemcpyHostToDevice, stream_), "h2d");
     cuda_check(embed_rows(token_embd_, t_embd_, H, c_.vocab, b_tok_, n, b_x_, err_, stream_, false), "embed");
     for (int i = 0; i < c_.layers; ++i) enqueue_batch_layer(i, n, splits);
     {
@@ -1380,13 +1446,49 @@ void Engine::decode_batch(int n, const int* seqs, const uint32_t* tokens, const 
         r.pdl = true;
         enqueue_product(r, pf_gemm_ ? pf_head_map_ : nullptr);
     }
-    argmax_rows_kernel<<<n, 1024, 0, stream_>>>(b_logits_, vocab_l, b_next_);
+    argmax_rows_kernel<<<n, 1024, 0, stream_>>>(b_logits_, vocab_l, b_next_, world_ > 1 ? b_cand_ : nullptr,
+                                                (uint32_t)vocab0_);
     cuda_check(cudaGetLastError(), "argmax launch");
+    if (world_ > 1) {
+        // each rank's shard winners, then the lowest-index-first merge per row
+        nccl_check(nccl().AllGather(b_cand_, b_cand_all_, 2 * (size_t)n, ncclUint32, comm_, stream_),
+                   "ncclAllGather");
+        merge_row_candidates_kernel<<<(n + 127) / 128, 128, 0, stream_>>>(b_cand_all_, world_, n, b_next_);
+        cuda_check(cudaGetLastError(), "merge launch");
+    }
     cuda_check(cudaMemcpyAsync(next_host, b_next_, sizeof(uint32_t) * n, cudaMemcpyDeviceToHost, stream_), "d2h");
     if (logits_host)
         cuda_check(cudaMemcpyAsync(logits_host, b_logits_, sizeof(float) * n * (size_t)vocab_l, cudaMemcpyDeviceToHost,
                                    stream_),
                    "d2h logits");
+    check_device_error();
+}
+
+void Engine::layer_batch(int layer, int n, const int* seqs, const int* positions, const float* x_host,
+                         float* x_out_host) {
+    if (layer < 0 || layer >= c_.layers) throw Error(Q4K_ERANGE, "layer out of range");
+    if (!x_host || !x_out_host) throw Error(Q4K_EINVAL, "layer rows need input and output");
+    const int splits = stage_batch(n, seqs, nullptr, positions);
+    const size_t bytes = sizeof(float) * (size_t)n * c_.hidden;
+    cuda_check(cudaMemcpyAsync(b_x_, x_host, bytes, cudaMemcpyHostToDevice, stream_), "h2d x");
+    enqueue_batch_layer(layer, n, splits);
+    cuda_check(cudaMemcpyAsync(x_out_host, b_x_, bytes, cudaMemcpyDeviceToHost, stream_), "d2h x");
+    check_device_error();
+}
+
+void Engine::layer_rows(int layer, int seq, int n, int position, const float* x_host, float* x_out_host) {
+    if (!loaded_) throw Error(Q4K_EINVAL, "weights are not loaded");
+    if (layer < 0 || layer >= c_.layers) throw Error(Q4K_ERANGE, "layer out of range");
+    if (seq < 0 || seq >= seqs_) throw Error(Q4K_ERANGE, "sequence out of range");
+    if (!x_host || !x_out_host || n <= 0) throw Error(Q4K_EINVAL, "layer rows need at least one row");
+    if (position < 0 || (long long)position + n > c_.capacity) throw Error(Q4K_ERANGE, "KV cache capacity exceeded");
+    ensure_prefill();
+    if (n > pf_rows_) throw Error(Q4K_ERANGE, "more rows than one prefill pass holds");
+    if (pf_gemm_) ensure_prefill_maps();
+    const size_t bytes = sizeof(float) * (size_t)n * c_.hidden;
+    cuda_check(cudaMemcpyAsync(pf_x_, x_host, bytes, cudaMemcpyHostToDevice, stream_), "h2d x");
+    enqueue_prefill_layer(layer, n, position, seq);
+    cuda_check(cudaMemcpyAsync(x_out_host, pf_x_, bytes, cudaMemcpyDeviceToHost, stream_), "d2h x");
     check_device_error();
 }
 

@@ -65,6 +65,14 @@ public:
                       float* logits_host);
     // One block on a given residual-stream input (tp_world == 1 or all ranks).
     void layer_step(int layer, const float* x_host, int position, float* x_out_host);
+    // One block of a prefill pass on given rows: n rows at positions
+    // position .. position+n-1 of sequence seq (the products and attention
+    // of prefill()), x_host [n][hidden] in, x_out_host [n][hidden] out.
+    void layer_rows(int layer, int seq, int n, int position, const float* x_host, float* x_out_host);
+    // One block of a batched decode step on given rows (decode_batch()'s
+    // products and attention): row i at positions[i] of sequence seqs[i].
+    void layer_batch(int layer, int n, const int* seqs, const int* positions, const float* x_host,
+                     float* x_out_host);
     // One step with every kernel CTA's %globaltimer start/end recorded.
     size_t trace_step(uint32_t token, int position, unsigned long long* records_host, size_t max_records);
     cudaStream_t stream() const { return stream_; }
@@ -95,6 +103,9 @@ private:
     const KvTensorMap* layer_maps(int layer, int slot) const;
     void ensure_batch();
     void enqueue_batch_layer(int i, int n, int splits);
+    // Checks a batched step's rows and stages seqs / positions on the
+    // device; returns the attention split count for them.
+    int stage_batch(int n, const int* seqs, const uint32_t* tokens, const int* positions);
     // L2 prefetch descriptors of layer i's weights (q, k, v; o; gate, up; down).
     L2Prefetch weight_prefetch(const uint8_t* w, int type, int K, int rows) const;
     void check_device_error();
@@ -149,6 +160,9 @@ private:
     unsigned* b_counters_ = nullptr;
     int *b_pos_ = nullptr, *b_seq_ = nullptr;
     uint32_t *b_tok_ = nullptr, *b_next_ = nullptr;
+    float* b_partial_ = nullptr;   // tp_world > 1: row-parallel partial sums [B][hidden]
+    uint32_t* b_cand_ = nullptr;   // tp_world > 1: [B] (score bits, global index) of this rank's head shard
+    uint32_t* b_cand_all_ = nullptr;  // [world][B][2]
     KvTensorMap pf_head_map_[kPrefillWeightMaps];  // token_embd as the output head
 
     int pf_rows_ = 0;  // prompt rows one prefill pass holds

@@ -131,7 +131,7 @@ struct PrefillGemmArgs {
     int epilogue = 0;                 // EPI_STORE, EPI_ADD or EPI_SWIGLU (segments 0, 1 paired; output in seg[0].y)
     const uint16_t* a = nullptr;      // prefill_quantise output [M][K]
     const float* row_scale = nullptr;  // [M]
-    float* partial = nullptr;          // optional split-K workspace (STORE / ADD products)
+    float* partial = nullptr;          // optional split-K workspace (STORE / ADD / SWIGLU products)
     size_t partial_floats = 0;
     int* err = nullptr;
 };

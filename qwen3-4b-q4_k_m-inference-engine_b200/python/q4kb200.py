@@ -32,7 +32,8 @@ EXPORTS = (
     "q4k_engine_stream", "q4k_tp_shard", "q4k_engine_layer", "q4k_engine_write_kv",
     "q4k_engine_trace", "q4k_attention_decode_f16_static", "q4k_gguf_open", "q4k_gguf_close",
     "q4k_gguf_tensor_count", "q4k_gguf_tensor_info", "q4k_gguf_meta_int", "q4k_gguf_meta_float",
-    "q4k_gguf_meta_string", "q4k_gguf_engine_config", "q4k_engine_load_gguf",
+    "q4k_gguf_meta_string", "q4k_gguf_engine_config", "q4k_engine_load_gguf", "q4k_engine_layer_rows",
+    "q4k_engine_layer_batch",
 )
 
 
@@ -111,6 +112,8 @@ def lib():
             "q4k_engine_generate": ([P, C.c_uint32, I, I, I, P], I),
             "q4k_engine_stream": ([P], P),
             "q4k_engine_layer": ([P, I, P, I, P], I),
+            "q4k_engine_layer_rows": ([P, I, I, I, I, P, P], I),
+            "q4k_engine_layer_batch": ([P, I, I, P, P, P, P], I),
             "q4k_engine_write_kv": ([P, I, P, P], I),
             "q4k_engine_trace": ([P, C.c_uint32, I, P, C.c_size_t, C.POINTER(C.c_size_t)], I),
             "q4k_tp_shard": ([C.POINTER(EngineConfig), I, I, I, C.POINTER(I64), C.POINTER(I64), C.POINTER(I64),
@@ -329,6 +332,13 @@ class Engine:
         v = None if v is None else np.ascontiguousarray(v, np.uint16)
         check(lib().q4k_engine_write_kv(self.h, layer, hptr(k), hptr(v)))
 
+    def _vocab_rows(self) -> int:
+        """Logits this rank holds: its shard of the vocabulary (all of it
+        with one GPU)."""
+        c = self.cfg
+        world = max(c.tp_world, 1)
+        return c.vocab * (c.tp_rank + 1) // world - c.vocab * c.tp_rank // world
+
     def decode(self, token: int, position: int, want_logits=False, want_hidden=False):
         c = self.cfg
         world = max(c.tp_world, 1)
@@ -356,7 +366,7 @@ class Engine:
     def prefill_seq(self, seq: int, tokens, position: int = 0, want_logits=False):
         """q4k_engine_prefill into sequence `seq`."""
         toks = np.ascontiguousarray(tokens, np.uint32)
-        logits = np.empty(self.cfg.vocab, np.float32) if want_logits else None
+        logits = np.empty(self._vocab_rows(), np.float32) if want_logits else None
         nxt = C.c_uint32()
         check(lib().q4k_engine_prefill_seq(self.h, seq, hptr(toks), int(toks.size), position, C.byref(nxt),
                                            hptr(logits)))
@@ -371,7 +381,7 @@ class Engine:
         n = int(sq.size)
         assert tk.size == n and ps.size == n
         out = np.empty(n, np.uint32)
-        logits = np.empty((n, self.cfg.vocab), np.float32) if want_logits else None
+        logits = np.empty((n, self._vocab_rows()), np.float32) if want_logits else None
         check(lib().q4k_engine_decode_batch(self.h, n, hptr(sq), hptr(tk), hptr(ps), hptr(out), hptr(logits)))
         return out, logits
 
@@ -385,6 +395,26 @@ class Engine:
         x = np.ascontiguousarray(x, np.float32)
         out = np.empty_like(x)
         check(lib().q4k_engine_layer(self.h, layer, hptr(x), position, hptr(out)))
+        return out
+
+    def layer_rows(self, layer: int, x: np.ndarray, position: int, seq: int = 0) -> np.ndarray:
+        """One block of a prompt pass over rows x [n][hidden] at positions
+        position .. position+n-1 of sequence seq (q4k_engine_layer_rows)."""
+        x = np.ascontiguousarray(x, np.float32)
+        n = x.size // self.cfg.hidden
+        out = np.empty_like(x)
+        check(lib().q4k_engine_layer_rows(self.h, layer, seq, n, position, hptr(x), hptr(out)))
+        return out
+
+    def layer_batch(self, layer: int, x: np.ndarray, seqs, positions) -> np.ndarray:
+        """One block of a batched decode step: row i at positions[i] of
+        sequence seqs[i] (q4k_engine_layer_batch)."""
+        x = np.ascontiguousarray(x, np.float32)
+        seqs = np.ascontiguousarray(seqs, np.int32)
+        positions = np.ascontiguousarray(positions, np.int32)
+        out = np.empty_like(x)
+        check(lib().q4k_engine_layer_batch(self.h, layer, seqs.size, hptr(seqs), hptr(positions), hptr(x),
+                                           hptr(out)))
         return out
 
     @property

@@ -1,0 +1,137 @@
+"""Layer-by-layer parity of the tensor-core paths against the reference's
+own kernels, on identical inputs (layer outputs within
+1e-3 relative L2).
+
+Every layer L of the engine is given the residual stream the reference's
+kernels produced entering layer L (and the same cache contents), and its
+output is compared with the reference's output of layer L:
+
+* a 512-token prompt pass (q4k_engine_layer_rows: the tcgen05 GEMM products
+  over all 512 rows, causal prefill attention) against ref_layer replaying
+  src/Engine.cpp:71-103 with tokens = 512;
+* a 64-sequence batched decode step whose contexts are uniform in
+  [512, 4096] (q4k_engine_layer_batch: M = 64 GEMM products, split-K decode
+  attention per sequence) against ref_layer run once per sequence, the
+  reference's one-ChatSession-per-sequence way.
+
+The K/V rows each layer writes are compared too. The two-GPU case (tp2
+against tp1, layer by layer) is in test_gpu_tp.py.
+"""
+import numpy as np
+import pytest
+
+import oracle as o
+import q4kb200 as q
+from conftest import rel_l2
+from test_gpu_engine import full_model, kv_f32  # noqa: F401 (fixture)
+from tiny_model import SEED
+
+pytestmark = pytest.mark.gpu
+
+LAYER_BAR = 1e-3  # relative L2 of a layer's output rows (north_star)
+
+
+def embed(tensors, toks, hidden):
+    """The reference's EmbedLookup rows (dequantised token_embd rows; the
+    engine's embedding is bit-identical to them, test_gpu_engine.py)."""
+    t, _, _, raw = tensors["token_embd.weight"]
+    rb = o.row_bytes(t, hidden)
+    rows = np.stack([raw[int(k) * rb:(int(k) + 1) * rb] for k in toks])
+    return o.dequantize_rows(rows.ravel(), t, len(toks), hidden, rb)
+
+
+def row_errors(got, want):
+    return [rel_l2(g, w) for g, w in zip(got, want)]
+
+
+def test_prefill_512_layers_match_reference_kernels(cuda, full_model):
+    import torch
+
+    if not o.ref_available():
+        pytest.fail("oracle/_ref/libq4kref.so (the reference kernels) was not built")
+    cfg, c, eng, tensors, handles = full_model
+    L, H, KVH, cap, n = c["layers"], c["hidden"], c["kv_heads"], 4096, 512
+    rng = np.random.default_rng(512)
+    toks = rng.integers(0, c["vocab"], n)
+    x = embed(tensors, toks, H)
+    kd = torch.zeros(cap * KVH * 128, device="cuda")
+    vd = torch.zeros_like(kd)
+    errs, row_worst, kv_errs = [], [], []
+    try:
+        for layer in range(L):
+            kd.zero_()
+            vd.zero_()
+            xd = torch.from_numpy(x).cuda()
+            o.ref_layer(handles, c, layer, xd.data_ptr(), kd.data_ptr(), vd.data_ptr(), cap, n, 0)
+            want = xd.cpu().numpy()
+            got = eng.layer_rows(layer, x, 0)
+            errs.append(rel_l2(got, want))
+            row_worst.append(max(row_errors(got, want)))
+            k, v = eng.read_kv(layer)
+            k = k.view(np.float16).astype(np.float32).reshape(KVH, cap, 128)[:, :n]
+            v = v.view(np.float16).astype(np.float32).reshape(KVH, cap, 128)[:, :n]
+            kr = kd.view(cap, KVH, 128)[:n].transpose(0, 1).cpu().numpy()
+            vr = vd.view(cap, KVH, 128)[:n].transpose(0, 1).cpu().numpy()
+            kv_errs.append(max(rel_l2(k, kr), rel_l2(v, vr)))
+            x = want  # identical inputs: the next layer starts from the reference's rows
+    finally:
+        eng.fill_kv_synthetic(SEED, 4095)
+    print(f"prefill-512 per layer vs reference kernels: rel-L2 max {max(errs):.2e} mean {np.mean(errs):.2e}; "
+          f"worst single row {max(row_worst):.2e}; K/V rows max {max(kv_errs):.2e}")
+    assert max(errs) < LAYER_BAR, errs
+    assert max(kv_errs) < LAYER_BAR, kv_errs
+
+
+def test_batch64_uniform_contexts_layers_match_reference_kernels(cuda, full_model):
+    import torch
+
+    if not o.ref_available():
+        pytest.fail("oracle/_ref/libq4kref.so (the reference kernels) was not built")
+    cfg, c, _, tensors, handles = full_model
+    L, H, KVH, cap, B = c["layers"], c["hidden"], c["kv_heads"], 4096, 64
+    rng = np.random.default_rng(64)
+    ctx = rng.integers(512, cap + 1, B)  # contexts uniform in [512, 4096]
+    pos = (ctx - 1).astype(np.int32)     # each sequence's new token
+    seqs = rng.permutation(B).astype(np.int32)
+    toks = rng.integers(0, c["vocab"], B)
+    bcfg = q.qwen3_4b_config(cap)
+    bcfg.sequences = B
+    beng = q.Engine(bcfg)
+    beng.load_synthetic(SEED)
+    beng.fill_kv_synthetic(SEED, cap - 1)
+    kc, vc = kv_f32(SEED, L, KVH, cap - 1, cap)
+    kc = kc.reshape(L, cap, KVH * 128)
+    vc = vc.reshape(L, cap, KVH * 128)
+    x = embed(tensors, toks, H)
+    errs, row_worst, kv_errs = [], [], []
+    try:
+        for layer in range(L):
+            kd = torch.from_numpy(kc[layer]).cuda()
+            vd = torch.from_numpy(vc[layer]).cuda()
+            want = np.empty_like(x)
+            kr = np.empty((B, KVH * 128), np.float32)
+            vr = np.empty_like(kr)
+            for i in range(B):
+                p = int(pos[i])
+                keep_k, keep_v = kd[p].clone(), vd[p].clone()
+                xd = torch.from_numpy(x[i].copy()).cuda()
+                o.ref_layer(handles, c, layer, xd.data_ptr(), kd.data_ptr(), vd.data_ptr(), cap, 1, p)
+                want[i] = xd.cpu().numpy()
+                kr[i], vr[i] = kd[p].cpu().numpy(), vd[p].cpu().numpy()
+                kd[p], vd[p] = keep_k, keep_v  # the other sequences see the shared synthetic rows
+            got = beng.layer_batch(layer, x, seqs, pos)
+            errs.append(rel_l2(got, want))
+            row_worst.append(max(row_errors(got, want)))
+            # the K/V row each sequence wrote (read_kv reads sequence 0)
+            i0 = int(np.nonzero(seqs == 0)[0][0])
+            k, v = beng.read_kv(layer)
+            k = k.view(np.float16).astype(np.float32).reshape(KVH, cap, 128)[:, pos[i0]].ravel()
+            v = v.view(np.float16).astype(np.float32).reshape(KVH, cap, 128)[:, pos[i0]].ravel()
+            kv_errs.append(max(rel_l2(k, kr[i0]), rel_l2(v, vr[i0])))
+            x = want
+    finally:
+        beng.close()
+    print(f"batch-64 (contexts {ctx.min()}..{ctx.max()}) per layer vs reference kernels: rel-L2 max {max(errs):.2e} "
+          f"mean {np.mean(errs):.2e}; worst single sequence {max(row_worst):.2e}; K/V row max {max(kv_errs):.2e}")
+    assert max(errs) < LAYER_BAR, errs
+    assert max(kv_errs) < LAYER_BAR, kv_errs

@@ -211,3 +211,32 @@ def test_forward_capacity_checks():
         model.forward(kc, kc.copy(), 2, [1, 2, 3], 0)
     with pytest.raises(RuntimeError):
         model.forward(kc, kc.copy(), 2, [cfg["vocab"]], 0)
+
+
+def test_oracle_synthetic_model_identical_to_library():
+    """The oracle's own generator (oracle/q4k_synth.c), which the reference
+    arm of bench.py uses so that it never loads the product library, writes
+    the same tensor list and the same bytes as q4k_synth_*_host: every
+    matrix kind and shape of the benchmark model (each tensor whole), the
+    norms, the head's first rows, the KV fill and the activation stream."""
+    import q4kb200 as q
+
+    cfg = q.qwen3_4b_config(4096)
+    lib_list = list(q.model_tensors(cfg))
+    assert lib_list == o.model_tensors(o.qwen3_4b_config(4096))
+    seed = 0x5EED
+    seen = set()
+    for name, t, a, b in lib_list:
+        kind = (t, a, b)
+        if kind in seen or name == "token_embd.weight":
+            continue
+        seen.add(kind)
+        want = q.synth_tensor_host(seed, name, t, a, b)
+        got = o.synth_tensor(seed, name, t, a, b)
+        assert np.array_equal(want.view(np.uint8), got.view(np.uint8)), name
+    head = o.synth_tensor(seed, "token_embd.weight", o.Q6_K, 2560, 151936)[: 64 * o.row_bytes(o.Q6_K, 2560)]
+    want = q.synth_tensor_host(seed, "token_embd.weight", q.Q6_K, 2560, 151936)[: head.size]
+    assert np.array_equal(want, head)
+    assert np.array_equal(q.synth_f16_host(seed, "kv.7.v", 3 << 20, 50000), o.synth_f16(seed, "kv.7.v", 3 << 20, 50000))
+    assert np.array_equal(q.synth_f32_host(seed, "bench.x", 9728), o.synth_f32(seed, "bench.x", 9728))
+    assert o.omp_threads(2) == 2

@@ -54,6 +54,7 @@ def lib():
         L.orc_float_to_half.argtypes = [C.c_float]
         L.orc_float_to_half.restype = C.c_uint16
         L.orc_forward.argtypes = [P, P, P, C.c_size_t, P, C.c_size_t, C.c_size_t, C.c_int, P, P, P, C.c_int]
+        L.orc_layer.argtypes = [P, C.c_int, P, P, P, C.c_size_t, C.c_size_t, C.c_size_t, C.c_int, C.c_int]
         L.orc_synth_key.argtypes = [C.c_uint64, C.c_char_p]
         L.orc_synth_key.restype = C.c_uint64
         L.orc_synth_tensor.argtypes = [C.c_uint64, C.c_char_p, C.c_int, C.c_int64, C.c_int64, P]
@@ -245,6 +246,18 @@ class Model:
         if rc:
             raise RuntimeError(f"orc_forward failed: {rc}")
         return int(nxt.value), logits, hidden
+
+    def layer(self, layer, x, k_cache, v_cache, capacity, pos, kv_round_f16=True, threads=0):
+        """One block (orc_layer) on rows x [tokens][hidden] at positions
+        pos.. ; k_cache / v_cache: this layer's fp32 caches
+        [capacity][kv_heads*head_dim] (written). Returns the new rows."""
+        y = np.array(x, np.float32, copy=True, order="C")
+        tokens = y.size // self.cfg["hidden"]
+        rc = lib().orc_layer(C.byref(self.m), layer, _p(y), _p(k_cache), _p(v_cache), capacity, tokens, pos,
+                             int(kv_round_f16), threads)
+        if rc:
+            raise RuntimeError(f"orc_layer failed: {rc}")
+        return y
 
 
 # --------------------------------------------------------------------------

@@ -297,6 +297,100 @@ static int matmul_f(const float* x, const void* w, int type, size_t K, size_t N,
     return 0;
 }
 
+/* Buffers of one block over T rows (Engine.cpp:57-67's per-step buffers). */
+typedef struct {
+    float *nrm, *q, *qn, *kk, *att, *branch, *gate, *up, *act;
+    double* tmp;
+} orc_work;
+
+static void work_free(orc_work* w) {
+    free(w->nrm);
+    free(w->q);
+    free(w->qn);
+    free(w->kk);
+    free(w->att);
+    free(w->branch);
+    free(w->gate);
+    free(w->up);
+    free(w->act);
+    free(w->tmp);
+}
+
+/* tmp_extra: doubles the caller needs from tmp besides the layer's products. */
+static int work_alloc(const orc_model* m, size_t T, size_t tmp_extra, orc_work* w) {
+    const size_t W = (size_t)m->hidden, QW = (size_t)m->heads * m->head_dim, KW = (size_t)m->kv_heads * m->head_dim;
+    const size_t F = (size_t)m->ffn;
+    const size_t big = (F > QW ? F : QW) > W ? (F > QW ? F : QW) : W;
+    w->nrm = (float*)malloc(sizeof(float) * T * W);
+    w->q = (float*)malloc(sizeof(float) * T * QW);
+    w->qn = (float*)malloc(sizeof(float) * T * QW);
+    w->kk = (float*)malloc(sizeof(float) * T * KW);
+    w->att = (float*)malloc(sizeof(float) * T * QW);
+    w->branch = (float*)malloc(sizeof(float) * T * W);
+    w->gate = (float*)malloc(sizeof(float) * T * F);
+    w->up = (float*)malloc(sizeof(float) * T * F);
+    w->act = (float*)malloc(sizeof(float) * T * F);
+    w->tmp = (double*)malloc(sizeof(double) * (T * big > tmp_extra ? T * big : tmp_extra));
+    if (!w->nrm || !w->q || !w->qn || !w->kk || !w->att || !w->branch || !w->gate || !w->up || !w->act || !w->tmp) {
+        work_free(w);
+        return -3;
+    }
+    return 0;
+}
+
+/* Engine.cpp:71-103: one block on rows x [T][hidden] (updated in place) at
+ * positions pos .. pos+T-1; kc/vc this layer's caches [capacity][kv_width]. */
+static int layer_body(const orc_model* m, int layer, float* x, float* kc, float* vc, size_t T, size_t pos,
+                      int kv_round_f16, orc_work* w, int threads) {
+    const size_t W = (size_t)m->hidden, H = (size_t)m->heads, KVH = (size_t)m->kv_heads, D = (size_t)m->head_dim;
+    const size_t F = (size_t)m->ffn, QW = H * D, KW = KVH * D;
+    const void* const* tp = m->tensors + ORC_SLOTS * layer;
+    const int* ty = m->types + ORC_SLOTS * layer;
+    float* new_k = kc + pos * KW;
+    float* new_v = vc + pos * KW;
+    int rc;
+    orc_rms_norm(x, (const float*)tp[ORC_ATTN_NORM], w->nrm, T, W, m->eps);
+    if ((rc = matmul_f(w->nrm, tp[ORC_Q], ty[ORC_Q], W, QW, T, w->q, w->tmp, threads))) return rc;
+    if ((rc = matmul_f(w->nrm, tp[ORC_K], ty[ORC_K], W, KW, T, w->kk, w->tmp, threads))) return rc;
+    if ((rc = matmul_f(w->nrm, tp[ORC_V], ty[ORC_V], W, KW, T, new_v, w->tmp, threads))) return rc;
+    orc_rms_norm(w->q, (const float*)tp[ORC_Q_NORM], w->qn, T * H, D, m->eps);
+    orc_rms_norm(w->kk, (const float*)tp[ORC_K_NORM], new_k, T * KVH, D, m->eps);
+    orc_rope(w->qn, T, H, D, pos, m->rope_base);
+    orc_rope(new_k, T, KVH, D, pos, m->rope_base);
+    if (kv_round_f16) {
+        for (size_t i = 0; i < T * KW; ++i) {
+            new_k[i] = orc_half_to_float(orc_float_to_half(new_k[i]));
+            new_v[i] = orc_half_to_float(orc_float_to_half(new_v[i]));
+        }
+    }
+    orc_attention(w->qn, kc, vc, w->att, T, H, KVH, D, pos);
+    if ((rc = matmul_f(w->att, tp[ORC_O], ty[ORC_O], QW, W, T, w->branch, w->tmp, threads))) return rc;
+    orc_residual_add(x, w->branch, T * W);
+    orc_rms_norm(x, (const float*)tp[ORC_FFN_NORM], w->nrm, T, W, m->eps);
+    if ((rc = matmul_f(w->nrm, tp[ORC_GATE], ty[ORC_GATE], W, F, T, w->gate, w->tmp, threads))) return rc;
+    if ((rc = matmul_f(w->nrm, tp[ORC_UP], ty[ORC_UP], W, F, T, w->up, w->tmp, threads))) return rc;
+    orc_silu_multiply(w->gate, w->up, w->act, T * F);
+    if ((rc = matmul_f(w->act, tp[ORC_DOWN], ty[ORC_DOWN], F, W, T, w->branch, w->tmp, threads))) return rc;
+    orc_residual_add(x, w->branch, T * W);
+    return 0;
+}
+
+int orc_layer(const orc_model* m, int layer, float* x, float* k_cache, float* v_cache, size_t capacity, size_t tokens,
+              size_t pos, int kv_round_f16, int threads) {
+    if (tokens == 0) return -1;
+    if (layer < 0 || layer >= m->layers) return -5;
+    if (pos + tokens > capacity) return -2;
+#ifdef _OPENMP
+    if (threads > 0) omp_set_num_threads(threads);
+#endif
+    orc_work w;
+    int rc = work_alloc(m, tokens, 0, &w);
+    if (rc) return rc;
+    rc = layer_body(m, layer, x, k_cache, v_cache, tokens, pos, kv_round_f16, &w, threads);
+    work_free(&w);
+    return rc;
+}
+
 /* Engine.cpp:37-114 (Engine::inference), one call over `tokens` new tokens. */
 int orc_forward(const orc_model* m, float* k_cache, float* v_cache, size_t capacity, const uint32_t* token_ids,
                 size_t tokens, size_t pos, int kv_round_f16, float* logits, float* hidden, uint32_t* next_token,
@@ -307,25 +401,14 @@ int orc_forward(const orc_model* m, float* k_cache, float* v_cache, size_t capac
     /* the attention's parallel region takes the same thread count */
     if (threads > 0) omp_set_num_threads(threads);
 #endif
-    const size_t W = (size_t)m->hidden, H = (size_t)m->heads, KVH = (size_t)m->kv_heads, D = (size_t)m->head_dim;
-    const size_t F = (size_t)m->ffn, V = (size_t)m->vocab;
-    const size_t QW = H * D, KW = KVH * D;
+    const size_t W = (size_t)m->hidden, V = (size_t)m->vocab, KW = (size_t)m->kv_heads * m->head_dim;
     const size_t T = tokens;
-    const size_t big = (F > QW ? F : QW) > W ? (F > QW ? F : QW) : W;
+    orc_work w;
+    if (work_alloc(m, T, V, &w)) return -3;
     float* x = (float*)malloc(sizeof(float) * T * W);
-    float* nrm = (float*)malloc(sizeof(float) * T * W);
-    float* q = (float*)malloc(sizeof(float) * T * QW);
-    float* qn = (float*)malloc(sizeof(float) * T * QW);
-    float* kk = (float*)malloc(sizeof(float) * T * KW);
-    float* att = (float*)malloc(sizeof(float) * T * QW);
-    float* branch = (float*)malloc(sizeof(float) * T * W);
-    float* gate = (float*)malloc(sizeof(float) * T * F);
-    float* up = (float*)malloc(sizeof(float) * T * F);
-    float* act = (float*)malloc(sizeof(float) * T * F);
-    double* tmp = (double*)malloc(sizeof(double) * (T * big > V ? T * big : V));
     float* lg = (float*)malloc(sizeof(float) * V);
     int rc = 0;
-    if (!x || !nrm || !q || !qn || !kk || !att || !branch || !gate || !up || !act || !tmp || !lg) {
+    if (!x || !lg) {
         rc = -3;
         goto done;
     }
@@ -346,62 +429,23 @@ int orc_forward(const orc_model* m, float* k_cache, float* v_cache, size_t capac
     if (hidden) memcpy(hidden, x + (T - 1) * W, sizeof(float) * W);
 
     for (int layer = 0; layer < m->layers; ++layer) {
-        const void* const* tp = m->tensors + ORC_SLOTS * layer;
-        const int* ty = m->types + ORC_SLOTS * layer;
-        float* kc = k_cache + (size_t)layer * capacity * KW;
-        float* vc = v_cache + (size_t)layer * capacity * KW;
-        float* new_k = kc + pos * KW;
-        float* new_v = vc + pos * KW;
-
-        orc_rms_norm(x, (const float*)tp[ORC_ATTN_NORM], nrm, T, W, m->eps);
-        if ((rc = matmul_f(nrm, tp[ORC_Q], ty[ORC_Q], W, QW, T, q, tmp, threads))) goto done;
-        if ((rc = matmul_f(nrm, tp[ORC_K], ty[ORC_K], W, KW, T, kk, tmp, threads))) goto done;
-        if ((rc = matmul_f(nrm, tp[ORC_V], ty[ORC_V], W, KW, T, new_v, tmp, threads))) goto done;
-
-        orc_rms_norm(q, (const float*)tp[ORC_Q_NORM], qn, T * H, D, m->eps);
-        orc_rms_norm(kk, (const float*)tp[ORC_K_NORM], new_k, T * KVH, D, m->eps);
-        orc_rope(qn, T, H, D, pos, m->rope_base);
-        orc_rope(new_k, T, KVH, D, pos, m->rope_base);
-        if (kv_round_f16) {
-            for (size_t i = 0; i < T * KW; ++i) {
-                new_k[i] = orc_half_to_float(orc_float_to_half(new_k[i]));
-                new_v[i] = orc_half_to_float(orc_float_to_half(new_v[i]));
-            }
-        }
-
-        orc_attention(qn, kc, vc, att, T, H, KVH, D, pos);
-        if ((rc = matmul_f(att, tp[ORC_O], ty[ORC_O], QW, W, T, branch, tmp, threads))) goto done;
-        orc_residual_add(x, branch, T * W);
-
-        orc_rms_norm(x, (const float*)tp[ORC_FFN_NORM], nrm, T, W, m->eps);
-        if ((rc = matmul_f(nrm, tp[ORC_GATE], ty[ORC_GATE], W, F, T, gate, tmp, threads))) goto done;
-        if ((rc = matmul_f(nrm, tp[ORC_UP], ty[ORC_UP], W, F, T, up, tmp, threads))) goto done;
-        orc_silu_multiply(gate, up, act, T * F);
-        if ((rc = matmul_f(act, tp[ORC_DOWN], ty[ORC_DOWN], F, W, T, branch, tmp, threads))) goto done;
-        orc_residual_add(x, branch, T * W);
+        if ((rc = layer_body(m, layer, x, k_cache + (size_t)layer * capacity * KW, v_cache + (size_t)layer * capacity * KW,
+                             T, pos, kv_round_f16, &w, threads)))
+            goto done;
         if (hidden) memcpy(hidden + (size_t)(layer + 1) * W, x + (T - 1) * W, sizeof(float) * W);
     }
 
     /* Engine.cpp:105-111: last token only, tied output head, greedy argmax. */
-    orc_rms_norm(x + (T - 1) * W, (const float*)m->tensors[ORC_SLOTS * m->layers + 0], nrm, 1, W, m->eps);
-    if ((rc = matmul_f(nrm, m->tensors[ORC_SLOTS * m->layers + 1], m->types[ORC_SLOTS * m->layers + 1], W, V, 1, lg,
-                       tmp, threads)))
+    orc_rms_norm(x + (T - 1) * W, (const float*)m->tensors[ORC_SLOTS * m->layers + 0], w.nrm, 1, W, m->eps);
+    if ((rc = matmul_f(w.nrm, m->tensors[ORC_SLOTS * m->layers + 1], m->types[ORC_SLOTS * m->layers + 1], W, V, 1, lg,
+                       w.tmp, threads)))
         goto done;
     if (logits) memcpy(logits, lg, sizeof(float) * V);
     if (next_token) *next_token = orc_argmax(lg, V);
 
 done:
     free(x);
-    free(nrm);
-    free(q);
-    free(qn);
-    free(kk);
-    free(att);
-    free(branch);
-    free(gate);
-    free(up);
-    free(act);
-    free(tmp);
     free(lg);
+    work_free(&w);
     return rc;
 }

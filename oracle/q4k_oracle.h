@@ -80,6 +80,13 @@ typedef struct {
     const int* types;           /* same indexing */
 } orc_model;
 
+/* One block (Engine.cpp:71-103) on given rows x [tokens][hidden], updated in
+ * place, at positions pos .. pos+tokens-1; k_cache / v_cache are this
+ * layer's fp32 caches [capacity][kv_heads*head_dim] (rows [0, pos) the
+ * prefix; the new rows are written, rounded to fp16 if kv_round_f16). */
+int orc_layer(const orc_model* model, int layer, float* x, float* k_cache, float* v_cache, size_t capacity,
+              size_t tokens, size_t pos, int kv_round_f16, int threads);
+
 int orc_forward(const orc_model* model, float* k_cache, float* v_cache, size_t capacity, const uint32_t* token_ids,
                 size_t tokens, size_t pos, int kv_round_f16, float* logits, float* hidden, uint32_t* next_token,
                 int threads);

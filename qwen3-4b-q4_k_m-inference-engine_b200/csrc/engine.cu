@@ -999,7 +999,8 @@ void Engine::ensure_prefill() {
     }
     if (pf_gemm_) {
         const size_t max_k = std::max<size_t>({H, (size_t)qd_, (size_t)ffn_l_});
-        pf_a_ = static_cast<uint16_t*>(alloc(sizeof(uint16_t) * rows * max_k));
+        pf_a_ = static_cast<uint16_t*>(alloc(sizeof(uint16_t) * 2 * rows * max_k));
+        pf_gsum_ = static_cast<float*>(alloc(sizeof(float) * rows * (max_k / 32)));
         pf_rs_ = static_cast<float*>(alloc(sizeof(float) * rows));
         // split-K workspace: the most any product of a layer (or the batched
         // head) would use at any row count of a pass, so that the engine's
@@ -1065,7 +1066,8 @@ void Engine::enqueue_product(GemvRequest& r, const KvTensorMap* wmaps) {
         return;
     }
     const int H = c_.hidden;
-    cuda_check(prefill_quantise(r.x, r.ldx ? r.ldx : r.K, r.gamma, r.eps, r.M, r.K, pf_a_, pf_rs_, stream_),
+    cuda_check(prefill_quantise(r.x, r.ldx ? r.ldx : r.K, r.gamma, r.eps, r.M, r.K, pf_a_, pf_rows_, pf_gsum_, pf_rs_,
+                                stream_),
                "prefill_quantise launch");
     PrefillGemmArgs g;
     g.nseg = r.nseg;
@@ -1080,6 +1082,7 @@ void Engine::enqueue_product(GemvRequest& r, const KvTensorMap* wmaps) {
     g.amap = &pf_amap_[r.K == H ? 0 : r.K == qd_ ? 1 : 2];
     g.a = pf_a_;
     g.row_scale = pf_rs_;
+    g.gsum = pf_gsum_;
     g.partial = pf_part_;
     g.partial_floats = pf_part_floats_;
     g.err = err_;

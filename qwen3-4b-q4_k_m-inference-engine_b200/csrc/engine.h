@@ -174,7 +174,8 @@ private:
     bool pf_maps_ready_ = false;  // pf_wmaps_ matches the placed tensors
     std::vector<KvTensorMap> pf_wmaps_;  // per layer: q, k, v, o, gate, up, down
     KvTensorMap pf_amap_[3];     // pf_a_ with K = hidden, q width, ffn width
-    uint16_t* pf_a_ = nullptr;   // fp16 activation operand [rows][max K]
+    uint16_t* pf_a_ = nullptr;   // fp16 activation operand [2][rows][max K] (hi, lo planes)
+    float* pf_gsum_ = nullptr;   // its 32-value group sums [rows][max K / 32]
     float* pf_rs_ = nullptr;     // its row scales
     float* pf_part_ = nullptr;   // split-K partial sums of the GEMM
     size_t pf_part_floats_ = 0;

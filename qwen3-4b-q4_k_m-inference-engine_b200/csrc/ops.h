@@ -108,11 +108,12 @@ cudaError_t prefill_attention(const PrefillAttnArgs& a, int tokens, cudaStream_t
 //
 // prefill_quantise: each of M activation rows (optionally RMSNorm-ed with
 // gamma) is Q8-quantised as the reference does (per 32 values, scale
-// amax/127, code roundf(x/amax*127)), and stored as fp16 code * (scale /
-// row_scale[m]), row_scale[m] being the row's largest group scale: the
-// Q8-dequantised activation over a per-row factor, within [-127, 127].
+// amax/127, code roundf(x/amax*127)); v = code * (scale / row_scale[m]),
+// row_scale[m] being the row's largest group scale (|v| <= 127), is stored
+// as fp16 hi and lo parts: a [2][a_rows][K] (hi plane, then lo plane), and
+// gsum[m][g] = the sum of v over 32-value group g ([M][K / 32]).
 cudaError_t prefill_quantise(const float* x, int ldx, const float* gamma, float eps, int M, int K, uint16_t* a,
-                             float* row_scale, cudaStream_t s);
+                             int a_rows, float* gsum, float* row_scale, cudaStream_t s);
 struct PrefillGemmSegment {
     const uint8_t* w = nullptr;  // device layout rows (q4k_format.h)
     int type = 0;                // Q4K_TYPE_Q4_K or Q4K_TYPE_Q6_K
@@ -129,21 +130,23 @@ struct PrefillGemmArgs {
     int nseg = 0;
     int K = 0, M = 0, ldy = 0;
     int epilogue = 0;                 // EPI_STORE, EPI_ADD or EPI_SWIGLU (segments 0, 1 paired; output in seg[0].y)
-    const uint16_t* a = nullptr;      // prefill_quantise output [M][K]
+    const uint16_t* a = nullptr;      // prefill_quantise output [2][rows of amap][K]
     const float* row_scale = nullptr;  // [M]
+    const float* gsum = nullptr;       // [M][K / 32] (prefill_quantise)
     float* partial = nullptr;          // optional split-K workspace (STORE / ADD / SWIGLU products)
     size_t partial_floats = 0;
     int* err = nullptr;
 };
-// y = (a * row_scale) . W^T over every segment, fp32 accumulation in TMEM.
+// y = row_scale * sum over super-blocks of (d P - dmin mins . gsum), P the
+// tensor-core product of a (hi + lo) with the exact integer weights.
 cudaError_t prefill_gemm(const PrefillGemmArgs& g, cudaStream_t s);
 // Floats of split-K workspace prefill_gemm would use for g's shapes given
 // unlimited room (0: it would not split).
 size_t prefill_gemm_partial_floats(const PrefillGemmArgs& g);
 // TMA maps of the GEMM's operands: a weight matrix's raw rows as 64-row
 // boxes (kPrefillWeightMaps maps written to out: one per Q4_K block or Q6_K
-// plane width); the fp16 activation operand as 64 x 128-row boxes, 128-byte
-// swizzle.
+// plane width); the fp16 activation operand [2][rows][K] (hi and lo planes)
+// as 64 x 128-row boxes of one plane, 128-byte swizzle.
 constexpr int kPrefillWeightMaps = 3;
 cudaError_t make_weight_map(const uint8_t* w, int type, int K, int rows, KvTensorMap* out);
 cudaError_t make_act_map(const uint16_t* a, int K, int rows, KvTensorMap* out);

@@ -1,33 +1,37 @@
-// Prompt-prefill products on the 5th-generation tensor cores (sm_100a).
+// Prompt-prefill products on the tensor cores (tcgen05, sm_100a).
 //
-// The reference's prefill pass multiplies all n prompt rows by each weight
-// matrix (matmul.cu:86-125 with rows = n): per 32 inputs, an integer dot of
-// Q8 activation codes with the 4-/6-bit weights, scaled by the activation
-// scale and the block's weight scales. Summed over the groups that is the
-// product of the Q8-dequantised activations (matmul.cu:8-22) with the
-// dequantised weights (embedding.cu:14-58), which is what runs here:
-//
-//   A  = fp16(code * scale / row_scale)   [M][K]  prefill_quantise
-//   B  = fp16((d*sc)*q - dmin*m)           [N][K]  dequantised per tile here
-//   y  = row_scale * (A . B^T)             fp32 accumulation in TMEM
-//
-// The rounding of A and B to fp16 (2^-11 relative) is the only departure from
-// the reference's arithmetic besides the summation order.
+// The reference multiplies Q8-quantised activations with Q4_K/Q6_K weights
+// in integer group dots (src/cuda/matmul.cu:24-84):
+//   y[m][n] = sum_g xs[m][g] * (d[n] sc[n][g] sum q*xq - dmin[n] m[n][g] sum xq).
+// The GEMM here keeps every factor that varies along K exact and applies the
+// per-super-block weight scales outside the tensor cores:
+//   A  = code * xs / row_scale, as fp16 hi + lo parts   [2][M][K]  prefill_quantise
+//   B  = sc * q (Q4_K) or sc * (q - 32) (Q6_K), fp16     [N][K]     exact integers,
+//        dequantised per tile here
+//   P_b = (A_hi + A_lo) . B^T over super-block b         fp32, in TMEM
+//   y  = row_scale * sum_b (d[n][b] P_b - dmin[n][b] sum_g m[n][g] gsum[m][g])
+// where gsum[m][g] is the group's sum of A (prefill_quantise). A's hi + lo
+// split carries 22 of its 24 bits and B is exact, so a product differs from
+// the reference's integer arithmetic only by fp32 rounding (~1e-7), not by
+// the 2^-11 of an fp16 operand: the layers of a prompt pass stay as close to
+// the reference as its own arithmetic in another summation order.
 //
 // One CTA computes 128 activation rows x 128 output columns (SwiGLU: 64 gate
-// and the same 64 up columns), K in 64-value stages:
-//   warp 0     TMA producer of the A boxes (128 rows x 64 fp16, 128-byte
-//              swizzle).
-//   warp 1     TMEM allocation; one thread issues 4 tcgen05.mma.kind::f16
-//              (M 128, N 128, K 16) per stage and commits each stage back to
-//              its empty barrier.
+// and the same 64 up columns), K in 64-value stages, four per super-block:
+//   warp 0     TMA producer of the A stages (hi and lo boxes, 128 rows x 64
+//              fp16 each, 128-byte swizzle).
+//   warp 1     TMEM allocation; one thread issues 2 x 4 tcgen05.mma.kind::f16
+//              (M 128, N 128, K 16) per stage into the super-block's
+//              accumulator (two, used in turn) and commits each stage back to
+//              its empty barriers and each super-block to its accumulator.
 //   warp 2     TMA producer of each super-block's raw weight rows (64-row
 //              boxes; Q6_K planes swizzled), after asking L2 for the CTA's
 //              whole weight slice.
-//   warps 3-18 dequantise each stage's weights into the K-major, 128-byte
-//              swizzled fp16 tile the MMA reads (thread: one row, 16 values),
-//              then the epilogue: tcgen05.ld of the accumulator, row scale,
-//              store / add / SwiGLU.
+//   warps 3-18 build each stage's B tile (K-major, 128-byte swizzled fp16;
+//              thread: one row, 16 values) and each super-block's d / dmin /
+//              mins, then read the previous super-block's accumulator out of
+//              TMEM (tcgen05.ld) and fold it into fp32 registers; at the end
+//              the row scale and store / add / SwiGLU.
 // Every wait is bounded (kWaitLimitNs): on a timeout the kernel records an
 // error bit, drains what it issued and releases its TMEM.
 #include <cuda.h>
@@ -48,22 +52,28 @@ namespace q4k {
 namespace {
 
 constexpr int BM = 128;                  // activation rows per CTA (MMA M)
-constexpr int BN = 128;                  // output columns per CTA (MMA N, TMEM columns)
+constexpr int BN = 128;                  // output columns per CTA (MMA N, TMEM columns per accumulator)
 constexpr int KS = 64;                   // K per stage: one 128-byte swizzle row of fp16
-constexpr int kStagesA = 7;              // activation stages (L2 latency to cover)
-constexpr int kStagesB = 3;              // dequantised weight stages
+constexpr int kStagesA = 3;              // activation stages (hi + lo boxes each)
+constexpr int kStagesB = 3;              // weight-operand stages
 constexpr int kRawStages = 2;            // raw weight super-block stages (the slice is prefetched to L2)
 constexpr int kDeqWarps = 16;
-constexpr int kThreads = (3 + kDeqWarps) * 32;  // A producer, MMA, raw producer, dequant
-constexpr int kStageA = BM * KS * 2;                 // 16 KB
+constexpr int kThreads = (3 + kDeqWarps) * 32;  // A producer, MMA, raw producer, operand builders
+constexpr int kBoxA = BM * KS * 2;                   // 16 KB: one hi or lo box
+constexpr int kStageA = 2 * kBoxA;                   // 32 KB
 constexpr int kStageB = BN * KS * 2;                 // 16 KB
 constexpr int kRawChunksQ4 = 9;                      // 144 B
 constexpr int kRawChunksQ6 = 14;                     // ql 128 B, qh 64 B, scales 16 B, d 16 B
 constexpr int kRawStage = kRawChunksQ6 * BN * 16;    // 28 KB
+constexpr int kAccCols = 2 * BN;                     // two accumulators, super-blocks in turn
+// per super-block and tile column: d, dmin and the 8 group mins, as floats
+constexpr int kSideFloats = BN * 10;
 constexpr int kOffB = kStagesA * kStageA;
 constexpr int kOffRaw = kOffB + kStagesB * kStageB;
-constexpr int kOffBars = kOffRaw + kRawStages * kRawStage;
+constexpr int kOffSide = kOffRaw + kRawStages * kRawStage;
+constexpr int kOffBars = kOffSide + 2 * kSideFloats * 4;
 constexpr int kSmemBytes = kOffBars + 256 + 1024;    // barriers, TMEM slot, alignment slack
+static_assert(kSmemBytes <= 227 * 1024, "shared memory of one CTA");
 
 struct Params {
     int nseg;
@@ -77,6 +87,7 @@ struct Params {
     int ntot;           // columns of a partial row (all segments)
     float* partial;     // [splits][M][ntot]
     const float* row_scale;
+    const float* gsum;  // [M][K / 32] group sums of A (the Q4_K min term)
     int* err;
 };
 
@@ -161,6 +172,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+            "r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ uint4 ld16(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
@@ -196,35 +215,33 @@ __device__ __forceinline__ void load_raw(uint8_t* dst, const Params& p, const Ma
     }
 }
 
-// Dequantise 16 values (quarter p of K-stage j of the super-block) of weight
-// row r into its row of the stage's B tile, in packed fp16 arithmetic:
-// each code byte q becomes the half 1024 + q by a byte permute with 0x64
-// (0x6400 | q), an exact subtraction gives q, then
-//   Q4_K  (embedding.cu:14-31): (q * sc) exact in fp16 (<= 945), times d,
-//         minus dmin * m (rounded to fp16 once), one rounding: fma
-//   Q6_K  (embedding.cu:42-58): (q - 32) * sc exact unless odd and above
-//         2048, times d.
+// The weight operand: 16 values (quarter p of K-stage j of the super-block)
+// of weight row r into its row of the stage's B tile, as exact fp16
+// integers in packed half arithmetic: each code byte q becomes the half
+// 1024 + q by a byte permute with 0x64 (0x6400 | q), an exact subtraction
+// gives q (Q6_K: q - 32), then
+//   Q4_K  (embedding.cu:14-31): q * sc, at most 15 * 63 = 945
+//   Q6_K  (embedding.cu:42-58): (q - 32) * sc, at most 32 * 32 = 1024
+// in magnitude, so every product is exact; the super-block's d and dmin are
+// applied to its accumulator (block_side, read_out).
 // Values k = 16p .. 16p+15 of the stage: 16-byte chunks 2p and 2p+1 of the
 // row's 128 bytes.
 __device__ __forceinline__ __half2 half2_bits(uint32_t v) { return *reinterpret_cast<const __half2*>(&v); }
 __device__ __forceinline__ uint32_t bits_half2(__half2 v) { return *reinterpret_cast<const uint32_t*>(&v); }
 
+// 6-bit scale (min = false) or min (min = true) of 32-value group g of a
+// Q4_K block whose first 16 bytes are `head` (matmul.cu:40-47).
+__device__ __forceinline__ uint32_t q4_field(const uint4& head, int g, bool min) {
+    if (g < 4) return byte_of(head, (min ? 8 : 4) + g) & 63;
+    return min ? (byte_of(head, 8 + g) >> 4) | ((byte_of(head, 4 + g) >> 6) << 4)
+               : (byte_of(head, 8 + g) & 15) | ((byte_of(head, g) >> 6) << 4);
+}
+
 __device__ __forceinline__ void dequant_q4(const uint8_t* raw, uint8_t* bt, int r, int p, int j) {
     const uint8_t* blk = raw + r * 144;
     const uint4 head = ld16(blk);
     const int g = 2 * j + (p >> 1);  // 32-value group of the super-block
-    // 6-bit scale and min of group g (matmul.cu:40-47): bytes 4..15
-    uint32_t sc, mn;
-    if (g < 4) {
-        sc = byte_of(head, 4 + g) & 63;
-        mn = byte_of(head, 8 + g) & 63;
-    } else {
-        sc = (byte_of(head, 8 + g) & 15) | ((byte_of(head, g) >> 6) << 4);
-        mn = (byte_of(head, 8 + g) >> 4) | ((byte_of(head, 4 + g) >> 6) << 4);
-    }
-    const __half2 d2 = half2_bits((head.x & 0xFFFFu) * 0x10001u);
-    const __half2 sc2 = __float2half2_rn((float)sc);
-    const __half2 ndm2 = __float2half2_rn(-(half_bits_to_float(head.x >> 16) * (float)mn));
+    const __half2 sc2 = __float2half2_rn((float)q4_field(head, g, false));
     const __half2 k1024 = half2_bits(0x64006400u);
     // nibbles of values 16(p&1) .. +15 of group g: bytes 16 + 32j + 16(p&1) .., low or high nibble
     const uint4 nb = ld16(blk + 16 * (1 + 2 * j + (p & 1)));
@@ -235,17 +252,14 @@ __device__ __forceinline__ void dequant_q4(const uint8_t* raw, uint8_t* bt, int 
         const uint32_t nib = (word_of(nb, t) >> shift) & 0x0F0F0F0Fu;
         const __half2 q01 = __hsub2(half2_bits(__byte_perm(nib, 0x64646464u, 0x5140u)), k1024);
         const __half2 q23 = __hsub2(half2_bits(__byte_perm(nib, 0x64646464u, 0x7362u)), k1024);
-        o[2 * t] = bits_half2(__hfma2(__hmul2(q01, sc2), d2, ndm2));
-        o[2 * t + 1] = bits_half2(__hfma2(__hmul2(q23, sc2), d2, ndm2));
+        o[2 * t] = bits_half2(__hmul2(q01, sc2));
+        o[2 * t + 1] = bits_half2(__hmul2(q23, sc2));
     }
     *reinterpret_cast<uint4*>(bt + swz(r, 2 * p)) = make_uint4(o[0], o[1], o[2], o[3]);
     *reinterpret_cast<uint4*>(bt + swz(r, 2 * p + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
-__device__ __forceinline__ void dequant_q6(const uint8_t* raw, uint8_t* bt, int r, int p, int j, int b) {
-    const uint4 dch = ld16(raw + kD + r * 16);
-    const uint32_t dbits = (word_of(dch, (b & 7) >> 1) >> (16 * (b & 1))) & 0xFFFFu;
-    const __half2 d2 = half2_bits(dbits * 0x10001u);
+__device__ __forceinline__ void dequant_q6(const uint8_t* raw, uint8_t* bt, int r, int p, int j) {
     const uint4 scw = ld16(raw + kSc + r * 16);
     const __half2 sc2 = __float2half2_rn((float)(int8_t)byte_of(scw, 4 * j + p));  // scale of these 16 values
     // ql: bytes 64(j>>1) + 16p .. ; qh: bytes 32(j>>1) + 16(p&1) ..
@@ -260,11 +274,31 @@ __device__ __forceinline__ void dequant_q6(const uint8_t* raw, uint8_t* bt, int 
         const uint32_t q = ((word_of(lq, t) >> s4) & 0x0F0F0F0Fu) | (((word_of(hq, t) >> s2) & 0x03030303u) << 4);
         const __half2 q01 = __hsub2(half2_bits(__byte_perm(q, 0x64646464u, 0x5140u)), k1056);
         const __half2 q23 = __hsub2(half2_bits(__byte_perm(q, 0x64646464u, 0x7362u)), k1056);
-        o[2 * t] = bits_half2(__hmul2(__hmul2(q01, sc2), d2));
-        o[2 * t + 1] = bits_half2(__hmul2(__hmul2(q23, sc2), d2));
+        o[2 * t] = bits_half2(__hmul2(q01, sc2));
+        o[2 * t + 1] = bits_half2(__hmul2(q23, sc2));
     }
     *reinterpret_cast<uint4*>(bt + swz(r, 2 * p)) = make_uint4(o[0], o[1], o[2], o[3]);
     *reinterpret_cast<uint4*>(bt + swz(r, 2 * p + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+// Per-column factors of super-block b for tile column r (weight row r of
+// the raw stage): side[r] = d, side[BN + r] = dmin, side[2 BN + 8 r + g] =
+// min of group g (Q4_K; Q6_K has d only).
+__device__ __forceinline__ void block_side(const uint8_t* raw, float* side, int r, int type, int b) {
+    if (type == Q4K_TYPE_Q4_K) {
+        const uint4 head = ld16(raw + r * 144);
+        side[r] = half_bits_to_float(head.x & 0xFFFFu);
+        side[BN + r] = half_bits_to_float(head.x >> 16);
+        float4* mn = reinterpret_cast<float4*>(side + 2 * BN + 8 * r);
+        mn[0] = make_float4((float)q4_field(head, 0, true), (float)q4_field(head, 1, true),
+                            (float)q4_field(head, 2, true), (float)q4_field(head, 3, true));
+        mn[1] = make_float4((float)q4_field(head, 4, true), (float)q4_field(head, 5, true),
+                            (float)q4_field(head, 6, true), (float)q4_field(head, 7, true));
+    } else {
+        const uint4 dch = ld16(raw + kD + r * 16);
+        side[r] = half_bits_to_float((word_of(dch, (b & 7) >> 1) >> (16 * (b & 1))) & 0xFFFFu);
+        side[BN + r] = 0.0f;
+    }
 }
 
 // Lane 0 polls the barrier (one poller per warp keeps the barrier traffic
@@ -278,6 +312,38 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
     return ok;
 }
 
+// Folds super-block b's accumulator (TMEM columns acc_col.. of this warp's
+// lanes) into the thread's 32 running sums of row m, columns c0 .. c0+31:
+//   acc += d[n] P[m][n] - dmin[n] sum_g min[n][g] gsum[m][g]   (Q4_K)
+//   acc += d[n] P[m][n]                                       (Q6_K)
+__device__ __forceinline__ void read_out(uint32_t taddr, const float* side, const float* gs, int c0, bool q4,
+                                         float (&acc)[32]) {
+    float v[32];
+    tmem_ld32(taddr, v);
+    tc_fence_before();
+    float g8[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) g8[k] = gs[k];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const int n = c0 + i;
+        acc[i] = fmaf(side[n], v[i], acc[i]);
+        if (q4) {
+            const float4 m0 = *reinterpret_cast<const float4*>(side + 2 * BN + 8 * n);
+            const float4 m1 = *reinterpret_cast<const float4*>(side + 2 * BN + 8 * n + 4);
+            float mt = m0.x * g8[0];
+            mt = fmaf(m0.y, g8[1], mt);
+            mt = fmaf(m0.z, g8[2], mt);
+            mt = fmaf(m0.w, g8[3], mt);
+            mt = fmaf(m1.x, g8[4], mt);
+            mt = fmaf(m1.y, g8[5], mt);
+            mt = fmaf(m1.z, g8[6], mt);
+            mt = fmaf(m1.w, g8[7], mt);
+            acc[i] = fmaf(-side[BN + n], mt, acc[i]);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ Maps maps) {
     extern __shared__ uint8_t smem_dyn[];
@@ -289,8 +355,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* b_empty = b_full + kStagesB;
     uint64_t* raw_full = b_empty + kStagesB;
     uint64_t* raw_empty = raw_full + kRawStages;
-    uint64_t* done = raw_empty + kRawStages;
+    uint64_t* acc_full = raw_empty + kRawStages;  // [2]: a super-block's MMAs are done
+    uint64_t* acc_empty = acc_full + 2;           // [2]: its accumulator has been read out
+    uint64_t* done = acc_empty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    float* sides = reinterpret_cast<float*>(smem + kOffSide);  // [2][kSideFloats]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool pair = p.epilogue == EPI_SWIGLU;
@@ -319,10 +388,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(raw_full + i, 1);
             mbar_init(raw_empty + i, kDeqWarps);
         }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(acc_full + i, 1);
+            mbar_init(acc_empty + i, kDeqWarps);
+        }
         mbar_init(done, 1);
         mbar_fence_init();
     }
-    if (warp == 1) tmem_alloc(tmem_slot, BN);
+    if (warp == 1) tmem_alloc(tmem_slot, kAccCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -330,13 +403,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            // ---------------- producer of the activation stages
+            // ---------------- producer of the activation stages (hi and lo boxes)
             int issued = 0;
             for (int s = 0; s < nsteps; ++s) {
                 const int st = s % kStagesA;
                 if (!mbar_wait_bounded(a_empty + st, ((s / kStagesA) & 1) ^ 1, p.err, ERR_WAIT_TIMEOUT_EMPTY)) break;
                 mbar_arrive_expect_tx(a_full + st, kStageA);
-                tma_load_2d(smem + st * kStageA, &maps.a, (4 * b_begin + s) * KS, m0, a_full + st);
+                const int x = (4 * b_begin + s) * KS;
+                tma_load_3d(smem + st * kStageA, &maps.a, x, m0, 0, a_full + st);
+                tma_load_3d(smem + st * kStageA + kBoxA, &maps.a, x, m0, 1, a_full + st);
                 ++issued;
             }
             // every copy issued has landed before the CTA can exit (the last
@@ -384,92 +459,140 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
-            // ---------------- MMA issue
-            for (int s = 0; s < nsteps; ++s) {
-                const int sa = s % kStagesA, sb = s % kStagesB;
-                if (!mbar_wait_bounded(a_full + sa, (s / kStagesA) & 1, p.err, ERR_WAIT_TIMEOUT_FULL)) break;
-                if (!mbar_wait_bounded(b_full + sb, (s / kStagesB) & 1, p.err, ERR_WAIT_TIMEOUT_FULL)) break;
+            // ---------------- MMA issue: super-block i accumulates in columns
+            // (i & 1) * BN.., once the read-out of super-block i - 2 freed them
+            bool ok = true;
+            for (int i = 0; i < nblk && ok; ++i) {
+                const uint32_t acc = tmem + (uint32_t)((i & 1) * BN);
+                if (i >= 2 && !mbar_wait_bounded(acc_empty + (i & 1), ((i - 2) >> 1) & 1, p.err,
+                                                 ERR_WAIT_TIMEOUT_EMPTY)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
-                const uint32_t a_addr = smem_addr(smem + sa * kStageA);
-                const uint32_t b_addr = smem_addr(smem + kOffB + sb * kStageB);
+                for (int j = 0; j < 4; ++j) {
+                    const int s = 4 * i + j;
+                    const int sa = s % kStagesA, sb = s % kStagesB;
+                    if (!mbar_wait_bounded(a_full + sa, (s / kStagesA) & 1, p.err, ERR_WAIT_TIMEOUT_FULL) ||
+                        !mbar_wait_bounded(b_full + sb, (s / kStagesB) & 1, p.err, ERR_WAIT_TIMEOUT_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_addr(smem + sa * kStageA);
+                    const uint32_t b_addr = smem_addr(smem + kOffB + sb * kStageB);
 #pragma unroll
-                for (int kk = 0; kk < KS / 16; ++kk)
-                    mma_f16(tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), (s | kk) != 0);
-                tc_commit(a_empty + sa);
-                tc_commit(b_empty + sb);
+                    for (int kk = 0; kk < KS / 16; ++kk) {
+                        const uint64_t bd = sw128_desc(b_addr + kk * 32);
+                        mma_f16(acc, sw128_desc(a_addr + kk * 32), bd, (j | kk) != 0);
+                        mma_f16(acc, sw128_desc(a_addr + kBoxA + kk * 32), bd, 1u);
+                    }
+                    tc_commit(a_empty + sa);
+                    tc_commit(b_empty + sb);
+                }
+                if (ok) tc_commit(acc_full + (i & 1));
             }
             tc_commit(done);  // also on an early exit: the epilogue and the TMEM release wait for it
             mbar_wait_bounded(done, 0, p.err, ERR_WAIT_TIMEOUT_FULL);
         }
         __syncwarp();
     } else {
-        // ---------------- dequantise, then the epilogue
+        // ---------------- weight operands and accumulator read-outs
         const int t = (warp - 3) * 32 + lane, r = t & (BN - 1), part = t >> 7;
-        bool ok = true;
-        for (int i = 0; i < nblk && ok; ++i) {
+        const int quad = warp & 3, cg = (warp - 3) >> 2;  // TMEM lanes 32 quad.., columns 32 cg..
+        const int row = 32 * quad + lane, m = m0 + row;
+        const int c0 = 32 * cg;
+        const bool q4 = type == Q4K_TYPE_Q4_K;
+        const uint32_t tlane = tmem + ((uint32_t)(32 * quad) << 16);
+        const int groups = p.K / 32;
+        float acc[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+        // rows past M read row 0's group sums; their results are never stored
+        const float* grow = p.gsum + (size_t)(m < p.M ? m : 0) * groups + 8 * b_begin;
+        // super-block i's accumulator is read out after super-block i + 1's
+        // operands are built, so that the tensor cores always have work
+        auto fold = [&](int i) {
+            if (!warp_wait(acc_full + (i & 1), (i >> 1) & 1, p.err, ERR_WAIT_TIMEOUT_FULL)) return false;
+            tc_fence_after();
+            read_out(tlane + (uint32_t)((i & 1) * BN + c0), sides + (i & 1) * kSideFloats, grow + 8 * i, c0, q4, acc);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + (i & 1));
+            return true;
+        };
+        // A wait that gives up (bounded) stops this warp's work; the warps
+        // agree at every super-block's barrier, so all leave the loop together.
+        bool good = true, ok = true;
+        for (int i = 0; i < nblk; ++i) {
             const int rs = i % kRawStages, b = b_begin + i;
-            ok = warp_wait(raw_full + rs, (i / kRawStages) & 1, p.err, ERR_WAIT_TIMEOUT_FULL);
-            if (!ok) break;
+            if (good) good = warp_wait(raw_full + rs, (i / kRawStages) & 1, p.err, ERR_WAIT_TIMEOUT_FULL);
             const uint8_t* raw = smem + kOffRaw + rs * kRawStage;
-            for (int j = 0; j < 4; ++j) {
+            for (int j = 0; j < 4 && good; ++j) {
                 const int s = 4 * i + j, st = s % kStagesB;
-                ok = warp_wait(b_empty + st, ((s / kStagesB) & 1) ^ 1, p.err, ERR_WAIT_TIMEOUT_EMPTY);
-                if (!ok) break;
+                good = warp_wait(b_empty + st, ((s / kStagesB) & 1) ^ 1, p.err, ERR_WAIT_TIMEOUT_EMPTY);
+                if (!good) break;
                 uint8_t* bt = smem + kOffB + st * kStageB;
-                if (type == Q4K_TYPE_Q4_K)
+                if (q4)
                     dequant_q4(raw, bt, r, part, j);
                 else
-                    dequant_q6(raw, bt, r, part, j, b);
+                    dequant_q6(raw, bt, r, part, j);
                 fence_proxy_async();  // generic stores -> the MMA's async-proxy reads
                 __syncwarp();
                 if (lane == 0) mbar_arrive(b_full + st);
             }
+            // every thread is past super-block i - 2's read-out: its side
+            // factors' buffer takes super-block i's
+            if (named_barrier_or(2, kDeqWarps * 32, !good)) {
+                ok = false;
+                break;
+            }
+            if (part == 0) block_side(raw, sides + (i & 1) * kSideFloats, r, type, b);
             __syncwarp();
             if (lane == 0) mbar_arrive(raw_empty + rs);
+            named_barrier(2, kDeqWarps * 32);
+            if (i >= 1) good = fold(i - 1);
         }
+        ok = ok && good;
+        if (ok && nblk > 0) ok = fold(nblk - 1);
         warp_wait(done, 0, p.err, ERR_WAIT_TIMEOUT_FULL);
         tc_fence_after();
-        const int quad = warp & 3, cg = (warp - 3) >> 2;  // TMEM lanes 32 quad.., columns 32 cg..
-        const int row = 32 * quad + lane, m = m0 + row;
         const float rsc = m < p.M ? p.row_scale[m] : 0.0f;
-        const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] *= rsc;
         const int rows = p.rows[seg];
         // the stage buffers are free once `done` has fired: each warp turns
         // its 32 x 32 block around in shared memory so that the global
         // stores are whole row segments
         float* st = reinterpret_cast<float*>(smem) + (warp - 3) * 32 * 33;
-        bool active = true;
-        int c0 = 32 * cg;
-        float v[32];
-        if (!pair || p.splits > 1) {
-            tmem_ld32(taddr + c0, v);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] *= rsc;
-        } else if (cg < 2) {
+        if (pair && p.splits == 1) {
             // SwiGLU: gate columns 0..63 and up columns 64..127 of the tile
-            float u[32];
-            tmem_ld32(taddr + c0, v);
-            tmem_ld32(taddr + BN / 2 + c0, u);
+            // are held by different warps; the up warps hand theirs over
+            float* up = reinterpret_cast<float*>(smem + kOffB) + (size_t)(32 * quad + lane) * 65;
+            named_barrier(2, kDeqWarps * 32);
+            if (cg >= 2)
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const float gv = v[i] * rsc, uv = u[i] * rsc;
-                v[i] = (gv / (1.0f + expf(-gv))) * uv;  // silu_multiply.cu:9-10
-            }
-        } else {
-            active = false;
+                for (int i = 0; i < 32; ++i) up[32 * (cg - 2) + i] = acc[i];
+            named_barrier(2, kDeqWarps * 32);
+            if (cg < 2)
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const float gv = acc[i], uv = up[32 * cg + i];
+                    acc[i] = (gv / (1.0f + expf(-gv))) * uv;  // silu_multiply.cu:9-10
+                }
         }
-        if (active) {
+        const bool active = !(pair && p.splits == 1) || cg < 2;
+        if (ok && active) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) st[lane * 33 + i] = v[i];
+            for (int i = 0; i < 32; ++i) st[lane * 33 + i] = acc[i];
             __syncwarp();
             // a SwiGLU tile's columns 0..63 are gate rows n0.., 64..127 the same up rows
             const int pseg = pair ? (cg >> 1) : seg;
             const int n = n0 + (pair ? 32 * (cg & 1) : c0) + lane;
             const bool col_ok = n < rows;
-            for (int r = 0; r < 32; ++r) {
-                const int mr = m0 + 32 * quad + r;
+            for (int rr = 0; rr < 32; ++rr) {
+                const int mr = m0 + 32 * quad + rr;
                 if (mr >= p.M || !col_ok) continue;
-                const float a = st[r * 33 + lane];
+                const float a = st[rr * 33 + lane];
                 if (p.splits > 1) {
                     // this K range's share, reduced in a fixed order by split_reduce_kernel
                     p.partial[((size_t)split * p.M + mr) * p.ntot + p.col_off[pseg] + n] = a;
@@ -487,7 +610,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, BN);
+        tmem_dealloc(tmem, kAccCols);
     }
 }
 
@@ -547,16 +670,20 @@ __global__ void __launch_bounds__(256) split_reduce_swiglu_kernel(const ReduceAr
     r.y0[(size_t)m * r.ldy + n] = (gs / (1.0f + expf(-gs))) * us;  // silu_multiply.cu:9-10
 }
 
-// Q8 codes of each row (matmul.cu:8-22) as fp16 code * (scale / row_scale).
-// One CTA per row; thread t holds elements 256 i + t, so warp w's lanes hold
-// 32-value group 8 i + w at step i and the row is read once.
+// Q8 codes of each row (matmul.cu:8-22) as the GEMM's A operand: the
+// value v = code * (scale / row_scale) in fp32, stored as fp16 hi = fp16(v)
+// and lo = fp16(v - hi) (hi + lo carry 22 of v's 24 bits), and each 32-value
+// group's sum of v (the Q4_K min term). One CTA per row; thread t holds
+// elements 256 i + t, so warp w's lanes hold 32-value group 8 i + w at step
+// i and the row is read once.
 constexpr int kQuantMaxSteps = 40;  // K <= 10240
 
 // kSteps: register slots per thread, the smallest instantiation >= K / 256
 // (fewer registers, more rows resident per SM for the common widths).
 template <int kSteps>
 __global__ void __launch_bounds__(256) prefill_quantise_kernel(const float* x, int ldx, const float* gamma, float eps,
-                                                               int K, __half* a, float* row_scale) {
+                                                               int K, __half* a_hi, __half* a_lo, float* gsum,
+                                                               float* row_scale) {
     const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float* xr = x + (size_t)m * ldx;
     const int steps = K / 256;
@@ -598,7 +725,16 @@ __global__ void __launch_bounds__(256) prefill_quantise_kernel(const float* x, i
         int8_t code = gemv_dev::q8_code_rn(v[i], __fdividef(127.0f, am[i]), near);
         if (!gemv_dev::q8_fast_ok(am[i]) || near) code = gemv_dev::q8_code_exact(v[i], am[i]);
         const float r = S > 0.0f ? __fdiv_rn(am[i] / 127.0f, S) : 0.0f;
-        a[(size_t)m * K + 256 * i + tid] = __float2half_rn((float)code * r);
+        const float val = (float)code * r;
+        const __half hi = __float2half_rn(val);
+        const size_t at = (size_t)m * K + 256 * i + tid;
+        a_hi[at] = hi;
+        a_lo[at] = __float2half_rn(val - __half2float(hi));
+        // the group's code sum is an exact integer: one rounding for its value
+        int cs = code;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
+        if (lane == 0) gsum[(size_t)m * (K / 32) + 8 * i + warp] = r * (float)cs;
     }
     if (tid == 0) row_scale[m] = S;
 }
@@ -610,17 +746,19 @@ using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, 
 }  // namespace
 
 cudaError_t prefill_quantise(const float* x, int ldx, const float* gamma, float eps, int M, int K, uint16_t* a,
-                             float* row_scale, cudaStream_t s) {
-    if (M <= 0 || K <= 0 || K % 256 || K / 256 > kQuantMaxSteps || ldx < K || !x || !a || !row_scale)
+                             int a_rows, float* gsum, float* row_scale, cudaStream_t s) {
+    if (M <= 0 || K <= 0 || K % 256 || K / 256 > kQuantMaxSteps || ldx < K || !x || !a || !gsum || !row_scale ||
+        a_rows < M)
         return cudaErrorInvalidValue;
-    __half* ah = reinterpret_cast<__half*>(a);
+    __half* hi = reinterpret_cast<__half*>(a);
+    __half* lo = hi + (size_t)a_rows * K;
     const int steps = K / 256;
     if (steps <= 10)
-        prefill_quantise_kernel<10><<<M, 256, 0, s>>>(x, ldx, gamma, eps, K, ah, row_scale);
+        prefill_quantise_kernel<10><<<M, 256, 0, s>>>(x, ldx, gamma, eps, K, hi, lo, gsum, row_scale);
     else if (steps <= 16)
-        prefill_quantise_kernel<16><<<M, 256, 0, s>>>(x, ldx, gamma, eps, K, ah, row_scale);
+        prefill_quantise_kernel<16><<<M, 256, 0, s>>>(x, ldx, gamma, eps, K, hi, lo, gsum, row_scale);
     else
-        prefill_quantise_kernel<kQuantMaxSteps><<<M, 256, 0, s>>>(x, ldx, gamma, eps, K, ah, row_scale);
+        prefill_quantise_kernel<kQuantMaxSteps><<<M, 256, 0, s>>>(x, ldx, gamma, eps, K, hi, lo, gsum, row_scale);
     return cudaGetLastError();
 }
 
@@ -664,12 +802,13 @@ cudaError_t make_act_map(const uint16_t* a, int K, int rows, KvTensorMap* out) {
     const EncodeTiled enc = reinterpret_cast<EncodeTiled>(tensor_map_encoder());
     if (!enc) return cudaErrorNotSupported;
     if (!a || reinterpret_cast<uintptr_t>(a) % 16 || rows <= 0 || K <= 0 || K % 256) return cudaErrorInvalidValue;
-    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-    const cuuint32_t box[2] = {KS, BM};
-    const cuuint32_t estr[2] = {1, 1};
+    // [2][rows][K]: the hi plane, then the lo plane
+    const cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, 2};
+    const cuuint64_t strides[2] = {(cuuint64_t)K * 2, (cuuint64_t)K * 2 * (cuuint64_t)rows};
+    const cuuint32_t box[3] = {KS, BM, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
     CUtensorMap map;
-    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(a), dims, strides, box, estr,
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<uint16_t*>(a), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return cudaErrorInvalidValue;
@@ -713,7 +852,7 @@ size_t prefill_gemm_partial_floats(const PrefillGemmArgs& g) {
 
 cudaError_t prefill_gemm(const PrefillGemmArgs& g, cudaStream_t s) {
     const bool pair = g.epilogue == EPI_SWIGLU;
-    if (g.nseg < 1 || g.nseg > 3 || g.K <= 0 || g.K % 256 || g.M <= 0 || g.ldy <= 0 || !g.a || !g.row_scale ||
+    if (g.nseg < 1 || g.nseg > 3 || g.K <= 0 || g.K % 256 || g.M <= 0 || g.ldy <= 0 || !g.a || !g.row_scale || !g.gsum ||
         (g.epilogue != EPI_STORE && g.epilogue != EPI_ADD && !pair))
         return cudaErrorInvalidValue;
     if (pair && (g.nseg != 2 || g.seg[0].type != g.seg[1].type || g.seg[0].rows != g.seg[1].rows))
@@ -727,6 +866,7 @@ cudaError_t prefill_gemm(const PrefillGemmArgs& g, cudaStream_t s) {
     p.ldy = g.ldy;
     p.epilogue = g.epilogue;
     p.row_scale = g.row_scale;
+    p.gsum = g.gsum;
     p.err = g.err;
     int tiles = 0, ntot = 0;
     for (int i = 0; i < g.nseg; ++i) {

@@ -66,9 +66,13 @@ def test_tiny_batch_decode_bit_identical_to_single(cuda, monkeypatch):
 
 
 def test_tiny_batch_decode_gemm_path(cuda):
-    """Twelve sequences in one step take the tensor-core products: each
-    sequence's logits stay within the whole-step bar of a one-sequence
-    engine, teacher-forced on the single engine's tokens for three steps."""
+    """Twelve sequences in one step take the tensor-core products: every
+    layer of the batched step is within 1e-3 relative L2 of a one-sequence
+    engine's layer (integer-exact GEMV products) on identical inputs, and each
+    sequence's logits stay within the whole-step bar (5e-2, as for the full
+    model: through the layers of a random-init model the ~1e-7 product
+    differences of the two paths flip Q8 codes), teacher-forced on the single
+    engine's tokens for three steps."""
     cap = 24
     rng = np.random.default_rng(7)
     n = 12
@@ -89,10 +93,20 @@ def test_tiny_batch_decode_gemm_path(cuda):
             t1, l1, _ = singles[s].decode(nxt[s], pos[s], want_logits=True)
             e = rel_l2(logits[s], l1)
             worst = max(worst, e)
-            assert e < 1e-2, (step, s, e)
+            assert e < 5e-2, (step, s, e)
             assert greedy_ok(int(toks[s]), t1, l1, logits[s]), (step, s)
             nxt[s], pos[s] = t1, pos[s] + 1
-    print(f"12-sequence batch on the GEMM path: worst logits rel-L2 {worst:.2e}")
+    # every layer on identical inputs: the batched step's rows against each
+    # sequence's own engine
+    x = rng.standard_normal((n, TINY["hidden"])).astype(np.float32)
+    layer_worst = 0.0
+    for layer in range(TINY["layers"]):
+        got = batch.layer_batch(layer, x, list(range(n)), pos)
+        want = np.stack([singles[s].layer(layer, x[s], pos[s]) for s in range(n)])
+        layer_worst = max(layer_worst, rel_l2(got, want))  # over all rows, as the full-model layer tests
+        x = want
+    print(f"12-sequence batch on the GEMM path: worst logits rel-L2 {worst:.2e}, worst layer {layer_worst:.2e}")
+    assert layer_worst < 1e-3
     batch.close()
     for e in singles:
         e.close()

@@ -361,7 +361,8 @@ Q4K_API int q4k_matmul_batch(const float* input, const float* norm_gamma, float 
         // per-call workspace, as the reference's matmul allocates one (matmul.cu:142-145)
         void* ws = nullptr;
         const size_t a_bytes = ((2 * rows * (size_t)ne0 * 2 + 255) / 256) * 256;  // hi and lo planes
-        const size_t s_bytes = ((rows * sizeof(float) * (1 + (size_t)ne0 / 32) + 255) / 256) * 256;
+        const size_t rows_pad = (rows + 63) / 64 * 64;  // the group sums start 256-byte aligned
+        const size_t s_bytes = ((sizeof(float) * (rows_pad + rows * (size_t)ne0 / 32) + 255) / 256) * 256;
         g.K = (int)ne0;
         g.M = (int)rows;
         g.epilogue = epilogue;
@@ -369,7 +370,7 @@ Q4K_API int q4k_matmul_batch(const float* input, const float* norm_gamma, float 
         launched(cudaMallocAsync(&ws, a_bytes + s_bytes + part_floats * sizeof(float), s));
         uint16_t* a = static_cast<uint16_t*>(ws);
         float* scale = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + a_bytes);
-        float* gsum = scale + rows;  // [rows][ne0 / 32]
+        float* gsum = scale + rows_pad;  // [rows][ne0 / 32]
         g.partial = part_floats ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + a_bytes + s_bytes) : nullptr;
         g.partial_floats = part_floats;
         cudaError_t e = q4k::prefill_quantise(input, (int)ne0, norm_gamma, epsilon, (int)rows, (int)ne0, a, (int)rows,

@@ -65,12 +65,20 @@ constexpr int kStageB = BN * KS * 2;                 // 16 KB
 constexpr int kRawChunksQ4 = 9;                      // 144 B
 constexpr int kRawChunksQ6 = 14;                     // ql 128 B, qh 64 B, scales 16 B, d 16 B
 constexpr int kRawStage = kRawChunksQ6 * BN * 16;    // 28 KB
-constexpr int kAccCols = 2 * BN;                     // two accumulators, super-blocks in turn
-// per super-block and tile column: d, dmin and the 8 group mins, as floats
-constexpr int kSideFloats = BN * 10;
+// TMEM: two accumulator sets, super-blocks in turn; a set is the product P
+// (BN columns) and the Q4_K min term Q (BN columns)
+constexpr int kAccSet = 2 * BN;
+constexpr int kAccCols = 2 * kAccSet;
+// per super-block and tile column: d and dmin, as floats
+constexpr int kSideFloats = BN * 2;
+// min-term operands of one super-block (K = 16, 32-byte swizzle): the 8
+// group sums of each activation row (hi and lo parts, then 8 zeros) and the
+// 8 group mins of each weight row (then 8 zeros)
+constexpr int kTile32 = BM * 32;  // 4 KB
 constexpr int kOffB = kStagesA * kStageA;
 constexpr int kOffRaw = kOffB + kStagesB * kStageB;
-constexpr int kOffSide = kOffRaw + kRawStages * kRawStage;
+constexpr int kOffMin = kOffRaw + kRawStages * kRawStage;  // G hi, G lo, M
+constexpr int kOffSide = kOffMin + 3 * kTile32;
 constexpr int kOffBars = kOffSide + 2 * kSideFloats * 4;
 constexpr int kSmemBytes = kOffBars + 256 + 1024;    // barriers, TMEM slot, alignment slack
 static_assert(kSmemBytes <= 227 * 1024, "shared memory of one CTA");
@@ -127,6 +135,17 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
     return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
+
+// The same for a K-major tile of 32-byte rows (one K = 16 step of fp16)
+// with the 32-byte swizzle, 8-row groups 256 bytes apart.
+__device__ __forceinline__ uint64_t sw32_desc(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(256 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)6 << 61);
+}
+
+// Byte offset of 16-byte chunk c (0, 1) of row r in a 128-row x 32-byte
+// tile with the 32-byte swizzle.
+__device__ __forceinline__ uint32_t swz32(int r, int c) { return (uint32_t)(r * 32 + ((c ^ ((r >> 2) & 1)) << 4)); }
 
 // Instruction descriptor of kind::f16: fp16 A and B (K-major), fp32 D,
 // M = BM, N = BN.
@@ -282,18 +301,36 @@ __device__ __forceinline__ void dequant_q6(const uint8_t* raw, uint8_t* bt, int 
 }
 
 // Per-column factors of super-block b for tile column r (weight row r of
-// the raw stage): side[r] = d, side[BN + r] = dmin, side[2 BN + 8 r + g] =
-// min of group g (Q4_K; Q6_K has d only).
-__device__ __forceinline__ void block_side(const uint8_t* raw, float* side, int r, int type, int b) {
+// the raw stage): side[r] = d, side[BN + r] = dmin; for Q4_K also row r of
+// the min-term operands: the 8 group mins of weight row r (M tile) and the 8
+// group sums g8 of activation row r (G tiles, hi and lo parts), each
+// followed by 8 zeros (the MMA's K is 16).
+__device__ __forceinline__ void block_side(const uint8_t* raw, float* side, uint8_t* mins, int r, int type, int b,
+                                           const float (&g8)[8]) {
     if (type == Q4K_TYPE_Q4_K) {
         const uint4 head = ld16(raw + r * 144);
         side[r] = half_bits_to_float(head.x & 0xFFFFu);
         side[BN + r] = half_bits_to_float(head.x >> 16);
-        float4* mn = reinterpret_cast<float4*>(side + 2 * BN + 8 * r);
-        mn[0] = make_float4((float)q4_field(head, 0, true), (float)q4_field(head, 1, true),
-                            (float)q4_field(head, 2, true), (float)q4_field(head, 3, true));
-        mn[1] = make_float4((float)q4_field(head, 4, true), (float)q4_field(head, 5, true),
-                            (float)q4_field(head, 6, true), (float)q4_field(head, 7, true));
+        uint32_t mw[4], hw[4], lw[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            mw[k] = bits_half2(
+                __floats2half2_rn((float)q4_field(head, 2 * k, true), (float)q4_field(head, 2 * k + 1, true)));
+            const __half2 hi = __floats2half2_rn(g8[2 * k], g8[2 * k + 1]);
+            const float2 hf = __half22float2(hi);
+            hw[k] = bits_half2(hi);
+            lw[k] = bits_half2(__floats2half2_rn(g8[2 * k] - hf.x, g8[2 * k + 1] - hf.y));
+        }
+        const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+        uint8_t* gh = mins;
+        uint8_t* gl = mins + kTile32;
+        uint8_t* mt = mins + 2 * kTile32;
+        *reinterpret_cast<uint4*>(mt + swz32(r, 0)) = make_uint4(mw[0], mw[1], mw[2], mw[3]);
+        *reinterpret_cast<uint4*>(mt + swz32(r, 1)) = zero;
+        *reinterpret_cast<uint4*>(gh + swz32(r, 0)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(gh + swz32(r, 1)) = zero;
+        *reinterpret_cast<uint4*>(gl + swz32(r, 0)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        *reinterpret_cast<uint4*>(gl + swz32(r, 1)) = zero;
     } else {
         const uint4 dch = ld16(raw + kD + r * 16);
         side[r] = half_bits_to_float((word_of(dch, (b & 7) >> 1) >> (16 * (b & 1))) & 0xFFFFu);
@@ -312,36 +349,22 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
     return ok;
 }
 
-// Folds super-block b's accumulator (TMEM columns acc_col.. of this warp's
-// lanes) into the thread's 32 running sums of row m, columns c0 .. c0+31:
-//   acc += d[n] P[m][n] - dmin[n] sum_g min[n][g] gsum[m][g]   (Q4_K)
-//   acc += d[n] P[m][n]                                       (Q6_K)
-__device__ __forceinline__ void read_out(uint32_t taddr, const float* side, const float* gs, int c0, bool q4,
-                                         float (&acc)[32]) {
+// Folds super-block b's accumulators (TMEM columns acc_addr.. of this warp's
+// lanes: P, then Q BN columns on) into the thread's 32 running sums of row m,
+// columns c0 .. c0+31:
+//   acc += d[n] P[m][n] - dmin[n] Q[m][n]   (Q = sum_g min[n][g] gsum[m][g]; Q4_K)
+//   acc += d[n] P[m][n]                     (Q6_K)
+__device__ __forceinline__ void read_out(uint32_t acc_addr, const float* side, int c0, bool q4, float (&acc)[32]) {
     float v[32];
-    tmem_ld32(taddr, v);
-    tc_fence_before();
-    float g8[8];
+    tmem_ld32(acc_addr, v);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) g8[k] = gs[k];
+    for (int i = 0; i < 32; ++i) acc[i] = fmaf(side[c0 + i], v[i], acc[i]);
+    if (q4) {
+        tmem_ld32(acc_addr + BN, v);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        const int n = c0 + i;
-        acc[i] = fmaf(side[n], v[i], acc[i]);
-        if (q4) {
-            const float4 m0 = *reinterpret_cast<const float4*>(side + 2 * BN + 8 * n);
-            const float4 m1 = *reinterpret_cast<const float4*>(side + 2 * BN + 8 * n + 4);
-            float mt = m0.x * g8[0];
-            mt = fmaf(m0.y, g8[1], mt);
-            mt = fmaf(m0.z, g8[2], mt);
-            mt = fmaf(m0.w, g8[3], mt);
-            mt = fmaf(m1.x, g8[4], mt);
-            mt = fmaf(m1.y, g8[5], mt);
-            mt = fmaf(m1.z, g8[6], mt);
-            mt = fmaf(m1.w, g8[7], mt);
-            acc[i] = fmaf(-side[BN + n], mt, acc[i]);
-        }
+        for (int i = 0; i < 32; ++i) acc[i] = fmaf(-side[BN + c0 + i], v[i], acc[i]);
     }
+    tc_fence_before();
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -356,10 +379,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* raw_full = b_empty + kStagesB;
     uint64_t* raw_empty = raw_full + kRawStages;
     uint64_t* acc_full = raw_empty + kRawStages;  // [2]: a super-block's MMAs are done
-    uint64_t* acc_empty = acc_full + 2;           // [2]: its accumulator has been read out
-    uint64_t* done = acc_empty + 2;
+    uint64_t* acc_empty = acc_full + 2;           // [2]: its accumulators have been read out
+    uint64_t* min_full = acc_empty + 2;           // the min-term operands of a super-block are written
+    uint64_t* min_done = min_full + 1;            // the min-term MMAs of a super-block are done
+    uint64_t* done = min_done + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     float* sides = reinterpret_cast<float*>(smem + kOffSide);  // [2][kSideFloats]
+    uint8_t* mins = smem + kOffMin;                             // G hi, G lo, M tiles
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool pair = p.epilogue == EPI_SWIGLU;
@@ -392,6 +418,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(acc_full + i, 1);
             mbar_init(acc_empty + i, kDeqWarps);
         }
+        mbar_init(min_full, kDeqWarps);
+        mbar_init(min_done, 1);
         mbar_init(done, 1);
         mbar_fence_init();
     }
@@ -459,11 +487,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
-            // ---------------- MMA issue: super-block i accumulates in columns
-            // (i & 1) * BN.., once the read-out of super-block i - 2 freed them
+            // ---------------- MMA issue: super-block i accumulates in set i & 1
+            // (P, then Q BN columns on), once the read-out of super-block
+            // i - 2 freed it
+            const bool q4 = type == Q4K_TYPE_Q4_K;
             bool ok = true;
             for (int i = 0; i < nblk && ok; ++i) {
-                const uint32_t acc = tmem + (uint32_t)((i & 1) * BN);
+                const uint32_t acc = tmem + (uint32_t)((i & 1) * kAccSet);
                 if (i >= 2 && !mbar_wait_bounded(acc_empty + (i & 1), ((i - 2) >> 1) & 1, p.err,
                                                  ERR_WAIT_TIMEOUT_EMPTY)) {
                     ok = false;
@@ -490,6 +520,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_commit(a_empty + sa);
                     tc_commit(b_empty + sb);
                 }
+                if (ok && q4) {
+                    // Q = G . M^T over the super-block's 8 groups (K = 16 with
+                    // 8 zeros), the group sums' hi and lo parts in turn
+                    if (!mbar_wait_bounded(min_full, i & 1, p.err, ERR_WAIT_TIMEOUT_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t md = sw32_desc(smem_addr(mins + 2 * kTile32));
+                    mma_f16(acc + BN, sw32_desc(smem_addr(mins)), md, 0u);
+                    mma_f16(acc + BN, sw32_desc(smem_addr(mins + kTile32)), md, 1u);
+                    tc_commit(min_done);
+                }
                 if (ok) tc_commit(acc_full + (i & 1));
             }
             tc_commit(done);  // also on an early exit: the epilogue and the TMEM release wait for it
@@ -508,14 +551,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         float acc[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
-        // rows past M read row 0's group sums; their results are never stored
-        const float* grow = p.gsum + (size_t)(m < p.M ? m : 0) * groups + 8 * b_begin;
-        // super-block i's accumulator is read out after super-block i + 1's
+        // group sums of activation row r (this thread's min-term row when
+        // part == 0); rows past M read row 0's, whose results are never stored
+        const float* grow = p.gsum + (size_t)(m0 + r < p.M ? m0 + r : 0) * groups + 8 * b_begin;
+        // super-block i's accumulators are read out after super-block i + 1's
         // operands are built, so that the tensor cores always have work
         auto fold = [&](int i) {
             if (!warp_wait(acc_full + (i & 1), (i >> 1) & 1, p.err, ERR_WAIT_TIMEOUT_FULL)) return false;
             tc_fence_after();
-            read_out(tlane + (uint32_t)((i & 1) * BN + c0), sides + (i & 1) * kSideFloats, grow + 8 * i, c0, q4, acc);
+            read_out(tlane + (uint32_t)((i & 1) * kAccSet + c0), sides + (i & 1) * kSideFloats, c0, q4, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty + (i & 1));
             return true;
@@ -525,6 +569,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool good = true, ok = true;
         for (int i = 0; i < nblk; ++i) {
             const int rs = i % kRawStages, b = b_begin + i;
+            // this super-block's 8 group sums, loaded while the stages are built
+            float g8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            if (q4 && part == 0) {
+                const float4 u = __ldg(reinterpret_cast<const float4*>(grow + 8 * i));
+                const float4 w = __ldg(reinterpret_cast<const float4*>(grow + 8 * i + 4));
+                g8[0] = u.x, g8[1] = u.y, g8[2] = u.z, g8[3] = u.w;
+                g8[4] = w.x, g8[5] = w.y, g8[6] = w.z, g8[7] = w.w;
+            }
             if (good) good = warp_wait(raw_full + rs, (i / kRawStages) & 1, p.err, ERR_WAIT_TIMEOUT_FULL);
             const uint8_t* raw = smem + kOffRaw + rs * kRawStage;
             for (int j = 0; j < 4 && good; ++j) {
@@ -546,9 +598,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ok = false;
                 break;
             }
-            if (part == 0) block_side(raw, sides + (i & 1) * kSideFloats, r, type, b);
+            // the min-term tiles are single: super-block i - 1's MMAs on them
+            // must be done before they take super-block i's
+            if (part == 0) {
+                if (q4 && i >= 1) good = warp_wait(min_done, (i - 1) & 1, p.err, ERR_WAIT_TIMEOUT_FULL);
+                block_side(raw, sides + (i & 1) * kSideFloats, mins, r, type, b, g8);
+                fence_proxy_async();  // generic stores -> the MMA's async-proxy reads
+            }
             __syncwarp();
-            if (lane == 0) mbar_arrive(raw_empty + rs);
+            if (lane == 0) {
+                if (q4) mbar_arrive(min_full);
+                mbar_arrive(raw_empty + rs);
+            }
             named_barrier(2, kDeqWarps * 32);
             if (i >= 1) good = fold(i - 1);
         }

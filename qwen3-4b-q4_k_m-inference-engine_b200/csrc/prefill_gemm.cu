@@ -357,12 +357,26 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
 __device__ __forceinline__ void read_out(uint32_t acc_addr, const float* side, int c0, bool q4, float (&acc)[32]) {
     float v[32];
     tmem_ld32(acc_addr, v);
+    const float4* d4 = reinterpret_cast<const float4*>(side + c0);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) acc[i] = fmaf(side[c0 + i], v[i], acc[i]);
+    for (int i = 0; i < 8; ++i) {
+        const float4 d = d4[i];
+        acc[4 * i] = fmaf(d.x, v[4 * i], acc[4 * i]);
+        acc[4 * i + 1] = fmaf(d.y, v[4 * i + 1], acc[4 * i + 1]);
+        acc[4 * i + 2] = fmaf(d.z, v[4 * i + 2], acc[4 * i + 2]);
+        acc[4 * i + 3] = fmaf(d.w, v[4 * i + 3], acc[4 * i + 3]);
+    }
     if (q4) {
         tmem_ld32(acc_addr + BN, v);
+        const float4* m4 = reinterpret_cast<const float4*>(side + BN + c0);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] = fmaf(-side[BN + c0 + i], v[i], acc[i]);
+        for (int i = 0; i < 8; ++i) {
+            const float4 m = m4[i];
+            acc[4 * i] = fmaf(-m.x, v[4 * i], acc[4 * i]);
+            acc[4 * i + 1] = fmaf(-m.y, v[4 * i + 1], acc[4 * i + 1]);
+            acc[4 * i + 2] = fmaf(-m.z, v[4 * i + 2], acc[4 * i + 2]);
+            acc[4 * i + 3] = fmaf(-m.w, v[4 * i + 3], acc[4 * i + 3]);
+        }
     }
     tc_fence_before();
 }
@@ -566,10 +580,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         // A wait that gives up (bounded) stops this warp's work; the warps
         // agree at every super-block's barrier, so all leave the loop together.
+        // Stage j of super-block i into its ring slot of B tiles.
+        auto build = [&](const uint8_t* raw, int i, int j) {
+            const int s = 4 * i + j, st = s % kStagesB;
+            if (!warp_wait(b_empty + st, ((s / kStagesB) & 1) ^ 1, p.err, ERR_WAIT_TIMEOUT_EMPTY)) return false;
+            uint8_t* bt = smem + kOffB + st * kStageB;
+            if (q4)
+                dequant_q4(raw, bt, r, part, j);
+            else
+                dequant_q6(raw, bt, r, part, j);
+            fence_proxy_async();  // generic stores -> the MMA's async-proxy reads
+            __syncwarp();
+            if (lane == 0) mbar_arrive(b_full + st);
+            return true;
+        };
+        // Super-block i: its first two stages are built, then (every warp
+        // past super-block i - 1) super-block i - 1's accumulators are read
+        // out while the tensor cores work on those stages, then the last two
+        // stages and super-block i's side factors and min-term tiles.
         bool good = true, ok = true;
         for (int i = 0; i < nblk; ++i) {
             const int rs = i % kRawStages, b = b_begin + i;
-            // this super-block's 8 group sums, loaded while the stages are built
+            if (good) good = warp_wait(raw_full + rs, (i / kRawStages) & 1, p.err, ERR_WAIT_TIMEOUT_FULL);
+            const uint8_t* raw = smem + kOffRaw + rs * kRawStage;
+            for (int j = 0; j < 2 && good; ++j) good = build(raw, i, j);
+            // every warp has written super-block i - 1's side factors and read
+            // out super-block i - 2
+            if (named_barrier_or(2, kDeqWarps * 32, !good)) {
+                ok = false;
+                break;
+            }
+            if (i >= 1) good = fold(i - 1);
+            // this super-block's 8 group sums, loaded while the last stages are built
             float g8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
             if (q4 && part == 0) {
                 const float4 u = __ldg(reinterpret_cast<const float4*>(grow + 8 * i));
@@ -577,31 +619,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 g8[0] = u.x, g8[1] = u.y, g8[2] = u.z, g8[3] = u.w;
                 g8[4] = w.x, g8[5] = w.y, g8[6] = w.z, g8[7] = w.w;
             }
-            if (good) good = warp_wait(raw_full + rs, (i / kRawStages) & 1, p.err, ERR_WAIT_TIMEOUT_FULL);
-            const uint8_t* raw = smem + kOffRaw + rs * kRawStage;
-            for (int j = 0; j < 4 && good; ++j) {
-                const int s = 4 * i + j, st = s % kStagesB;
-                good = warp_wait(b_empty + st, ((s / kStagesB) & 1) ^ 1, p.err, ERR_WAIT_TIMEOUT_EMPTY);
-                if (!good) break;
-                uint8_t* bt = smem + kOffB + st * kStageB;
-                if (q4)
-                    dequant_q4(raw, bt, r, part, j);
-                else
-                    dequant_q6(raw, bt, r, part, j);
-                fence_proxy_async();  // generic stores -> the MMA's async-proxy reads
-                __syncwarp();
-                if (lane == 0) mbar_arrive(b_full + st);
-            }
-            // every thread is past super-block i - 2's read-out: its side
-            // factors' buffer takes super-block i's
-            if (named_barrier_or(2, kDeqWarps * 32, !good)) {
-                ok = false;
-                break;
-            }
-            // the min-term tiles are single: super-block i - 1's MMAs on them
-            // must be done before they take super-block i's
+            for (int j = 2; j < 4 && good; ++j) good = build(raw, i, j);
+            // side factors: buffer i & 1 was last read by super-block i - 2's
+            // read-out (before the barrier above); the min-term tiles are
+            // single, so super-block i - 1's MMAs on them must be done
             if (part == 0) {
-                if (q4 && i >= 1) good = warp_wait(min_done, (i - 1) & 1, p.err, ERR_WAIT_TIMEOUT_FULL);
+                if (q4 && i >= 1 && good) good = warp_wait(min_done, (i - 1) & 1, p.err, ERR_WAIT_TIMEOUT_FULL);
                 block_side(raw, sides + (i & 1) * kSideFloats, mins, r, type, b, g8);
                 fence_proxy_async();  // generic stores -> the MMA's async-proxy reads
             }
@@ -610,10 +633,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (q4) mbar_arrive(min_full);
                 mbar_arrive(raw_empty + rs);
             }
-            named_barrier(2, kDeqWarps * 32);
-            if (i >= 1) good = fold(i - 1);
         }
-        ok = ok && good;
+        // the last super-block's side factors are visible to every warp
+        if (named_barrier_or(2, kDeqWarps * 32, !(ok && good))) ok = false;
         if (ok && nblk > 0) ok = fold(nblk - 1);
         warp_wait(done, 0, p.err, ERR_WAIT_TIMEOUT_FULL);
         tc_fence_after();

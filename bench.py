@@ -570,9 +570,9 @@ def run_decode(args, world, rank, local):
         prefill["roofline"] = prefill_roofline(q, torch, peaks)
         step_bytes = (2503489024 + 36 * 2 * CTX * 8 * 128 * 2) / world
         value = args.steps / secs
-        # embed, 36 x 5, head, finish; with tp the 72 residual adds after the
-        # all-reduces (the NCCL kernels themselves are not counted)
-        kernels_per_step = 1 + 36 * 5 + 2 + (72 if world > 1 else 0)
+        # embed, 36 x 5, head, finish (with tp the row-parallel sums travel
+        # inside the products; the step's one NCCL all-gather is not counted)
+        kernels_per_step = 1 + 36 * 5 + 2
         result = {
             "metric": METRIC_DECODE,
             "value": round(value * 1.0, 2),

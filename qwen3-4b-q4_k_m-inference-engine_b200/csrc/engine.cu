@@ -78,7 +78,8 @@ const char* const kSlotNames[11] = {"attn_norm", "attn_q",     "attn_k",   "attn
                                     "attn_output", "ffn_norm", "ffn_gate", "ffn_up",   "ffn_down"};
 
 __global__ void finish_step_kernel(uint32_t* token, int* pos, const int* advance, uint32_t* history,
-                                   unsigned* history_n, unsigned history_cap, const uint32_t* tp_cand, int world) {
+                                   unsigned* history_n, unsigned history_cap, const uint32_t* tp_cand, int world,
+                                   int* epoch) {
     pdl_wait();
     if (threadIdx.x != 0) return;
     if (tp_cand) {
@@ -100,6 +101,7 @@ __global__ void finish_step_kernel(uint32_t* token, int* pos, const int* advance
     if (n < history_cap) history[n] = *token;
     *history_n = n + 1;
     *pos += *advance;
+    if (epoch) *epoch += 1;  // a decode step that used the peer receive slots
 }
 
 // Greedy token of each of n logit rows (argmax.cu:25-98 semantics: the
@@ -302,6 +304,7 @@ Engine::Engine(const q4k_engine_config& cfg, const void* nccl_id) : c_(cfg) {
     tp_cand_local_ = static_cast<float*>(alloc(64));
     tp_cand_all_ = static_cast<float*>(alloc(sizeof(float) * 2 * world_ + 64));
     cuda_check(cudaMallocHost(&host_io_, 64), "cudaMallocHost");
+    if (world_ > 1) setup_peer_slots();
     {
         // Q4K_STEP_KERNEL=1: decode with the persistent decode-step kernel
         // (or fail saying why it cannot run); otherwise the launch sequence,
@@ -329,6 +332,8 @@ Engine::Engine(const q4k_engine_config& cfg, const void* nccl_id) : c_(cfg) {
 Engine::~Engine() {
     if (exec_) cudaGraphExecDestroy(exec_);
     if (stream_) cudaStreamSynchronize(stream_);
+    for (int r = 0; r < world_ && r < kMaxRanks; ++r)
+        if (r != rank_ && ar_peer_[r]) cudaIpcCloseMemHandle(ar_peer_[r]);
     if (comm_) nccl().CommDestroy(comm_);
     for (void* p : allocations_) cudaFree(p);
     if (host_io_) cudaFreeHost(host_io_);
@@ -504,6 +509,70 @@ void Engine::write_kv(int layer, const uint16_t* k_host, const uint16_t* v_host)
     cuda_check(cudaStreamSynchronize(stream_), "write_kv");
 }
 
+// Maps every rank's receive slots for the fused row-parallel sums. All ranks
+// take part (two all-gathers over the engine's communicator) and agree: the
+// fused path is used only if every rank exported its slots and opened every
+// other rank's; otherwise every rank keeps the ncclAllReduce path.
+// Q4K_TP_FUSED=0 turns it off.
+void Engine::setup_peer_slots() {
+    const int H = c_.hidden;
+    bool want = world_ <= kMaxRanks;
+    if (const char* e = std::getenv("Q4K_TP_FUSED")) want = want && e[0] != '0';
+    ar_flag_bytes_ = ((size_t)2 * c_.layers * sizeof(unsigned) + 255) / 256 * 256;
+    ar_base_ = static_cast<uint8_t*>(alloc(ar_flag_bytes_ + (size_t)2 * c_.layers * world_ * H * sizeof(float)));
+    ar_epoch_ = static_cast<int*>(alloc(64));
+    xb_ = static_cast<float*>(alloc(sizeof(float) * H));
+    constexpr size_t kRec = 128;  // per rank: IPC handle (64 bytes), then a status word
+    static_assert(sizeof(cudaIpcMemHandle_t) <= 64, "IPC handle size");
+    uint8_t* rec = static_cast<uint8_t*>(alloc(kRec * world_));
+    std::vector<uint8_t> host(kRec * world_, 0), mine(kRec, 0);
+    auto exchange = [&](int status) {
+        mine[64] = (uint8_t)status;
+        cuda_check(cudaMemcpyAsync(rec + kRec * rank_, mine.data(), kRec, cudaMemcpyHostToDevice, stream_), "h2d");
+        nccl_check(nccl().AllGather(rec + kRec * rank_, rec, kRec, ncclUint8, comm_, stream_), "ncclAllGather");
+        cuda_check(cudaMemcpyAsync(host.data(), rec, kRec * world_, cudaMemcpyDeviceToHost, stream_), "d2h");
+        cuda_check(cudaStreamSynchronize(stream_), "peer slot exchange");
+        bool all = true;
+        for (int r = 0; r < world_; ++r) all = all && host[kRec * r + 64] == 1;
+        return all;
+    };
+    cudaIpcMemHandle_t h{};
+    int status = 0;
+    if (want && cudaIpcGetMemHandle(&h, ar_base_) == cudaSuccess) {
+        std::memcpy(mine.data(), &h, sizeof h);
+        status = 1;
+    }
+    cudaGetLastError();
+    if (!exchange(status)) return;
+    status = 1;
+    ar_peer_[rank_] = ar_base_;
+    for (int r = 0; r < world_; ++r) {
+        if (r == rank_) continue;
+        cudaIpcMemHandle_t hr;
+        std::memcpy(&hr, host.data() + kRec * r, sizeof hr);
+        if (cudaIpcOpenMemHandle(&ar_peer_[r], hr, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            ar_peer_[r] = nullptr;
+            status = 0;
+        }
+    }
+    cudaGetLastError();
+    if (!exchange(status)) {
+        for (int r = 0; r < world_; ++r)
+            if (r != rank_ && ar_peer_[r]) cudaIpcCloseMemHandle(ar_peer_[r]);
+        std::fill(std::begin(ar_peer_), std::end(ar_peer_), nullptr);
+        cudaGetLastError();
+        return;
+    }
+    tp_fused_ = true;
+}
+
+float* Engine::peer_recv(int rank, int slot) const {
+    return reinterpret_cast<float*>(static_cast<uint8_t*>(ar_peer_[rank]) + ar_flag_bytes_) +
+           (size_t)slot * world_ * c_.hidden;
+}
+
+unsigned* Engine::peer_flag(int rank, int slot) const { return static_cast<unsigned*>(ar_peer_[rank]) + slot; }
+
 // One transformer block (Engine.cpp:71-103) on the device buffers: x is
 L2Prefetch Engine::weight_prefetch(const uint8_t* w, int type, int K, int rows) const {
     L2Prefetch f;
@@ -515,10 +584,34 @@ L2Prefetch Engine::weight_prefetch(const uint8_t* w, int type, int K, int rows) 
     return f;
 }
 
-// updated in place, layer i's K/V rows at *pos_ are written.
-void Engine::enqueue_layer(int i) {
+// updated in place, layer i's K/V rows at *pos_ are written. With fused
+// tensor parallelism the residual stream alternates between x_ and xb_ inside
+// the layer (x_ again at its end, before the ffn_down ranks' partial sums
+// are added by the next product).
+void Engine::enqueue_layer(int i, bool fused) {
     const auto& c = c_;
     const int H = c.hidden;
+    fused = fused && tp_fused_;
+    // slot of layer l's attn_output (0) or ffn_down (1) partial sums
+    auto slot = [&](int l, int k) { return 2 * l + k; };
+    // EPI_PEER into every rank's slot s
+    auto peer_out = [&](GemvRequest& r, int s_) {
+        r.epilogue = EPI_PEER;
+        r.seg[0].y = nullptr;
+        r.peer_out.world = world_;
+        for (int k = 0; k < world_; ++k) {
+            r.peer_out.recv[k] = peer_recv(k, s_) + (size_t)rank_ * H;
+            r.peer_out.flag[k] = peer_flag(k, s_);
+        }
+    };
+    // the product's input: x plus every rank's partial sums of slot s_ (none: s_ < 0), also stored to x_out
+    auto peer_in = [&](GemvRequest& r, int s_, float* x_out) {
+        r.peer_in.world = s_ >= 0 ? world_ : 0;
+        r.peer_in.parts = s_ >= 0 ? peer_recv(rank_, s_) : nullptr;
+        r.peer_in.flag = s_ >= 0 ? peer_flag(rank_, s_) : nullptr;
+        r.peer_in.epoch = ar_epoch_;
+        r.peer_in.x_out = x_out;
+    };
     auto gemv = [&](GemvRequest& r) { cuda_check(launch_gemv(r, stream_), "gemv launch"); };
     auto all_reduce_into_x = [&]() {
         nccl_check(nccl().AllReduce(partial_, partial_, H, ncclFloat, ncclSum, comm_, stream_), "ncclAllReduce");
@@ -534,6 +627,7 @@ void Engine::enqueue_layer(int i) {
         r.seg[2] = {L.v, qkv_ + qd_ + kvd_, L.tv, kvd_};
         r.K = H;
         r.x = x_;
+        if (fused) peer_in(r, i > 0 ? slot(i - 1, 1) : -1, xb_);
         r.gamma = L.attn_norm;
         r.eps = c.eps;
         r.epilogue = EPI_STORE;
@@ -587,6 +681,7 @@ void Engine::enqueue_layer(int i) {
         r.K = qd_;
         r.x = att_;
         r.epilogue = world_ > 1 ? EPI_STORE : EPI_ADD;
+        if (fused) peer_out(r, slot(i, 0));
         r.err = err_;
         r.pdl = true;
         r.trace = trace_;
@@ -595,7 +690,7 @@ void Engine::enqueue_layer(int i) {
         r.prefetch[1] = weight_prefetch(L.up, L.tup, H, ffn_l_);
         if (act_images_) r.in_image = att_img_;
         gemv(r);
-        if (world_ > 1) all_reduce_into_x();
+        if (world_ > 1 && !fused) all_reduce_into_x();
     }
     {
         GemvRequest r;
@@ -604,6 +699,10 @@ void Engine::enqueue_layer(int i) {
         r.seg[1] = {L.up, act_, L.tup, ffn_l_};
         r.K = H;
         r.x = x_;
+        if (fused) {
+            r.x = xb_;
+            peer_in(r, slot(i, 0), x_);
+        }
         r.gamma = L.ffn_norm;
         r.eps = c.eps;
         r.epilogue = EPI_SWIGLU;
@@ -622,6 +721,7 @@ void Engine::enqueue_layer(int i) {
         r.K = ffn_l_;
         r.x = act_;
         r.epilogue = world_ > 1 ? EPI_STORE : EPI_ADD;
+        if (fused) peer_out(r, slot(i, 1));
         r.err = err_;
         r.pdl = true;
         r.trace = trace_;
@@ -634,7 +734,7 @@ void Engine::enqueue_layer(int i) {
             r.prefetch[2] = weight_prefetch(N.v, N.tv, H, kvd_);
         }
         gemv(r);
-        if (world_ > 1) all_reduce_into_x();
+        if (world_ > 1 && !fused) all_reduce_into_x();
     }
 }
 
@@ -651,18 +751,20 @@ void Engine::enqueue_step(bool record_hidden) {
     cuda_check(embed_rows(token_embd_, t_embd_, H, c.vocab, token_, 1, x_, err_, stream_, false), "embed");
     snapshot(0);
     for (int i = 0; i < c.layers; ++i) {
-        enqueue_layer(i);
+        enqueue_layer(i, true);
         snapshot(i + 1);
     }
-    enqueue_head();
+    enqueue_head(true);
 }
 
 // Output head on x_ (Engine.cpp:106-111): final RMSNorm, the token_embd
 // product with the greedy choice fused, the shard merge when tp_world > 1, and
-// the step's bookkeeping (token_, history, *pos_ += *advance_).
-void Engine::enqueue_head() {
+// the step's bookkeeping (token_, history, *pos_ += *advance_). fused: the
+// last layer's ffn_down partial sums are still in the receive slots.
+void Engine::enqueue_head(bool fused) {
     const auto& c = c_;
     const int H = c.hidden;
+    fused = fused && tp_fused_;
     auto gemv = [&](GemvRequest& r) { cuda_check(launch_gemv(r, stream_), "gemv launch"); };
     {
         GemvRequest r;
@@ -671,6 +773,12 @@ void Engine::enqueue_head() {
         r.seg[0] = {token_embd_ + (size_t)vocab0_ * row_bytes, logits_, t_embd_, (int)(vocab1_ - vocab0_)};
         r.K = H;
         r.x = x_;
+        if (fused) {
+            r.peer_in.world = world_;
+            r.peer_in.parts = peer_recv(rank_, 2 * (c.layers - 1) + 1);
+            r.peer_in.flag = peer_flag(rank_, 2 * (c.layers - 1) + 1);
+            r.peer_in.epoch = ar_epoch_;
+        }
         r.gamma = output_norm_;
         r.eps = c.eps;
         r.epilogue = EPI_ARGMAX;
@@ -708,7 +816,8 @@ void Engine::enqueue_head() {
         cfg.numAttrs = 1;
         cuda_check(cudaLaunchKernelEx(&cfg, finish_step_kernel, token_, pos_, (const int*)advance_, history_,
                                       history_n_, (unsigned)c.capacity,
-                                      world_ > 1 ? reinterpret_cast<const uint32_t*>(tp_cand_all_) : nullptr, world_),
+                                      world_ > 1 ? reinterpret_cast<const uint32_t*>(tp_cand_all_) : nullptr, world_,
+                                      fused ? ar_epoch_ : nullptr),
                    "finish launch");
     }
 }
@@ -1237,7 +1346,7 @@ uint32_t Engine::prefill(const uint32_t* tokens_host, int n, int position, float
     cuda_check(cudaMemcpyAsync(x_, pf_x_ + (size_t)(rows - 1) * H, sizeof(float) * H, cudaMemcpyDeviceToDevice,
                                stream_),
                "last row");
-    enqueue_head();
+    enqueue_head(false);
     cuda_check(cudaMemcpyAsync(&host_io_[4], token_, 4, cudaMemcpyDeviceToHost, stream_), "d2h");
     if (logits_host)
         cuda_check(cudaMemcpyAsync(logits_host, logits_, sizeof(float) * (vocab1_ - vocab0_), cudaMemcpyDeviceToHost,
@@ -1502,7 +1611,7 @@ void Engine::layer_step(int layer, const float* x_host, int position, float* x_o
     host_io_[1] = (uint32_t)position;
     cuda_check(cudaMemcpyAsync(pos_, &host_io_[1], 4, cudaMemcpyHostToDevice, stream_), "h2d");
     cuda_check(cudaMemcpyAsync(x_, x_host, sizeof(float) * c_.hidden, cudaMemcpyHostToDevice, stream_), "h2d x");
-    enqueue_layer(layer);
+    enqueue_layer(layer, false);
     cuda_check(cudaMemcpyAsync(x_out_host, x_, sizeof(float) * c_.hidden, cudaMemcpyDeviceToHost, stream_), "d2h x");
     check_device_error();
 }

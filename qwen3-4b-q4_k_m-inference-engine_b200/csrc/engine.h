@@ -91,8 +91,15 @@ private:
     void** tensor_slot(const TensorSpec& t, int** type_slot);
     void place(const TensorSpec& t, const void* raw_device);
     void enqueue_step(bool record_hidden);
-    void enqueue_layer(int i);
-    void enqueue_head();
+    // fused: the row-parallel sums go through the peer receive slots (the
+    // decode step); otherwise through ncclAllReduce (layer_step)
+    void enqueue_layer(int i, bool fused);
+    // Tensor parallelism without a collective launch (tp_world > 1): maps
+    // every rank's receive slots into this process (cudaIpc over NCCL).
+    void setup_peer_slots();
+    float* peer_recv(int rank, int slot) const;  // rank's slot, [world][hidden]
+    unsigned* peer_flag(int rank, int slot) const;
+    void enqueue_head(bool fused);
     // Prompt rows per prefill pass and their buffers (allocated on first use).
     void ensure_prefill();
     void enqueue_prefill_layer(int i, int rows, int pos0, int seq);
@@ -180,6 +187,16 @@ private:
     float* pf_part_ = nullptr;   // split-K partial sums of the GEMM
     size_t pf_part_floats_ = 0;
 
+    // Fused tensor-parallel sums (decode step): slot 2i takes layer i's
+    // attn_output partial sums, 2i + 1 its ffn_down ones, from every rank;
+    // one cudaMalloc per rank ([flags][slots][world][hidden]), mapped by the
+    // others. xb_ is the second residual buffer (x_ and xb_ in turn).
+    bool tp_fused_ = false;
+    uint8_t* ar_base_ = nullptr;
+    void* ar_peer_[8] = {};  // every rank's allocation (this rank's own at rank_)
+    size_t ar_flag_bytes_ = 0;
+    int* ar_epoch_ = nullptr;  // decode steps run, as every rank counts them
+    float* xb_ = nullptr;
     cudaGraphExec_t exec_ = nullptr;
     bool l2_prefetch_ = true;        // each launch prefetches the next one's operands into L2
     bool act_images_ = true;         // SwiGLU and attention hand the next product a quantised activation

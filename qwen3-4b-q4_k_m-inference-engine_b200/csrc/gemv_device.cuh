@@ -354,7 +354,8 @@ __device__ __forceinline__ void quantise_rows(const float* x, int ldx, int m0, i
                                               float eps, int K, uint8_t* xq4, uint8_t* xq6, float* xs, int* xsum16,
                                               float* xsum32, float* red, int tid, int lane, int warp, int nthreads,
                                               int barrier_id, unsigned long long* trace = nullptr,
-                                              int trace_tag = 0) {
+                                              int trace_tag = 0, const float* parts = nullptr, int nparts = 0,
+                                              float* x_out = nullptr) {
     const int nvec = K / 4;
     // kHeld: float4s of the row a thread keeps in registers (K <= kHeld * 4 * nthreads)
     for (int m = 0; m < mcount; ++m) {
@@ -365,6 +366,34 @@ __device__ __forceinline__ void quantise_rows(const float* x, int ldx, int m0, i
         for (int k = 0; k < kHeld; ++k) {
             const int i = tid + k * nthreads;
             if (i < nvec) held[k] = __ldcg(xr + i);  // may have been written by other SMs in this launch
+        }
+        if (parts && m == 0) {
+            // tensor parallelism: x + the ranks' partial sums (rank order), the
+            // residual stream every rank computes alike
+#pragma unroll
+            for (int k = 0; k < kHeld; ++k) {
+                const int i = tid + k * nthreads;
+                if (i >= nvec) continue;
+                float4 sum = __ldcg(reinterpret_cast<const float4*>(parts) + i);
+                for (int r = 1; r < nparts; ++r) {
+                    const float4 t = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)r * K) + i);
+                    sum.x += t.x;
+                    sum.y += t.y;
+                    sum.z += t.z;
+                    sum.w += t.w;
+                }
+                held[k].x += sum.x;
+                held[k].y += sum.y;
+                held[k].z += sum.z;
+                held[k].w += sum.w;
+            }
+        }
+        if (x_out && m == 0) {
+#pragma unroll
+            for (int k = 0; k < kHeld; ++k) {
+                const int i = tid + k * nthreads;
+                if (i < nvec) reinterpret_cast<float4*>(x_out)[i] = held[k];
+            }
         }
         if (trace && tid == 0 && m == 0) {
             // timeline: when thread 0's first activation load has landed

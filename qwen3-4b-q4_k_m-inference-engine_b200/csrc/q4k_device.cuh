@@ -18,6 +18,7 @@ enum : int {
     ERR_BAD_POSITION = 4,        // a position read from device memory was out of range
     ERR_BAD_TOKEN = 8,           // a token id read from device memory was out of range
     ERR_WAIT_TIMEOUT_DEP = 16,   // a CTA gave up waiting for the other CTAs to finish a phase
+    ERR_WAIT_TIMEOUT_PEER = 32,  // a product gave up waiting for the other ranks' partial sums
 };
 
 // A waiting thread gives up after this many nanoseconds of %globaltimer.
@@ -31,6 +32,31 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
+}
+
+// A counter other GPUs add to (system-scope acquire, so that the data they
+// stored before adding is visible after it).
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Waits until *flag has reached `target` (counters that wrap: the signed
+// difference decides), giving up after limit_ns of %globaltimer with `code`
+// in *err. Returns whether it was reached.
+__device__ __forceinline__ bool flag_wait_bounded(const unsigned* flag, unsigned target, uint64_t limit_ns, int* err,
+                                                  int code) {
+    if ((int)(ld_acquire_sys(flag) - target) >= 0) return true;
+    const uint64_t start = global_timer_ns();
+    for (;;) {
+        __nanosleep(64);
+        if ((int)(ld_acquire_sys(flag) - target) >= 0) return true;
+        if (global_timer_ns() - start > limit_ns) {
+            if (err) atomicOr(err, code);
+            return false;
+        }
+    }
 }
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

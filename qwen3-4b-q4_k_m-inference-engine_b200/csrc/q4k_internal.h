@@ -14,6 +14,35 @@ enum Epilogue : int {
     EPI_ADD = 1,     // y[m][n] += dot            (residual stream update)
     EPI_SWIGLU = 2,  // y[m][n] = silu(gate) * up (segments 0 and 1 paired row by row)
     EPI_ARGMAX = 3,  // greedy token over all rows (M == 1), optional logits in y
+    EPI_PEER = 4,    // tensor-parallel partial sums (M == 1) stored into every rank's receive slot (PeerOut)
+};
+
+// Tensor-parallel row-parallel product (EPI_PEER): output row n's partial
+// sum goes to recv[r][n] of every rank r (rank r's receive slot for this
+// product, this rank's row of it; peer memory mapped over NVLink), then each
+// CTA adds its share of kPeerUnits to every rank's flag for the slot (the
+// shares of all CTAs sum to exactly kPeerUnits per rank and product).
+constexpr int kMaxRanks = 8;
+constexpr unsigned kPeerUnits = 1u << 16;
+struct PeerOut {
+    float* recv[kMaxRanks] = {};
+    unsigned* flag[kMaxRanks] = {};
+    int world = 0;
+};
+
+// The consuming side (a product with an RMSNorm prologue): its input row is
+// x + sum over ranks r = 0 .. world-1, in that order, of parts[r * K ..],
+// once *flag has reached (*epoch + 1) * world * kPeerUnits (all ranks'
+// partial sums of this step have landed); the row is also written to x_out
+// (the residual stream for the products after this one). world may be 0: x
+// is only copied to x_out.
+struct PeerIn {
+    const float* parts = nullptr;
+    int world = -1;  // < 0: not used
+    const unsigned* flag = nullptr;
+    const int* epoch = nullptr;
+    float* x_out = nullptr;
+    unsigned long long wait_ns = 2000000000ull;
 };
 
 constexpr int kMaxSegments = 4;
@@ -81,6 +110,8 @@ struct GemvRequest {
     L2Prefetch prefetch[kMaxPrefetch];  // the next kernel's operands (optional)
     ActImage in_image;   // M == 1, no gamma: copy this quantised activation instead of quantising x
     ActImage out_image;  // EPI_SWIGLU, M == 1: also quantise the output rows into this image
+    PeerOut peer_out;    // EPI_PEER
+    PeerIn peer_in;      // M == 1: sum the ranks' partial sums into x first (with gamma)
 };
 
 // Plans and launches one product. Returns cudaErrorInvalidValue for shapes it

@@ -518,8 +518,7 @@ void Engine::setup_peer_slots() {
     const int H = c_.hidden;
     bool want = world_ <= kMaxRanks;
     if (const char* e = std::getenv("Q4K_TP_FUSED")) want = want && e[0] != '0';
-    ar_flag_bytes_ = ((size_t)2 * c_.layers * sizeof(unsigned) + 255) / 256 * 256;
-    ar_base_ = static_cast<uint8_t*>(alloc(ar_flag_bytes_ + (size_t)2 * c_.layers * world_ * H * sizeof(float)));
+    ar_base_ = static_cast<uint8_t*>(alloc((size_t)2 * c_.layers * world_ * H * sizeof(unsigned long long)));
     ar_epoch_ = static_cast<int*>(alloc(64));
     xb_ = static_cast<float*>(alloc(sizeof(float) * H));
     constexpr size_t kRec = 128;  // per rank: IPC handle (64 bytes), then a status word
@@ -566,12 +565,9 @@ void Engine::setup_peer_slots() {
     tp_fused_ = true;
 }
 
-float* Engine::peer_recv(int rank, int slot) const {
-    return reinterpret_cast<float*>(static_cast<uint8_t*>(ar_peer_[rank]) + ar_flag_bytes_) +
-           (size_t)slot * world_ * c_.hidden;
+unsigned long long* Engine::peer_recv(int rank, int slot) const {
+    return static_cast<unsigned long long*>(ar_peer_[rank]) + (size_t)slot * world_ * c_.hidden;
 }
-
-unsigned* Engine::peer_flag(int rank, int slot) const { return static_cast<unsigned*>(ar_peer_[rank]) + slot; }
 
 // One transformer block (Engine.cpp:71-103) on the device buffers: x is
 L2Prefetch Engine::weight_prefetch(const uint8_t* w, int type, int K, int rows) const {
@@ -599,16 +595,13 @@ void Engine::enqueue_layer(int i, bool fused) {
         r.epilogue = EPI_PEER;
         r.seg[0].y = nullptr;
         r.peer_out.world = world_;
-        for (int k = 0; k < world_; ++k) {
-            r.peer_out.recv[k] = peer_recv(k, s_) + (size_t)rank_ * H;
-            r.peer_out.flag[k] = peer_flag(k, s_);
-        }
+        r.peer_out.epoch = ar_epoch_;
+        for (int k = 0; k < world_; ++k) r.peer_out.recv[k] = peer_recv(k, s_) + (size_t)rank_ * H;
     };
     // the product's input: x plus every rank's partial sums of slot s_ (none: s_ < 0), also stored to x_out
     auto peer_in = [&](GemvRequest& r, int s_, float* x_out) {
         r.peer_in.world = s_ >= 0 ? world_ : 0;
         r.peer_in.parts = s_ >= 0 ? peer_recv(rank_, s_) : nullptr;
-        r.peer_in.flag = s_ >= 0 ? peer_flag(rank_, s_) : nullptr;
         r.peer_in.epoch = ar_epoch_;
         r.peer_in.x_out = x_out;
     };
@@ -776,7 +769,6 @@ void Engine::enqueue_head(bool fused) {
         if (fused) {
             r.peer_in.world = world_;
             r.peer_in.parts = peer_recv(rank_, 2 * (c.layers - 1) + 1);
-            r.peer_in.flag = peer_flag(rank_, 2 * (c.layers - 1) + 1);
             r.peer_in.epoch = ar_epoch_;
         }
         r.gamma = output_norm_;

@@ -97,8 +97,7 @@ private:
     // Tensor parallelism without a collective launch (tp_world > 1): maps
     // every rank's receive slots into this process (cudaIpc over NCCL).
     void setup_peer_slots();
-    float* peer_recv(int rank, int slot) const;  // rank's slot, [world][hidden]
-    unsigned* peer_flag(int rank, int slot) const;
+    unsigned long long* peer_recv(int rank, int slot) const;  // rank's slot, [world][hidden] (value, tag) words
     void enqueue_head(bool fused);
     // Prompt rows per prefill pass and their buffers (allocated on first use).
     void ensure_prefill();
@@ -189,12 +188,11 @@ private:
 
     // Fused tensor-parallel sums (decode step): slot 2i takes layer i's
     // attn_output partial sums, 2i + 1 its ffn_down ones, from every rank;
-    // one cudaMalloc per rank ([flags][slots][world][hidden]), mapped by the
+    // one cudaMalloc per rank ([slots][world][hidden] words), mapped by the
     // others. xb_ is the second residual buffer (x_ and xb_ in turn).
     bool tp_fused_ = false;
     uint8_t* ar_base_ = nullptr;
     void* ar_peer_[8] = {};  // every rank's allocation (this rank's own at rank_)
-    size_t ar_flag_bytes_ = 0;
     int* ar_epoch_ = nullptr;  // decode steps run, as every rank counts them
     float* xb_ = nullptr;
     cudaGraphExec_t exec_ = nullptr;

@@ -94,23 +94,15 @@ __device__ __forceinline__ void quantise_activation(const GemvPlan& p, int m0, i
                                                     int lane, int warp, int nthreads) {
     const float* gamma = p.gamma ? reinterpret_cast<const float*>(smem + p.off_gamma) : nullptr;
     const PeerIn& pin = p.peer_in;
-    if (pin.world > 0) {
-        // every rank's partial sums of this step have landed in this rank's
-        // receive slot once its flag has reached the step's count
-        // once a wait of this step has given up, the later ones do not wait
-        // again (the step's result is void; the host reads the error word)
-        if (tid == 0 && !(p.err && (*reinterpret_cast<volatile int*>(p.err) & ERR_WAIT_TIMEOUT_PEER))) {
-            const unsigned target = (unsigned)(*pin.epoch + 1) * (unsigned)pin.world * kPeerUnits;
-            flag_wait_bounded(pin.flag, target, pin.wait_ns, p.err, ERR_WAIT_TIMEOUT_PEER);
-        }
-        named_barrier(kAllConsumersBarrier, nthreads);
-    }
+    // tensor parallelism: every rank's partial sums of this step, read until
+    // each word carries this step's tag
+    const unsigned tag = pin.world > 0 ? (unsigned)(*pin.epoch + 1) : 0u;
     quantise_rows<kHeldVec4>(p.x, p.ldx, m0, mcount, gamma, p.eps, p.K, p.off_xq4 >= 0 ? smem + p.off_xq4 : nullptr,
                   p.off_xq6 >= 0 ? smem + p.off_xq6 : nullptr, reinterpret_cast<float*>(smem + p.off_xs),
                   reinterpret_cast<int*>(smem + p.off_xsum16), reinterpret_cast<float*>(smem + p.off_xsum32),
                   reinterpret_cast<float*>(smem + p.off_misc), tid, lane, warp, nthreads, kAllConsumersBarrier,
-                  p.trace, p.trace_tag, pin.world > 0 ? pin.parts : nullptr, pin.world,
-                  pin.world >= 0 && blockIdx.x == 0 ? pin.x_out : nullptr);
+                  p.trace, p.trace_tag, pin.world > 0 ? pin.parts : nullptr, pin.world, tag, p.err, pin.wait_ns,
+                  ERR_WAIT_TIMEOUT_PEER, pin.world >= 0 && blockIdx.x == 0 ? pin.x_out : nullptr);
 }
 
 // Batch of one whose activation the preceding kernel already quantised:
@@ -285,6 +277,8 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     const int* xsum16 = reinterpret_cast<const int*>(smem + p.off_xsum16);
     const float* xsum32 = reinterpret_cast<const float*>(smem + p.off_xsum32);
 
+    // the step's tag of EPI_PEER words (read after the dependency wait)
+    const unsigned peer_tag = p.epilogue == EPI_PEER ? (unsigned)(*p.peer_out.epoch + 1) : 0u;
     const int team = warp / kTeamWarps;
     const int team_threads = kTeamWarps * 32;
     const int LPR = p.lpr;
@@ -402,8 +396,11 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
                 } else if (p.epilogue == EPI_ADD) {
                     *out += acc[0][m];
                 } else if (p.epilogue == EPI_PEER) {
-                    // this rank's partial sum of row `row`, into every rank's receive slot
-                    for (int r = 0; r < p.peer_out.world; ++r) p.peer_out.recv[r][row] = acc[0][m];
+                    // this rank's partial sum of row `row` with this step's tag, one
+                    // 8-byte word into every rank's receive slot
+                    const unsigned long long word =
+                        (unsigned long long)__float_as_uint(acc[0][m]) | ((unsigned long long)peer_tag << 32);
+                    for (int r = 0; r < p.peer_out.world; ++r) p.peer_out.recv[r][row] = word;
                 } else if (p.epilogue == EPI_SWIGLU) {
                     const float g = acc[0][m], up = acc[NR - 1][m];
                     const float a = (g / (1.0f + expf(-g))) * up;  // silu_multiply.cu:9-10
@@ -422,17 +419,6 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     }
 
     if (tid == 0) trace_at(p.trace, p.trace_tag, 4);
-    if (p.epilogue == EPI_PEER) {
-        // this CTA's rows are stored (every consumer thread is past its
-        // stores): add its share of kPeerUnits to every rank's flag
-        named_barrier(kAllConsumersBarrier, nthreads);
-        if (tid == 0) {
-            __threadfence_system();
-            const unsigned share = (unsigned)(((unsigned long long)(blockIdx.x + 1) * kPeerUnits) / G -
-                                              ((unsigned long long)blockIdx.x * kPeerUnits) / G);
-            for (int r = 0; r < p.peer_out.world; ++r) atomicAdd_system(p.peer_out.flag[r], share);
-        }
-    }
     if (PAIR && p.out_image.base) {
         named_barrier(kAllConsumersBarrier, nthreads);  // every output row of this CTA is written
         quantise_output_groups(p, s_begin * p.rows_per_stage, min(s_end * p.rows_per_stage, p.seg[0].rows), smem,
@@ -582,12 +568,12 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     if (rq.epilogue == EPI_PEER) {
         if (rq.M != 1 || rq.nseg != 1 || p.peer_out.world < 1 || p.peer_out.world > kMaxRanks)
             return cudaErrorInvalidValue;
+        if (!p.peer_out.epoch) return cudaErrorInvalidValue;
         for (int r = 0; r < p.peer_out.world; ++r)
-            if (!p.peer_out.recv[r] || !p.peer_out.flag[r]) return cudaErrorInvalidValue;
+            if (!p.peer_out.recv[r]) return cudaErrorInvalidValue;
     }
-    if (p.peer_in.world >= 0 &&
-        (rq.M != 1 || !rq.gamma || p.peer_in.world > kMaxRanks || (rq.K / 4) % 1 != 0 ||
-         (p.peer_in.world > 0 && (!p.peer_in.parts || !p.peer_in.flag || !p.peer_in.epoch))))
+    if (p.peer_in.world >= 0 && (rq.M != 1 || !rq.gamma || p.peer_in.world > kMaxRanks ||
+                                 (p.peer_in.world > 0 && (!p.peer_in.parts || !p.peer_in.epoch))))
         return cudaErrorInvalidValue;
     if (p.in_image.base && (rq.M != 1 || rq.gamma || p.in_image.K != rq.K)) return cudaErrorInvalidValue;
     if (p.out_image.base && (!pair || rq.M != 1 || p.out_image.K != rq.seg[0].rows || p.out_image.K % 256 != 0))

@@ -354,8 +354,9 @@ __device__ __forceinline__ void quantise_rows(const float* x, int ldx, int m0, i
                                               float eps, int K, uint8_t* xq4, uint8_t* xq6, float* xs, int* xsum16,
                                               float* xsum32, float* red, int tid, int lane, int warp, int nthreads,
                                               int barrier_id, unsigned long long* trace = nullptr,
-                                              int trace_tag = 0, const float* parts = nullptr, int nparts = 0,
-                                              float* x_out = nullptr) {
+                                              int trace_tag = 0, const unsigned long long* parts = nullptr,
+                                              int nparts = 0, unsigned parts_tag = 0, int* err = nullptr,
+                                              uint64_t wait_ns = 0, int err_code = 0, float* x_out = nullptr) {
     const int nvec = K / 4;
     // kHeld: float4s of the row a thread keeps in registers (K <= kHeld * 4 * nthreads)
     for (int m = 0; m < mcount; ++m) {
@@ -374,9 +375,9 @@ __device__ __forceinline__ void quantise_rows(const float* x, int ldx, int m0, i
             for (int k = 0; k < kHeld; ++k) {
                 const int i = tid + k * nthreads;
                 if (i >= nvec) continue;
-                float4 sum = __ldcg(reinterpret_cast<const float4*>(parts) + i);
+                float4 sum = tagged_load4(parts + 4 * (size_t)i, parts_tag, wait_ns, err, err_code);
                 for (int r = 1; r < nparts; ++r) {
-                    const float4 t = __ldcg(reinterpret_cast<const float4*>(parts + (size_t)r * K) + i);
+                    const float4 t = tagged_load4(parts + (size_t)r * K + 4 * (size_t)i, parts_tag, wait_ns, err, err_code);
                     sum.x += t.x;
                     sum.y += t.y;
                     sum.z += t.z;

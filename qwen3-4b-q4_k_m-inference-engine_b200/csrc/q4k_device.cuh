@@ -34,29 +34,41 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
     return t;
 }
 
-// A counter other GPUs add to (system-scope acquire, so that the data they
-// stored before adding is visible after it).
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
+// Two consecutive 8-byte words, each read whole (a 64-bit element is
+// single-copy atomic), from L2 at system scope: words other GPUs store.
+__device__ __forceinline__ void ld_words2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
+    asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
-// Waits until *flag has reached `target` (counters that wrap: the signed
-// difference decides), giving up after limit_ns of %globaltimer with `code`
-// in *err. Returns whether it was reached.
-__device__ __forceinline__ bool flag_wait_bounded(const unsigned* flag, unsigned target, uint64_t limit_ns, int* err,
-                                                  int code) {
-    if ((int)(ld_acquire_sys(flag) - target) >= 0) return true;
-    const uint64_t start = global_timer_ns();
-    for (;;) {
-        __nanosleep(64);
-        if ((int)(ld_acquire_sys(flag) - target) >= 0) return true;
-        if (global_timer_ns() - start > limit_ns) {
-            if (err) atomicOr(err, code);
-            return false;
+// Four (value, tag) words (value in the low half, tag in the high half) that
+// other GPUs store into this GPU's memory: read until every tag is `tag`,
+// giving up after limit_ns of %globaltimer with `code` in *err (at once if
+// another wait already gave up). Returns the four values.
+__device__ __forceinline__ float4 tagged_load4(const unsigned long long* p, unsigned tag, uint64_t limit_ns, int* err,
+                                               int code) {
+    unsigned long long w0, w1, w2, w3;
+    ld_words2(p, w0, w1);
+    ld_words2(p + 2, w2, w3);
+    auto ready = [&] {
+        return (unsigned)(w0 >> 32) == tag && (unsigned)(w1 >> 32) == tag && (unsigned)(w2 >> 32) == tag &&
+               (unsigned)(w3 >> 32) == tag;
+    };
+    if (!ready()) {
+        const uint64_t start = global_timer_ns();
+        for (;;) {
+            if (err && (*reinterpret_cast<volatile int*>(err) & code)) break;
+            __nanosleep(32);
+            ld_words2(p, w0, w1);
+            ld_words2(p + 2, w2, w3);
+            if (ready()) break;
+            if (global_timer_ns() - start > limit_ns) {
+                if (err) atomicOr(err, code);
+                break;
+            }
         }
     }
+    return make_float4(__uint_as_float((unsigned)w0), __uint_as_float((unsigned)w1), __uint_as_float((unsigned)w2),
+                       __uint_as_float((unsigned)w3));
 }
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

@@ -18,28 +18,27 @@ enum Epilogue : int {
 };
 
 // Tensor-parallel row-parallel product (EPI_PEER): output row n's partial
-// sum goes to recv[r][n] of every rank r (rank r's receive slot for this
-// product, this rank's row of it; peer memory mapped over NVLink), then each
-// CTA adds its share of kPeerUnits to every rank's flag for the slot (the
-// shares of all CTAs sum to exactly kPeerUnits per rank and product).
+// sum goes, as one 8-byte word (value in the low half, tag in the high
+// half), to recv[r][n] of every rank r (rank r's receive slot for this
+// product, this rank's row of it; peer memory mapped over NVLink). The tag
+// is *epoch + 1, the decode step's number as every rank counts it, so a
+// reader knows a word is this step's without a separate flag, fence or
+// atomic.
 constexpr int kMaxRanks = 8;
-constexpr unsigned kPeerUnits = 1u << 16;
 struct PeerOut {
-    float* recv[kMaxRanks] = {};
-    unsigned* flag[kMaxRanks] = {};
+    unsigned long long* recv[kMaxRanks] = {};
     int world = 0;
+    const int* epoch = nullptr;
 };
 
 // The consuming side (a product with an RMSNorm prologue): its input row is
-// x + sum over ranks r = 0 .. world-1, in that order, of parts[r * K ..],
-// once *flag has reached (*epoch + 1) * world * kPeerUnits (all ranks'
-// partial sums of this step have landed); the row is also written to x_out
-// (the residual stream for the products after this one). world may be 0: x
-// is only copied to x_out.
+// x + sum over ranks r = 0 .. world-1, in that order, of the values of
+// parts[r * K ..] (waiting, bounded, until every word carries this step's
+// tag *epoch + 1); the row is also written to x_out (the residual stream for
+// the products after this one). world may be 0: x is only copied to x_out.
 struct PeerIn {
-    const float* parts = nullptr;
+    const unsigned long long* parts = nullptr;
     int world = -1;  // < 0: not used
-    const unsigned* flag = nullptr;
     const int* epoch = nullptr;
     float* x_out = nullptr;
     unsigned long long wait_ns = 2000000000ull;

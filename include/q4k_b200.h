@@ -9,6 +9,10 @@
  *   Q4K_EINVAL (1)    invalid argument   (the reference throws std::invalid_argument)
  *   Q4K_ERANGE (2)    size/capacity out of range (std::out_of_range / std::length_error)
  *   Q4K_ECUDA (3)     CUDA launch/runtime failure (std::runtime_error from check_launch)
+ *   Q4K_ETIMEOUT (4)  a bounded wait gave up: inside a kernel (another rank's
+ *                     partial sums, a copy that never landed) or on the host
+ *                     (a tensor-parallel step that did not complete in time);
+ *                     no counterpart in the reference, which has no waits
  *
  * and q4k_last_error() returns the calling thread's last message. Kernels
  * are asynchronous on `stream` unless stated otherwise; zero-size work
@@ -31,6 +35,7 @@ extern "C" {
 #define Q4K_EINVAL 1
 #define Q4K_ERANGE 2
 #define Q4K_ECUDA 3
+#define Q4K_ETIMEOUT 4
 
 /* GGML tensor type ids (the GGUF file's values). */
 #define Q4K_TYPE_F32 0
@@ -320,6 +325,32 @@ int q4k_engine_layer_batch(q4k_engine* engine, int layer, int n, const int* seqs
 
 /* Stream the engine launches on (cudaStream_t), e.g. to time with events. */
 void* q4k_engine_stream(q4k_engine* engine);
+
+/* Failure handling under tensor parallelism (no reference counterpart: the
+ * reference runs on one GPU). device_wait_ns bounds every wait inside a
+ * kernel for another rank's partial sums (default 2 s; 0 keeps the current
+ * value): a wait that gives up makes the call fail with Q4K_ETIMEOUT, and
+ * the kernels return, so the context stays usable. host_wait_ms bounds how
+ * long a synchronous call waits for its step when tp_world > 1 (default 0:
+ * no bound); past it the engine aborts its NCCL communicator and the call
+ * fails with Q4K_ETIMEOUT. q4k_engine_abort may be called from any thread,
+ * e.g. by a watchdog that learnt a peer process is gone: a call waiting on
+ * the step returns Q4K_ETIMEOUT, and every later call on this engine fails
+ * with Q4K_ETIMEOUT (destroy it and create a new one). */
+int q4k_engine_set_limits(q4k_engine* engine, uint64_t device_wait_ns, int host_wait_ms);
+int q4k_engine_abort(q4k_engine* engine);
+
+/* The receiving side of the engine's fused tensor-parallel sum, on its own
+ * (no reference counterpart). parts holds `world` slots of `count` 8-byte
+ * words, slot r written by rank r: word i = (tag << 32) | bits of rank r's
+ * partial sum i. Waits (bounded by wait_ns) until every word carries `tag`,
+ * then out[i] = residual[i] + (slot 0 + slot 1 + ... in rank order) in fp32
+ * (residual may be NULL: zero). count a multiple of 4, 1 <= world <= 8,
+ * 16-byte aligned buffers; err_device is one int of device memory the call
+ * clears. Synchronous: returns Q4K_ETIMEOUT if a wait gave up (out is then
+ * undefined), Q4K_OK otherwise. */
+int q4k_tp_sum_parts(const void* parts, int world, int64_t count, uint32_t tag, const float* residual, float* out,
+                     uint64_t wait_ns, int* err_device, void* stream);
 
 /* ------------------------------------------------------ GGUF model files */
 

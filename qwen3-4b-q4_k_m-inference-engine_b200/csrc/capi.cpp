@@ -792,3 +792,37 @@ Q4K_API int q4k_engine_trace(q4k_engine* e, uint32_t token, int position, unsign
 }
 
 Q4K_API void* q4k_engine_stream(q4k_engine* e) { return e ? static_cast<void*>(e->impl.stream()) : nullptr; }
+
+Q4K_API int q4k_engine_set_limits(q4k_engine* e, uint64_t device_wait_ns, int host_wait_ms) {
+    return guarded([&] {
+        if (!e) invalid("engine required");
+        e->impl.set_limits(device_wait_ns, host_wait_ms);
+    });
+}
+
+Q4K_API int q4k_engine_abort(q4k_engine* e) {
+    return guarded([&] {
+        if (!e) invalid("engine required");
+        e->impl.abort();
+    });
+}
+
+Q4K_API int q4k_tp_sum_parts(const void* parts, int world, int64_t count, uint32_t tag, const float* residual,
+                             float* out, uint64_t wait_ns, int* err_device, void* stream) {
+    return guarded_cuda([&] {
+        if (!parts || !out || !err_device) invalid("tp_sum_parts needs parts, out and an error word");
+        if (world < 1 || world > 8 || count < 0 || count % 4) invalid("1 <= world <= 8 and count a multiple of 4");
+        if (reinterpret_cast<uintptr_t>(parts) % 16 || reinterpret_cast<uintptr_t>(out) % 16 ||
+            (residual && reinterpret_cast<uintptr_t>(residual) % 16))
+            invalid("tp_sum_parts buffers must be 16-byte aligned");
+        if (wait_ns == 0) invalid("wait_ns must be positive");
+        cudaStream_t s = as_stream(stream);
+        q4k::cuda_check(cudaMemsetAsync(err_device, 0, sizeof(int), s), "memset");
+        launched(q4k::tp_sum_parts(static_cast<const unsigned long long*>(parts), world, (size_t)count, tag,
+                                   residual, out, wait_ns, err_device, s));
+        int err = 0;
+        q4k::cuda_check(cudaMemcpyAsync(&err, err_device, sizeof(int), cudaMemcpyDeviceToHost, s), "read err");
+        q4k::cuda_check(cudaStreamSynchronize(s), "tp_sum_parts");
+        if (err) throw q4k::Error(Q4K_ETIMEOUT, "tp_sum_parts: a partial sum never carried the tag (wait gave up)");
+    });
+}

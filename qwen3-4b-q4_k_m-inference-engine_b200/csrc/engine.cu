@@ -29,6 +29,8 @@
 #include <cstring>
 #include <mutex>
 
+#include <chrono>
+#include <thread>
 #include "nccl_api.h"
 
 #include "ops.h"
@@ -59,6 +61,7 @@ const NcclApi& nccl() {
         api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
         api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(dlsym(h, "ncclCommInitRank"));
         api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
+        api.CommAbort = reinterpret_cast<decltype(api.CommAbort)>(dlsym(h, "ncclCommAbort"));
         api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(dlsym(h, "ncclAllReduce"));
         api.AllGather = reinterpret_cast<decltype(api.AllGather)>(dlsym(h, "ncclAllGather"));
         api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
@@ -334,7 +337,7 @@ Engine::~Engine() {
     if (stream_) cudaStreamSynchronize(stream_);
     for (int r = 0; r < world_ && r < kMaxRanks; ++r)
         if (r != rank_ && ar_peer_[r]) cudaIpcCloseMemHandle(ar_peer_[r]);
-    if (comm_) nccl().CommDestroy(comm_);
+    if (comm_ && !comm_aborted_) nccl().CommDestroy(comm_);
     for (void* p : allocations_) cudaFree(p);
     if (host_io_) cudaFreeHost(host_io_);
     if (stream_) cudaStreamDestroy(stream_);
@@ -604,6 +607,7 @@ void Engine::enqueue_layer(int i, bool fused) {
         r.peer_in.parts = s_ >= 0 ? peer_recv(rank_, s_) : nullptr;
         r.peer_in.epoch = ar_epoch_;
         r.peer_in.x_out = x_out;
+        r.peer_in.wait_ns = dev_wait_ns_;
     };
     auto gemv = [&](GemvRequest& r) { cuda_check(launch_gemv(r, stream_), "gemv launch"); };
     auto all_reduce_into_x = [&]() {
@@ -770,6 +774,7 @@ void Engine::enqueue_head(bool fused) {
             r.peer_in.world = world_;
             r.peer_in.parts = peer_recv(rank_, 2 * (c.layers - 1) + 1);
             r.peer_in.epoch = ar_epoch_;
+            r.peer_in.wait_ns = dev_wait_ns_;
         }
         r.gamma = output_norm_;
         r.eps = c.eps;
@@ -951,21 +956,85 @@ void Engine::ensure_graph() {
     cuda_check(e, "graph instantiate");
 }
 
+void Engine::set_limits(uint64_t device_wait_ns, int host_wait_ms) {
+    if (host_wait_ms < 0) throw Error(Q4K_EINVAL, "host_wait_ms must be >= 0");
+    if (device_wait_ns && device_wait_ns != dev_wait_ns_) {
+        dev_wait_ns_ = device_wait_ns;
+        // the limit is a kernel parameter of the captured step: capture again
+        if (exec_) cudaGraphExecDestroy(exec_);
+        exec_ = nullptr;
+    }
+    host_wait_ms_ = host_wait_ms;
+}
+
+void Engine::abort() {
+    aborted_.store(true);
+    std::lock_guard<std::mutex> lock(abort_mu_);
+    if (comm_ && !comm_aborted_) {
+        // makes the NCCL kernels in flight on this rank return, so that the
+        // stream drains; the communicator is freed and never used again
+        const NcclApi& api = nccl();
+        if (api.CommAbort) api.CommAbort(comm_);
+        comm_aborted_ = true;
+    }
+}
+
+void Engine::host_wait(const char* what) {
+    if (world_ == 1 || (host_wait_ms_ == 0 && !aborted_.load())) {
+        cuda_check(cudaStreamSynchronize(stream_), what);
+        // an abort from another thread ends NCCL's kernels, so the stream
+        // drains; the step did not complete
+        if (aborted_.load()) throw Error(Q4K_ETIMEOUT, std::string(what) + ": tensor-parallel step aborted");
+        return;
+    }
+    // tensor parallelism: poll, so that a peer that never arrives (or an
+    // abort from another thread) ends the wait instead of blocking for good
+    const auto start = std::chrono::steady_clock::now();
+    for (long spins = 0;; ++spins) {
+        const cudaError_t e = cudaStreamQuery(stream_);
+        if (e == cudaSuccess) return;
+        if (e != cudaErrorNotReady) cuda_check(e, what);
+        const bool late = host_wait_ms_ > 0 && std::chrono::steady_clock::now() - start >
+                                                    std::chrono::milliseconds(host_wait_ms_);
+        if (late || aborted_.load()) {
+            abort();
+            // NCCL kernels end once the communicator is aborted, and every
+            // wait inside this library's kernels is bounded: drain the stream
+            // so that no kernel of this rank is left running
+            cudaStreamSynchronize(stream_);
+            throw Error(Q4K_ETIMEOUT, std::string(what) + ": tensor-parallel step " +
+                                          (late ? "did not complete within the host limit" : "aborted") +
+                                          "; the communicator is aborted");
+        }
+        if (spins > 1000) std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
 void Engine::check_device_error() {
     int err = 0;
     cuda_check(cudaMemcpyAsync(&host_io_[3], err_, sizeof(int), cudaMemcpyDeviceToHost, stream_), "read err");
-    cuda_check(cudaStreamSynchronize(stream_), "step");
+    host_wait("step");
     err = (int)host_io_[3];
     if (err) {
         cudaMemsetAsync(err_, 0, sizeof(int), stream_);
         cudaStreamSynchronize(stream_);
         char msg[96];
         std::snprintf(msg, sizeof msg, "device reported error bits 0x%x", err);
-        throw Error((err & (ERR_BAD_POSITION | ERR_BAD_TOKEN)) ? Q4K_ERANGE : Q4K_ECUDA, msg);
+        int status = Q4K_ECUDA;
+        if (err & (ERR_WAIT_TIMEOUT_FULL | ERR_WAIT_TIMEOUT_EMPTY | ERR_WAIT_TIMEOUT_DEP | ERR_WAIT_TIMEOUT_PEER))
+            status = Q4K_ETIMEOUT;
+        else if (err & (ERR_BAD_POSITION | ERR_BAD_TOKEN))
+            status = Q4K_ERANGE;
+        throw Error(status, msg);
     }
 }
 
+void Engine::require_live() const {
+    if (aborted_.load()) throw Error(Q4K_ETIMEOUT, "the engine was aborted (tensor-parallel failure); create a new one");
+}
+
 uint32_t Engine::decode(uint32_t token, int position, float* logits_host, float* hidden_host) {
+    require_live();
     if (!loaded_) throw Error(Q4K_EINVAL, "weights are not loaded");
     if (token >= (uint32_t)c_.vocab) throw Error(Q4K_ERANGE, "Token ID out of range");
     if (position < 0 || position >= c_.capacity) throw Error(Q4K_ERANGE, "KV cache capacity exceeded");
@@ -1000,6 +1069,7 @@ uint32_t Engine::decode(uint32_t token, int position, float* logits_host, float*
 }
 
 void Engine::generate(uint32_t token, int position, int steps, int advance, uint32_t* tokens_host) {
+    require_live();
     if (!loaded_) throw Error(Q4K_EINVAL, "weights are not loaded");
     if (token >= (uint32_t)c_.vocab) throw Error(Q4K_ERANGE, "Token ID out of range");
     if (steps < 0 || steps > c_.capacity) throw Error(Q4K_ERANGE, "too many steps");
@@ -1030,6 +1100,7 @@ void Engine::generate(uint32_t token, int position, int steps, int advance, uint
 }
 
 size_t Engine::trace_step(uint32_t token, int position, unsigned long long* records_host, size_t max_records) {
+    require_live();
     if (!loaded_) throw Error(Q4K_EINVAL, "weights are not loaded");
     if (token >= (uint32_t)c_.vocab) throw Error(Q4K_ERANGE, "Token ID out of range");
     if (position < 0 || position >= c_.capacity) throw Error(Q4K_ERANGE, "KV cache capacity exceeded");
@@ -1309,6 +1380,7 @@ void Engine::enqueue_prefill_layer(int i, int rows, int pos0, int seq) {
 }
 
 uint32_t Engine::prefill(const uint32_t* tokens_host, int n, int position, float* logits_host, int seq) {
+    require_live();
     if (!loaded_) throw Error(Q4K_EINVAL, "weights are not loaded");
     if (seq < 0 || seq >= seqs_) throw Error(Q4K_ERANGE, "sequence out of range");
     if (n <= 0 || !tokens_host) throw Error(Q4K_EINVAL, "prefill needs at least one token");
@@ -1526,6 +1598,7 @@ int Engine::stage_batch(int n, const int* seqs, const uint32_t* tokens, const in
 
 void Engine::decode_batch(int n, const int* seqs, const uint32_t* tokens, const int* positions, uint32_t* next_host,
                           float* logits_host) {
+    require_live();
     if (!tokens) throw Error(Q4K_EINVAL, "batched decode needs tokens");
     const int splits = stage_batch(n, seqs, tokens, positions);
     const int H = c_.hidden;
@@ -1570,6 +1643,7 @@ void Engine::decode_batch(int n, const int* seqs, const uint32_t* tokens, const 
 
 void Engine::layer_batch(int layer, int n, const int* seqs, const int* positions, const float* x_host,
                          float* x_out_host) {
+    require_live();
     if (layer < 0 || layer >= c_.layers) throw Error(Q4K_ERANGE, "layer out of range");
     if (!x_host || !x_out_host) throw Error(Q4K_EINVAL, "layer rows need input and output");
     const int splits = stage_batch(n, seqs, nullptr, positions);
@@ -1581,6 +1655,7 @@ void Engine::layer_batch(int layer, int n, const int* seqs, const int* positions
 }
 
 void Engine::layer_rows(int layer, int seq, int n, int position, const float* x_host, float* x_out_host) {
+    require_live();
     if (!loaded_) throw Error(Q4K_EINVAL, "weights are not loaded");
     if (layer < 0 || layer >= c_.layers) throw Error(Q4K_ERANGE, "layer out of range");
     if (seq < 0 || seq >= seqs_) throw Error(Q4K_ERANGE, "sequence out of range");
@@ -1597,6 +1672,7 @@ void Engine::layer_rows(int layer, int seq, int n, int position, const float* x_
 }
 
 void Engine::layer_step(int layer, const float* x_host, int position, float* x_out_host) {
+    require_live();
     if (!loaded_) throw Error(Q4K_EINVAL, "weights are not loaded");
     if (layer < 0 || layer >= c_.layers) throw Error(Q4K_ERANGE, "layer out of range");
     if (position < 0 || position >= c_.capacity) throw Error(Q4K_ERANGE, "KV cache capacity exceeded");

@@ -5,6 +5,8 @@
 #include <nccl.h>
 
 #include <stdexcept>
+#include <atomic>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -73,6 +75,18 @@ public:
     // products and attention): row i at positions[i] of sequence seqs[i].
     void layer_batch(int layer, int n, const int* seqs, const int* positions, const float* x_host,
                      float* x_out_host);
+    // Failure handling under tensor parallelism. device_wait_ns bounds every
+    // in-kernel wait for another rank's partial sums (0 keeps the current
+    // limit); host_wait_ms bounds how long a synchronous call waits for the
+    // stream (0: no limit), after which the communicator is aborted and the
+    // call fails with Q4K_ETIMEOUT. abort() may be called from any thread
+    // (a watchdog that learnt a peer is gone): it aborts the communicator,
+    // a synchronous call waiting on the stream returns Q4K_ETIMEOUT, and
+    // every later call fails. The device limit is captured into the decode
+    // graph, which is rebuilt on the next step.
+    void set_limits(uint64_t device_wait_ns, int host_wait_ms);
+    void abort();
+    bool aborted() const { return aborted_.load(); }
     // One step with every kernel CTA's %globaltimer start/end recorded.
     size_t trace_step(uint32_t token, int position, unsigned long long* records_host, size_t max_records);
     cudaStream_t stream() const { return stream_; }
@@ -196,6 +210,13 @@ private:
     int* ar_epoch_ = nullptr;  // decode steps run, as every rank counts them
     float* xb_ = nullptr;
     cudaGraphExec_t exec_ = nullptr;
+    uint64_t dev_wait_ns_ = 2000000000ull;  // in-kernel waits for other ranks' partial sums
+    int host_wait_ms_ = 0;                  // synchronous calls under tensor parallelism (0: unbounded)
+    std::atomic<bool> aborted_{false};
+    std::mutex abort_mu_;                   // one ncclCommAbort, whichever thread gets there first
+    bool comm_aborted_ = false;
+    void host_wait(const char* what);
+    void require_live() const;       // stream drained, bounded by host_wait_ms_ when world_ > 1
     bool l2_prefetch_ = true;        // each launch prefetches the next one's operands into L2
     bool act_images_ = true;         // SwiGLU and attention hand the next product a quantised activation
     ActImage act_img_, att_img_;     // quantised act_ (for ffn_down) and att_ (for attn_output)

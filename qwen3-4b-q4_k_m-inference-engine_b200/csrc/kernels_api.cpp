@@ -28,40 +28,64 @@ void cuda(cudaError_t e, const char* what) {
 }  // namespace
 
 // ------------------------------------------------------------ DeviceBuffer
-Q4K_CXX_API DeviceBuffer::DeviceBuffer(const void* source, std::size_t source_bytes, cudaStream_t s) : stream(s) {
-    if (source_bytes == 0) return;
-    if (!source) throw std::invalid_argument("Nonempty DeviceBuffer requires host data");
-    cuda(cudaMallocAsync(&data, source_bytes, stream), "cudaMallocAsync failed: ");
-    cudaError_t e = cudaMemcpyAsync(data, source, source_bytes, cudaMemcpyHostToDevice, stream);
+// Every buffer is one stream-ordered allocation on its own stream; the
+// owning handle is (data, bytes, stream) and a moved-from buffer is empty.
+// Errors: a null host source for a non-empty upload is the caller's mistake
+// (std::invalid_argument); anything CUDA reports is std::runtime_error, and
+// a failed upload releases the allocation before throwing.
+namespace {
+
+void* stream_allocate(std::size_t n, cudaStream_t s) {
+    void* p = nullptr;
+    if (n == 0) return p;
+    const cudaError_t e = cudaMallocAsync(&p, n, s);
+    if (e != cudaSuccess) {
+        // an allocation failure is not sticky: clear it so that the next
+        // launch check does not report it again
+        (void)cudaGetLastError();
+        throw std::runtime_error(std::string("DeviceBuffer allocation: ") + cudaGetErrorString(e));
+    }
+    return p;
+}
+
+void stream_release(void* p, cudaStream_t s) noexcept {
+    if (p) cudaFreeAsync(p, s);
+}
+
+}  // namespace
+
+Q4K_CXX_API DeviceBuffer::DeviceBuffer(std::size_t n, cudaStream_t s)
+    : data(stream_allocate(n, s)), bytes(n), stream(s) {}
+
+Q4K_CXX_API DeviceBuffer::DeviceBuffer(const void* source, std::size_t n, cudaStream_t s)
+    : DeviceBuffer((n > 0 && !source) ? throw std::invalid_argument("DeviceBuffer: no host bytes to upload") : n, s) {
+    if (n == 0) return;
+    // the copy is complete before the constructor returns, so the caller
+    // may release the host bytes at once (the reference relies on this)
+    cudaError_t e = cudaMemcpyAsync(data, source, n, cudaMemcpyHostToDevice, stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
     if (e != cudaSuccess) {
-        cudaFreeAsync(data, stream);
-        data = nullptr;
-        throw std::runtime_error(std::string("Host-to-device copy failed: ") + cudaGetErrorString(e));
+        stream_release(std::exchange(data, nullptr), stream);
+        bytes = 0;
+        throw std::runtime_error(std::string("DeviceBuffer upload: ") + cudaGetErrorString(e));
     }
-    bytes = source_bytes;
 }
 
-Q4K_CXX_API DeviceBuffer::DeviceBuffer(std::size_t source_bytes, cudaStream_t s) : stream(s) {
-    if (source_bytes == 0) return;
-    cuda(cudaMallocAsync(&data, source_bytes, stream), "cudaMallocAsync failed: ");
-    bytes = source_bytes;
-}
+Q4K_CXX_API DeviceBuffer::~DeviceBuffer() { stream_release(data, stream); }
 
-Q4K_CXX_API DeviceBuffer::~DeviceBuffer() {
-    if (data) cudaFreeAsync(data, stream);
+Q4K_CXX_API DeviceBuffer::DeviceBuffer(DeviceBuffer&& o) noexcept : data(o.data), bytes(o.bytes), stream(o.stream) {
+    o.data = nullptr;
+    o.bytes = 0;
+    o.stream = nullptr;
 }
-
-Q4K_CXX_API DeviceBuffer::DeviceBuffer(DeviceBuffer&& o) noexcept
-    : data(std::exchange(o.data, nullptr)), bytes(std::exchange(o.bytes, 0)), stream(std::exchange(o.stream, nullptr)) {}
 
 Q4K_CXX_API DeviceBuffer& DeviceBuffer::operator=(DeviceBuffer&& o) noexcept {
-    if (this != &o) {
-        if (data) cudaFreeAsync(data, stream);
-        data = std::exchange(o.data, nullptr);
-        bytes = std::exchange(o.bytes, 0);
-        stream = std::exchange(o.stream, nullptr);
-    }
+    // take o's buffer into a temporary and swap: the old one is released
+    // by the temporary's destructor, and self-assignment is a no-op swap
+    DeviceBuffer taken(std::move(o));
+    std::swap(data, taken.data);
+    std::swap(bytes, taken.bytes);
+    std::swap(stream, taken.stream);
     return *this;
 }
 

@@ -137,6 +137,30 @@ __global__ void residual_add_kernel(float* state, const float* branch, size_t co
     if (i < count) state[i] += branch[i];
 }
 
+// The receiving side of the fused tensor-parallel sum: 4 outputs per thread,
+// every slot's words read (bounded) until they carry `tag`, then summed in
+// rank order and added to the residual, as the product prologue does
+// (gemv_device.cuh quantise_rows).
+__global__ void tp_sum_parts_kernel(const unsigned long long* parts, int world, size_t n4, unsigned tag,
+                                    const float* residual, float* out, unsigned long long wait_ns, int* err) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        float4 sum = tagged_load4(parts + 4 * i, tag, wait_ns, err, ERR_WAIT_TIMEOUT_PEER);
+        for (int r = 1; r < world; ++r) {
+            const float4 t = tagged_load4(parts + (size_t)r * 4 * n4 + 4 * i, tag, wait_ns, err, ERR_WAIT_TIMEOUT_PEER);
+            sum.x += t.x;
+            sum.y += t.y;
+            sum.z += t.z;
+            sum.w += t.w;
+        }
+        float4 x = residual ? reinterpret_cast<const float4*>(residual)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        x.x += sum.x;
+        x.y += sum.y;
+        x.z += sum.z;
+        x.w += sum.w;
+        reinterpret_cast<float4*>(out)[i] = x;
+    }
+}
+
 __global__ void silu_multiply_kernel(const float* gate, const float* up, float* out, size_t count) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < count) {
@@ -328,6 +352,15 @@ cudaError_t attention_f32(const float* q, const float* k, const float* v, float*
 
 cudaError_t residual_add(float* state, const float* branch, size_t count, cudaStream_t s) {
     residual_add_kernel<<<blocks_for(count), kThreads, 0, s>>>(state, branch, count);
+    return cudaGetLastError();
+}
+
+cudaError_t tp_sum_parts(const unsigned long long* parts, int world, size_t count, unsigned tag,
+                         const float* residual, float* out, unsigned long long wait_ns, int* err, cudaStream_t s) {
+    const size_t n4 = count / 4;
+    const unsigned blocks = (unsigned)std::min<size_t>((n4 + kThreads - 1) / kThreads, 4 * 148);
+    if (n4 == 0) return cudaSuccess;
+    tp_sum_parts_kernel<<<blocks, kThreads, 0, s>>>(parts, world, n4, tag, residual, out, wait_ns, err);
     return cudaGetLastError();
 }
 

@@ -15,6 +15,9 @@ cudaError_t attention_f32(const float* q, const float* k, const float* v, float*
                           size_t kv_heads, size_t head_dim, size_t offset, cudaStream_t s);
 cudaError_t residual_add(float* state, const float* branch, size_t count, cudaStream_t s);
 cudaError_t silu_multiply(const float* gate, const float* up, float* out, size_t count, cudaStream_t s);
+// out = residual + sum over ranks of tagged partial sums (q4k_tp_sum_parts)
+cudaError_t tp_sum_parts(const unsigned long long* parts, int world, size_t count, unsigned tag,
+                         const float* residual, float* out, unsigned long long wait_ns, int* err, cudaStream_t s);
 cudaError_t dequantize_raw(const void* packed, float* out, size_t rows, size_t width, size_t row_bytes, int type,
                            cudaStream_t s);
 cudaError_t embed_rows(const void* table, int type, size_t width, size_t vocab, const uint32_t* tokens, size_t count,

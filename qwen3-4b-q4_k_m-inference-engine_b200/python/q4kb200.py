@@ -16,7 +16,7 @@ import numpy as np
 PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LIB_PATH = os.path.join(PKG_DIR, "lib", "libq4kb200.so")
 
-OK, EINVAL, ERANGE, ECUDA = 0, 1, 2, 3
+OK, EINVAL, ERANGE, ECUDA, ETIMEOUT = 0, 1, 2, 3, 4
 F32, F16, Q4_K, Q6_K = 0, 1, 12, 14
 EPI_STORE, EPI_ADD, EPI_SWIGLU, EPI_ARGMAX = 0, 1, 2, 3
 
@@ -34,6 +34,9 @@ EXPORTS = (
     "q4k_gguf_tensor_count", "q4k_gguf_tensor_info", "q4k_gguf_meta_int", "q4k_gguf_meta_float",
     "q4k_gguf_meta_string", "q4k_gguf_engine_config", "q4k_engine_load_gguf", "q4k_engine_layer_rows",
     "q4k_engine_layer_batch",
+    "q4k_engine_set_limits",
+    "q4k_engine_abort",
+    "q4k_tp_sum_parts",
 )
 
 
@@ -49,6 +52,12 @@ class InvalidArgument(Q4KError, ValueError):
 
 class OutOfRange(Q4KError, IndexError):
     pass
+
+
+class Timeout(Q4KError, TimeoutError):
+    """A bounded wait gave up (Q4K_ETIMEOUT): another rank's partial sums
+    never arrived, a tensor-parallel step overran the host limit, or the
+    engine was aborted."""
 
 
 class EngineConfig(C.Structure):
@@ -111,6 +120,9 @@ def lib():
             "q4k_engine_decode_batch": ([P, I, P, P, P, P, P], I),
             "q4k_engine_generate": ([P, C.c_uint32, I, I, I, P], I),
             "q4k_engine_stream": ([P], P),
+            "q4k_engine_set_limits": ([P, U64, I], I),
+            "q4k_engine_abort": ([P], I),
+            "q4k_tp_sum_parts": ([P, I, I64, C.c_uint32, P, P, U64, P, P], I),
             "q4k_engine_layer": ([P, I, P, I, P], I),
             "q4k_engine_layer_rows": ([P, I, I, I, I, P, P], I),
             "q4k_engine_layer_batch": ([P, I, I, P, P, P, P], I),
@@ -145,6 +157,8 @@ def check(status: int) -> None:
         raise InvalidArgument(status, msg)
     if status == ERANGE:
         raise OutOfRange(status, msg)
+    if status == ETIMEOUT:
+        raise Timeout(status, msg)
     raise Q4KError(status, msg)
 
 
@@ -421,6 +435,18 @@ class Engine:
     def stream(self) -> int:
         return lib().q4k_engine_stream(self.h)
 
+    def set_limits(self, device_wait_ns: int = 0, host_wait_ms: int = 0):
+        """Bound the in-kernel waits for other ranks' partial sums
+        (device_wait_ns; 0 keeps the current 2 s) and how long a synchronous
+        call waits for a tensor-parallel step (host_wait_ms; 0: unbounded).
+        Either running out raises Timeout."""
+        check(lib().q4k_engine_set_limits(self.h, device_wait_ns, host_wait_ms))
+
+    def abort(self):
+        """Abort the engine's communicator (safe from another thread): a call
+        waiting on a step raises Timeout, and so does every later call."""
+        check(lib().q4k_engine_abort(self.h))
+
     def trace(self, token: int, position: int) -> np.ndarray:
         """One traced decode step: [256 launches][1024 CTAs][8 slots] of
         %globaltimer ns (0 = not recorded)."""
@@ -434,3 +460,63 @@ def nccl_unique_id() -> bytes:
     buf = C.create_string_buffer(128)
     check(lib().q4k_nccl_unique_id(buf))
     return buf.raw
+
+
+class PeerLost(RuntimeError):
+    """Another tensor-parallel rank left or stopped beating (PeerWatch)."""
+
+
+class PeerWatch:
+    """Host-side liveness of the tensor-parallel ranks over a key-value store
+    (a torch.distributed Store: TCPStore, FileStore, ...). No counterpart in
+    the reference, which runs on one GPU.
+
+    Every rank calls beat() before it launches a step and check() before its
+    next launch: check() raises PeerLost when another rank said it left
+    (leave(), called between steps) or when its beat has not changed for
+    `timeout_s` seconds of this process's monotonic clock (a rank that
+    crashed or hangs). With `engine` given, a lost peer also aborts that
+    engine's communicator, so that a call still waiting on a collective
+    returns (Timeout) instead of blocking for good. Beats are step counters,
+    not wall-clock times, so ranks on different hosts need no common clock."""
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 10.0, engine=None, prefix: str = "q4k/peer"):
+        import time
+
+        self._time = time.monotonic
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout_s, self.engine, self.prefix = timeout_s, engine, prefix
+        self.step = 0
+        now = self._time()
+        self._seen = {r: (None, now) for r in range(world) if r != rank}
+        self.store.set(self._key(rank), "0")
+
+    def _key(self, r: int) -> str:
+        return f"{self.prefix}/{r}"
+
+    def beat(self):
+        self.step += 1
+        self.store.set(self._key(self.rank), str(self.step))
+
+    def leave(self):
+        self.store.set(self._key(self.rank), "left")
+
+    def _lost(self, why: str):
+        if self.engine is not None:
+            try:
+                self.engine.abort()
+            except Exception:  # noqa: BLE001 - the peer is gone either way
+                pass
+        raise PeerLost(why)
+
+    def check(self):
+        now = self._time()
+        for r, (last, since) in list(self._seen.items()):
+            key = self._key(r)
+            value = self.store.get(key).decode() if self.store.check([key]) else None
+            if value == "left":
+                self._lost(f"rank {r} left")
+            if value != last:
+                self._seen[r] = (value, now)
+            elif now - since > self.timeout_s:
+                self._lost(f"rank {r} has not beaten for {now - since:.1f} s (last beat {last})")

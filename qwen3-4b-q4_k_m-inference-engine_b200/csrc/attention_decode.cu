@@ -43,11 +43,15 @@ constexpr int T = kAttnTile;  // positions per tile
 constexpr int kComputeWarps = 8;
 constexpr int kComputeThreads = kComputeWarps * 32;
 constexpr int kStageBytes = 2 * kTileBytes;  // K + V
-// The merging CTA stages every split's (m, l) pair of its G heads in the
-// stage buffers, reading up to a whole kBatch of splits past the last one:
-// (splits rounded up to kBatch) x G x 2 floats must fit in them.
-constexpr int kMergeBatch = 24;
-constexpr int kMaxSplits = 3 * kStageBytes / (G * 2 * 4) - kMergeBatch;
+// Ring depth: a multiple of the two consumer groups, so that slot t % kStages
+// is only ever consumed by group t % 2 and each group waits on its slots'
+// mbarrier phases in order (with a depth the groups do not divide, a group
+// running ahead could wait on a slot whose last phase is two uses old, see
+// its parity as complete and read the slot early).
+constexpr int kStages = 4;
+// The merging CTA takes its splits 32 at a time, one per lane.
+constexpr int kMergeBatch = 32;  // one split per lane
+constexpr int kMaxSplits = 1024;
 
 struct Args {
     const float* qkv;
@@ -84,7 +88,7 @@ struct SmemTail {
     uint64_t full[8];
     uint64_t empty[8];
     int last;
-    int abort[2];  // per tile parity: a fast warp's next tile never clears the current flag
+    int abort[4];  // [group][parity of the group's tile]: a fast warp's next tile never sets the flag its group is reading
 };
 
 __global__ void __launch_bounds__(kComputeThreads + 32, 1)
@@ -128,7 +132,7 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], 1);
         }
-        sm.abort[0] = sm.abort[1] = 0;
+        sm.abort[0] = sm.abort[1] = sm.abort[2] = sm.abort[3] = 0;
         mbar_fence_init();
     }
     __syncthreads();
@@ -227,99 +231,110 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
     named_barrier(1, kComputeThreads);
     if (tid == 0) trace_at(trace, a.trace_tag, 1);
 
-    // ---------------- tiles: this warp owns tile rows [8w, 8w + 8) ----------------
+    // ---------------- tiles ----------------
+    // The eight warps form two groups of four: group k takes tiles k, k + 2,
+    // ...; warp wg of a group owns positions [16 wg, 16 wg + 16) of each of
+    // its tiles. Per 16 positions a warp runs 16 QK and 16 PV MMAs of shape
+    // m16n8k16 whose A rows 0-3 carry the fp16 hi parts of the 4 heads' Q (or
+    // P) and rows 8-11 their lo parts, so one MMA yields both products:
+    //   scores   S[h][pos] = D[h][pos] + D[h + 8][pos],  B = K^T (16 dims x 8 positions)
+    //   output   O[h][dim] += D[h][dim] + D[h + 8][dim], B = V (16 positions x 8 dims)
+    const int grp = warp >> 2, wg = warp & 3;
     const float scale = rsqrtf((float)D);  // attention.cu:40
-    const int r_lane = 8 * warp + (lane & 7);  // tile row this lane addresses for ldmatrix
     float m_run = -CUDART_INF_F, l_run = 0.0f;  // per head g (lanes with g < 4)
-    float o[16][2];                             // O[g][8j + 2tq, +1]
+    float o[16][4];  // dim chunk c: hi rows (O[g][8c + 2tq, +1]) and lo rows (the same dims)
 #pragma unroll
-    for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = 0.0f;
+    for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+    const int rA = 16 * wg + (lane & 7);                      // K rows: positions 0-7, then 8-15, of the slab
+    const int vr = 16 * wg + (lane & 7) + 8 * ((lane >> 3) & 1);  // V rows for the transposed loads
+    const int gbar = 2 + grp;                                 // named barrier of this warp's group
 
-    for (int t = 0; t < tiles; ++t) {
+    for (int t = grp; t < tiles; t += 2) {
         const int s = t % S, use = t / S;
-        // A warp whose wait gave up flags the CTA; every warp still reaches the
-        // end-of-tile barrier, after which all leave together.
+        // A warp whose wait gave up flags the CTA; its group still meets at
+        // the end-of-tile barrier, after which the group leaves.
         const bool landed = mbar_wait_bounded(&sm.full[s], use & 1, a.err, ERR_WAIT_TIMEOUT_FULL);
-        if (tid == 0 && (t == 0 || t == tiles - 1)) trace_at(trace, a.trace_tag, t == 0 ? 2 : 3);
-        if (!__all_sync(0xffffffffu, landed) && lane == 0) sm.abort[t & 1] = 1;
+        if (tid == 0 && t == 0) trace_at(trace, a.trace_tag, 2);
+        if (warp == 0 && lane == 0 && t + 2 >= tiles) trace_at(trace, a.trace_tag, 3);
+        const int flag = 2 * grp + ((t >> 1) & 1);
+        if (!__all_sync(0xffffffffu, landed) && lane == 0) sm.abort[flag] = 1;
         const int lo = p0 + t * T;
         const int n = min(T, p1 - lo);
         uint8_t* kt = smem + s * kStageBytes;
         uint8_t* vt = kt + kTileBytes;
         // the new token's row: this warp's slab holds it in the owner CTA
         const int prow = pos - lo;
-        if (owner && prow >= 8 * warp && prow < 8 * warp + 8) {
+        const bool mine = owner && prow >= 16 * wg && prow < 16 * wg + 16;
+        if (mine) {
             if (lane < 16) {
                 *reinterpret_cast<uint4*>(kt + tile_off(prow, lane)) = *reinterpret_cast<const uint4*>(sm.k_new + 8 * lane);
                 *reinterpret_cast<uint4*>(vt + tile_off(prow, lane)) = *reinterpret_cast<const uint4*>(sm.v_new + 8 * lane);
             }
             __syncwarp();
         }
-        // scores for 8 positions x 4 heads
-        // four independent accumulator chains (hi / lo parts of the even /
-        // odd k-steps), summed at the end, instead of one chain of 16 MMAs
-        float ca[4] = {0.0f, 0.0f, 0.0f, 0.0f}, cb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        float cc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, cd[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        // scores of positions 0-7 (sa: even k-steps, sb: odd) and 8-15 (ta, tb) of the slab
+        float sa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        float ta[4] = {0.0f, 0.0f, 0.0f, 0.0f}, tb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         const uint32_t kbase = smem_addr(kt);
 #pragma unroll
         for (int s2 = 0; s2 < 8; s2 += 2) {
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4(kbase + tile_off(r_lane, 2 * s2 + (lane >> 3)), b0, b1, b2, b3);
+            uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+            ldsm_x4(kbase + tile_off(rA, 2 * s2 + (lane >> 3)), a0, a1, a2, a3);
+            ldsm_x4(kbase + tile_off(rA + 8, 2 * s2 + (lane >> 3)), b0, b1, b2, b3);
             const uint4 fa = sm.qf[s2][lane], fb = sm.qf[s2 + 1][lane];
-            mma16816(ca, fa.x, fa.z, b0, b1);  // hi parts
-            mma16816(cb, fa.y, fa.w, b0, b1);  // lo parts
-            mma16816(cc, fb.x, fb.z, b2, b3);
-            mma16816(cd, fb.y, fb.w, b2, b3);
+            mma16816_hilo(sa, fa, a0, a1);
+            mma16816_hilo(sb, fb, a2, a3);
+            mma16816_hilo(ta, fa, b0, b1);
+            mma16816_hilo(tb, fb, b2, b3);
         }
-        float sc[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) sc[i] = (ca[i] + cc[i]) + (cb[i] + cd[i]);
-        // online softmax over this warp's 8 positions (lane (g, tq): positions 2tq, 2tq+1)
-        const int c0 = 8 * warp + 2 * tq;
-        const float s0 = c0 < n ? sc[0] * scale : -CUDART_INF_F;
-        const float s1 = c0 + 1 < n ? sc[1] * scale : -CUDART_INF_F;
-        float tmax = fmaxf(s0, s1);
+        // online softmax over the slab (lane (g, tq): positions 2tq, 2tq+1, 2tq+8, 2tq+9)
+        const int c0 = 16 * wg + 2 * tq;
+        const float x0 = c0 < n ? ((sa[0] + sb[0]) + (sa[2] + sb[2])) * scale : -CUDART_INF_F;
+        const float x1 = c0 + 1 < n ? ((sa[1] + sb[1]) + (sa[3] + sb[3])) * scale : -CUDART_INF_F;
+        const float x2 = c0 + 8 < n ? ((ta[0] + tb[0]) + (ta[2] + tb[2])) * scale : -CUDART_INF_F;
+        const float x3 = c0 + 9 < n ? ((ta[1] + tb[1]) + (ta[3] + tb[3])) * scale : -CUDART_INF_F;
+        float tmax = fmaxf(fmaxf(x0, x1), fmaxf(x2, x3));
         tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
         tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
         const float m_new = fmaxf(m_run, tmax);
         // branch-free: selects give the values of the empty case (every
         // score so far masked) without a branch around the exponentials
         const bool any = m_new != -CUDART_INF_F;
-        const float e0 = expf(s0 - m_new), e1 = expf(s1 - m_new), er = expf(m_run - m_new);
-        const float p0v = any ? e0 : 0.0f, p1v = any ? e1 : 0.0f, rescale = any ? er : 1.0f;
-        float psum = p0v + p1v;
+        const float e0 = expf(x0 - m_new), e1 = expf(x1 - m_new), e2 = expf(x2 - m_new), e3 = expf(x3 - m_new);
+        const float er = expf(m_run - m_new);
+        const float q0 = any ? e0 : 0.0f, q1 = any ? e1 : 0.0f, q2 = any ? e2 : 0.0f, q3 = any ? e3 : 0.0f;
+        const float rescale = any ? er : 1.0f;
+        float psum = (q0 + q1) + (q2 + q3);
         psum += __shfl_xor_sync(0xffffffffu, psum, 1);
         psum += __shfl_xor_sync(0xffffffffu, psum, 2);
         l_run = l_run * rescale + psum;
         m_run = m_new;
-        uint32_t pa_h, pa_l;
-        split2(p0v, p1v, pa_h, pa_l);
-        if (g >= G) pa_h = pa_l = 0u;
-        // O += P V over this warp's 8 positions, 128 dims in 16 column tiles
+        uint32_t ph0, pl0, ph1, pl1;
+        split2(q0, q1, ph0, pl0);
+        split2(q2, q3, ph1, pl1);
+        if (g >= G) ph0 = pl0 = ph1 = pl1 = 0u;
+        // O += P V over the slab's 16 positions, 128 dims in 16 chunks of 8
         const uint32_t vbase = smem_addr(vt);
 #pragma unroll
-        for (int j4 = 0; j4 < 16; j4 += 4) {
+        for (int c2 = 0; c2 < 16; c2 += 2) {
             uint32_t b0, b1, b2, b3;
-            ldsm_x4_t(vbase + tile_off(r_lane, j4 + (lane >> 3)), b0, b1, b2, b3);
-            const uint32_t bb[4] = {b0, b1, b2, b3};
+            ldsm_x4_t(vbase + tile_off(vr, c2 + (lane >> 4)), b0, b1, b2, b3);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                float c0f = o[j4 + q][0] * rescale, c1f = o[j4 + q][1] * rescale;
-                mma1688(c0f, c1f, pa_h, bb[q]);
-                mma1688(c0f, c1f, pa_l, bb[q]);
-                o[j4 + q][0] = c0f;
-                o[j4 + q][1] = c1f;
+                o[c2][q] *= rescale;
+                o[c2 + 1][q] *= rescale;
             }
+            mma16816_acc(o[c2], ph0, pl0, ph1, pl1, b0, b1);
+            mma16816_acc(o[c2 + 1], ph0, pl0, ph1, pl1, b2, b3);
         }
-        if (owner && prow >= 8 * warp && prow < 8 * warp + 8)
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes before the next TMA
+        if (mine) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes before the next TMA
         __syncwarp();
         // the slot is reused only when the ring wraps; then it is free once
-        // all eight warps are done with it
+        // the four warps of this group are done with it
         if (t + S < tiles) {
-            named_barrier(1, kComputeThreads);
-            if (tid == 0) mbar_arrive(&sm.empty[s]);
-            if (sm.abort[t & 1]) break;
+            named_barrier(gbar, kComputeThreads / 2);
+            if (wg == 0 && lane == 0) mbar_arrive(&sm.empty[s]);
+            if (sm.abort[flag]) break;
         }
     }
     named_barrier(1, kComputeThreads);
@@ -328,7 +343,7 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
     float* wm = reinterpret_cast<float*>(smem);            // [warps][G]
     float* wl = wm + kComputeWarps * G;                    // [warps][G]
     float* wo = wl + kComputeWarps * G;                    // [warps][G][D]
-    const bool aborted = sm.abort[0] | sm.abort[1];
+    const bool aborted = (sm.abort[0] | sm.abort[1] | sm.abort[2] | sm.abort[3]) != 0;
     if (!aborted) {
         if (g < G) {
             if (tq == 0) {
@@ -337,8 +352,8 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
             }
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-                wo[(warp * G + g) * D + 8 * j + 2 * tq] = o[j][0];
-                wo[(warp * G + g) * D + 8 * j + 2 * tq + 1] = o[j][1];
+                wo[(warp * G + g) * D + 8 * j + 2 * tq] = o[j][0] + o[j][2];
+                wo[(warp * G + g) * D + 8 * j + 2 * tq + 1] = o[j][1] + o[j][3];
             }
         }
     }
@@ -383,39 +398,54 @@ __global__ void __launch_bounds__(kComputeThreads + 32, 1)
     }
     __threadfence();
     if (tid == 0) trace_at(trace, a.trace_tag, 3);  // the merging CTA: last arrival seen
-    // The merge is on the critical path of the step: the o partials of the
-    // first kBatch splits are loaded in the same round trip as every
-    // split's (m, l) (into shared memory; the stage buffers are free).
+    // The merge is on the critical path of the step. Lane u of each warp
+    // takes splits u, u + 32, ...: the head's maximum and the splits'
+    // weights are found across lanes (one exponential per lane, sums in a
+    // fixed shuffle order), and the o partials of 32 splits at a time are
+    // loaded in the same round trip as every split's (m, l).
     constexpr int kBatch = kMergeBatch;
     const float2* po = reinterpret_cast<const float2*>(partial_o + ((size_t)kvh * splits * G + hq) * D + d0);
     float2 v[kBatch];
 #pragma unroll
     for (int u = 0; u < kBatch; ++u)
         v[u] = u < splits ? __ldcg(po + (size_t)u * (G * D / 2)) : make_float2(0.0f, 0.0f);
-    float* mls = reinterpret_cast<float*>(smem);  // [splits][G][2]
-    const float* ml_head = partial_ml + (size_t)kvh * splits * G * 2;
-    for (int i = tid; i < splits * G * 2; i += kComputeThreads) mls[i] = __ldcg(ml_head + i);
-    named_barrier(1, kComputeThreads);
-    if (tid == 0) trace_at(trace, a.trace_tag, 5);
+    const float* mlh = partial_ml + ((size_t)kvh * splits * G + hq) * 2;  // split sp at mlh + sp * G * 2
+    float my_m = -CUDART_INF_F, my_l = 0.0f;  // split `lane`
     float MM = -CUDART_INF_F;
-    for (int sp = 0; sp < splits; ++sp)
-        MM = fmaxf(MM, mls[(sp * G + hq) * 2 + 1] > 0.0f ? mls[(sp * G + hq) * 2] : -CUDART_INF_F);
+    for (int sp = lane; sp < splits; sp += 32) {
+        const float2 ml = __ldcg(reinterpret_cast<const float2*>(mlh + (size_t)sp * G * 2));
+        if (sp == lane) {
+            my_m = ml.x;
+            my_l = ml.y;
+        }
+        MM = fmaxf(MM, ml.y > 0.0f ? ml.x : -CUDART_INF_F);
+    }
+    MM = warp_max(MM);
+    if (tid == 0) trace_at(trace, a.trace_tag, 5);
     float LL = 0.0f, o0 = 0.0f, o1 = 0.0f;
     for (int sp0 = 0; sp0 < splits; sp0 += kBatch) {
+        float m = my_m, l = my_l;
         if (sp0 > 0) {
+            m = -CUDART_INF_F;
+            l = 0.0f;
+            if (sp0 + lane < splits) {
+                const float2 ml = __ldcg(reinterpret_cast<const float2*>(mlh + (size_t)(sp0 + lane) * G * 2));
+                m = ml.x;
+                l = ml.y;
+            }
 #pragma unroll
             for (int u = 0; u < kBatch; ++u)
                 v[u] = sp0 + u < splits ? __ldcg(po + (size_t)(sp0 + u) * (G * D / 2)) : make_float2(0.0f, 0.0f);
         }
-        // branch-free, as above: all exponentials of the batch in flight
+        const bool live = sp0 + lane < splits && l > 0.0f;
+        const float f = live ? expf(m - MM) : 0.0f;
+        LL += warp_sum(live ? l * f : 0.0f);
+        // a dead split's weight is 0 and its partial 0: adding nothing
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
-            const float l = mls[((sp0 + u) * G + hq) * 2 + 1];
-            const bool live = sp0 + u < splits && l > 0.0f;
-            const float f = expf(mls[((sp0 + u) * G + hq) * 2] - MM);
-            LL = live ? LL + l * f : LL;
-            o0 = live ? o0 + v[u].x * f : o0;
-            o1 = live ? o1 + v[u].y * f : o1;
+            const float fu = __shfl_sync(0xffffffffu, f, u);
+            o0 += v[u].x * fu;
+            o1 += v[u].y * fu;
         }
     }
     float* out = a.out + (size_t)z * a.heads * D + ((size_t)kvh * G + hq) * D;
@@ -526,13 +556,13 @@ cudaError_t decode_attention(const DecodeAttnArgs& in, const KvTensorMap& kmap, 
     a.ld_qkv = in.ld_qkv;
     a.seq_cache_elems = in.seq_cache_elems;
     if (in.batch < 1 || (in.batch > 1 && (a.out_image.base || in.ld_qkv <= 0))) return cudaErrorInvalidValue;
-    a.stages = 3;
+    a.stages = kStages;
     const size_t smem = smem_bytes(a.stages);
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
     std::call_once(once, [] {
         attr = cudaFuncSetAttribute(decode_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)smem_bytes(3));
+                                    (int)smem_bytes(kStages));
     });
     if (attr != cudaSuccess) return attr;
     CUtensorMap km, vm;

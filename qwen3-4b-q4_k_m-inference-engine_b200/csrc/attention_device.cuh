@@ -60,6 +60,27 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a2
         : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
+// m16n8k16 with A rows 0-7 = (q or p) hi parts and rows 8-15 = lo parts:
+// f = (a0 hi, a1 lo, a2 hi, a3 lo) of lane (g, t) as the fragments of rows g
+// and g + 8.
+__device__ __forceinline__ void mma16816_hilo(float (&c)[4], uint4 f, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(f.x), "r"(f.y), "r"(f.z), "r"(f.w), "r"(b0), "r"(b1));
+}
+
+// m16n8k16 with all four A fragments given.
+__device__ __forceinline__ void mma16816_acc(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 __device__ __forceinline__ void mma1688(float& c0, float& c1, uint32_t a0, uint32_t b0) {
     float c2 = 0.0f, c3 = 0.0f;  // rows 8..15: zero A rows, results unused
     asm volatile(

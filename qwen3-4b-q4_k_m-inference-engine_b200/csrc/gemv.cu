@@ -76,6 +76,7 @@ struct GemvPlan {
     L2Prefetch prefetch[kMaxPrefetch];  // the next kernel's operands, after this CTA's first S stages
     ActImage in_image;   // copy this quantised activation instead of quantising x (M == 1)
     ActImage out_image;  // SwiGLU: quantise this CTA's output rows into it (M == 1)
+    int inflight;        // stages the producer keeps in flight (issued, not landed); 0: the whole ring
     int group_stages;    // stages per 32-row group: CTA shares start on group boundaries (out_image)
     int off_ostage;      // this CTA's output rows (out_image)
     PeerOut peer_out;    // EPI_PEER
@@ -236,6 +237,13 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
                 const int slot = i % S, use = i / S;
                 uint64_t* fb = full + slot;
                 if (use > 0 && !mbar_wait_bounded(empty + slot, (use - 1) & 1, p.err, ERR_WAIT_TIMEOUT_EMPTY)) break;
+                // bounded queue: stage i is issued once stage i - inflight has
+                // landed (its slot is not re-armed before stage i is issued,
+                // so the parity names that stage's phase)
+                if (p.inflight > 0 && i >= p.inflight) {
+                    const int j = i - p.inflight;
+                    if (!mbar_wait_bounded(full + j % S, (j / S) & 1, p.err, ERR_WAIT_TIMEOUT_FULL)) break;
+                }
                 int seg, r0, nr;
                 stage_rows(p, st, seg, r0, nr);
                 const int rb = p.row_bytes[seg];
@@ -684,6 +692,8 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     S -= S % teams;
     if (off + S * stage_bytes + 2 * S * 8 > 220 * 1024) return cudaErrorInvalidValue;
     p.lpr = lpr;
+    p.inflight = std::max(0, env_int("Q4K_GEMV_INFLIGHT", 0));
+    if (p.inflight >= S) p.inflight = 0;
     p.mma = mma ? 1 : 0;
     p.rows_per_stage = R;
     p.stage_bytes = stage_bytes;

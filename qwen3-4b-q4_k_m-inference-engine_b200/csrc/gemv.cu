@@ -77,6 +77,8 @@ struct GemvPlan {
     ActImage in_image;   // copy this quantised activation instead of quantising x (M == 1)
     ActImage out_image;  // SwiGLU: quantise this CTA's output rows into it (M == 1)
     int inflight;        // stages the producer keeps in flight (issued, not landed); 0: the whole ring
+    int prefetch_landed; // issue the L2 prefetch once the first ring of stages has landed
+    int off_xbuf;        // >= 0: the batch-of-one activation comes in by one bulk copy into shared memory
     int group_stages;    // stages per 32-row group: CTA shares start on group boundaries (out_image)
     int off_ostage;      // this CTA's output rows (out_image)
     PeerOut peer_out;    // EPI_PEER
@@ -98,12 +100,14 @@ __device__ __forceinline__ void quantise_activation(const GemvPlan& p, int m0, i
     // tensor parallelism: every rank's partial sums of this step, read until
     // each word carries this step's tag
     const unsigned tag = pin.world > 0 ? (unsigned)(*pin.epoch + 1) : 0u;
-    quantise_rows<kHeldVec4>(p.x, p.ldx, m0, mcount, gamma, p.eps, p.K, p.off_xq4 >= 0 ? smem + p.off_xq4 : nullptr,
+    const bool x_shared = p.off_xbuf >= 0;
+    const float* x = x_shared ? reinterpret_cast<const float*>(smem + p.off_xbuf) : p.x;
+    quantise_rows<kHeldVec4>(x, x_shared ? p.K : p.ldx, x_shared ? 0 : m0, mcount, gamma, p.eps, p.K, p.off_xq4 >= 0 ? smem + p.off_xq4 : nullptr,
                   p.off_xq6 >= 0 ? smem + p.off_xq6 : nullptr, reinterpret_cast<float*>(smem + p.off_xs),
                   reinterpret_cast<int*>(smem + p.off_xsum16), reinterpret_cast<float*>(smem + p.off_xsum32),
                   reinterpret_cast<float*>(smem + p.off_misc), tid, lane, warp, nthreads, kAllConsumersBarrier,
                   p.trace, p.trace_tag, pin.world > 0 ? pin.parts : nullptr, pin.world, tag, p.err, pin.wait_ns,
-                  ERR_WAIT_TIMEOUT_PEER, pin.world >= 0 && blockIdx.x == 0 ? pin.x_out : nullptr);
+                  ERR_WAIT_TIMEOUT_PEER, pin.world >= 0 && blockIdx.x == 0 ? pin.x_out : nullptr, x_shared);
 }
 
 // Batch of one whose activation the preceding kernel already quantised:
@@ -224,6 +228,7 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
             mbar_init(empty + i, MMA ? 1 : kTeamWarps);
         }
         for (int k = 0; k < 4; ++k) team_abort[k] = 0;
+        if (p.off_xbuf >= 0) mbar_init(full + 2 * S, 1);
         mbar_fence_init();
     }
     __syncthreads();
@@ -257,8 +262,13 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
                     bulk_g2s_hint(dst, p.seg[seg].w + (size_t)r0 * rb, nr * rb, fb, policy);
                 }
                 // the ring is full (or this CTA's stages are all issued):
-                // let HBM go on with the next kernel's operands
-                if ((i == S - 1 || st == s_end - 1) && blockIdx.y == 0) issue_l2_prefetch(p.prefetch, blockIdx.x, G);
+                // let HBM go on with the next kernel's operands, either at
+                // once or once those stages have landed (prefetch_landed), so
+                // that the prefetch does not share HBM with this CTA's own ring
+                if ((i == S - 1 || st == s_end - 1) && blockIdx.y == 0) {
+                    if (p.prefetch_landed && !mbar_wait_bounded(fb, use & 1, p.err, ERR_WAIT_TIMEOUT_FULL)) break;
+                    issue_l2_prefetch(p.prefetch, blockIdx.x, G);
+                }
             }
         }
         return;
@@ -274,6 +284,16 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     pdl_wait();
     if (tid == 0) trace_at(p.trace, p.trace_tag, 1);
     const int nthreads = W * 32;
+    if (p.off_xbuf >= 0) {
+        // one bulk copy of the activation row (written by the preceding
+        // kernel, complete once the dependency wait has returned)
+        uint64_t* xbar = full + 2 * S;
+        if (tid == 0) {
+            mbar_arrive_expect_tx(xbar, (uint32_t)K * 4u);
+            bulk_g2s(smem + p.off_xbuf, p.x + (size_t)m0 * p.ldx, (uint32_t)K * 4u, xbar);
+        }
+        if (!mbar_wait_bounded(xbar, 0, p.err, ERR_WAIT_TIMEOUT_FULL)) team_abort[0] = 1;
+    }
     if (p.in_image.base)
         copy_image(p, smem, tid, nthreads);
     else
@@ -636,6 +656,12 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     p.off_mred = off;
     off += 4 * 2 * kTeamWarps * 16 * 4;  // [team][2][warp][16 rows] partials of tensor-core stages
     off = align_up(off, 128);
+    p.off_xbuf = -1;
+    if (rq.M == 1 && !rq.in_image.base && rq.peer_in.world <= 0 && reinterpret_cast<uintptr_t>(rq.x) % 16 == 0 &&
+        env_int("Q4K_X_BULK", 0) != 0) {
+        p.off_xbuf = off;
+        off += align_up(rq.K * 4, 128);
+    }
 
     // Lanes per row: about five 64-value chunks per lane per stage.
     const int chunks = p.nb * 4;
@@ -690,9 +716,10 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     // every ring slot belongs to one team: teams <= S and S a multiple of it
     const int teams = std::min(W / kTeamWarps, S);
     S -= S % teams;
-    if (off + S * stage_bytes + 2 * S * 8 > 220 * 1024) return cudaErrorInvalidValue;
+    if (off + S * stage_bytes + (2 * S + 1) * 8 > 220 * 1024) return cudaErrorInvalidValue;
     p.lpr = lpr;
     p.inflight = std::max(0, env_int("Q4K_GEMV_INFLIGHT", 0));
+    p.prefetch_landed = env_int("Q4K_PREFETCH_LANDED", 0) != 0;
     if (p.inflight >= S) p.inflight = 0;
     p.mma = mma ? 1 : 0;
     p.rows_per_stage = R;
@@ -702,7 +729,7 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     p.off_bufs = off;
     off += S * stage_bytes;
     p.off_bars = off;
-    off += 2 * S * 8;
+    off += (2 * S + 1) * 8;  // full, empty, and the activation copy's barrier
     const size_t smem = (size_t)off;
     const dim3 grid(ctas, (rq.M + MT - 1) / MT), block((W + 1) * 32);
 

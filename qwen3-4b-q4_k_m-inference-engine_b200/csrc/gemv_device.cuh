@@ -229,32 +229,53 @@ __device__ __forceinline__ void q6_quarter(const uint8_t* const (&rows)[NR], int
     }
 }
 
-__device__ __forceinline__ int8_t q8_code(float v, float amax) {
-    // matmul.cu:19: roundf((value / maximum) * 127), IEEE division.
-    return amax == 0.0f ? 0 : static_cast<int8_t>(roundf(__fmul_rn(__fdiv_rn(v, amax), 127.0f)));
+// 1/a for a positive finite float a, as a double with relative error below
+// 2^-51: the hardware's approximate double reciprocal refined by two
+// Newton-Raphson steps r <- r + r (1 - a r) (each roughly squares the
+// relative error, down to the double rounding). Every float, normal or
+// subnormal, is a normal double, so no range needs special handling.
+__device__ __forceinline__ double recip_refined(float a) {
+    const double ad = (double)a;
+    double r;
+    asm("rcp.approx.ftz.f64 %0, %1;" : "=d"(r) : "d"(ad));
+    r = fma(r, fma(-ad, r, 1.0), r);
+    r = fma(r, fma(-ad, r, 1.0), r);
+    return r;
 }
 
-// The same code, bit for bit, without a division per value and without a
-// branch (so that the codes of many values are computed side by side).
-// c127 is 127 / amax from __fdividef (at most 2 ulp, i.e. 4 * 2^-24
-// relative, off for amax in [2^-126, 2^126]: see q8_fast_ok), so
-// q = v * c127 is within 5 * 2^-24 (relative) of the true 127 v / amax, and
-// the reference's fl(fl(v / amax) * 127) within 2 * 2^-24: as |q| <= 127 the
-// two differ by less than 7 * 2^-24 * 127 < 6e-5. When q is more than 2e-4
-// from a rounding boundary k + 0.5, both round to the same integer, and
-// there round-to-nearest-even (rintf) equals roundf. Closer to a boundary
-// (or for NaN) `near` is set and the caller takes q8_code_exact instead.
-__device__ __forceinline__ int8_t q8_code_rn(float v, float c127, bool& near) {
-    const float q = v * c127;
-    const float r = rintf(q);
-    near = !(fabsf(fabsf(q - r) - 0.5f) > 2e-4f);
-    return static_cast<int8_t>(static_cast<int>(r));
+// The reference's code roundf(fl(fl(v / amax) * 127)) (matmul.cu:19) bit
+// for bit, without a division or a branch, given ra = recip_refined(amax)
+// for a positive finite amax (and |v| <= amax).
+// Why fl(v / amax) = fl32(v * ra): write v = V 2^i, amax = A 2^j (V, A
+// integers below 2^24) and a float32 rounding boundary (midpoint) as
+// M = N 2^k with N odd, 2^24 <= N < 2^25. The quotient v / amax is never
+// exactly M (V = A N 2^(j+k-i) would need a factor N >= 2^24 in V), and
+// when it is not, |v - amax M| >= min(2^i, 2^(j+k)), i.e. the quotient is at
+// least 2^-50 (relative) from every midpoint in the normal range. v * ra is
+// within 2^-51 * 1.5 of it, so both round to the same float. Quotients
+// below 2^-126 give codes of 0 either way (127 t < 0.5). The product with
+// 127 and the rounding (halves away from zero, as roundf) then follow the
+// reference exactly: u - trunc(u) is exact.
+__device__ __forceinline__ int8_t q8_code_r(float v, double ra) {
+    const float t = __double2float_rn(__dmul_rn((double)v, ra));
+    const float u = __fmul_rn(t, 127.0f);
+    const float tr = truncf(u);
+    const float c = fabsf(u - tr) >= 0.5f ? tr + copysignf(1.0f, u) : tr;
+    return static_cast<int8_t>(static_cast<int>(c));
 }
-// Out of line: rarely taken.
-static __device__ __noinline__ int8_t q8_code_exact(float v, float amax) { return q8_code(v, amax); }
 
-// Whether the fast path's error bound holds for this group maximum.
-__device__ __forceinline__ bool q8_fast_ok(float amax) { return amax >= 1.2e-38f && amax <= 8.0e37f; }
+// Whether q8_code_r applies (amax positive and finite); otherwise every code
+// of the group is 0, as the reference's for a zero maximum.
+__device__ __forceinline__ bool q8_codes_defined(float amax) { return amax > 0.0f && amax <= 3.402823466e38f; }
+
+// The group scale fl(amax / 127) (matmul.cu:18), bit for bit, without a
+// division: amax * fl64(1/127) is within 2^-52 (relative) of amax / 127,
+// which is never a float32 midpoint (127 is odd) and, as above, at least
+// 2^-50 from one, subnormal results included (their grid is coarser).
+// Infinities and NaNs pass through as amax / 127 would.
+__device__ __forceinline__ float q8_scale(float amax) {
+    return __double2float_rn(__dmul_rn((double)amax, 1.0 / 127.0));
+}
 
 // Quantise MT activation rows into shared memory: codes (in the Q4_K and/or
 // Q6_K permuted order), one fp32 scale per 32 values, code sums per 16 and
@@ -269,16 +290,10 @@ __device__ __forceinline__ void quantise_vec4(float4 v, int e, int K, int m, uin
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-    const float c127 = __fdividef(127.0f, amax);
-    bool n0, n1, n2, n3;
-    int8_t c0 = q8_code_rn(v.x, c127, n0), c1 = q8_code_rn(v.y, c127, n1);
-    int8_t c2 = q8_code_rn(v.z, c127, n2), c3 = q8_code_rn(v.w, c127, n3);
-    if (!q8_fast_ok(amax) || n0 || n1 || n2 || n3) {  // rare: the exact form decides all four
-        c0 = q8_code_exact(v.x, amax);
-        c1 = q8_code_exact(v.y, amax);
-        c2 = q8_code_exact(v.z, amax);
-        c3 = q8_code_exact(v.w, amax);
-    }
+    const bool defined = q8_codes_defined(amax);
+    const double ra = recip_refined(defined ? amax : 1.0f);
+    const int8_t c0 = defined ? q8_code_r(v.x, ra) : 0, c1 = defined ? q8_code_r(v.y, ra) : 0;
+    const int8_t c2 = defined ? q8_code_r(v.z, ra) : 0, c3 = defined ? q8_code_r(v.w, ra) : 0;
     const uint32_t word = (uint32_t)(uint8_t)c0 | ((uint32_t)(uint8_t)c1 << 8) |
                           ((uint32_t)(uint8_t)c2 << 16) | ((uint32_t)(uint8_t)c3 << 24);
     int run = (int)c0 + (int)c1 + (int)c2 + (int)c3;
@@ -294,7 +309,7 @@ __device__ __forceinline__ void quantise_vec4(float4 v, int e, int K, int m, uin
         xsum16[m * (K / 16) + b * 16 + 4 * (2 * (r16 >> 3) + (r16 & 1)) + ((r16 >> 1) & 3)] = 32 * run;
     if ((lane & 7) == 0) {
         xsum32[m * (K / 32) + (e >> 5)] = (float)group;
-        xs[m * (K / 32) + (e >> 5)] = amax / 127.0f;  // matmul.cu:18
+        xs[m * (K / 32) + (e >> 5)] = q8_scale(amax);  // matmul.cu:18
     }
 }
 
@@ -307,13 +322,9 @@ __device__ __forceinline__ void quantise_pair(float v0, float v1, int e, int K, 
     float amax = fmaxf(fabsf(v0), fabsf(v1));
 #pragma unroll
     for (int o = 1; o < 16; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float c127 = __fdividef(127.0f, amax);
-    bool n0, n1;
-    int8_t c0 = q8_code_rn(v0, c127, n0), c1 = q8_code_rn(v1, c127, n1);
-    if (!q8_fast_ok(amax) || n0 || n1) {  // rare
-        c0 = q8_code_exact(v0, amax);
-        c1 = q8_code_exact(v1, amax);
-    }
+    const bool defined = q8_codes_defined(amax);
+    const double ra = recip_refined(defined ? amax : 1.0f);
+    const int8_t c0 = defined ? q8_code_r(v0, ra) : 0, c1 = defined ? q8_code_r(v1, ra) : 0;
     int run = (int)c0 + (int)c1;
     run += __shfl_xor_sync(0xffffffffu, run, 1);
     run += __shfl_xor_sync(0xffffffffu, run, 2);
@@ -327,7 +338,7 @@ __device__ __forceinline__ void quantise_pair(float v0, float v1, int e, int K, 
         xsum16[b * 16 + 4 * (2 * (r16 >> 3) + (r16 & 1)) + ((r16 >> 1) & 3)] = 32 * run;
     if ((lane & 15) == 0) {
         xsum32[e >> 5] = (float)group;
-        xs[e >> 5] = amax / 127.0f;  // matmul.cu:18
+        xs[e >> 5] = q8_scale(amax);  // matmul.cu:18
     }
 }
 
@@ -356,7 +367,8 @@ __device__ __forceinline__ void quantise_rows(const float* x, int ldx, int m0, i
                                               int barrier_id, unsigned long long* trace = nullptr,
                                               int trace_tag = 0, const unsigned long long* parts = nullptr,
                                               int nparts = 0, unsigned parts_tag = 0, int* err = nullptr,
-                                              uint64_t wait_ns = 0, int err_code = 0, float* x_out = nullptr) {
+                                              uint64_t wait_ns = 0, int err_code = 0, float* x_out = nullptr,
+                                              bool x_shared = false) {
     const int nvec = K / 4;
     // kHeld: float4s of the row a thread keeps in registers (K <= kHeld * 4 * nthreads)
     for (int m = 0; m < mcount; ++m) {
@@ -366,7 +378,8 @@ __device__ __forceinline__ void quantise_rows(const float* x, int ldx, int m0, i
 #pragma unroll
         for (int k = 0; k < kHeld; ++k) {
             const int i = tid + k * nthreads;
-            if (i < nvec) held[k] = __ldcg(xr + i);  // may have been written by other SMs in this launch
+            // global rows may have been written by other SMs in this launch
+            if (i < nvec) held[k] = x_shared ? xr[i] : __ldcg(xr + i);
         }
         if (parts && m == 0) {
             // tensor parallelism: x + the ranks' partial sums (rank order), the
@@ -417,6 +430,7 @@ __device__ __forceinline__ void quantise_rows(const float* x, int ldx, int m0, i
             ss = warp_sum(ss);
             if (lane == 0) red[warp] = ss;
             named_barrier(barrier_id, nthreads);
+            if (trace && tid == 0 && m == 0) trace_at(trace, trace_tag, 6);  // PROBE
             float total = 0.0f;
             for (int i = 0; i < nthreads / 32; ++i) total += red[i];
             inv = rsqrtf(total / (float)K + eps);  // rms_norm.cu:17

@@ -800,14 +800,13 @@ __global__ void __launch_bounds__(256) prefill_quantise_kernel(const float* x, i
     __syncthreads();
     float rmax = 0.0f;
     for (int i = 0; i < 8; ++i) rmax = fmaxf(rmax, red[i]);
-    const float S = rmax / 127.0f;  // the largest group scale (matmul.cu:18)
+    const float S = gemv_dev::q8_scale(rmax);  // the largest group scale (matmul.cu:18)
 #pragma unroll
     for (int i = 0; i < kSteps; ++i) {
         if (i >= steps) break;
-        bool near;
-        int8_t code = gemv_dev::q8_code_rn(v[i], __fdividef(127.0f, am[i]), near);
-        if (!gemv_dev::q8_fast_ok(am[i]) || near) code = gemv_dev::q8_code_exact(v[i], am[i]);
-        const float r = S > 0.0f ? __fdiv_rn(am[i] / 127.0f, S) : 0.0f;
+        const bool defined = gemv_dev::q8_codes_defined(am[i]);
+        const int8_t code = defined ? gemv_dev::q8_code_r(v[i], gemv_dev::recip_refined(am[i])) : 0;
+        const float r = S > 0.0f ? __fdiv_rn(gemv_dev::q8_scale(am[i]), S) : 0.0f;
         const float val = (float)code * r;
         const __half hi = __float2half_rn(val);
         const size_t at = (size_t)m * K + 256 * i + tid;

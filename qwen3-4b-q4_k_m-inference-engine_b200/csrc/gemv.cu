@@ -79,6 +79,8 @@ struct GemvPlan {
     int inflight;        // stages the producer keeps in flight (issued, not landed); 0: the whole ring
     int prefetch_landed; // issue the L2 prefetch once the first ring of stages has landed
     int off_xbuf;        // >= 0: the batch-of-one activation comes in by one bulk copy into shared memory
+    int off_resid;       // >= 0 (EPI_ADD, one segment, image input): this CTA's residual rows, fetched
+                         // with the image so that the epilogue adds from shared memory
     int group_stages;    // stages per 32-row group: CTA shares start on group boundaries (out_image)
     int off_ostage;      // this CTA's output rows (out_image)
     PeerOut peer_out;    // EPI_PEER
@@ -113,7 +115,8 @@ __device__ __forceinline__ void quantise_activation(const GemvPlan& p, int m0, i
 // Batch of one whose activation the preceding kernel already quantised:
 // copy the image's parts this product uses into shared memory, all loads
 // of a thread in flight at once (16-byte units; at most 4 per thread).
-__device__ __forceinline__ void copy_image(const GemvPlan& p, uint8_t* smem, int tid, int nthreads) {
+__device__ __forceinline__ void copy_image(const GemvPlan& p, uint8_t* smem, int tid, int nthreads, int resid_row0,
+                                           int resid_rows) {
     const int K = p.K;
     const ImageParts src = image_parts(p.in_image.base, K);
     const int n4 = p.off_xq4 >= 0 ? K / 16 : 0, n6 = p.off_xq6 >= 0 ? K / 16 : 0;
@@ -158,6 +161,10 @@ __device__ __forceinline__ void copy_image(const GemvPlan& p, uint8_t* smem, int
             v[k] = __ldcg(from);  // written by the preceding kernel
         }
     }
+    // the residual rows this CTA adds to, in the same round trip
+    float rv = 0.0f;
+    const bool resid = p.off_resid >= 0 && tid < resid_rows;
+    if (resid) rv = __ldcg(p.seg[0].y + resid_row0 + tid);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int u = tid + k * nthreads;
@@ -168,6 +175,7 @@ __device__ __forceinline__ void copy_image(const GemvPlan& p, uint8_t* smem, int
             *to = v[k];
         }
     }
+    if (resid) reinterpret_cast<float*>(smem + p.off_resid)[tid] = rv;
     named_barrier(kAllConsumersBarrier, nthreads);
 }
 
@@ -294,8 +302,10 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
         }
         if (!mbar_wait_bounded(xbar, 0, p.err, ERR_WAIT_TIMEOUT_FULL)) team_abort[0] = 1;
     }
+    const int resid_row0 = s_begin * p.rows_per_stage;
+    const int resid_rows = p.off_resid >= 0 ? min(s_end * p.rows_per_stage, p.seg[0].rows) - resid_row0 : 0;
     if (p.in_image.base)
-        copy_image(p, smem, tid, nthreads);
+        copy_image(p, smem, tid, nthreads, resid_row0, resid_rows);
     else
         quantise_activation(p, m0, mcount, smem, tid, lane, warp, nthreads);
     if (tid == 0) trace_at(p.trace, p.trace_tag, 2);
@@ -422,7 +432,10 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
                 if (p.epilogue == EPI_STORE) {
                     *out = acc[0][m];
                 } else if (p.epilogue == EPI_ADD) {
-                    *out += acc[0][m];
+                    if (p.off_resid >= 0)
+                        *out = reinterpret_cast<const float*>(smem + p.off_resid)[row - resid_row0] + acc[0][m];
+                    else
+                        *out += acc[0][m];
                 } else if (p.epilogue == EPI_PEER) {
                     // this rank's partial sum of row `row` with this step's tag, one
                     // 8-byte word into every rank's receive slot
@@ -709,6 +722,15 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
         const int max_rows = p.group_stages * ((units + ctas - 1) / ctas) * R;
         p.off_ostage = off;
         off += align_up(max_rows * 4, 128);
+    }
+    p.off_resid = -1;
+    if (rq.epilogue == EPI_ADD && rq.M == 1 && p.nseg == 1 && p.in_image.base && p.group_stages == 1 &&
+        env_int("Q4K_RESID_PREFETCH", 1) != 0) {
+        const int max_rows = ((stages + ctas - 1) / ctas) * R;
+        if (max_rows <= W * 32) {  // one row per consumer thread
+            p.off_resid = off;
+            off += align_up(max_rows * 4, 128);
+        }
     }
     const int budget = std::max(env_int("Q4K_GEMV_SMEM_KB", 200) * 1024 - off, stage_bytes);
     int S = std::min(budget / stage_bytes, 8);

@@ -36,6 +36,7 @@
 #include <algorithm>
 #include <cstdlib>
 #include <mutex>
+#include <type_traits>
 
 #include "q4k_device.cuh"
 #include "q4k_internal.h"
@@ -78,7 +79,6 @@ struct GemvPlan {
     ActImage out_image;  // SwiGLU: quantise this CTA's output rows into it (M == 1)
     int inflight;        // stages the producer keeps in flight (issued, not landed); 0: the whole ring
     int prefetch_landed; // issue the L2 prefetch once the first ring of stages has landed
-    int off_xbuf;        // >= 0: the batch-of-one activation comes in by one bulk copy into shared memory
     int off_resid;       // >= 0 (EPI_ADD, one segment, image input): this CTA's residual rows, fetched
                          // with the image so that the epilogue adds from shared memory
     int group_stages;    // stages per 32-row group: CTA shares start on group boundaries (out_image)
@@ -95,6 +95,7 @@ __device__ __forceinline__ void stage_rows(const GemvPlan& p, int i, int& seg, i
     nr = min(p.rows_per_stage, p.seg[seg].rows - r0);
 }
 
+template <int HELD>
 __device__ __forceinline__ void quantise_activation(const GemvPlan& p, int m0, int mcount, uint8_t* smem, int tid,
                                                     int lane, int warp, int nthreads) {
     const float* gamma = p.gamma ? reinterpret_cast<const float*>(smem + p.off_gamma) : nullptr;
@@ -102,14 +103,12 @@ __device__ __forceinline__ void quantise_activation(const GemvPlan& p, int m0, i
     // tensor parallelism: every rank's partial sums of this step, read until
     // each word carries this step's tag
     const unsigned tag = pin.world > 0 ? (unsigned)(*pin.epoch + 1) : 0u;
-    const bool x_shared = p.off_xbuf >= 0;
-    const float* x = x_shared ? reinterpret_cast<const float*>(smem + p.off_xbuf) : p.x;
-    quantise_rows<kHeldVec4>(x, x_shared ? p.K : p.ldx, x_shared ? 0 : m0, mcount, gamma, p.eps, p.K, p.off_xq4 >= 0 ? smem + p.off_xq4 : nullptr,
+    quantise_rows<HELD>(p.x, p.ldx, m0, mcount, gamma, p.eps, p.K, p.off_xq4 >= 0 ? smem + p.off_xq4 : nullptr,
                   p.off_xq6 >= 0 ? smem + p.off_xq6 : nullptr, reinterpret_cast<float*>(smem + p.off_xs),
                   reinterpret_cast<int*>(smem + p.off_xsum16), reinterpret_cast<float*>(smem + p.off_xsum32),
                   reinterpret_cast<float*>(smem + p.off_misc), tid, lane, warp, nthreads, kAllConsumersBarrier,
                   p.trace, p.trace_tag, pin.world > 0 ? pin.parts : nullptr, pin.world, tag, p.err, pin.wait_ns,
-                  ERR_WAIT_TIMEOUT_PEER, pin.world >= 0 && blockIdx.x == 0 ? pin.x_out : nullptr, x_shared);
+                  ERR_WAIT_TIMEOUT_PEER, pin.world >= 0 && blockIdx.x == 0 ? pin.x_out : nullptr);
 }
 
 // Batch of one whose activation the preceding kernel already quantised:
@@ -202,7 +201,12 @@ __device__ __forceinline__ void quantise_output_groups(const GemvPlan& p, int lo
 
 // MMA: the tensor-core stage path is compiled in (a separate instance, so
 // that the default instances keep their registers for the dp4a loop).
-template <int MT, int NR, bool MMA>
+// TYPES: the weight types the instance handles (1: Q4_K, 2: Q6_K, 3: both).
+// HELD: activation float4s a consumer thread holds while quantising (0: the
+// input is an already quantised image, copied). Each launch runs its code
+// cold, so an instance compiles in only the paths it takes: instruction
+// fetch, not arithmetic, was the leading stall of the decode products.
+template <int MT, int NR, bool MMA, int TYPES, int HELD>
 __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant__ GemvPlan p) {
     static_assert(!MMA || MT == 1, "tensor-core stages take a batch of one");
     constexpr bool PAIR = NR == 2;  // gate and up rows worked together (SwiGLU)
@@ -236,7 +240,6 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
             mbar_init(empty + i, MMA ? 1 : kTeamWarps);
         }
         for (int k = 0; k < 4; ++k) team_abort[k] = 0;
-        if (p.off_xbuf >= 0) mbar_init(full + 2 * S, 1);
         mbar_fence_init();
     }
     __syncthreads();
@@ -292,22 +295,12 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     pdl_wait();
     if (tid == 0) trace_at(p.trace, p.trace_tag, 1);
     const int nthreads = W * 32;
-    if (p.off_xbuf >= 0) {
-        // one bulk copy of the activation row (written by the preceding
-        // kernel, complete once the dependency wait has returned)
-        uint64_t* xbar = full + 2 * S;
-        if (tid == 0) {
-            mbar_arrive_expect_tx(xbar, (uint32_t)K * 4u);
-            bulk_g2s(smem + p.off_xbuf, p.x + (size_t)m0 * p.ldx, (uint32_t)K * 4u, xbar);
-        }
-        if (!mbar_wait_bounded(xbar, 0, p.err, ERR_WAIT_TIMEOUT_FULL)) team_abort[0] = 1;
-    }
     const int resid_row0 = s_begin * p.rows_per_stage;
     const int resid_rows = p.off_resid >= 0 ? min(s_end * p.rows_per_stage, p.seg[0].rows) - resid_row0 : 0;
-    if (p.in_image.base)
+    if constexpr (HELD == 0)
         copy_image(p, smem, tid, nthreads, resid_row0, resid_rows);
     else
-        quantise_activation(p, m0, mcount, smem, tid, lane, warp, nthreads);
+        quantise_activation<HELD>(p, m0, mcount, smem, tid, lane, warp, nthreads);
     if (tid == 0) trace_at(p.trace, p.trace_tag, 2);
     const uint8_t* xq4 = p.off_xq4 >= 0 ? smem + p.off_xq4 : nullptr;
     const uint8_t* xq6 = p.off_xq6 >= 0 ? smem + p.off_xq6 : nullptr;
@@ -351,7 +344,7 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
             for (int m = 0; m < MT; ++m) acc[r][m] = 0.0f;
         // tensor-core stages: 16 rows (8 gate + 8 up rows for SwiGLU), the
         // team's 4 warps take every 4th super-block
-        const bool mma = MMA && p.seg[seg].type == Q4K_TYPE_Q4_K;
+        const bool mma = MMA && (TYPES & 1) != 0 && p.seg[seg].type == Q4K_TYPE_Q4_K;
         const int par = (i / T) & 1;  // double buffer of the cross-warp partials
         float* mred = reinterpret_cast<float*>(smem + p.off_mred) + (team * 2 + par) * kTeamWarps * 16;
         if (mma) {
@@ -369,20 +362,25 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
                 mred[wt * 16 + gq] = ag;
                 mred[wt * 16 + gq + 8] = ah;
             }
-        } else if (p.seg[seg].type == Q4K_TYPE_Q4_K) {
-            // unconditional chunks, then at most one guarded remainder (no
-            // branch inside the unrolled loop)
+        } else if (TYPES == 1 || (TYPES == 3 && p.seg[seg].type == Q4K_TYPE_Q4_K)) {
+            if constexpr ((TYPES & 1) != 0) {
+                // unconditional chunks, then at most one guarded remainder (no
+                // branch inside the unrolled loop)
 #pragma unroll 2
-            for (int k = 0; k < full_iters; ++k)
-                q4_pair<MT, NR>(rows, sub + LPR * k, lane_part, xq4, xs, xsum32, K, mcount, acc);
-            if (sub + LPR * full_iters < chunks)
-                q4_pair<MT, NR>(rows, sub + LPR * full_iters, lane_part, xq4, xs, xsum32, K, mcount, acc);
+                for (int k = 0; k < full_iters; ++k)
+                    q4_pair<MT, NR>(rows, sub + LPR * k, lane_part, xq4, xs, xsum32, K, mcount, acc);
+                if (sub + LPR * full_iters < chunks)
+                    q4_pair<MT, NR>(rows, sub + LPR * full_iters, lane_part, xq4, xs, xsum32, K, mcount, acc);
+            }
         } else {
+            if constexpr ((TYPES & 2) != 0) {
 #pragma unroll 2
-            for (int k = 0; k < full_iters; ++k)
-                q6_quarter<MT, NR>(rows, p.nb, sub + LPR * k, lane_part, xq6, xs, xsum16, K, mcount, acc);
-            if (sub + LPR * full_iters < chunks)
-                q6_quarter<MT, NR>(rows, p.nb, sub + LPR * full_iters, lane_part, xq6, xs, xsum16, K, mcount, acc);
+                for (int k = 0; k < full_iters; ++k)
+                    q6_quarter<MT, NR>(rows, p.nb, sub + LPR * k, lane_part, xq6, xs, xsum16, K, mcount, acc);
+                if (sub + LPR * full_iters < chunks)
+                    q6_quarter<MT, NR>(rows, p.nb, sub + LPR * full_iters, lane_part, xq6, xs, xsum16, K, mcount,
+                                       acc);
+            }
         }
         // this warp's reads of the stage are done (its results are computed):
         // release its share of the slot; no team barrier on the dp4a path,
@@ -532,7 +530,7 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     if (tid == 0) trace_at(p.trace, p.trace_tag, 7);
 }
 
-template <int MT, int NR, bool MMA = false>
+template <int MT, int NR, bool MMA = false, int TYPES = 3, int HELD = kHeldVec4>
 cudaError_t launch_instance(const GemvPlan& plan, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl) {
     static std::once_flag once;
     static cudaError_t attr_status = cudaSuccess;
@@ -540,10 +538,10 @@ cudaError_t launch_instance(const GemvPlan& plan, dim3 grid, dim3 block, size_t 
     std::call_once(once, [] {
         // static + dynamic shared memory must fit the 227 KB per-block limit
         cudaFuncAttributes fa{};
-        attr_status = cudaFuncGetAttributes(&fa, gemv_kernel<MT, NR, MMA>);
+        attr_status = cudaFuncGetAttributes(&fa, gemv_kernel<MT, NR, MMA, TYPES, HELD>);
         if (attr_status != cudaSuccess) return;
         max_dynamic = 227 * 1024 - fa.sharedSizeBytes;
-        attr_status = cudaFuncSetAttribute(gemv_kernel<MT, NR, MMA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        attr_status = cudaFuncSetAttribute(gemv_kernel<MT, NR, MMA, TYPES, HELD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)max_dynamic);
     });
     if (attr_status != cudaSuccess) return attr_status;
@@ -558,7 +556,7 @@ cudaError_t launch_instance(const GemvPlan& plan, dim3 grid, dim3 block, size_t 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<MT, NR, MMA>, plan);
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<MT, NR, MMA, TYPES, HELD>, plan);
 }
 
 int align_up(int v, int a) { return (v + a - 1) / a * a; }
@@ -669,12 +667,6 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     p.off_mred = off;
     off += 4 * 2 * kTeamWarps * 16 * 4;  // [team][2][warp][16 rows] partials of tensor-core stages
     off = align_up(off, 128);
-    p.off_xbuf = -1;
-    if (rq.M == 1 && !rq.in_image.base && rq.peer_in.world <= 0 && reinterpret_cast<uintptr_t>(rq.x) % 16 == 0 &&
-        env_int("Q4K_X_BULK", 0) != 0) {
-        p.off_xbuf = off;
-        off += align_up(rq.K * 4, 128);
-    }
 
     // Lanes per row: about five 64-value chunks per lane per stage.
     const int chunks = p.nb * 4;
@@ -738,7 +730,7 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     // every ring slot belongs to one team: teams <= S and S a multiple of it
     const int teams = std::min(W / kTeamWarps, S);
     S -= S % teams;
-    if (off + S * stage_bytes + (2 * S + 1) * 8 > 220 * 1024) return cudaErrorInvalidValue;
+    if (off + S * stage_bytes + 2 * S * 8 > 220 * 1024) return cudaErrorInvalidValue;
     p.lpr = lpr;
     p.inflight = std::max(0, env_int("Q4K_GEMV_INFLIGHT", 0));
     p.prefetch_landed = env_int("Q4K_PREFETCH_LANDED", 0) != 0;
@@ -751,11 +743,29 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     p.off_bufs = off;
     off += S * stage_bytes;
     p.off_bars = off;
-    off += (2 * S + 1) * 8;  // full, empty, and the activation copy's barrier
+    off += 2 * S * 8;
     const size_t smem = (size_t)off;
     const dim3 grid(ctas, (rq.M + MT - 1) / MT), block((W + 1) * 32);
 
     const int NR = pair ? 2 : 1;
+    if (MT == 1 && !mma) {
+        // batch of one: an instance with only the weight types and input path used
+        const int types = (need_q4 ? 1 : 0) | (need_q6 ? 2 : 0);
+        const int held = p.in_image.base ? 0 : rq.K / 4 <= 2 * W * 32 ? 2 : kHeldVec4;
+        auto pick = [&](auto nr_tag) -> cudaError_t {
+            constexpr int R_ = decltype(nr_tag)::value;
+            auto by_held = [&](auto types_tag) -> cudaError_t {
+                constexpr int T_ = decltype(types_tag)::value;
+                if (held == 0) return launch_instance<1, R_, false, T_, 0>(p, grid, block, smem, stream, rq.pdl);
+                if (held == 2) return launch_instance<1, R_, false, T_, 2>(p, grid, block, smem, stream, rq.pdl);
+                return launch_instance<1, R_, false, T_, kHeldVec4>(p, grid, block, smem, stream, rq.pdl);
+            };
+            if (types == 1) return by_held(std::integral_constant<int, 1>{});
+            if (types == 2) return by_held(std::integral_constant<int, 2>{});
+            return by_held(std::integral_constant<int, 3>{});
+        };
+        return NR == 2 ? pick(std::integral_constant<int, 2>{}) : pick(std::integral_constant<int, 1>{});
+    }
     switch (MT * 4 + NR) {
         case 1 * 4 + 1:
             return mma ? launch_instance<1, 1, true>(p, grid, block, smem, stream, rq.pdl)

@@ -367,8 +367,7 @@ __device__ __forceinline__ void quantise_rows(const float* x, int ldx, int m0, i
                                               int barrier_id, unsigned long long* trace = nullptr,
                                               int trace_tag = 0, const unsigned long long* parts = nullptr,
                                               int nparts = 0, unsigned parts_tag = 0, int* err = nullptr,
-                                              uint64_t wait_ns = 0, int err_code = 0, float* x_out = nullptr,
-                                              bool x_shared = false) {
+                                              uint64_t wait_ns = 0, int err_code = 0, float* x_out = nullptr) {
     const int nvec = K / 4;
     // kHeld: float4s of the row a thread keeps in registers (K <= kHeld * 4 * nthreads)
     for (int m = 0; m < mcount; ++m) {
@@ -378,8 +377,7 @@ __device__ __forceinline__ void quantise_rows(const float* x, int ldx, int m0, i
 #pragma unroll
         for (int k = 0; k < kHeld; ++k) {
             const int i = tid + k * nthreads;
-            // global rows may have been written by other SMs in this launch
-            if (i < nvec) held[k] = x_shared ? xr[i] : __ldcg(xr + i);
+            if (i < nvec) held[k] = __ldcg(xr + i);  // may have been written by other SMs in this launch
         }
         if (parts && m == 0) {
             // tensor parallelism: x + the ranks' partial sums (rank order), the

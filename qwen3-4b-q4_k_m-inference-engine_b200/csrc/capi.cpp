@@ -201,6 +201,12 @@ Q4K_API int q4k_matmul(const float* input, const void* weight, int type, int64_t
         r.x = input;
         r.ldy = (int)ne1;
         r.epilogue = q4k::EPI_STORE;
+        // programmatic dependent launch: the weight stream starts while the
+        // preceding kernel on the stream finishes; the input is read and the
+        // output written only after the dependency wait, and a preceding
+        // kernel that does not signal early (everything that writes weights)
+        // still completes first
+        r.pdl = true;
         launched(q4k::launch_gemv(r, as_stream(stream)));
     });
 }
@@ -327,6 +333,7 @@ Q4K_API int q4k_matmul_ex(const float* input, const float* norm_gamma, float eps
         r.eps = epsilon;
         r.ldy = (int)out_rows[0];
         r.epilogue = epilogue;
+        r.pdl = true;  // as in q4k_matmul
         launched(q4k::launch_gemv(r, as_stream(stream)));
     });
 }

@@ -614,6 +614,33 @@ def run_decode(args, world, rank, local):
     return result
 
 
+def run_step(args, world, rank, local):
+    """The batch-1 decode step alone, one sequence (3.1 GB on the device):
+    the command the decode profiles under profiles/ are captured with. The
+    driver's line is the default workload."""
+    import torch
+
+    import q4kb200 as q
+
+    torch.cuda.set_device(local)
+    eng, _ = make_engine(q, torch, 1, 0, local, None, sequences=1)
+    stream = torch.cuda.ExternalStream(eng.stream)
+    eng.generate(TOKEN0, POS, max(args.warmup, 3), advance=False, want_tokens=False)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    eng.generate(TOKEN0, POS, args.steps, advance=False, want_tokens=False)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    secs = ev0.elapsed_time(ev1) / 1e3
+    eng.close()
+    return {"metric": METRIC_DECODE, "value": round(args.steps / secs, 2), "unit": "tok/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(secs / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "data": "synthetic",
+            "config": {"workload": "decode step alone, one sequence (profiling)", "seq_len": CTX,
+                       "parallelism": "tp1"}, "gpu_launches": args.steps * 183}
+
+
 def run_gemv(args, world, rank, local):
     import torch
 
@@ -803,7 +830,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("decode", "gemv", "swiglu", "attention", "prefill", "batch"),
+    ap.add_argument("--workload", choices=("decode", "step", "gemv", "swiglu", "attention", "prefill", "batch"),
                     default="decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -817,6 +844,8 @@ def main() -> None:
 
     if args.workload == "decode":
         out = run_decode(args, world, rank, local)
+    elif args.workload == "step":
+        out = run_step(args, world, rank, local) if rank == 0 else None
     elif args.workload == "attention":
         out = run_attention(args, world, rank, local)
     elif args.workload == "swiglu":

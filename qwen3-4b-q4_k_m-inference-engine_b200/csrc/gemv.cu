@@ -679,12 +679,20 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     // Opt-in (Q4K_GEMV_MMA=1): measured no faster than the dp4a path here.
     const bool mma = rq.M == 1 && any_q4 && rq.K <= 3072 && env_int("Q4K_GEMV_MMA", 0) != 0;
     if (mma) lpr = pair ? 16 : 8;
-    // consumer warps: teams of four (16 by default); K/4 float4s of the
-    // activation row must fit the prologue's registers (kHeldVec4 per thread)
-    int W = env_int("Q4K_GEMV_WARPS", 16);
-    if (W != 8 && W != 12 && W != 16) W = 16;
-    if (rq.K / 4 > kHeldVec4 * W * 32) return cudaErrorInvalidValue;
+    // consumer warps: teams of four, 12 by default (measured 1.6% faster
+    // than 16 in the decode step); K/4 float4s of an activation row that is
+    // quantised here must fit the prologue's registers (kHeldVec4 per
+    // thread), which takes 16 warps past K = 9216
     const int R = kTeamWarps * 32 / lpr;
+    // long products (the output head: dozens of stages per CTA) stream in
+    // steady state, where 16 warps keep up with HBM better
+    long long total_rows = 0;
+    for (int s2 = 0; s2 < (pair ? 1 : rq.nseg); ++s2) total_rows += rq.seg[s2].rows;
+    const bool long_product = total_rows / R > 8LL * sm_count();
+    int W = env_int("Q4K_GEMV_WARPS", long_product ? 16 : 12);
+    if (W != 8 && W != 12 && W != 16) W = 12;
+    if (!rq.in_image.base && rq.K / 4 > kHeldVec4 * W * 32) W = 16;
+    if (!rq.in_image.base && rq.K / 4 > kHeldVec4 * W * 32) return cudaErrorInvalidValue;
     const int rows_in_stage = pair ? 2 * R : R;
     const int stage_bytes = align_up(rows_in_stage * max_row, 128);
 

@@ -284,33 +284,59 @@ __device__ __forceinline__ float q8_scale(float amax) {
 // RMSNorm-ed if the product has a norm): the 8 lanes i..i+7 of a warp hold
 // one 32-group (matmul.cu:8-22). Stores the codes (Q4_K and/or Q6_K
 // permuted order), the group scale, and the 16- and 32-value code sums.
+// quantise_vec4 for N float4s of a thread side by side (their dependent
+// chains interleave); vector n is element e[n] of row m.
+template <int N>
+__device__ __forceinline__ void quantise_vecs(const float4 (&v)[N], const int (&e)[N], int K, int m, uint8_t* xq4,
+                                              uint8_t* xq6, float* xs, int* xsum16, float* xsum32, int lane,
+                                              bool store = true) {
+    float amax[N];
+#pragma unroll
+    for (int n = 0; n < N; ++n) amax[n] = fmaxf(fmaxf(fabsf(v[n].x), fabsf(v[n].y)), fmaxf(fabsf(v[n].z), fabsf(v[n].w)));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+        for (int n = 0; n < N; ++n) amax[n] = fmaxf(amax[n], __shfl_xor_sync(0xffffffffu, amax[n], o));
+    uint32_t word[N];
+    int run[N];
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+        const bool defined = q8_codes_defined(amax[n]);
+        const double ra = recip_refined(defined ? amax[n] : 1.0f);
+        const int8_t c0 = defined ? q8_code_r(v[n].x, ra) : 0, c1 = defined ? q8_code_r(v[n].y, ra) : 0;
+        const int8_t c2 = defined ? q8_code_r(v[n].z, ra) : 0, c3 = defined ? q8_code_r(v[n].w, ra) : 0;
+        word[n] = (uint32_t)(uint8_t)c0 | ((uint32_t)(uint8_t)c1 << 8) | ((uint32_t)(uint8_t)c2 << 16) |
+                  ((uint32_t)(uint8_t)c3 << 24);
+        run[n] = (int)c0 + (int)c1 + (int)c2 + (int)c3;
+    }
+#pragma unroll
+    for (int n = 0; n < N; ++n) run[n] += __shfl_xor_sync(0xffffffffu, run[n], 1);
+#pragma unroll
+    for (int n = 0; n < N; ++n) run[n] += __shfl_xor_sync(0xffffffffu, run[n], 2);
+    int group[N];
+#pragma unroll
+    for (int n = 0; n < N; ++n) group[n] = run[n] + __shfl_xor_sync(0xffffffffu, run[n], 4);
+    if (!store) return;  // a lane that only took part in its warp's shuffles
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+        const int b = e[n] >> 8, r16 = (e[n] & 255) >> 4, o = e[n] & 15;
+        if (xq4) *reinterpret_cast<uint32_t*>(xq4 + m * K + b * 256 + 16 * perm_q4(r16, b) + o) = word[n];
+        if (xq6) *reinterpret_cast<uint32_t*>(xq6 + m * K + b * 256 + 16 * perm_q6(r16, b) + o) = word[n];
+        // run r16 = 8h + 2g + l is stored at quarter (2h + l), slot g
+        if ((lane & 3) == 0)
+            xsum16[m * (K / 16) + b * 16 + 4 * (2 * (r16 >> 3) + (r16 & 1)) + ((r16 >> 1) & 3)] = 32 * run[n];
+        if ((lane & 7) == 0) {
+            xsum32[m * (K / 32) + (e[n] >> 5)] = (float)group[n];
+            xs[m * (K / 32) + (e[n] >> 5)] = q8_scale(amax[n]);  // matmul.cu:18
+        }
+    }
+}
+
 __device__ __forceinline__ void quantise_vec4(float4 v, int e, int K, int m, uint8_t* xq4, uint8_t* xq6, float* xs,
                                               int* xsum16, float* xsum32, int lane, bool store = true) {
-    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-    const bool defined = q8_codes_defined(amax);
-    const double ra = recip_refined(defined ? amax : 1.0f);
-    const int8_t c0 = defined ? q8_code_r(v.x, ra) : 0, c1 = defined ? q8_code_r(v.y, ra) : 0;
-    const int8_t c2 = defined ? q8_code_r(v.z, ra) : 0, c3 = defined ? q8_code_r(v.w, ra) : 0;
-    const uint32_t word = (uint32_t)(uint8_t)c0 | ((uint32_t)(uint8_t)c1 << 8) |
-                          ((uint32_t)(uint8_t)c2 << 16) | ((uint32_t)(uint8_t)c3 << 24);
-    int run = (int)c0 + (int)c1 + (int)c2 + (int)c3;
-    run += __shfl_xor_sync(0xffffffffu, run, 1);
-    run += __shfl_xor_sync(0xffffffffu, run, 2);
-    const int group = run + __shfl_xor_sync(0xffffffffu, run, 4);
-    if (!store) return;  // a lane that only took part in its warp's shuffles
-    const int b = e >> 8, r16 = (e & 255) >> 4, o = e & 15;
-    if (xq4) *reinterpret_cast<uint32_t*>(xq4 + m * K + b * 256 + 16 * perm_q4(r16, b) + o) = word;
-    if (xq6) *reinterpret_cast<uint32_t*>(xq6 + m * K + b * 256 + 16 * perm_q6(r16, b) + o) = word;
-    // run r16 = 8h + 2g + l is stored at quarter (2h + l), slot g
-    if ((lane & 3) == 0)
-        xsum16[m * (K / 16) + b * 16 + 4 * (2 * (r16 >> 3) + (r16 & 1)) + ((r16 >> 1) & 3)] = 32 * run;
-    if ((lane & 7) == 0) {
-        xsum32[m * (K / 32) + (e >> 5)] = (float)group;
-        xs[m * (K / 32) + (e >> 5)] = q8_scale(amax);  // matmul.cu:18
-    }
+    const float4 vv[1] = {v};
+    const int ee[1] = {e};
+    quantise_vecs<1>(vv, ee, K, m, xq4, xq6, xs, xsum16, xsum32, lane, store);
 }
 
 // Q8-quantise elements e and e + 1 (e even) of a row whose 32-value group
@@ -428,27 +454,42 @@ __device__ __forceinline__ void quantise_rows(const float* x, int ldx, int m0, i
             ss = warp_sum(ss);
             if (lane == 0) red[warp] = ss;
             named_barrier(barrier_id, nthreads);
-            if (trace && tid == 0 && m == 0) trace_at(trace, trace_tag, 6);  // PROBE
-            float total = 0.0f;
-            for (int i = 0; i < nthreads / 32; ++i) total += red[i];
+            // every warp sums the per-warp partials in the same shuffle tree
+            const float total = warp_sum(lane < nthreads / 32 ? red[lane] : 0.0f);
             inv = rsqrtf(total / (float)K + eps);  // rms_norm.cu:17
-            named_barrier(barrier_id, nthreads);
+            // `red` is written again only for the next row
+            if (m + 1 < mcount) named_barrier(barrier_id, nthreads);
         }
         // element e = 4*i of the row; the 8 lanes i..i+7 hold one 32-group
-#pragma unroll
-        for (int k = 0; k < kHeld; ++k) {
+        auto normed = [&](int k) {
             const int i = tid + k * nthreads;
-            if (i >= nvec) break;
-            const int e = 4 * i;
             float4 v = held[k];
-            if (gamma) {
+            if (gamma && i < nvec) {
                 const float4 gm = reinterpret_cast<const float4*>(gamma)[i];
                 v.x = (v.x * inv) * gm.x;  // rms_norm.cu:19: input * inverse_rms * scale
                 v.y = (v.y * inv) * gm.y;
                 v.z = (v.z * inv) * gm.z;
                 v.w = (v.w * inv) * gm.w;
             }
-            quantise_vec4(v, e, K, m, xq4, xq6, xs, xsum16, xsum32, lane);
+            return v;
+        };
+        if constexpr (kHeld == 2) {
+            // a thread's two float4s side by side (which warps hold a second
+            // one is warp-uniform: nvec and nthreads are multiples of 32)
+            if (tid + nthreads < nvec) {
+                const float4 vv[2] = {normed(0), normed(1)};
+                const int ee[2] = {4 * tid, 4 * (tid + nthreads)};
+                quantise_vecs<2>(vv, ee, K, m, xq4, xq6, xs, xsum16, xsum32, lane);
+            } else if (tid < nvec) {
+                quantise_vec4(normed(0), 4 * tid, K, m, xq4, xq6, xs, xsum16, xsum32, lane);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < kHeld; ++k) {
+                const int i = tid + k * nthreads;
+                if (i >= nvec) break;
+                quantise_vec4(normed(k), 4 * i, K, m, xq4, xq6, xs, xsum16, xsum32, lane);
+            }
         }
     }
     named_barrier(barrier_id, nthreads);

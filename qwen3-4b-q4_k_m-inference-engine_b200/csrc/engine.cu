@@ -283,12 +283,16 @@ Engine::Engine(const q4k_engine_config& cfg, const void* nccl_id) : c_(cfg) {
     partial_ = static_cast<float*>(alloc(sizeof(float) * H));
     logits_ = static_cast<float*>(alloc(sizeof(float) * (vocab1_ - vocab0_)));
     hidden_ = static_cast<float*>(alloc(sizeof(float) * H * (c.layers + 1)));
-    token_ = static_cast<uint32_t*>(alloc(64));
-    pos_ = static_cast<int*>(alloc(64));
-    advance_ = static_cast<int*>(alloc(64));
-    err_ = static_cast<int*>(alloc(64));
+    // the step's small device words in one block, so that a decode call
+    // moves them with one copy each way: token, position, advance and the
+    // history count (host -> device), token .. error word (device -> host)
+    io_ = static_cast<uint32_t*>(alloc(256));
+    token_ = io_ + kIoToken;
+    pos_ = reinterpret_cast<int*>(io_ + kIoPos);
+    advance_ = reinterpret_cast<int*>(io_ + kIoAdvance);
+    err_ = reinterpret_cast<int*>(io_ + kIoErr);
     history_ = static_cast<uint32_t*>(alloc(sizeof(uint32_t) * (size_t)c.capacity));
-    history_n_ = static_cast<unsigned*>(alloc(64));
+    history_n_ = io_ + kIoHistoryN;
     // [sequence][layer][kv head][position][128]: sequence 0 first
     seq_elems_ = (size_t)c.layers * KVHl_ * c.capacity * c.head_dim;
     const size_t kv_elems = seq_elems_ * seqs_;
@@ -1010,11 +1014,18 @@ void Engine::host_wait(const char* what) {
     }
 }
 
-void Engine::check_device_error() {
+void Engine::check_device_error(bool with_token) {
     int err = 0;
-    cuda_check(cudaMemcpyAsync(&host_io_[3], err_, sizeof(int), cudaMemcpyDeviceToHost, stream_), "read err");
+    // with_token: the step's token and the error word in one copy
+    if (with_token)
+        cuda_check(cudaMemcpyAsync(&host_io_[kHostOut], io_, (kIoErr + 1) * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                                   stream_),
+                   "read token and err");
+    else
+        cuda_check(cudaMemcpyAsync(&host_io_[kHostOut + kIoErr], err_, sizeof(int), cudaMemcpyDeviceToHost, stream_),
+                   "read err");
     host_wait("step");
-    err = (int)host_io_[3];
+    err = (int)host_io_[kHostOut + kIoErr];
     if (err) {
         cudaMemsetAsync(err_, 0, sizeof(int), stream_);
         cudaStreamSynchronize(stream_);
@@ -1033,19 +1044,21 @@ void Engine::require_live() const {
     if (aborted_.load()) throw Error(Q4K_ETIMEOUT, "the engine was aborted (tensor-parallel failure); create a new one");
 }
 
+void Engine::stage_io(uint32_t token, int position, uint32_t advance) {
+    host_io_[kIoToken] = token;
+    host_io_[kIoPos] = (uint32_t)position;
+    host_io_[kIoAdvance] = advance;
+    host_io_[kIoHistoryN] = 0;
+    cuda_check(cudaMemcpyAsync(io_, host_io_, kIoIn * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_), "h2d");
+}
+
 uint32_t Engine::decode(uint32_t token, int position, float* logits_host, float* hidden_host) {
     require_live();
     if (!loaded_) throw Error(Q4K_EINVAL, "weights are not loaded");
     if (token >= (uint32_t)c_.vocab) throw Error(Q4K_ERANGE, "Token ID out of range");
     if (position < 0 || position >= c_.capacity) throw Error(Q4K_ERANGE, "KV cache capacity exceeded");
     if (hidden_host && world_ > 1) throw Error(Q4K_EINVAL, "hidden snapshots need tp_world == 1");
-    host_io_[0] = token;
-    host_io_[1] = (uint32_t)position;
-    host_io_[2] = 0;
-    cuda_check(cudaMemcpyAsync(token_, &host_io_[0], 4, cudaMemcpyHostToDevice, stream_), "h2d");
-    cuda_check(cudaMemcpyAsync(pos_, &host_io_[1], 4, cudaMemcpyHostToDevice, stream_), "h2d");
-    cuda_check(cudaMemcpyAsync(advance_, &host_io_[2], 4, cudaMemcpyHostToDevice, stream_), "h2d");
-    cuda_check(cudaMemsetAsync(history_n_, 0, 4, stream_), "memset");
+    stage_io(token, position, 0);
     if (hidden_host) {
         enqueue_step(true);
     } else if (step_kernel_) {
@@ -1055,7 +1068,6 @@ uint32_t Engine::decode(uint32_t token, int position, float* logits_host, float*
         ensure_graph();
         cuda_check(cudaGraphLaunch(exec_, stream_), "graph launch");
     }
-    cuda_check(cudaMemcpyAsync(&host_io_[4], token_, 4, cudaMemcpyDeviceToHost, stream_), "d2h");
     if (logits_host)
         cuda_check(cudaMemcpyAsync(logits_host, logits_, sizeof(float) * (vocab1_ - vocab0_), cudaMemcpyDeviceToHost,
                                    stream_),
@@ -1064,8 +1076,8 @@ uint32_t Engine::decode(uint32_t token, int position, float* logits_host, float*
         cuda_check(cudaMemcpyAsync(hidden_host, hidden_, sizeof(float) * c_.hidden * (c_.layers + 1),
                                    cudaMemcpyDeviceToHost, stream_),
                    "d2h hidden");
-    check_device_error();
-    return host_io_[4];
+    check_device_error(true);
+    return host_io_[kHostOut + kIoToken];
 }
 
 void Engine::generate(uint32_t token, int position, int steps, int advance, uint32_t* tokens_host) {
@@ -1080,13 +1092,7 @@ void Engine::generate(uint32_t token, int position, int steps, int advance, uint
         ensure_step_plan();
     else
         ensure_graph();
-    host_io_[0] = token;
-    host_io_[1] = (uint32_t)position;
-    host_io_[2] = advance ? 1u : 0u;
-    cuda_check(cudaMemcpyAsync(token_, &host_io_[0], 4, cudaMemcpyHostToDevice, stream_), "h2d");
-    cuda_check(cudaMemcpyAsync(pos_, &host_io_[1], 4, cudaMemcpyHostToDevice, stream_), "h2d");
-    cuda_check(cudaMemcpyAsync(advance_, &host_io_[2], 4, cudaMemcpyHostToDevice, stream_), "h2d");
-    cuda_check(cudaMemsetAsync(history_n_, 0, 4, stream_), "memset");
+    stage_io(token, position, advance ? 1u : 0u);
     for (int s = 0; s < steps; ++s) {
         if (step_kernel_)
             enqueue_step_kernel();
@@ -1118,12 +1124,7 @@ size_t Engine::trace_step(uint32_t token, int position, unsigned long long* reco
             ensure_step_plan();
         else
             ensure_graph();
-        host_io_[0] = token;
-        host_io_[1] = (uint32_t)position;
-        host_io_[2] = 0;
-        cuda_check(cudaMemcpyAsync(token_, &host_io_[0], 4, cudaMemcpyHostToDevice, stream_), "h2d");
-        cuda_check(cudaMemcpyAsync(pos_, &host_io_[1], 4, cudaMemcpyHostToDevice, stream_), "h2d");
-        cuda_check(cudaMemcpyAsync(advance_, &host_io_[2], 4, cudaMemcpyHostToDevice, stream_), "h2d");
+        stage_io(token, position, 0);
         if (step_kernel_)
             enqueue_step_kernel();
         else
@@ -1391,11 +1392,8 @@ uint32_t Engine::prefill(const uint32_t* tokens_host, int n, int position, float
     ensure_prefill();
     if (pf_gemm_) ensure_prefill_maps();
     const int H = c_.hidden;
-    host_io_[1] = (uint32_t)(position + n - 1);
-    host_io_[2] = 0;
-    cuda_check(cudaMemcpyAsync(pos_, &host_io_[1], 4, cudaMemcpyHostToDevice, stream_), "h2d");
-    cuda_check(cudaMemcpyAsync(advance_, &host_io_[2], 4, cudaMemcpyHostToDevice, stream_), "h2d");
-    cuda_check(cudaMemsetAsync(history_n_, 0, 4, stream_), "memset");
+    // the head's argmax writes the token; the position is the last row's
+    stage_io(0, position + n - 1, 0);
     int rows = 0;
     for (int t0 = 0; t0 < n; t0 += pf_rows_) {
         rows = std::min(pf_rows_, n - t0);
@@ -1411,13 +1409,12 @@ uint32_t Engine::prefill(const uint32_t* tokens_host, int n, int position, float
                                stream_),
                "last row");
     enqueue_head(false);
-    cuda_check(cudaMemcpyAsync(&host_io_[4], token_, 4, cudaMemcpyDeviceToHost, stream_), "d2h");
     if (logits_host)
         cuda_check(cudaMemcpyAsync(logits_host, logits_, sizeof(float) * (vocab1_ - vocab0_), cudaMemcpyDeviceToHost,
                                    stream_),
                    "d2h logits");
-    check_device_error();
-    return host_io_[4];
+    check_device_error(true);
+    return host_io_[kHostOut + kIoToken];
 }
 
 void Engine::ensure_batch() {
@@ -1676,8 +1673,8 @@ void Engine::layer_step(int layer, const float* x_host, int position, float* x_o
     if (!loaded_) throw Error(Q4K_EINVAL, "weights are not loaded");
     if (layer < 0 || layer >= c_.layers) throw Error(Q4K_ERANGE, "layer out of range");
     if (position < 0 || position >= c_.capacity) throw Error(Q4K_ERANGE, "KV cache capacity exceeded");
-    host_io_[1] = (uint32_t)position;
-    cuda_check(cudaMemcpyAsync(pos_, &host_io_[1], 4, cudaMemcpyHostToDevice, stream_), "h2d");
+    host_io_[kIoPos] = (uint32_t)position;
+    cuda_check(cudaMemcpyAsync(pos_, &host_io_[kIoPos], 4, cudaMemcpyHostToDevice, stream_), "h2d");
     cuda_check(cudaMemcpyAsync(x_, x_host, sizeof(float) * c_.hidden, cudaMemcpyHostToDevice, stream_), "h2d x");
     enqueue_layer(layer, false);
     cuda_check(cudaMemcpyAsync(x_out_host, x_, sizeof(float) * c_.hidden, cudaMemcpyDeviceToHost, stream_), "d2h x");

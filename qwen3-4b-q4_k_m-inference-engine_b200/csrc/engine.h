@@ -128,7 +128,7 @@ private:
     int stage_batch(int n, const int* seqs, const uint32_t* tokens, const int* positions);
     // L2 prefetch descriptors of layer i's weights (q, k, v; o; gate, up; down).
     L2Prefetch weight_prefetch(const uint8_t* w, int type, int K, int rows) const;
-    void check_device_error();
+    void check_device_error(bool with_token = false);
     void ensure_graph();
     // Persistent decode-step kernel (tp_world == 1): one launch per token.
     void ensure_step_plan();
@@ -154,6 +154,12 @@ private:
 
     float *x_ = nullptr, *qkv_ = nullptr, *att_ = nullptr, *act_ = nullptr, *partial_ = nullptr,
           *logits_ = nullptr, *hidden_ = nullptr;
+    // io_ (device) word layout; host_io_ (pinned) holds the words going in
+    // at the same indices and those coming back from kHostOut on
+    static constexpr int kIoToken = 0, kIoPos = 1, kIoAdvance = 2, kIoHistoryN = 3, kIoIn = 4, kIoErr = 4;
+    static constexpr int kHostOut = 8;
+    uint32_t* io_ = nullptr;
+    void stage_io(uint32_t token, int position, uint32_t advance);
     uint32_t* token_ = nullptr;     // device: token to embed (and the step's result)
     int* pos_ = nullptr;            // device: position of the token
     int* advance_ = nullptr;        // device: position increment per step

@@ -317,6 +317,7 @@ Engine::Engine(const q4k_engine_config& cfg, const void* nccl_id) : c_(cfg) {
         // (or fail saying why it cannot run); otherwise the launch sequence,
         // which measures faster today
         if (const char* pf = std::getenv("Q4K_L2_PREFETCH")) l2_prefetch_ = pf[0] != '0';
+        if (const char* pp = std::getenv("Q4K_PREFETCH_PLAN")) prefetch_plan_ = std::atoi(pp) == 1 ? 1 : 2;
         const char* env = std::getenv("Q4K_STEP_KERNEL");
         const bool wanted = env && env[0] == '1';
         std::string why;
@@ -577,6 +578,18 @@ unsigned long long* Engine::peer_recv(int rank, int slot) const {
 }
 
 // One transformer block (Engine.cpp:71-103) on the device buffers: x is
+void Engine::kv_prefetch(int layer, L2Prefetch* f) const {
+    if (!l2_prefetch_) return;
+    const size_t kv_layer = (size_t)layer * KVHl_ * c_.capacity * c_.head_dim;
+    for (int e = 0; e < 2; ++e) {
+        f[e].base = (e == 0 ? kcache_ : vcache_) + kv_layer;
+        f[e].bytes = (unsigned long long)c_.head_dim * 2;
+        f[e].stride = (unsigned long long)c_.capacity * c_.head_dim * 2;
+        f[e].count = KVHl_;
+        f[e].position = pos_;
+    }
+}
+
 L2Prefetch Engine::weight_prefetch(const uint8_t* w, int type, int K, int rows) const {
     L2Prefetch f;
     if (!l2_prefetch_ || !w) return f;
@@ -636,17 +649,7 @@ void Engine::enqueue_layer(int i, bool fused) {
         r.pdl = true;
         r.trace = trace_;
         r.trace_tag = 5 * i;
-        if (l2_prefetch_) {
-            // the attention's K and V rows 0..*pos_ of every KV head
-            for (int e = 0; e < 2; ++e) {
-                L2Prefetch& f = r.prefetch[e];
-                f.base = (e == 0 ? kcache_ : vcache_) + kv_layer;
-                f.bytes = (unsigned long long)c.head_dim * 2;
-                f.stride = (unsigned long long)c.capacity * c.head_dim * 2;
-                f.count = KVHl_;
-                f.position = pos_;
-            }
-        }
+        kv_prefetch(i, r.prefetch);  // the attention's K and V rows
         gemv(r);
     }
     {
@@ -672,6 +675,12 @@ void Engine::enqueue_layer(int i, bool fused) {
         a.trace = trace_;
         a.trace_tag = 5 * i + 1;
         a.prefetch[0] = weight_prefetch(L.o, L.to, qd_, H);
+        if (prefetch_plan_ == 2) {
+            // the long attention launch also asks for the gate/up weights, so
+            // that the short O launch ends without a 28 MB prefetch in flight
+            a.prefetch[1] = weight_prefetch(L.gate, L.tgate, H, ffn_l_);
+            a.prefetch[2] = weight_prefetch(L.up, L.tup, H, ffn_l_);
+        }
         if (act_images_) a.out_image = att_img_;
         cuda_check(decode_attention(a, kmap_, vmap_, stream_, true), "attention launch");
     }
@@ -687,8 +696,10 @@ void Engine::enqueue_layer(int i, bool fused) {
         r.pdl = true;
         r.trace = trace_;
         r.trace_tag = 5 * i + 2;
-        r.prefetch[0] = weight_prefetch(L.gate, L.tgate, H, ffn_l_);
-        r.prefetch[1] = weight_prefetch(L.up, L.tup, H, ffn_l_);
+        if (prefetch_plan_ == 1) {
+            r.prefetch[0] = weight_prefetch(L.gate, L.tgate, H, ffn_l_);
+            r.prefetch[1] = weight_prefetch(L.up, L.tup, H, ffn_l_);
+        }
         if (act_images_) r.in_image = att_img_;
         gemv(r);
         if (world_ > 1 && !fused) all_reduce_into_x();

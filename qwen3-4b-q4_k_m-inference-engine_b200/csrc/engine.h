@@ -128,6 +128,8 @@ private:
     int stage_batch(int n, const int* seqs, const uint32_t* tokens, const int* positions);
     // L2 prefetch descriptors of layer i's weights (q, k, v; o; gate, up; down).
     L2Prefetch weight_prefetch(const uint8_t* w, int type, int K, int rows) const;
+    // the K and V cache rows 0..*pos_ of every KV head of `layer` (sequence 0), into f[0] and f[1]
+    void kv_prefetch(int layer, L2Prefetch* f) const;
     void check_device_error(bool with_token = false);
     void ensure_graph();
     // Persistent decode-step kernel (tp_world == 1): one launch per token.
@@ -223,6 +225,13 @@ private:
     bool comm_aborted_ = false;
     void host_wait(const char* what);
     void require_live() const;       // stream drained, bounded by host_wait_ms_ when world_ > 1
+    // L2 prefetch plan. 1: each launch asks for the next launch's operands.
+    // 2 (default, +0.8%): the attention launch also asks for the gate/up
+    // weights and O for nothing: O is short, and a grid is complete only once
+    // its prefetches are, so a 28 MB prefetch issued by O delayed gate/up's
+    // dependency wait (1.66 -> 1.09 us). Moving more (the next layer's K/V
+    // rows to ffn_down, its q/k/v weights to gate/up) measured 4.5% slower.
+    int prefetch_plan_ = 2;
     bool l2_prefetch_ = true;        // each launch prefetches the next one's operands into L2
     bool act_images_ = true;         // SwiGLU and attention hand the next product a quantised activation
     ActImage act_img_, att_img_;     // quantised act_ (for ffn_down) and att_ (for attn_output)

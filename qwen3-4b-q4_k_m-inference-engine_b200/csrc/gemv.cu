@@ -79,6 +79,7 @@ struct GemvPlan {
     ActImage out_image;  // SwiGLU: quantise this CTA's output rows into it (M == 1)
     int inflight;        // stages the producer keeps in flight (issued, not landed); 0: the whole ring
     int prefetch_landed; // issue the L2 prefetch once the first ring of stages has landed
+    int gamma_bulk;      // the RMSNorm weight comes in by one bulk copy, ahead of the ring
     int off_resid;       // >= 0 (EPI_ADD, one segment, image input): this CTA's residual rows, fetched
                          // with the image so that the epilogue adds from shared memory
     int group_stages;    // stages per 32-row group: CTA shares start on group boundaries (out_image)
@@ -240,6 +241,7 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
             mbar_init(empty + i, MMA ? 1 : kTeamWarps);
         }
         for (int k = 0; k < 4; ++k) team_abort[k] = 0;
+        if (p.gamma_bulk) mbar_init(full + 2 * S, 1);
         mbar_fence_init();
     }
     __syncthreads();
@@ -249,6 +251,12 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
         // ---------------- producer ----------------
         if (lane == 0) {
             const uint64_t policy = policy_evict_first();
+            if (p.gamma_bulk) {
+                // a weight, independent of the preceding kernel: first in the
+                // copy engine's queue, so that no consumer waits for it
+                mbar_arrive_expect_tx(full + 2 * S, (uint32_t)K * 4u);
+                bulk_g2s(smem + p.off_gamma, p.gamma, (uint32_t)K * 4u, full + 2 * S);
+            }
             for (int i = 0, st = s_begin; st < s_end; ++i, ++st) {
                 const int slot = i % S, use = i / S;
                 uint64_t* fb = full + slot;
@@ -286,13 +294,15 @@ __global__ void __launch_bounds__(17 * 32, 1) gemv_kernel(const __grid_constant_
     }
 
     // ---------------- consumers ----------------
-    if (p.gamma) {
+    if (p.gamma && !p.gamma_bulk) {
         // a weight: independent of the preceding kernel, so it is staged
         // before the wait and the quantisation needs one global round trip
         float4* g4 = reinterpret_cast<float4*>(smem + p.off_gamma);
         for (int i = tid; i < K / 4; i += W * 32) g4[i] = __ldg(reinterpret_cast<const float4*>(p.gamma) + i);
     }
     pdl_wait();
+    // the bulk-copied RMSNorm weight (issued first at the CTA's start)
+    if (p.gamma_bulk && !mbar_wait_bounded(full + 2 * S, 0, p.err, ERR_WAIT_TIMEOUT_FULL)) team_abort[0] = 1;
     if (tid == 0) trace_at(p.trace, p.trace_tag, 1);
     const int nthreads = W * 32;
     const int resid_row0 = s_begin * p.rows_per_stage;
@@ -738,10 +748,11 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     // every ring slot belongs to one team: teams <= S and S a multiple of it
     const int teams = std::min(W / kTeamWarps, S);
     S -= S % teams;
-    if (off + S * stage_bytes + 2 * S * 8 > 220 * 1024) return cudaErrorInvalidValue;
+    if (off + S * stage_bytes + (2 * S + 1) * 8 > 220 * 1024) return cudaErrorInvalidValue;
     p.lpr = lpr;
     p.inflight = std::max(0, env_int("Q4K_GEMV_INFLIGHT", 0));
     p.prefetch_landed = env_int("Q4K_PREFETCH_LANDED", 0) != 0;
+    p.gamma_bulk = rq.gamma && reinterpret_cast<uintptr_t>(rq.gamma) % 16 == 0 && env_int("Q4K_GAMMA_BULK", 1) != 0;
     if (p.inflight >= S) p.inflight = 0;
     p.mma = mma ? 1 : 0;
     p.rows_per_stage = R;
@@ -751,7 +762,7 @@ cudaError_t launch_gemv(const GemvRequest& rq, cudaStream_t stream) {
     p.off_bufs = off;
     off += S * stage_bytes;
     p.off_bars = off;
-    off += 2 * S * 8;
+    off += (2 * S + 1) * 8;  // full, empty, and the RMSNorm weight's copy
     const size_t smem = (size_t)off;
     const dim3 grid(ctas, (rq.M + MT - 1) / MT), block((W + 1) * 32);
 

@@ -66,7 +66,7 @@ struct L2Prefetch {
     int count = 0;
     const int* position = nullptr;
 };
-constexpr int kMaxPrefetch = 3;
+constexpr int kMaxPrefetch = 5;
 
 // A batch-of-one activation already quantised the way the product kernel
 // holds it in shared memory (gemv_device.cuh), written by the kernel that

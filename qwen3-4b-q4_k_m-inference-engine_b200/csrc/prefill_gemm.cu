@@ -256,11 +256,30 @@ __device__ __forceinline__ uint32_t q4_field(const uint4& head, int g, bool min)
                : (byte_of(head, 8 + g) & 15) | ((byte_of(head, g) >> 6) << 4);
 }
 
-__device__ __forceinline__ void dequant_q4(const uint8_t* raw, uint8_t* bt, int r, int p, int j) {
+// The 4 scales a builder thread (weight row r, quarter p of each stage)
+// applies in the 4 stages j of a super-block, decoded once per super-block:
+// Q4_K group 2j + (p >> 1)'s 6-bit scale (matmul.cu:40-47: groups 0-3 from
+// bytes 4-7, groups 4-7 from the low nibbles of bytes 12-15 and the top two
+// bits of bytes 4-7), Q6_K the int8 scale 4j + p of the 16 (embedding.cu:42-58).
+__device__ __forceinline__ void stage_scales(const uint8_t* raw, int type, int r, int p, __half2 (&sc)[4]) {
+    if (type == Q4K_TYPE_Q4_K) {
+        const uint4 head = ld16(raw + r * 144);
+        const uint32_t lo = head.y & 0x3f3f3f3fu;                                       // groups 0-3
+        const uint32_t hi = (head.w & 0x0f0f0f0fu) | ((head.y >> 2) & 0x30303030u);     // groups 4-7
+        const int h = p >> 1;
+        sc[0] = __float2half2_rn((float)((lo >> (8 * h)) & 0xffu));
+        sc[1] = __float2half2_rn((float)((lo >> (8 * (2 + h))) & 0xffu));
+        sc[2] = __float2half2_rn((float)((hi >> (8 * h)) & 0xffu));
+        sc[3] = __float2half2_rn((float)((hi >> (8 * (2 + h))) & 0xffu));
+    } else {
+        const uint4 scw = ld16(raw + kSc + r * 16);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sc[j] = __float2half2_rn((float)(int8_t)byte_of(scw, 4 * j + p));
+    }
+}
+
+__device__ __forceinline__ void dequant_q4(const uint8_t* raw, uint8_t* bt, int r, int p, int j, __half2 sc2) {
     const uint8_t* blk = raw + r * 144;
-    const uint4 head = ld16(blk);
-    const int g = 2 * j + (p >> 1);  // 32-value group of the super-block
-    const __half2 sc2 = __float2half2_rn((float)q4_field(head, g, false));
     const __half2 k1024 = half2_bits(0x64006400u);
     // nibbles of values 16(p&1) .. +15 of group g: bytes 16 + 32j + 16(p&1) .., low or high nibble
     const uint4 nb = ld16(blk + 16 * (1 + 2 * j + (p & 1)));
@@ -278,9 +297,7 @@ __device__ __forceinline__ void dequant_q4(const uint8_t* raw, uint8_t* bt, int 
     *reinterpret_cast<uint4*>(bt + swz(r, 2 * p + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
-__device__ __forceinline__ void dequant_q6(const uint8_t* raw, uint8_t* bt, int r, int p, int j) {
-    const uint4 scw = ld16(raw + kSc + r * 16);
-    const __half2 sc2 = __float2half2_rn((float)(int8_t)byte_of(scw, 4 * j + p));  // scale of these 16 values
+__device__ __forceinline__ void dequant_q6(const uint8_t* raw, uint8_t* bt, int r, int p, int j, __half2 sc2) {
     // ql: bytes 64(j>>1) + 16p .. ; qh: bytes 32(j>>1) + 16(p&1) ..
     const int cl = (j >> 1) * 4 + p, ch = (j >> 1) * 2 + (p & 1);  // ql chunk 0..7, qh chunk 0..3
     const uint4 lq = ld16(raw + kQl + r * 128 + ((cl ^ (r & 7)) << 4));
@@ -581,14 +598,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         // A wait that gives up (bounded) stops this warp's work; the warps
         // agree at every super-block's barrier, so all leave the loop together.
         // Stage j of super-block i into its ring slot of B tiles.
+        __half2 sc4[4];  // this super-block's 4 scales of this thread (stage_scales)
         auto build = [&](const uint8_t* raw, int i, int j) {
             const int s = 4 * i + j, st = s % kStagesB;
             if (!warp_wait(b_empty + st, ((s / kStagesB) & 1) ^ 1, p.err, ERR_WAIT_TIMEOUT_EMPTY)) return false;
             uint8_t* bt = smem + kOffB + st * kStageB;
             if (q4)
-                dequant_q4(raw, bt, r, part, j);
+                dequant_q4(raw, bt, r, part, j, sc4[j]);
             else
-                dequant_q6(raw, bt, r, part, j);
+                dequant_q6(raw, bt, r, part, j, sc4[j]);
             fence_proxy_async();  // generic stores -> the MMA's async-proxy reads
             __syncwarp();
             if (lane == 0) mbar_arrive(b_full + st);
@@ -603,6 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int rs = i % kRawStages, b = b_begin + i;
             if (good) good = warp_wait(raw_full + rs, (i / kRawStages) & 1, p.err, ERR_WAIT_TIMEOUT_FULL);
             const uint8_t* raw = smem + kOffRaw + rs * kRawStage;
+            if (good) stage_scales(raw, type, r, part, sc4);
             for (int j = 0; j < 2 && good; ++j) good = build(raw, i, j);
             // every warp has written super-block i - 1's side factors and read
             // out super-block i - 2

@@ -58,56 +58,105 @@ def load_peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms."""
+    """nvidia-smi clocks and throttle reasons of every GPU of the job, one
+    sample per GPU every 200 ms, from ONE nvidia-smi process on rank 0 that
+    starts before the model is built: its start-up (about a second on an
+    8-GPU host, during which eight concurrent per-rank samplers were seen to
+    stall a tensor-parallel step) stays outside every timed region. Each timed
+    region registers a record with begin()/end(); stop() fills the records
+    from the samples stamped inside their regions."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, device: int):
-        self.device = device
+    def __init__(self, devices=()):
+        self.devices = list(devices)
         self.proc = None
-        self.t0 = self.t1 = None
+        self.records = []
+
+    @staticmethod
+    def gpu_ids(devices) -> list:
+        """nvidia-smi ids of CUDA devices: their UUIDs (CUDA_VISIBLE_DEVICES
+        renumbers devices, nvidia-smi does not), else the indices."""
+        try:
+            import torch
+
+            ids = []
+            for d in devices:
+                u = str(torch.cuda.get_device_properties(d).uuid)
+                ids.append(u if u.startswith("GPU-") else "GPU-" + u)
+            return ids
+        except Exception:
+            return [str(d) for d in devices]
 
     def start(self):
+        if not self.devices:
+            return
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200", "-i",
-                 str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 ",".join(self.gpu_ids(self.devices))], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
 
-    def mark(self, begin: bool):
-        if begin:
-            self.t0 = time.time()
-        else:
-            self.t1 = time.time()
+    def begin(self) -> dict:
+        rec = {"_t0": time.time()}
+        self.records.append(rec)
+        return rec
 
-    def stop(self) -> dict:
+    @staticmethod
+    def end(rec: dict):
+        rec["_t1"] = time.time()
+
+    @staticmethod
+    def _stamp(s: str) -> float:
+        import datetime
+
+        return datetime.datetime.strptime(s.strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+
+    def stop(self):
+        rows = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            for line in out.splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 10:
+                    continue
+                try:
+                    rows.append((self._stamp(parts[0]), float(parts[2]), float(parts[3]),
+                                 [p.lower().startswith("active") for p in parts[6:10]]))
+                except ValueError:
+                    continue
+        for rec in self.records:
+            t0, t1 = rec.pop("_t0"), rec.pop("_t1", time.time())
+            rec.update(self.summary(rows, t0, t1))
+
+    def summary(self, rows, t0, t1) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
-        rows = []
-        for line in out.splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append((float(parts[1]), float(parts[2]), parts[4:]))
-            except ValueError:
-                continue
-        if not rows:
+        inside = [r for r in rows if t0 - 0.05 <= r[0] <= t1 + 0.05]
+        where = "inside the timed region"
+        if not inside:
+            # a region shorter than the sampling period: the samples within
+            # half a second of it (warm-up before, the e2e loop after)
+            inside = [r for r in rows if t0 - 0.5 <= r[0] <= t1 + 0.5]
+            where = "within 0.5 s of the timed region (shorter than the 200 ms period)"
+        if not inside:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
-        loaded = [r for r in rows if r[0] > 0.5 * r[1]] or rows
-        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in loaded for i in range(1, 5) if r[2][i].lower().startswith("active")})
-        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(loaded)}
+        loaded = [r for r in inside if r[1] > 0.5 * r[2]] or inside
+        return {"sm_mhz": statistics.median(r[1] for r in loaded), "sm_max_mhz": max(r[2] for r in inside),
+                "reasons": sorted({self.REASONS[i] for r in loaded for i in range(4) if r[3][i]}),
+                "samples": len(loaded), "gpus": len(self.devices), "window": where}
+
+
+CLOCKS = ClockSampler()
 
 
 def dist_init():
@@ -371,13 +420,11 @@ def time_prefill(q, torch, eng, args, dist, local, peaks, world):
     for _ in range(warm):
         eng.prefill_seq(1, toks, 0)
     stream = torch.cuda.ExternalStream(eng.stream)
-    clocks = ClockSampler(local)
-    clocks.start()
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks.mark(True)
+    clk = CLOCKS.begin()
     t0 = time.perf_counter()
     ev0.record(stream)
     for _ in range(args.steps):
@@ -385,10 +432,9 @@ def time_prefill(q, torch, eng, args, dist, local, peaks, world):
     ev1.record(stream)
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
-    clocks.mark(False)
+    CLOCKS.end(clk)
     dev = max_over_ranks(torch, dist, ev0.elapsed_time(ev1) / 1e3) / args.steps
     wall = max_over_ranks(torch, dist, wall) / args.steps
-    clk = clocks.stop()
     return {"metric": "Qwen3-4B prompt prefill tok/s (512-token prompt, BASELINE configs[3])",
             "value": round(PREFILL_N / dev, 1), "unit": "tok/s", "steps": args.steps, "warmup": warm,
             "ms_per_step": round(dev * 1e3, 3), "higher_is_better": True,
@@ -451,13 +497,11 @@ def time_batch(q, torch, eng, args, dist, local, peaks, world):
     for _ in range(warm):
         toks, _ = eng.decode_batch(seqs, toks, pos)
     stream = torch.cuda.ExternalStream(eng.stream)
-    clocks = ClockSampler(local)
-    clocks.start()
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks.mark(True)
+    clk = CLOCKS.begin()
     t0 = time.perf_counter()
     ev0.record(stream)
     for _ in range(args.steps):
@@ -465,10 +509,9 @@ def time_batch(q, torch, eng, args, dist, local, peaks, world):
     ev1.record(stream)
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
-    clocks.mark(False)
+    CLOCKS.end(clk)
     dev = max_over_ranks(torch, dist, ev0.elapsed_time(ev1) / 1e3) / args.steps
     wall = max_over_ranks(torch, dist, wall) / args.steps
-    clk = clocks.stop()
     cfg = eng.cfg
     # bytes a step must stream per GPU: this rank's weights once, its KV heads
     # of every sequence up to its position
@@ -496,6 +539,32 @@ def time_batch(q, torch, eng, args, dist, local, peaks, world):
             "clocks": clk}
 
 
+def tp_exchange_us(recs, layers: int) -> dict:
+    """Cost of the fused all-reduce of a tensor-parallel decode step, from
+    traced steps (q4k_engine_trace: [launch][CTA][slot] %globaltimer ns).
+    A consumer of row-parallel partial sums (the QKV product of layers 1..,
+    every gate/up product, the head) records slot 1 when its dependency wait
+    returns and slot 5 once its activation, summed over the ranks' words, has
+    landed: the interval is the all-reduce's cost on the critical path (the
+    peers' words crossing NVLink, their skew, the loads), where one GPU only
+    loads the activation."""
+    per = []
+    consumers = [5 * l for l in range(1, layers)] + [5 * l + 3 for l in range(layers)] + [5 * layers]
+    for rec in recs:
+        rec = np.asarray(rec).astype(np.int64)
+        for launch in consumers:
+            r = rec[launch]
+            ok = (r[:, 1] > 0) & (r[:, 5] > 0)
+            if ok.any():
+                per.append(float(np.median(r[ok, 5] - r[ok, 1])) / 1e3)
+    if not per:
+        return {"us_per_allreduce": None, "allreduces_per_token": 2 * layers}
+    return {"us_per_allreduce": round(float(np.median(per)), 3), "allreduces_per_token": 2 * layers,
+            "us_p90": round(float(np.percentile(per, 90)), 3), "launches_sampled": len(per),
+            "how": "traced steps: a partial-sum consumer's dependency-wait return to its rank-summed activation "
+                   "landing, median over CTAs, then over the QKV, gate/up and head launches of 3 steps (rank 0)"}
+
+
 def run_decode(args, world, rank, local):
     import torch
 
@@ -514,23 +583,20 @@ def run_decode(args, world, rank, local):
     eng, cfg = make_engine(q, torch, world, rank, local, dist, sequences=BATCH)
 
     stream = torch.cuda.ExternalStream(eng.stream)
-    clocks = ClockSampler(local)
-    clocks.start()
     eng.generate(TOKEN0, POS, max(args.warmup, 3), advance=False, want_tokens=False)
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks.mark(True)
+    clk = CLOCKS.begin()
     ev0.record(stream)
     eng.generate(TOKEN0, POS, args.steps, advance=False, want_tokens=False)
     ev1.record(stream)
     torch.cuda.synchronize()
-    clocks.mark(False)
+    CLOCKS.end(clk)
     if dist:
         dist.barrier()
     secs = max_over_ranks(torch, dist, ev0.elapsed_time(ev1) / 1e3)
-    clk = clocks.stop()
 
     # e2e: the public API call per token, host buffers, H2D token+position,
     # D2H next token, synchronous (host wall clock, max over ranks)
@@ -543,6 +609,16 @@ def run_decode(args, world, rank, local):
     for _ in range(e2e_steps):
         tok, _, _ = eng.decode(tok, POS)
     e2e_secs = max_over_ranks(torch, dist, time.perf_counter() - t0)
+
+    # the fused all-reduce, as its consumer sees it: traced steps (every rank
+    # takes part; rank 0's records are read)
+    exchange = None
+    if dist:
+        recs = []
+        for _ in range(3):
+            dist.barrier()
+            recs.append(eng.trace(TOKEN0, POS))
+        exchange = tp_exchange_us(recs, cfg.layers)
 
     prefill = time_prefill(q, torch, eng, args, dist, local, peaks, world)
     batch = time_batch(q, torch, eng, args, dist, local, peaks, world)
@@ -605,6 +681,7 @@ def run_decode(args, world, rank, local):
                            "D2H of the token and the error word, stream sync), host wall clock"},
             "gpu_launches": kernels_per_step * args.steps,
             "clocks": clk,
+            "tp_exchange": exchange,
             "prefill": prefill,
             "batch": batch,
         }
@@ -648,12 +725,9 @@ def run_gemv(args, world, rank, local):
 
     torch.cuda.set_device(local)
     peaks = load_peaks()
-    clocks = ClockSampler(local)
-    clocks.start()
-    clocks.mark(True)
+    clk = CLOCKS.begin()
     t = time_gemv(q, torch, q.Q4_K, 2560, 9728, copies=20, reps=args.steps)
-    clocks.mark(False)
-    clk = clocks.stop()
+    CLOCKS.end(clk)
     b = gemv_bytes(q, q.Q4_K, 2560, 9728)
     gbs = b / t / 1e9
     return {"metric": METRIC_GEMV, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
@@ -842,6 +916,11 @@ def main() -> None:
             print(json.dumps(out), flush=True)
         return
 
+    if rank == 0 and args.workload != "step":
+        # one sampler for the job's GPUs (one process per GPU on one node:
+        # rank r drives local device r), started before any model is built
+        CLOCKS.devices = list(range(world)) if world > 1 else [local]
+        CLOCKS.start()
     if args.workload == "decode":
         out = run_decode(args, world, rank, local)
     elif args.workload == "step":
@@ -856,6 +935,7 @@ def main() -> None:
         out = run_batch(args, world, rank, local)
     else:
         out = run_gemv(args, world, rank, local)
+    CLOCKS.stop()
     if rank == 0 and out is not None:
         if world == 1 and args.workload in ("decode", "prefill", "batch") and not args.no_cpu_baseline:
             if args.workload == "decode":

@@ -412,14 +412,8 @@ __device__ __forceinline__ void quantise_rows(const float* x, int ldx, int m0, i
             for (int k = 0; k < kHeld; ++k) {
                 const int i = tid + k * nthreads;
                 if (i >= nvec) continue;
-                float4 sum = tagged_load4(parts + 4 * (size_t)i, parts_tag, wait_ns, err, err_code);
-                for (int r = 1; r < nparts; ++r) {
-                    const float4 t = tagged_load4(parts + (size_t)r * K + 4 * (size_t)i, parts_tag, wait_ns, err, err_code);
-                    sum.x += t.x;
-                    sum.y += t.y;
-                    sum.z += t.z;
-                    sum.w += t.w;
-                }
+                const float4 sum =
+                    sum_tagged4<kMaxRanks>(parts + 4 * (size_t)i, (size_t)K, nparts, parts_tag, wait_ns, err, err_code);
                 held[k].x += sum.x;
                 held[k].y += sum.y;
                 held[k].z += sum.z;

@@ -144,14 +144,7 @@ __global__ void residual_add_kernel(float* state, const float* branch, size_t co
 __global__ void tp_sum_parts_kernel(const unsigned long long* parts, int world, size_t n4, unsigned tag,
                                     const float* residual, float* out, unsigned long long wait_ns, int* err) {
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
-        float4 sum = tagged_load4(parts + 4 * i, tag, wait_ns, err, ERR_WAIT_TIMEOUT_PEER);
-        for (int r = 1; r < world; ++r) {
-            const float4 t = tagged_load4(parts + (size_t)r * 4 * n4 + 4 * i, tag, wait_ns, err, ERR_WAIT_TIMEOUT_PEER);
-            sum.x += t.x;
-            sum.y += t.y;
-            sum.z += t.z;
-            sum.w += t.w;
-        }
+        const float4 sum = sum_tagged4<kMaxRanks>(parts + 4 * i, 4 * n4, world, tag, wait_ns, err, ERR_WAIT_TIMEOUT_PEER);
         float4 x = residual ? reinterpret_cast<const float4*>(residual)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
         x.x += sum.x;
         x.y += sum.y;

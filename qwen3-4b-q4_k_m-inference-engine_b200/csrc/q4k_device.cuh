@@ -71,6 +71,52 @@ __device__ __forceinline__ float4 tagged_load4(const unsigned long long* p, unsi
                        __uint_as_float((unsigned)w3));
 }
 
+// Sum, in rank order, of the four (value, tag) words at p + r * stride of
+// ranks r < nparts (nparts <= kRanks). Every rank's words are loaded back to
+// back and their tags checked together, so the sum costs one memory round
+// trip when all words are there; tagged_load4 per rank is the wait for words
+// still in flight (no branch on a loaded value separates the first loads, which
+// a per-rank check would: one round trip per rank). Both paths add the ranks
+// in the same order, so the result does not depend on which one ran.
+template <int kRanks>
+__device__ __forceinline__ float4 sum_tagged4(const unsigned long long* p, size_t stride, int nparts, unsigned tag,
+                                              uint64_t limit_ns, int* err, int code) {
+    unsigned long long w[kRanks][4];
+#pragma unroll
+    for (int r = 0; r < kRanks; ++r) {
+        w[r][0] = w[r][1] = w[r][2] = w[r][3] = 0ull;
+        if (r < nparts) {
+            ld_words2(p + r * stride, w[r][0], w[r][1]);
+            ld_words2(p + r * stride + 2, w[r][2], w[r][3]);
+        }
+    }
+    bool ready = true;
+    float4 s = make_float4(__uint_as_float((unsigned)w[0][0]), __uint_as_float((unsigned)w[0][1]),
+                           __uint_as_float((unsigned)w[0][2]), __uint_as_float((unsigned)w[0][3]));
+#pragma unroll
+    for (int r = 0; r < kRanks; ++r) {
+        if (r >= nparts) break;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ready &= (unsigned)(w[r][j] >> 32) == tag;
+        if (r > 0) {
+            s.x += __uint_as_float((unsigned)w[r][0]);
+            s.y += __uint_as_float((unsigned)w[r][1]);
+            s.z += __uint_as_float((unsigned)w[r][2]);
+            s.w += __uint_as_float((unsigned)w[r][3]);
+        }
+    }
+    if (ready) return s;
+    s = tagged_load4(p, tag, limit_ns, err, code);
+    for (int r = 1; r < nparts; ++r) {
+        const float4 t = tagged_load4(p + r * stride, tag, limit_ns, err, code);
+        s.x += t.x;
+        s.y += t.y;
+        s.z += t.z;
+        s.w += t.w;
+    }
+    return s;
+}
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
 }

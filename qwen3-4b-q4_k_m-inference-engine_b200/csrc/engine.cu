@@ -116,7 +116,31 @@ __global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* logits, 
     const float* row = logits + (size_t)blockIdx.x * vocab;
     float bs = -CUDART_INF_F;
     uint32_t bi = 0xFFFFFFFFu;
-    for (int i = threadIdx.x; i < vocab; i += blockDim.x)
+    // four running candidates per thread over 16-byte loads keep several
+    // loads in flight per thread (one CTA per row streams its 0.6 MB row);
+    // candidate_better orders ties by index, so the merge order is free
+    const int n4 = (reinterpret_cast<uintptr_t>(row) & 15u) == 0 ? vocab / 4 : 0;
+    const float4* row4 = reinterpret_cast<const float4*>(row);
+    float cs[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
+    uint32_t ci[4] = {0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu};
+#pragma unroll 4
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        const float4 v = __ldcs(row4 + i);
+        const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            if (candidate_better(e[c], (uint32_t)(4 * i + c), cs[c], ci[c])) {
+                cs[c] = e[c];
+                ci[c] = (uint32_t)(4 * i + c);
+            }
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        if (candidate_better(cs[c], ci[c], bs, bi)) {
+            bs = cs[c];
+            bi = ci[c];
+        }
+    for (int i = 4 * n4 + threadIdx.x; i < vocab; i += blockDim.x)
         if (candidate_better(row[i], (uint32_t)i, bs, bi)) {
             bs = row[i];
             bi = (uint32_t)i;

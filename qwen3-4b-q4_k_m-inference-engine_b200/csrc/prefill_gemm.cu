@@ -54,8 +54,8 @@ namespace {
 constexpr int BM = 128;                  // activation rows per CTA (MMA M)
 constexpr int BN = 128;                  // output columns per CTA (MMA N, TMEM columns per accumulator)
 constexpr int KS = 64;                   // K per stage: one 128-byte swizzle row of fp16
-constexpr int kStagesA = 3;              // activation stages (hi + lo boxes each)
-constexpr int kStagesB = 3;              // weight-operand stages
+constexpr int kStagesA = 2;              // activation stages (hi + lo boxes each)
+constexpr int kStagesB = 4;              // weight-operand stages (4 x 16 KB with 2 activation stages measured +1.8% batched decode, +2.7% prefill over 3 + 3)
 constexpr int kRawStages = 2;            // raw weight super-block stages (the slice is prefetched to L2)
 constexpr int kDeqWarps = 16;
 constexpr int kThreads = (3 + kDeqWarps) * 32;  // A producer, MMA, raw producer, operand builders

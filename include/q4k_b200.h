@@ -144,11 +144,16 @@ size_t q4k_matmul_argmax_scratch_bytes(void);
  * kernels::matmul with rows = n prompt tokens, src/Engine.cpp:83-101) on the
  * tensor cores (tcgen05, fp32 accumulation in tensor memory). Each row is
  * Q8-quantised as the reference does (after RMSNorm with norm_gamma, if
- * given); the codes times their scales and the dequantised weights meet as
- * fp16 (2^-11 relative rounding of each) instead of in an integer dot.
+ * given); the codes times their scales enter the tensor cores as fp16 hi +
+ * lo parts against the exact integer products of the weight codes and
+ * sub-block scales, and each super-block's d / dmin are applied in fp32, so
+ * a product stays within ~1e-6 of the reference's integer dots.
  * count: 1..3 weights; outputs[i][m * ld_out + n] (SWIGLU: two weights of one
  * type and shape, output in outputs[0]). epilogue: Q4K_EPI_STORE, _ADD or
- * _SWIGLU. ne0 <= 10240. Allocates its workspace on the stream. */
+ * _SWIGLU. ne0 <= 10240. Allocates its workspace on the stream. Its kernels
+ * launch with programmatic dependent launch: the first may start while the
+ * stream's previous kernel runs, but reads its inputs (and writes its
+ * outputs) only after that kernel has completed. */
 int q4k_matmul_batch(const float* input, const float* norm_gamma, float epsilon, int count, const void* const* weights,
                      const int* types, const int64_t* out_rows, float* const* outputs, int64_t ld_out, int64_t ne0,
                      size_t rows, int epilogue, void* stream);
